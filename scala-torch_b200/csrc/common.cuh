@@ -1,0 +1,138 @@
+// Shared internals of libstb200.so: status plumbing, the session object, small device helpers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstdio>
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <thread>
+
+#include "../../include/stb200.h"
+
+namespace stb {
+
+// Error carried to the C boundary as a status code plus a thread-local message.
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+
+void set_last_error(const std::string &msg);
+
+#define STB_REQUIRE(cond, msg)                                      \
+  do {                                                              \
+    if (!(cond)) throw ::stb::Error(STB_ERR_INVALID, (msg));        \
+  } while (0)
+
+#define STB_CUDA(call)                                                                       \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      throw ::stb::Error(STB_ERR_CUDA, std::string(#call) + " failed: " + cudaGetErrorString(e_)); \
+  } while (0)
+
+// Runs `body` and maps every exception to a status; nothing escapes the C ABI.
+template <typename F>
+int guarded(F &&body) {
+  try {
+    body();
+    set_last_error("");
+    return STB_OK;
+  } catch (const Error &e) {
+    set_last_error(e.what());
+    return e.code;
+  } catch (const std::bad_alloc &) {
+    set_last_error("host allocation failed");
+    return STB_ERR_BUDGET;
+  } catch (const std::exception &e) {
+    set_last_error(e.what());
+    return STB_ERR_CUDA;
+  } catch (...) {
+    set_last_error("unknown failure");
+    return STB_ERR_CUDA;
+  }
+}
+
+}  // namespace stb
+
+struct stb_session {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint64_t max_bytes = 0, allocated = 0;
+  std::map<uint64_t, uint64_t> allocations;  // device address -> bytes
+  std::thread::id owner;
+  void *staging = nullptr;  // pinned host staging for pageable transfers
+  uint64_t staging_bytes = 0;
+  cudaEvent_t staging_done[2] = {nullptr, nullptr};
+  void *nccl = nullptr;  // ncclComm_t
+  int tp_rank = 0, tp_size = 1;
+  std::atomic<uint64_t> launches{0};
+  bool closed = false;
+};
+
+namespace stb {
+
+// Validates a session handle, its owner thread, and makes its device current.
+void enter(stb_session *s);
+uint64_t session_alloc(stb_session *s, uint64_t bytes);
+void session_free(stb_session *s, uint64_t ptr);
+inline void count_launch(stb_session *s, uint64_t n = 1) { s->launches += n; }
+void check_launch(const char *what);
+void upload(stb_session *s, const void *host, uint64_t bytes, uint64_t dst);
+void download(stb_session *s, uint64_t src, void *host, uint64_t bytes);
+void fill_normal(stb_session *s, uint64_t dst, int dtype, uint64_t count, uint64_t seed, uint64_t stream,
+                 double stddev);
+void fill_value(stb_session *s, uint64_t dst, int dtype, uint64_t count, float value);
+
+// ---------------------------------------------------------------- device helpers
+
+__device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Widen two packed half words (low half first in memory) to Float32, exactly.
+template <typename WT>
+__device__ __forceinline__ float2 widen2(uint32_t u);
+
+template <>
+__device__ __forceinline__ float2 widen2<__nv_bfloat16>(uint32_t u) {
+  // SafeTensors.scala:72: bits << 16 is the Float32 with the same value.
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+
+template <>
+__device__ __forceinline__ float2 widen2<__half>(uint32_t u) {
+  __half2 h = *reinterpret_cast<__half2 *>(&u);
+  return __half22float2(h);
+}
+
+template <typename WT>
+__device__ __forceinline__ float widen1(uint16_t u);
+template <>
+__device__ __forceinline__ float widen1<__nv_bfloat16>(uint16_t u) {
+  return __uint_as_float(((uint32_t)u) << 16);
+}
+template <>
+__device__ __forceinline__ float widen1<__half>(uint16_t u) {
+  return __half2float(__ushort_as_half(u));
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float value) {
+  // SafeTensorsWriter.scala:58-61.
+  uint32_t bits = __float_as_uint(value);
+  if ((bits & 0x7f800000u) == 0x7f800000u && (bits & 0x007fffffu) != 0)
+    return (uint16_t)((bits >> 16) | 0x40u);
+  return (uint16_t)((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);
+}
+
+}  // namespace stb

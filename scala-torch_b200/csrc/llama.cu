@@ -1,0 +1,1008 @@
+// Llama decode runtime: the prepared, resident model of BackendLlama (models/src/main/scala/
+// scalatorch/models/BackendLlama.scala) with its resident KV cache (BackendLlamaCache.scala),
+// rebuilt around the B200 GEMV family.
+//
+// Per layer the reference runs ~20 separate backend ops with a stream synchronisation after each
+// (CudaSession.scala:829-850).  Here one layer is five launches on the session stream:
+//   1. QKV GEMV: input RMSNorm prologue, RoPE + KV-cache append epilogue  (q,k,v rows paired)
+//   2. causal GQA attention over the HBM-resident cache (double accumulation as CpuAttention)
+//   3. O GEMV with the residual add fused (h = x + attn)
+//   4. gate/up GEMV: post RMSNorm prologue, SiLU(gate)*up epilogue (interleaved rows)
+//   5. down GEMV with the residual add fused
+// then the final-norm + lm_head GEMV with per-block greedy candidates and one finalize kernel that
+// picks the token (TokenSampler strict '>'), feeds it back as the next input, appends it to the
+// output and advances the device-side position.  A decode step therefore needs no host
+// interaction and is captured once as a CUDA graph and replayed per generated token.
+//
+// Tensor parallel (tp_size > 1): q/k/v/gate/up are split by output rows (heads / intermediate),
+// o/down by input columns; each row-split projection's partial sums are joined by one NCCL
+// allreduce which also carries the residual (rank 0 adds it before the reduction).  lm_head is
+// split by vocabulary; ranks exchange their (value, index) candidates with one allgather.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "gemv.cuh"
+#include "rng.cuh"
+
+namespace stb {
+void allreduce_sum_f32(stb_session *s, void *buf, uint64_t count);
+void allgather_bytes(stb_session *s, const void *send, void *recv, uint64_t bytes);
+}  // namespace stb
+
+using namespace stb;
+
+namespace {
+
+struct Layer {
+  uint64_t in_norm = 0, post_norm = 0;  // f32 [H]
+  uint64_t qkv = 0;                     // half [(nh+2kv)*hd][H], rows paired (d, d+hd/2)
+  uint64_t o = 0;                       // half [H][nh*hd] (this rank's input columns)
+  uint64_t gu = 0;                      // half [2*I][H], rows interleaved gate/up
+  uint64_t down = 0;                    // half [H][I] (this rank's input columns)
+};
+
+}  // namespace
+
+struct stb_llama {
+  stb_session *s = nullptr;
+  stb_llama_config c{};
+  int H = 0, NH = 0, KV = 0, hd = 0, I = 0, V = 0;  // local (this rank) sizes; H full
+  int v0 = 0;                                       // vocabulary offset of this rank's lm_head rows
+  int rank = 0, tp = 1;
+  uint64_t embed = 0, final_norm = 0, lm_head = 0;  // lm_head may alias embed (tied, tp == 1)
+  bool head_aliases_embed = false;
+  std::vector<Layer> layers;
+  uint64_t rope = 0;  // double2 [max_positions][hd/2]
+  std::vector<uint64_t> owned;
+  uint64_t weight_bytes = 0;
+  bool weights_ready[16] = {};
+};
+
+struct stb_llama_cache {
+  stb_llama *m = nullptr;
+  int batch = 0, capacity = 0, used = 0;
+  uint64_t kv = 0;  // [layers][2][batch][kvh][capacity][hd] f32
+  // scratch sized for `rows` token rows
+  int rows = 0, parts = 0;
+  uint64_t hidden = 0, qbuf = 0, att = 0, act = 0, sum = 0, logits = 0, pval = 0, pidx = 0, gval = 0, gidx = 0;
+  uint64_t tokens = 0;  // int64 [rows]
+  uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
+  uint64_t out_ids = 0;
+  int out_stride = 0;
+  uint64_t eos = 0;
+  int eos_count = 0;
+  cudaGraphExec_t graph = nullptr;
+  int graph_nodes = 0;
+  std::vector<uint64_t> owned;
+};
+
+namespace {
+
+uint64_t alloc_owned(stb_session *s, std::vector<uint64_t> &owned, uint64_t bytes) {
+  uint64_t p = session_alloc(s, bytes);
+  owned.push_back(p);
+  return p;
+}
+
+void free_owned(stb_session *s, std::vector<uint64_t> &owned) {
+  for (auto it = owned.rbegin(); it != owned.rend(); ++it) {
+    try {
+      session_free(s, *it);
+    } catch (...) {
+    }
+  }
+  owned.clear();
+}
+
+size_t esize(int dtype) { return dtype == STB_F32 ? 4 : 2; }
+
+// ---------------------------------------------------------------- kernels
+
+__global__ void embed_kernel(const int64_t *tokens, const uint16_t *table, int dtype, int H, int V, float *hidden,
+                             int rows, const int *stop) {
+  if (stop && *stop) return;
+  const int m = blockIdx.x;
+  if (m >= rows) return;
+  int64_t id = tokens[m];
+  if (id < 0 || id >= V) id = 0;  // host validates; device-fed ids come from argmax over [0, V)
+  const uint16_t *src = table + (size_t)id * H;
+  for (int k = threadIdx.x; k < H; k += blockDim.x)
+    hidden[(size_t)m * H + k] = dtype == STB_BF16 ? widen1<__nv_bfloat16>(src[k]) : widen1<__half>(src[k]);
+}
+
+// Causal grouped-query attention of CpuAttention.causal (cpu/.../CpuAttention.scala:20-50):
+// scores, softmax and the weighted value sum in double; one block per (token row, query head).
+__global__ void attention_kernel(const float *q, int ldq, const float *kcache, const float *vcache, float *out,
+                                 int ldo, int rows, int count, int nh, int kvh, int hd, int capacity,
+                                 const int *pos_dev, int pos0, const int *stop) {
+  extern __shared__ double s_p[];  // [capacity] scores, then 32 reduction slots
+  if (stop && *stop) return;
+  const int m = blockIdx.x / nh, h = blockIdx.x % nh;
+  if (m >= rows) return;
+  const int b = m / count, t = m % count;
+  const int pos = (pos_dev ? *pos_dev : pos0) + t;
+  const int keys = pos + 1;
+  const int g = h / (nh / kvh);
+  const float *qr = q + (size_t)m * ldq + (size_t)h * hd;
+  const size_t base = ((size_t)b * kvh + g) * capacity;
+  const float *K = kcache + base * hd;
+  const float *Vc = vcache + base * hd;
+  double *red = s_p + capacity;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const double scale = 1.0 / sqrt((double)hd);
+  double local_max = -(double)INFINITY;
+  for (int j = warp; j < keys; j += nwarps) {
+    double dot = 0.0;
+    for (int d = lane; d < hd; d += 32) dot += (double)qr[d] * (double)K[(size_t)j * hd + d];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const double sc = dot * scale;
+    if (lane == 0) s_p[j] = sc;
+    local_max = fmax(local_max, sc);
+  }
+  if (lane == 0) red[warp] = local_max;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double mx = red[0];
+    for (int i = 1; i < nwarps; i++) mx = fmax(mx, red[i]);
+    red[0] = mx;
+  }
+  __syncthreads();
+  const double mx = red[0];
+  __syncthreads();
+  for (int j = threadIdx.x; j < keys; j += blockDim.x) s_p[j] = exp(s_p[j] - mx);
+  __syncthreads();
+  if (threadIdx.x == 0) {  // sequential denominator, as the reference
+    double den = 0.0;
+    for (int j = 0; j < keys; j++) den += s_p[j];
+    red[0] = den;
+  }
+  __syncthreads();
+  const double den = red[0];
+  for (int j = threadIdx.x; j < keys; j += blockDim.x) s_p[j] = s_p[j] / den;
+  __syncthreads();
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    double sum = 0.0;
+    for (int j = 0; j < keys; j++) sum += s_p[j] * (double)Vc[(size_t)j * hd + d];
+    out[(size_t)m * ldo + (size_t)h * hd + d] = (float)sum;
+  }
+}
+
+// Greedy pick over every rank's per-block candidates (strict '>' in increasing id order, i.e.
+// lowest id on ties), token feedback, output append, EOS stop and position advance.
+__global__ void finalize_kernel(const float *pval, const int *pidx, int nparts_total, int batch, int count,
+                                int64_t *tokens, int *state, int64_t *out_ids, int out_stride, const int64_t *eos,
+                                int eos_count, int64_t *next_ids, int advance) {
+  if (state[1]) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  int *stopped = state + 2;
+  int *out_count = state + 2 + batch;
+  for (int b = warp; b < batch; b += nwarps) {
+    float best = 0.0f;
+    int besti = -1;
+    for (int i = lane; i < nparts_total; i += 32) {
+      const float v = pval[(size_t)b * nparts_total + i];
+      const int id = pidx[(size_t)b * nparts_total + i];
+      if (id < 0) continue;
+      if (besti < 0 || v > best || (v == best && id < besti)) {
+        best = v;
+        besti = id;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, besti, off);
+      if (oi >= 0 && (besti < 0 || ov > best || (ov == best && oi < besti))) {
+        best = ov;
+        besti = oi;
+      }
+    }
+    if (lane == 0) {
+      if (next_ids) next_ids[b] = besti;
+      if (out_ids && !stopped[b]) {
+        out_ids[(size_t)b * out_stride + out_count[b]] = besti;
+        out_count[b] += 1;
+        for (int e = 0; e < eos_count; e++)
+          if (eos[e] == besti) stopped[b] = 1;
+      }
+      tokens[(size_t)b * count + (count - 1)] = besti;  // next step's input (count == 1 in decode)
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (advance) state[0] += advance;
+    if (out_ids) {
+      int all = 1;
+      for (int b = 0; b < batch; b++) all &= stopped[b];
+      state[1] = all;
+    }
+  }
+}
+
+// dst[i][j] = widen/copy of src[rowmap[i]][col0 + j] (half -> half).  Packs a full (out,in) tensor
+// into this rank's fused layout (paired q/k/v rows, interleaved gate/up rows, column shards).
+__global__ void pack_rows_kernel(uint16_t *dst, const uint16_t *src, const uint32_t *rowmap, int rows, int cols,
+                                 int src_cols, int col0) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)rows * cols;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    dst[i] = src[(size_t)rowmap[r] * src_cols + col0 + c];
+  }
+}
+
+}  // namespace
+
+namespace {
+
+// Same generator as stb_fill_normal, addressed by (stream_i, logical_row_i * src_cols + col0 + j).
+__global__ void fill_rows_kernel(void *dst, int dtype, const uint64_t *rowmap, int rows, int cols, int src_cols,
+                                 int col0, uint64_t seed, double stddev) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)rows * cols;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    const uint64_t stream = rowmap[r] >> 32, lrow = rowmap[r] & 0xffffffffULL;
+    const float v = __double2float_rn(
+        __dmul_rn(stddev, rng_normal_dev(seed, stream, lrow * (uint64_t)src_cols + (uint64_t)(col0 + c))));
+    if (dtype == STB_BF16) ((uint16_t *)dst)[i] = f32_to_bf16_rne(v);
+    else ((__half *)dst)[i] = __float2half_rn(v);
+  }
+}
+
+unsigned grid_for(size_t n) {
+  size_t b = (n + 255) / 256;
+  return (unsigned)(b > 148 * 32 ? 148 * 32 : (b ? b : 1));
+}
+
+// ---------------------------------------------------------------- layout maps
+
+enum Which { W_EMBED = 0, W_FINAL = 1, W_HEAD = 2, W_IN = 3, W_POST = 4, W_Q = 5, W_K = 6, W_V = 7, W_O = 8,
+             W_GATE = 9, W_UP = 10, W_DOWN = 11 };
+
+uint64_t stream_of(int which, int layer) {
+  return (which == W_EMBED || which == W_FINAL || which == W_HEAD) ? 4096ull + which : (uint64_t)layer * 16 + which;
+}
+
+// Physical row -> (logical tensor, logical row) for the paired QKV layout of this rank.
+void qkv_rowmap(const stb_llama *m, std::vector<int> &which, std::vector<uint32_t> &lrow) {
+  const int half = m->hd / 2;
+  const int rows = (m->NH + 2 * m->KV) * m->hd;
+  which.assign(rows, 0);
+  lrow.assign(rows, 0);
+  const int h0q = m->rank * m->NH, h0k = m->rank * m->KV;
+  for (int pi = 0; pi < rows / 2; pi++) {
+    int w, head, d;
+    if (pi < m->NH * half) {
+      w = W_Q; head = h0q + pi / half; d = pi % half;
+    } else if (pi < (m->NH + m->KV) * half) {
+      const int l = pi - m->NH * half;
+      w = W_K; head = h0k + l / half; d = l % half;
+    } else {
+      const int l = pi - (m->NH + m->KV) * half;
+      w = W_V; head = h0k + l / half; d = l % half;
+    }
+    which[2 * pi] = which[2 * pi + 1] = w;
+    lrow[2 * pi] = (uint32_t)(head * m->hd + d);
+    lrow[2 * pi + 1] = (uint32_t)(head * m->hd + d + half);
+  }
+}
+
+void gu_rowmap(const stb_llama *m, std::vector<int> &which, std::vector<uint32_t> &lrow) {
+  which.assign(2 * m->I, 0);
+  lrow.assign(2 * m->I, 0);
+  const int i0 = m->rank * m->I;
+  for (int i = 0; i < m->I; i++) {
+    which[2 * i] = W_GATE;
+    which[2 * i + 1] = W_UP;
+    lrow[2 * i] = lrow[2 * i + 1] = (uint32_t)(i0 + i);
+  }
+}
+
+struct Target {
+  uint64_t dst;
+  int rows, cols, src_cols, col0;
+  std::vector<int> which;
+  std::vector<uint32_t> lrow;
+};
+
+// Where a named full tensor lands in this rank's resident layout.
+Target target_of(stb_llama *m, int which, int layer) {
+  Target t{};
+  const int H = m->H;
+  auto ident = [&](int rows, int row0) {
+    t.which.assign(rows, which);
+    t.lrow.resize(rows);
+    for (int i = 0; i < rows; i++) t.lrow[i] = (uint32_t)(row0 + i);
+  };
+  switch (which) {
+    case W_EMBED:
+      t.dst = m->embed; t.rows = m->c.vocab_size; t.cols = H; t.src_cols = H; t.col0 = 0; ident(t.rows, 0);
+      break;
+    case W_HEAD:
+      t.dst = m->lm_head; t.rows = m->V; t.cols = H; t.src_cols = H; t.col0 = 0; ident(t.rows, m->v0);
+      break;
+    case W_Q: case W_K: case W_V:
+      t.dst = m->layers[layer].qkv; t.rows = (m->NH + 2 * m->KV) * m->hd; t.cols = H; t.src_cols = H; t.col0 = 0;
+      qkv_rowmap(m, t.which, t.lrow);
+      break;
+    case W_O:
+      t.dst = m->layers[layer].o; t.rows = H; t.cols = m->NH * m->hd; t.src_cols = m->c.hidden_size;
+      t.col0 = m->rank * m->NH * m->hd; ident(H, 0);
+      break;
+    case W_GATE: case W_UP:
+      t.dst = m->layers[layer].gu; t.rows = 2 * m->I; t.cols = H; t.src_cols = H; t.col0 = 0;
+      gu_rowmap(m, t.which, t.lrow);
+      break;
+    case W_DOWN:
+      t.dst = m->layers[layer].down; t.rows = H; t.cols = m->I; t.src_cols = m->c.intermediate_size;
+      t.col0 = m->rank * m->I; ident(H, 0);
+      break;
+    default:
+      throw Error(STB_ERR_INVALID, "not a matrix weight");
+  }
+  return t;
+}
+
+uint64_t logical_rows(const stb_llama *m, int which) {
+  const auto &c = m->c;
+  const int hd = c.hidden_size / c.num_attention_heads;
+  switch (which) {
+    case W_EMBED: case W_HEAD: return c.vocab_size;
+    case W_Q: case W_O: case W_DOWN: case W_FINAL: case W_IN: case W_POST: return c.hidden_size;
+    case W_K: case W_V: return (uint64_t)c.num_key_value_heads * hd;
+    case W_GATE: case W_UP: return c.intermediate_size;
+  }
+  return 0;
+}
+uint64_t logical_cols(const stb_llama *m, int which) {
+  const auto &c = m->c;
+  if (which == W_FINAL || which == W_IN || which == W_POST) return 1;
+  if (which == W_DOWN) return c.intermediate_size;
+  return c.hidden_size;
+}
+
+// ---------------------------------------------------------------- cache scratch & steps
+
+void ensure_rows(stb_llama_cache *c, int rows) {
+  stb_llama *m = c->m;
+  stb_session *s = m->s;
+  if (rows <= c->rows) return;
+  // grow: free old scratch (not the KV cache), drop the graph
+  if (c->graph) {
+    cudaGraphExecDestroy(c->graph);
+    c->graph = nullptr;
+  }
+  const uint64_t kv = c->kv;
+  std::vector<uint64_t> keep;
+  for (uint64_t p : c->owned)
+    if (p == kv) keep.push_back(p);
+    else session_free(s, p);
+  c->owned = keep;
+  // candidate slots per row: the most row blocks any lm_head launch shape of <= rows rows uses
+  c->parts = 0;
+  for (int mm : {1, 2, 4, 8, c->batch, rows})
+    if (mm <= rows) c->parts = std::max(c->parts, gemv_row_blocks(m->V, choose_gemv(mm, m->V, m->H, false)));
+  const int qw = m->NH * m->hd;
+  c->hidden = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
+  c->sum = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
+  c->qbuf = alloc_owned(s, c->owned, (uint64_t)rows * qw * 4);
+  c->att = alloc_owned(s, c->owned, (uint64_t)rows * qw * 4);
+  c->act = alloc_owned(s, c->owned, (uint64_t)rows * m->I * 4);
+  c->logits = alloc_owned(s, c->owned, (uint64_t)rows * m->V * 4);
+  c->pval = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4);
+  c->pidx = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4);
+  c->gval = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
+  c->gidx = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
+  c->tokens = alloc_owned(s, c->owned, (uint64_t)rows * 8);
+  c->state = alloc_owned(s, c->owned, (uint64_t)(2 + 2 * c->batch) * 4);
+  c->rows = rows;
+}
+
+struct StepArgs {
+  int rows, count;          // token rows in this chunk and tokens per batch row
+  bool device_pos;          // read position from state[0] (graph) instead of c->used
+  bool all_logits;          // logits for every row (decode API) or only each batch row's last token
+  int64_t *next_ids = nullptr;
+  bool append = false;      // append picks to out_ids (generation)
+  int advance = 0;          // position increment done on device
+};
+
+// Enqueues one forward chunk on the session stream.
+int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
+  stb_llama *m = c->m;
+  stb_session *s = m->s;
+  cudaStream_t st = s->stream;
+  const int H = m->H, rows = a.rows;
+  const int *state = (const int *)c->state;
+  const int *stop = a.append ? state + 1 : nullptr;
+  const int *posd = a.device_pos ? state : nullptr;
+  int launches = 0;
+  const int wdt = m->c.weight_dtype;
+
+  embed_kernel<<<rows, 128, 0, st>>>((const int64_t *)c->tokens, (const uint16_t *)m->embed, wdt, H,
+                                     m->c.vocab_size, (float *)c->hidden, rows, stop);
+  check_launch("embed");
+  launches++;
+  const float eps = 0;  // unused
+  (void)eps;
+  const size_t kv_layer = (size_t)2 * c->batch * m->KV * c->capacity * m->hd;
+  const size_t kv_half = kv_layer / 2;
+  const int qw = m->NH * m->hd;
+  for (size_t l = 0; l < m->layers.size(); l++) {
+    const Layer &L = m->layers[l];
+    float *kc = (float *)c->kv + l * kv_layer;
+    float *vc = kc + kv_half;
+    {  // 1. QKV + RoPE + cache append
+      GemvParams p;
+      p.x = (const float *)c->hidden; p.ldx = H; p.w = (const void *)L.qkv;
+      p.M = rows; p.N = (m->NH + 2 * m->KV) * m->hd; p.K = H;
+      p.y = (float *)c->qbuf; p.ldy = qw;
+      p.norm_w = (const float *)L.in_norm; p.norm_eps = m->c.rms_norm_eps;
+      p.rope = (const double2 *)m->rope; p.pos_dev = posd; p.pos0 = c->used; p.count = a.count;
+      p.nh = m->NH; p.kvh = m->KV; p.hd = m->hd; p.capacity = c->capacity; p.k_cache = kc; p.v_cache = vc;
+      p.stop = stop;
+      launch_gemv<EPI_QKV>(p, wdt, choose_gemv(rows, p.N, p.K, true), st);
+      launches++;
+    }
+    {  // 2. attention
+      const size_t smem = (size_t)(c->capacity + 32) * sizeof(double);
+      attention_kernel<<<rows * m->NH, 128, smem, st>>>((const float *)c->qbuf, qw, kc, vc, (float *)c->att, qw,
+                                                        rows, a.count, m->NH, m->KV, m->hd, c->capacity, posd,
+                                                        c->used, stop);
+      check_launch("attention");
+      launches++;
+    }
+    for (int half = 0; half < 2; half++) {  // 3. O (+residual)   then   4./5. MLP (+residual)
+      if (half == 1) {
+        GemvParams p;
+        p.x = (const float *)c->hidden; p.ldx = H; p.w = (const void *)L.gu;
+        p.M = rows; p.N = 2 * m->I; p.K = H;
+        p.y = (float *)c->act; p.ldy = m->I;
+        p.norm_w = (const float *)L.post_norm; p.norm_eps = m->c.rms_norm_eps;
+        p.stop = stop;
+        launch_gemv<EPI_SILU>(p, wdt, choose_gemv(rows, p.N, p.K, true), st);
+        launches++;
+      }
+      GemvParams p;
+      p.x = (const float *)(half == 0 ? c->att : c->act);
+      p.ldx = half == 0 ? qw : m->I;
+      p.w = (const void *)(half == 0 ? L.o : L.down);
+      p.M = rows; p.N = H; p.K = half == 0 ? qw : m->I;
+      p.stop = stop;
+      if (m->tp == 1) {
+        p.y = (float *)c->hidden; p.ldy = H; p.residual = (const float *)c->hidden; p.ldr = H;
+        launch_gemv<EPI_RESID>(p, wdt, choose_gemv(rows, p.N, p.K, false), st);
+        launches++;
+      } else {
+        p.y = (float *)c->sum; p.ldy = H;
+        if (m->rank == 0) {
+          p.residual = (const float *)c->hidden; p.ldr = H;
+          launch_gemv<EPI_RESID>(p, wdt, choose_gemv(rows, p.N, p.K, false), st);
+        } else {
+          launch_gemv<EPI_PLAIN>(p, wdt, choose_gemv(rows, p.N, p.K, false), st);
+        }
+        launches++;
+        allreduce_sum_f32(s, (void *)c->sum, (uint64_t)rows * H);
+        std::swap(c->hidden, c->sum);
+      }
+    }
+  }
+  // final norm + lm_head (+ greedy candidates)
+  const int brows = a.all_logits ? rows : c->batch;
+  {
+    GemvParams p;
+    if (a.all_logits) {
+      p.x = (const float *)c->hidden; p.ldx = H;
+    } else {
+      p.x = (const float *)c->hidden + (size_t)(a.count - 1) * H; p.ldx = a.count * H;
+    }
+    p.w = (const void *)m->lm_head;
+    p.M = brows; p.N = m->V; p.K = H;
+    p.y = (float *)c->logits; p.ldy = m->V;
+    p.norm_w = (const float *)m->final_norm; p.norm_eps = m->c.rms_norm_eps;
+    p.part_val = (float *)c->pval; p.part_idx = (int *)c->pidx; p.row_offset = m->v0;
+    p.stop = stop;
+    GemvConfig cfg = choose_gemv(brows, p.N, p.K, false);
+    const int parts = launch_gemv<EPI_LOGITS>(p, wdt, cfg, st);
+    launches++;
+    if (parts != c->parts && !a.all_logits) {
+      // candidate buffers are sized for c->parts per row; configs for fewer rows never exceed it
+    }
+    const float *gv = (const float *)c->pval;
+    const int *gi = (const int *)c->pidx;
+    int nparts = parts;
+    if (!a.all_logits && m->tp > 1) {
+      // [rank][batch][parts] after the gather; re-laid as [batch][rank*parts] by reading strided
+      allgather_bytes(s, (const void *)c->pval, (void *)c->gval, (uint64_t)brows * parts * 4);
+      allgather_bytes(s, (const void *)c->pidx, (void *)c->gidx, (uint64_t)brows * parts * 4);
+      gv = (const float *)c->gval;
+      gi = (const int *)c->gidx;
+      nparts = parts;  // handled by finalize via per-rank stride below
+    }
+    if (!a.all_logits || a.next_ids) {
+      if (m->tp > 1 && !a.all_logits) {
+        // finalize over rank-major candidates: treat [rank][batch][parts] as batch-major by running
+        // one finalize per rank would lose the cross-rank max, so transpose through a tiny copy.
+        // (For batch rows b, the candidates of all ranks are at r*brows*parts + b*parts + i.)
+        for (int r = 0; r < m->tp; r++)
+          STB_CUDA(cudaMemcpy2DAsync((void *)(c->pval + (uint64_t)r * parts * 4), (size_t)m->tp * parts * 4,
+                                     (const void *)((const char *)gv + (size_t)r * brows * parts * 4),
+                                     (size_t)parts * 4, (size_t)parts * 4, brows, cudaMemcpyDeviceToDevice, st));
+        for (int r = 0; r < m->tp; r++)
+          STB_CUDA(cudaMemcpy2DAsync((void *)(c->pidx + (uint64_t)r * parts * 4), (size_t)m->tp * parts * 4,
+                                     (const void *)((const char *)gi + (size_t)r * brows * parts * 4),
+                                     (size_t)parts * 4, (size_t)parts * 4, brows, cudaMemcpyDeviceToDevice, st));
+        gv = (const float *)c->pval;
+        gi = (const int *)c->pidx;
+        nparts = parts * m->tp;
+      }
+      finalize_kernel<<<1, 256, 0, st>>>(gv, gi, nparts, brows, a.all_logits ? 1 : a.count, (int64_t *)c->tokens,
+                                         (int *)c->state, a.append ? (int64_t *)c->out_ids : nullptr,
+                                         c->out_stride, (const int64_t *)c->eos, c->eos_count, a.next_ids,
+                                         a.advance);
+      check_launch("finalize");
+      launches++;
+    }
+  }
+  return launches;
+}
+
+void check_config(const stb_llama_config &c) {
+  STB_REQUIRE(c.vocab_size > 0 && c.hidden_size > 0 && c.intermediate_size > 0 && c.num_layers > 0 &&
+                  c.max_positions > 0,
+              "invalid Llama dimensions");
+  STB_REQUIRE(c.num_attention_heads > 0 && c.num_key_value_heads > 0 &&
+                  c.hidden_size % c.num_attention_heads == 0 && c.num_attention_heads % c.num_key_value_heads == 0,
+              "invalid Llama head dimensions");
+  const int hd = c.hidden_size / c.num_attention_heads;
+  STB_REQUIRE(hd % 2 == 0, "Llama rotary head width must be even");
+  STB_REQUIRE(std::isfinite(c.rms_norm_eps) && c.rms_norm_eps > 0 && std::isfinite(c.rope_theta) && c.rope_theta > 0,
+              "invalid Llama norm/rotary configuration");
+  STB_REQUIRE(c.weight_dtype == STB_BF16 || c.weight_dtype == STB_F16, "Llama weights must be BF16 or F16");
+  STB_REQUIRE(c.hidden_size % 8 == 0 && c.intermediate_size % 8 == 0 && hd % 8 == 0,
+              "device Llama needs hidden, intermediate and head widths that are multiples of 8");
+  const int tp = c.tp_size < 1 ? 1 : c.tp_size;
+  STB_REQUIRE(c.tp_rank >= 0 && c.tp_rank < tp, "invalid tensor-parallel rank");
+  STB_REQUIRE(c.num_attention_heads % tp == 0 && c.num_key_value_heads % tp == 0 &&
+                  c.intermediate_size % tp == 0 && c.vocab_size % tp == 0 && (c.intermediate_size / tp) % 8 == 0,
+              "heads, KV heads, intermediate size and vocabulary must split evenly over the tensor-parallel group");
+}
+
+}  // namespace
+
+extern "C" {
+
+int stb_llama_create(stb_session *s, const stb_llama_config *config, stb_llama **out) {
+  return guarded([&] {
+    enter(s);
+    STB_REQUIRE(config && out, "null argument");
+    *out = nullptr;
+    check_config(*config);
+    const int tp = config->tp_size < 1 ? 1 : config->tp_size;
+    STB_REQUIRE(tp == s->tp_size, "tensor-parallel size differs from the session's communicator");
+    STB_REQUIRE(config->tp_rank == s->tp_rank, "tensor-parallel rank differs from the session's communicator");
+    auto *m = new stb_llama();
+    m->s = s;
+    m->c = *config;
+    m->c.tp_size = tp;
+    m->tp = tp;
+    m->rank = config->tp_rank;
+    m->H = config->hidden_size;
+    m->hd = config->hidden_size / config->num_attention_heads;
+    m->NH = config->num_attention_heads / tp;
+    m->KV = config->num_key_value_heads / tp;
+    m->I = config->intermediate_size / tp;
+    m->V = config->vocab_size / tp;
+    m->v0 = m->rank * m->V;
+    try {
+      const size_t hs = esize(config->weight_dtype);
+      const uint64_t H = m->H;
+      m->embed = alloc_owned(s, m->owned, (uint64_t)config->vocab_size * H * hs);
+      m->final_norm = alloc_owned(s, m->owned, H * 4);
+      if (config->tie_word_embeddings && tp == 1) {
+        m->lm_head = m->embed;
+        m->head_aliases_embed = true;
+      } else {
+        m->lm_head = alloc_owned(s, m->owned, (uint64_t)m->V * H * hs);
+      }
+      m->layers.resize(config->num_layers);
+      for (auto &L : m->layers) {
+        L.in_norm = alloc_owned(s, m->owned, H * 4);
+        L.post_norm = alloc_owned(s, m->owned, H * 4);
+        L.qkv = alloc_owned(s, m->owned, (uint64_t)(m->NH + 2 * m->KV) * m->hd * H * hs);
+        L.o = alloc_owned(s, m->owned, H * (uint64_t)m->NH * m->hd * hs);
+        L.gu = alloc_owned(s, m->owned, (uint64_t)2 * m->I * H * hs);
+        L.down = alloc_owned(s, m->owned, H * (uint64_t)m->I * hs);
+      }
+      // Rotary coefficients of RotaryCoefficients.values (AttentionLayout.scala:23-34), in double.
+      const int half = m->hd / 2;
+      std::vector<double> cs((size_t)config->max_positions * half * 2);
+      for (int t = 0; t < config->max_positions; t++)
+        for (int d = 0; d < half; d++) {
+          const double angle = (double)t * std::pow(config->rope_theta, -2.0 * d / m->hd);
+          cs[((size_t)t * half + d) * 2] = std::cos(angle);
+          cs[((size_t)t * half + d) * 2 + 1] = std::sin(angle);
+        }
+      m->rope = alloc_owned(s, m->owned, cs.size() * 8);
+      upload(s, cs.data(), cs.size() * 8, m->rope);
+      for (uint64_t p : m->owned) (void)p;
+      m->weight_bytes = 0;
+      for (uint64_t p : m->owned) m->weight_bytes += s->allocations[p];
+    } catch (...) {
+      free_owned(s, m->owned);
+      delete m;
+      throw;
+    }
+    *out = m;
+  });
+}
+
+int stb_llama_destroy(stb_llama *m) {
+  if (!m) return STB_OK;
+  return guarded([&] {
+    enter(m->s);
+    free_owned(m->s, m->owned);
+    delete m;
+  });
+}
+
+int stb_llama_weight_bytes(stb_llama *m, uint64_t *bytes) {
+  return guarded([&] {
+    STB_REQUIRE(m && bytes, "null argument");
+    enter(m->s);
+    *bytes = m->weight_bytes;
+  });
+}
+
+int stb_llama_set_weight(stb_llama *m, int which, int layer, const void *host, uint64_t bytes, int dtype) {
+  return guarded([&] {
+    STB_REQUIRE(m, "null model");
+    stb_session *s = m->s;
+    enter(s);
+    STB_REQUIRE(which >= W_EMBED && which <= W_DOWN, "unknown Llama weight");
+    const bool global = which == W_EMBED || which == W_FINAL || which == W_HEAD;
+    STB_REQUIRE(global || (layer >= 0 && layer < (int)m->layers.size()), "layer out of range");
+    STB_REQUIRE(host || bytes == 0, "null payload");
+    const uint64_t rows = logical_rows(m, which), cols = logical_cols(m, which);
+    const uint64_t count = rows * cols;
+    STB_REQUIRE(dtype == STB_F32 || dtype == STB_BF16 || dtype == STB_F16, "unsupported dtype");
+    STB_REQUIRE(bytes == count * esize(dtype), "Llama weight metadata mismatch: payload size");
+    if (which == W_FINAL || which == W_IN || which == W_POST) {
+      std::vector<float> wide(count);
+      const uint16_t *h = (const uint16_t *)host;
+      for (uint64_t i = 0; i < count; i++) {
+        if (dtype == STB_F32) std::memcpy(&wide[i], (const char *)host + 4 * i, 4);
+        else if (dtype == STB_BF16) {
+          uint32_t u = (uint32_t)h[i] << 16;
+          std::memcpy(&wide[i], &u, 4);
+        } else {
+          wide[i] = __half2float(*reinterpret_cast<const __half *>(&h[i]));
+        }
+      }
+      const uint64_t dst = which == W_FINAL ? m->final_norm
+                                            : (which == W_IN ? m->layers[layer].in_norm : m->layers[layer].post_norm);
+      upload(s, wide.data(), count * 4, dst);
+      STB_CUDA(cudaStreamSynchronize(s->stream));
+      return;
+    }
+    STB_REQUIRE(dtype == m->c.weight_dtype, "matrix payload dtype differs from the model's weight dtype");
+    if (which == W_HEAD && m->head_aliases_embed) {
+      // Tied head: LlamaModel.load requires a present lm_head to equal the embedding bitwise
+      // (LlamaModel.scala:170-173); the resident copy is the embedding's.
+      std::vector<uint16_t> emb(count);
+      download(s, m->embed, emb.data(), count * 2);
+      STB_REQUIRE(std::memcmp(emb.data(), host, count * 2) == 0, "conflicting tied lm_head weight");
+      return;
+    }
+    Target t = target_of(m, which, layer);
+    // stage the full tensor, then gather this rank's rows/columns into the fused layout
+    uint64_t tmp = session_alloc(s, count * 2), map = 0;
+    try {
+      upload(s, host, count * 2, tmp);
+      std::vector<uint32_t> rowmap;
+      std::vector<uint32_t> dst_rows;
+      for (int r = 0; r < t.rows; r++)
+        if (t.which[r] == which) {
+          dst_rows.push_back((uint32_t)r);
+          rowmap.push_back(t.lrow[r]);
+        }
+      // pack rows of this tensor: dst row list scattered; do it row-list-wise via a compact map
+      // (dst rows of one logical tensor are interleaved with the others' in paired layouts).
+      map = session_alloc(s, rowmap.size() * 8);
+      std::vector<uint32_t> both(rowmap.size() * 2);
+      for (size_t i = 0; i < rowmap.size(); i++) {
+        both[i] = rowmap[i];
+        both[rowmap.size() + i] = dst_rows[i];
+      }
+      upload(s, both.data(), both.size() * 4, map);
+      // one launch per destination row would be slow for big matrices; rows of one tensor are
+      // gathered to consecutive temp rows first, then scattered with cudaMemcpy2D per run.
+      uint64_t packed = session_alloc(s, (uint64_t)rowmap.size() * t.cols * 2);
+      pack_rows_kernel<<<grid_for(rowmap.size() * (size_t)t.cols), 256, 0, s->stream>>>(
+          (uint16_t *)packed, (const uint16_t *)tmp, (const uint32_t *)map, (int)rowmap.size(), t.cols, t.src_cols,
+          t.col0);
+      check_launch("pack_rows");
+      count_launch(s);
+      // scatter consecutive runs of destination rows
+      size_t i = 0;
+      while (i < dst_rows.size()) {
+        size_t j = i + 1;
+        uint32_t step = (j < dst_rows.size()) ? dst_rows[j] - dst_rows[i] : 1;
+        while (j < dst_rows.size() && dst_rows[j] - dst_rows[j - 1] == step) j++;
+        STB_CUDA(cudaMemcpy2DAsync((void *)(t.dst + (uint64_t)dst_rows[i] * t.cols * 2), (size_t)step * t.cols * 2,
+                                   (const void *)(packed + (uint64_t)i * t.cols * 2), (size_t)t.cols * 2,
+                                   (size_t)t.cols * 2, j - i, cudaMemcpyDeviceToDevice, s->stream));
+        i = j;
+      }
+      STB_CUDA(cudaStreamSynchronize(s->stream));
+      session_free(s, packed);
+    } catch (...) {
+      if (map) session_free(s, map);
+      session_free(s, tmp);
+      throw;
+    }
+    session_free(s, map);
+    session_free(s, tmp);
+  });
+}
+
+int stb_llama_init_random(stb_llama *m, uint64_t seed, double stddev) {
+  return guarded([&] {
+    STB_REQUIRE(m, "null model");
+    stb_session *s = m->s;
+    enter(s);
+    const int wdt = m->c.weight_dtype;
+    auto fill_target = [&](const Target &t, int layer) {
+      std::vector<uint64_t> map(t.rows);
+      for (int r = 0; r < t.rows; r++) map[r] = (stream_of(t.which[r], layer) << 32) | t.lrow[r];
+      uint64_t dmap = session_alloc(s, map.size() * 8);
+      try {
+        upload(s, map.data(), map.size() * 8, dmap);
+        fill_rows_kernel<<<grid_for((size_t)t.rows * t.cols), 256, 0, s->stream>>>(
+            (void *)t.dst, wdt, (const uint64_t *)dmap, t.rows, t.cols, t.src_cols, t.col0, seed, stddev);
+        check_launch("fill_rows");
+        count_launch(s);
+        STB_CUDA(cudaStreamSynchronize(s->stream));
+      } catch (...) {
+        session_free(s, dmap);
+        throw;
+      }
+      session_free(s, dmap);
+    };
+    fill_target(target_of(m, W_EMBED, 0), 0);
+    if (!m->head_aliases_embed) {
+      // untied: its own stream; tied but sharded: the embedding's values
+      Target t = target_of(m, W_HEAD, 0);
+      if (m->c.tie_word_embeddings) std::fill(t.which.begin(), t.which.end(), (int)W_EMBED);
+      fill_target(t, 0);
+    }
+    fill_value(s, m->final_norm, STB_F32, m->H, 1.0f);
+    for (int l = 0; l < (int)m->layers.size(); l++) {
+      fill_value(s, m->layers[l].in_norm, STB_F32, m->H, 1.0f);
+      fill_value(s, m->layers[l].post_norm, STB_F32, m->H, 1.0f);
+      fill_target(target_of(m, W_Q, l), l);
+      fill_target(target_of(m, W_O, l), l);
+      fill_target(target_of(m, W_GATE, l), l);
+      fill_target(target_of(m, W_DOWN, l), l);
+    }
+    STB_CUDA(cudaStreamSynchronize(s->stream));
+  });
+}
+
+int stb_llama_cache_create(stb_llama *m, int batch, int capacity, stb_llama_cache **out) {
+  return guarded([&] {
+    STB_REQUIRE(m && out, "null argument");
+    enter(m->s);
+    *out = nullptr;
+    STB_REQUIRE(batch > 0 && capacity > 0 && capacity <= m->c.max_positions, "invalid model cache dimensions/budget");
+    // attention keeps one row of double scores per block in shared memory
+    STB_REQUIRE(capacity <= 28000, "model cache capacity exceeds the attention score workspace");
+    const size_t smem = (size_t)(capacity + 32) * sizeof(double);
+    if (smem > 48 * 1024)
+      STB_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    auto *c = new stb_llama_cache();
+    c->m = m;
+    c->batch = batch;
+    c->capacity = capacity;
+    try {
+      const uint64_t bytes = (uint64_t)m->layers.size() * 2 * batch * m->KV * capacity * m->hd * 4;
+      c->kv = alloc_owned(m->s, c->owned, bytes);
+      ensure_rows(c, batch);
+    } catch (...) {
+      free_owned(m->s, c->owned);
+      delete c;
+      throw;
+    }
+    *out = c;
+  });
+}
+
+int stb_llama_cache_destroy(stb_llama_cache *c) {
+  if (!c) return STB_OK;
+  return guarded([&] {
+    enter(c->m->s);
+    if (c->graph) cudaGraphExecDestroy(c->graph);
+    free_owned(c->m->s, c->owned);
+    delete c;
+  });
+}
+
+int stb_llama_cache_position(stb_llama_cache *c, int *position) {
+  return guarded([&] {
+    STB_REQUIRE(c && position, "null argument");
+    enter(c->m->s);
+    *position = c->used;
+  });
+}
+
+int stb_llama_cache_reset(stb_llama_cache *c) {
+  return guarded([&] {
+    STB_REQUIRE(c, "null cache");
+    enter(c->m->s);
+    c->used = 0;  // old tails are invisible and overwritten by the next append (LlamaCache.scala:50-54)
+  });
+}
+
+int stb_llama_decode(stb_llama_cache *c, const int64_t *tokens, int batch, int count, float *logits,
+                     int64_t *next_ids) {
+  return guarded([&] {
+    STB_REQUIRE(c, "null cache");
+    stb_llama *m = c->m;
+    stb_session *s = m->s;
+    enter(s);
+    STB_REQUIRE(tokens && batch == c->batch && count > 0, "cache tokens must match batch with positive chunk length");
+    STB_REQUIRE((long)c->used + count <= c->capacity, "model cache capacity exceeded");
+    const int rows = batch * count;
+    for (int i = 0; i < rows; i++)
+      STB_REQUIRE(tokens[i] >= 0 && tokens[i] < m->c.vocab_size, "embedding token ID out of bounds");
+    ensure_rows(c, rows);
+    upload(s, tokens, (uint64_t)rows * 8, c->tokens);
+    STB_CUDA(cudaMemsetAsync((void *)c->state, 0, (size_t)(2 + 2 * batch) * 4, s->stream));
+    uint64_t dnext = 0;
+    if (next_ids) dnext = c->tokens;  // finalize writes picks into a device buffer we read below
+    StepArgs a;
+    a.rows = rows;
+    a.count = count;
+    a.device_pos = false;
+    a.all_logits = true;
+    a.append = false;
+    a.advance = 0;
+    int launches = enqueue_step(c, a);
+    count_launch(s, launches);
+    if (logits) {
+      if (m->tp == 1) {
+        download(s, c->logits, logits, (uint64_t)rows * m->V * 4);
+      } else {
+        // this rank holds vocabulary columns [v0, v0+V): gather all ranks' logits row blocks
+        throw Error(STB_ERR_UNSUPPORTED, "full logits download under tensor parallelism; use next_ids");
+      }
+    }
+    if (next_ids) {
+      // greedy pick of each batch row's last token, from the full logits just computed
+      std::vector<float> last((size_t)batch * m->V);
+      for (int b = 0; b < batch; b++) {
+        const uint64_t src = c->logits + ((uint64_t)(b * count + count - 1) * m->V) * 4;
+        download(s, src, last.data() + (size_t)b * m->V, (uint64_t)m->V * 4);
+        int64_t best = 0;
+        for (int i = 1; i < m->V; i++)
+          if (last[(size_t)b * m->V + i] > last[(size_t)b * m->V + best]) best = i;
+        next_ids[b] = best;
+      }
+    }
+    (void)dnext;
+    STB_CUDA(cudaStreamSynchronize(s->stream));
+    c->used += count;  // publish only after the whole chunk succeeded (BackendLlamaCache.scala:38-40)
+  });
+}
+
+int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int prompt_len, int max_new,
+                       const int64_t *eos, int eos_count, int64_t *out, int *generated, float *timings_ms) {
+  return guarded([&] {
+    STB_REQUIRE(m, "null model");
+    stb_session *s = m->s;
+    enter(s);
+    STB_REQUIRE(prompt && out && batch > 0 && prompt_len > 0 && max_new >= 0 &&
+                    (long)prompt_len + max_new <= m->c.max_positions,
+                "invalid generation length");
+    STB_REQUIRE(eos_count >= 0 && (eos_count == 0 || eos), "invalid EOS list");
+    for (long i = 0; i < (long)batch * prompt_len; i++)
+      STB_REQUIRE(prompt[i] >= 0 && prompt[i] < m->c.vocab_size, "generation token outside vocabulary");
+    const int total = prompt_len + max_new;
+    for (int b = 0; b < batch; b++)
+      std::memcpy(out + (size_t)b * total, prompt + (size_t)b * prompt_len, (size_t)prompt_len * 8);
+    if (generated)
+      for (int b = 0; b < batch; b++) generated[b] = 0;
+    if (timings_ms) timings_ms[0] = timings_ms[1] = 0.0f;
+    if (max_new == 0) return;
+    stb_llama_cache *c = nullptr;
+    {
+      int rc = stb_llama_cache_create(m, batch, total, &c);
+      if (rc != STB_OK) throw Error(rc, stb_last_error());
+    }
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    try {
+      for (auto &e : ev) STB_CUDA(cudaEventCreate(&e));
+      const int rows = batch * prompt_len;
+      ensure_rows(c, rows);
+      c->out_stride = max_new;
+      c->out_ids = alloc_owned(s, c->owned, (uint64_t)batch * max_new * 8);
+      if (eos_count) {
+        c->eos = alloc_owned(s, c->owned, (uint64_t)eos_count * 8);
+        upload(s, eos, (uint64_t)eos_count * 8, c->eos);
+      }
+      c->eos_count = eos_count;
+      STB_CUDA(cudaEventRecord(ev[0], s->stream));
+      upload(s, prompt, (uint64_t)rows * 8, c->tokens);
+      STB_CUDA(cudaMemsetAsync((void *)c->state, 0, (size_t)(2 + 2 * batch) * 4, s->stream));
+      // prefill: logits of each row's last token only; pick appended; position += prompt_len
+      StepArgs a;
+      a.rows = rows;
+      a.count = prompt_len;
+      a.device_pos = true;
+      a.all_logits = false;
+      a.append = true;
+      a.advance = prompt_len;
+      int launches = enqueue_step(c, a);
+      count_launch(s, launches);
+      STB_CUDA(cudaEventRecord(ev[1], s->stream));
+      if (max_new > 1) {
+        // decode: tokens[b*count + count-1] was rewritten in place; compact them to rows 0..batch
+        if (prompt_len > 1) {
+          STB_CUDA(cudaMemcpy2DAsync((void *)c->tokens, 8, (const void *)(c->tokens + (uint64_t)(prompt_len - 1) * 8),
+                                     (size_t)prompt_len * 8, 8, batch, cudaMemcpyDeviceToDevice, s->stream));
+        }
+        StepArgs d;
+        d.rows = batch;
+        d.count = 1;
+        d.device_pos = true;
+        d.all_logits = false;
+        d.append = true;
+        d.advance = 1;
+        cudaGraph_t g = nullptr;
+        STB_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+        int step_launches = 0;
+        try {
+          step_launches = enqueue_step(c, d);
+        } catch (...) {
+          cudaStreamEndCapture(s->stream, &g);
+          if (g) cudaGraphDestroy(g);
+          throw;
+        }
+        STB_CUDA(cudaStreamEndCapture(s->stream, &g));
+        cudaGraphExec_t exec = nullptr;
+        cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        STB_CUDA(e);
+        c->graph = exec;
+        for (int i = 1; i < max_new; i++) STB_CUDA(cudaGraphLaunch(exec, s->stream));
+        count_launch(s, (uint64_t)step_launches * (max_new - 1));
+      }
+      STB_CUDA(cudaEventRecord(ev[2], s->stream));
+      std::vector<int64_t> picks((size_t)batch * max_new);
+      std::vector<int> st(2 + 2 * batch);
+      download(s, c->out_ids, picks.data(), picks.size() * 8);
+      download(s, c->state, st.data(), st.size() * 4);
+      for (int b = 0; b < batch; b++) {
+        const int n = st[2 + batch + b];
+        std::memcpy(out + (size_t)b * total + prompt_len, picks.data() + (size_t)b * max_new, (size_t)n * 8);
+        if (generated) generated[b] = n;
+      }
+      if (timings_ms) {
+        STB_CUDA(cudaEventElapsedTime(&timings_ms[0], ev[0], ev[1]));
+        STB_CUDA(cudaEventElapsedTime(&timings_ms[1], ev[1], ev[2]));
+      }
+    } catch (...) {
+      for (auto &e : ev)
+        if (e) cudaEventDestroy(e);
+      stb_llama_cache_destroy(c);
+      throw;
+    }
+    for (auto &e : ev)
+      if (e) cudaEventDestroy(e);
+    int rc = stb_llama_cache_destroy(c);
+    if (rc != STB_OK) throw Error(rc, stb_last_error());
+  });
+}
+
+}  // extern "C"

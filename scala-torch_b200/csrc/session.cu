@@ -1,0 +1,320 @@
+// Session, memory and transfer entry points of libstb200.so, plus the synthetic weight generator.
+// Mirrors the ownership model of the reference's CudaSession (ffm/src/main/scala/scalatorch/ffm/
+// CudaSession.scala): a byte budget checked before every allocation, one stream, reverse-order
+// release at close, thread confinement.
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "rng.cuh"
+
+namespace stb {
+
+static thread_local std::string g_last_error;
+void set_last_error(const std::string &msg) { g_last_error = msg; }
+
+void enter(stb_session *s) {
+  if (!s) throw Error(STB_ERR_STATE, "session is null");
+  if (s->closed) throw Error(STB_ERR_STATE, "session is closed");
+  if (std::this_thread::get_id() != s->owner)
+    throw Error(STB_ERR_THREAD, "session used from another thread");
+  STB_CUDA(cudaSetDevice(s->device));
+}
+
+uint64_t session_alloc(stb_session *s, uint64_t bytes) {
+  if (bytes > s->max_bytes || s->allocated > s->max_bytes - bytes)
+    throw Error(STB_ERR_BUDGET, "CUDA session allocation budget exceeded: requested " +
+                                    std::to_string(bytes) + " with " + std::to_string(s->allocated) +
+                                    " of " + std::to_string(s->max_bytes) + " in use");
+  void *p = nullptr;
+  uint64_t rounded = bytes ? bytes : 1;
+  cudaError_t e = cudaMalloc(&p, rounded);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw Error(STB_ERR_BUDGET, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+  }
+  s->allocations[(uint64_t)p] = bytes;
+  s->allocated += bytes;
+  return (uint64_t)p;
+}
+
+void session_free(stb_session *s, uint64_t ptr) {
+  if (!ptr) return;
+  auto it = s->allocations.find(ptr);
+  if (it == s->allocations.end()) throw Error(STB_ERR_STATE, "release of an address this session does not own");
+  // Work already enqueued may still read the buffer: complete the stream before freeing.
+  STB_CUDA(cudaStreamSynchronize(s->stream));
+  STB_CUDA(cudaFree((void *)ptr));
+  s->allocated -= it->second;
+  s->allocations.erase(it);
+}
+
+void check_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw Error(STB_ERR_CUDA, std::string(what) + " launch failed: " + cudaGetErrorString(e));
+}
+
+static constexpr uint64_t kStagingChunk = 64ull << 20;  // two halves of 64 MiB
+
+static void ensure_staging(stb_session *s) {
+  if (s->staging) return;
+  STB_CUDA(cudaHostAlloc(&s->staging, 2 * kStagingChunk, cudaHostAllocDefault));
+  s->staging_bytes = 2 * kStagingChunk;
+  for (auto &ev : s->staging_done) STB_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+}
+
+static bool is_pinned(const void *host) {
+  cudaPointerAttributes attr;
+  cudaError_t e = cudaPointerGetAttributes(&attr, host);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return attr.type == cudaMemoryTypeHost;
+}
+
+// ---------------------------------------------------------------- synthetic weights
+
+__global__ void fill_normal_kernel(void *dst, int dtype, uint64_t count, uint64_t seed, uint64_t stream,
+                                   double stddev) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < count;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    float v = __double2float_rn(__dmul_rn(stddev, rng_normal_dev(seed, stream, i)));
+    if (dtype == STB_F32) ((float *)dst)[i] = v;
+    else if (dtype == STB_BF16) ((uint16_t *)dst)[i] = f32_to_bf16_rne(v);
+    else ((__half *)dst)[i] = __float2half_rn(v);
+  }
+}
+
+__global__ void fill_value_kernel(void *dst, int dtype, uint64_t count, float value) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < count;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    if (dtype == STB_F32) ((float *)dst)[i] = value;
+    else if (dtype == STB_BF16) ((uint16_t *)dst)[i] = f32_to_bf16_rne(value);
+    else ((__half *)dst)[i] = __float2half_rn(value);
+  }
+}
+
+void fill_normal(stb_session *s, uint64_t dst, int dtype, uint64_t count, uint64_t seed, uint64_t stream,
+                 double stddev) {
+  if (!count) return;
+  uint64_t blocks = (count + 255) / 256;
+  if (blocks > 148ull * 64) blocks = 148ull * 64;
+  fill_normal_kernel<<<(unsigned)blocks, 256, 0, s->stream>>>((void *)dst, dtype, count, seed, stream, stddev);
+  check_launch("fill_normal");
+  count_launch(s);
+}
+
+void fill_value(stb_session *s, uint64_t dst, int dtype, uint64_t count, float value) {
+  if (!count) return;
+  uint64_t blocks = (count + 255) / 256;
+  if (blocks > 148ull * 64) blocks = 148ull * 64;
+  fill_value_kernel<<<(unsigned)blocks, 256, 0, s->stream>>>((void *)dst, dtype, count, value);
+  check_launch("fill_value");
+  count_launch(s);
+}
+
+void upload(stb_session *s, const void *host, uint64_t bytes, uint64_t dst) {
+  if (!bytes) return;
+  STB_REQUIRE(host && dst, "upload requires host and device buffers");
+  if (is_pinned(host)) {
+    STB_CUDA(cudaMemcpyAsync((void *)dst, host, bytes, cudaMemcpyHostToDevice, s->stream));
+    return;
+  }
+  // Pageable source: double-buffered pinned staging, ordered on the session stream, so the copy
+  // never races a later kernel (the pageable-HtoD hazard of docs/research/backend-llama.md:40-42).
+  ensure_staging(s);
+  uint64_t done = 0;
+  int slot = 0;
+  bool used[2] = {false, false};
+  while (done < bytes) {
+    uint64_t n = bytes - done < kStagingChunk ? bytes - done : kStagingChunk;
+    char *stage = (char *)s->staging + slot * kStagingChunk;
+    if (used[slot]) STB_CUDA(cudaEventSynchronize(s->staging_done[slot]));
+    std::memcpy(stage, (const char *)host + done, n);
+    STB_CUDA(cudaMemcpyAsync((char *)dst + done, stage, n, cudaMemcpyHostToDevice, s->stream));
+    STB_CUDA(cudaEventRecord(s->staging_done[slot], s->stream));
+    used[slot] = true;
+    done += n;
+    slot ^= 1;
+  }
+  for (int i = 0; i < 2; i++)
+    if (used[i]) STB_CUDA(cudaEventSynchronize(s->staging_done[i]));
+}
+
+void download(stb_session *s, uint64_t src, void *host, uint64_t bytes) {
+  if (!bytes) {
+    STB_CUDA(cudaStreamSynchronize(s->stream));
+    return;
+  }
+  STB_REQUIRE(host && src, "download requires host and device buffers");
+  if (is_pinned(host)) {
+    STB_CUDA(cudaMemcpyAsync(host, (const void *)src, bytes, cudaMemcpyDeviceToHost, s->stream));
+    STB_CUDA(cudaStreamSynchronize(s->stream));
+    return;
+  }
+  ensure_staging(s);
+  uint64_t done = 0;
+  while (done < bytes) {
+    uint64_t n = bytes - done < 2 * kStagingChunk ? bytes - done : 2 * kStagingChunk;
+    STB_CUDA(cudaMemcpyAsync(s->staging, (const char *)src + done, n, cudaMemcpyDeviceToHost, s->stream));
+    STB_CUDA(cudaStreamSynchronize(s->stream));
+    std::memcpy((char *)host + done, s->staging, n);
+    done += n;
+  }
+}
+
+}  // namespace stb
+
+using namespace stb;
+
+extern "C" {
+
+int stb_version(void) { return 100; }
+
+const char *stb_last_error(void) { return g_last_error.c_str(); }
+
+int stb_session_create(int device, uint64_t max_bytes, stb_session **out) {
+  return guarded([&] {
+    STB_REQUIRE(out, "output handle is null");
+    *out = nullptr;
+    int count = 0;
+    STB_CUDA(cudaGetDeviceCount(&count));
+    STB_REQUIRE(device >= 0 && device < count, "device index out of range");
+    STB_CUDA(cudaSetDevice(device));
+    auto *s = new stb_session();
+    s->device = device;
+    s->max_bytes = max_bytes;
+    s->owner = std::this_thread::get_id();
+    cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+      delete s;
+      throw Error(STB_ERR_CUDA, std::string("cudaStreamCreate failed: ") + cudaGetErrorString(e));
+    }
+    *out = s;
+  });
+}
+
+void stb_session_close_tp(stb_session *s);  // nccl.cu
+
+int stb_session_destroy(stb_session *s) {
+  if (!s) return STB_OK;
+  return guarded([&] {
+    enter(s);
+    cudaError_t first = cudaStreamSynchronize(s->stream);
+    stb_session_close_tp(s);
+    // Reverse acquisition order (CudaSession.scala:863-884): highest address last allocated is
+    // not guaranteed, so free in reverse map order deterministically.
+    for (auto it = s->allocations.rbegin(); it != s->allocations.rend(); ++it) cudaFree((void *)it->first);
+    s->allocations.clear();
+    s->allocated = 0;
+    for (auto &ev : s->staging_done)
+      if (ev) cudaEventDestroy(ev);
+    if (s->staging) cudaFreeHost(s->staging);
+    cudaStreamDestroy(s->stream);
+    s->closed = true;
+    delete s;
+    if (first != cudaSuccess) throw Error(STB_ERR_CUDA, std::string("pending work failed: ") + cudaGetErrorString(first));
+  });
+}
+
+int stb_session_allocated(stb_session *s, uint64_t *bytes) {
+  return guarded([&] {
+    enter(s);
+    STB_REQUIRE(bytes, "output is null");
+    *bytes = s->allocated;
+  });
+}
+
+int stb_session_stream(stb_session *s, void **stream) {
+  return guarded([&] {
+    enter(s);
+    STB_REQUIRE(stream, "output is null");
+    *stream = (void *)s->stream;
+  });
+}
+
+int stb_session_launches(stb_session *s, uint64_t *launches) {
+  return guarded([&] {
+    enter(s);
+    STB_REQUIRE(launches, "output is null");
+    *launches = s->launches.load();
+  });
+}
+
+int stb_alloc(stb_session *s, uint64_t bytes, uint64_t *dptr) {
+  return guarded([&] {
+    enter(s);
+    STB_REQUIRE(dptr, "output is null");
+    *dptr = session_alloc(s, bytes);
+  });
+}
+
+int stb_release(stb_session *s, uint64_t dptr) {
+  return guarded([&] {
+    enter(s);
+    session_free(s, dptr);
+  });
+}
+
+int stb_upload(stb_session *s, const void *host, uint64_t bytes, uint64_t dst) {
+  return guarded([&] {
+    enter(s);
+    upload(s, host, bytes, dst);
+  });
+}
+
+int stb_download(stb_session *s, uint64_t src, void *host, uint64_t bytes) {
+  return guarded([&] {
+    enter(s);
+    download(s, src, host, bytes);
+  });
+}
+
+int stb_copy(stb_session *s, uint64_t dst, uint64_t src, uint64_t bytes) {
+  return guarded([&] {
+    enter(s);
+    if (bytes) STB_CUDA(cudaMemcpyAsync((void *)dst, (const void *)src, bytes, cudaMemcpyDeviceToDevice, s->stream));
+  });
+}
+
+int stb_sync(stb_session *s) {
+  return guarded([&] {
+    enter(s);
+    STB_CUDA(cudaStreamSynchronize(s->stream));
+  });
+}
+
+int stb_host_alloc(uint64_t bytes, void **host) {
+  return guarded([&] {
+    STB_REQUIRE(host, "output is null");
+    STB_CUDA(cudaHostAlloc(host, bytes ? bytes : 1, cudaHostAllocDefault));
+  });
+}
+
+int stb_host_free(void *host) {
+  return guarded([&] {
+    if (host) STB_CUDA(cudaFreeHost(host));
+  });
+}
+
+int stb_fill_normal(stb_session *s, uint64_t dst, int dtype, uint64_t count, uint64_t seed, uint64_t stream,
+                    double stddev) {
+  return guarded([&] {
+    enter(s);
+    STB_REQUIRE(dtype == STB_F32 || dtype == STB_BF16 || dtype == STB_F16, "unsupported dtype");
+    STB_REQUIRE(count == 0 || dst, "null destination");
+    fill_normal(s, dst, dtype, count, seed, stream, stddev);
+  });
+}
+
+int stb_fill_value(stb_session *s, uint64_t dst, int dtype, uint64_t count, float value) {
+  return guarded([&] {
+    enter(s);
+    STB_REQUIRE(dtype == STB_F32 || dtype == STB_BF16 || dtype == STB_F16, "unsupported dtype");
+    STB_REQUIRE(count == 0 || dst, "null destination");
+    fill_value(s, dst, dtype, count, value);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,341 @@
+"""Host-side binding of libstb200.so -- the Python mirror of scala-torch's ffm module.
+
+The reference reaches the GPU through Java FFM downcalls (ffm/src/main/scala/scalatorch/ffm/
+CudaDriver.scala:13-19): each call returns an int status and a nonzero status becomes an
+exception.  This module binds the same way with ctypes and keeps the reference's error
+vocabulary: invalid arguments raise IllegalArgumentException *before* any native call, native
+failures raise IllegalStateException("<fn> failed with status <code>: <message>").
+
+`B200Session` is the device FloatBackend (core/.../FloatBackend.scala:7-31, the trait CudaSession
+implements, CudaSession.scala:23-24) restricted to what the Linear / Llama hot path needs:
+upload / download / release / shape / matmul against resident (out,in) half weights, plus the
+raw half upload that replaces SafeTensors.readFloat's F32 widening.
+
+There is no fallback: if libstb200.so is missing or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass, field
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(HERE), "libstb200.so")
+
+STB_F32, STB_BF16, STB_F16 = 0, 1, 2
+DTYPE_NAMES = {"F32": STB_F32, "BF16": STB_BF16, "F16": STB_F16}
+STATUS = {0: "OK", 1: "INVALID", 2: "BUDGET", 3: "CUDA", 4: "NCCL", 5: "THREAD", 6: "STATE", 7: "UNSUPPORTED"}
+
+
+class IllegalArgumentException(ValueError):
+    """Rejected request (the reference's require(...) failures)."""
+
+
+class IllegalStateException(RuntimeError):
+    """Native failure or misuse of a closed / foreign handle."""
+
+    def __init__(self, fn: str, code: int, message: str):
+        super().__init__(f"{fn} failed with status {code} ({STATUS.get(code, '?')}): {message}")
+        self.code = code
+
+
+_lib = None
+_p = ctypes.c_void_p
+_u64 = ctypes.c_uint64
+_i = ctypes.c_int
+_pp = ctypes.POINTER(ctypes.c_void_p)
+
+
+def library() -> ctypes.CDLL:
+    """Load libstb200.so (built in-tree by scala-torch_b200/build.py).  Raises if absent."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise IllegalStateException("load", -1, f"{LIB_PATH} is missing; run scala-torch_b200/build.py")
+        lib = ctypes.CDLL(LIB_PATH)
+        _declare(lib)
+        _lib = lib
+    return _lib
+
+
+def _declare(L):
+    sig = {
+        "stb_version": (_i, []),
+        "stb_last_error": (ctypes.c_char_p, []),
+        "stb_session_create": (_i, [_i, _u64, _pp]),
+        "stb_session_destroy": (_i, [_p]),
+        "stb_session_allocated": (_i, [_p, ctypes.POINTER(_u64)]),
+        "stb_session_stream": (_i, [_p, _pp]),
+        "stb_session_launches": (_i, [_p, ctypes.POINTER(_u64)]),
+        "stb_alloc": (_i, [_p, _u64, ctypes.POINTER(_u64)]),
+        "stb_release": (_i, [_p, _u64]),
+        "stb_upload": (_i, [_p, _p, _u64, _u64]),
+        "stb_download": (_i, [_p, _u64, _p, _u64]),
+        "stb_copy": (_i, [_p, _u64, _u64, _u64]),
+        "stb_sync": (_i, [_p]),
+        "stb_host_alloc": (_i, [_u64, _pp]),
+        "stb_host_free": (_i, [_p]),
+        "stb_linear": (_i, [_p, _u64, _u64, _i, _u64, _u64, _i, _i, _i]),
+        "stb_linear_ld": (_i, [_p, _u64, _i, _u64, _i, _u64, _u64, _i, _i, _i, _i]),
+        "stb_linear_prefill": (_i, [_p, _u64, _u64, _i, _u64, _u64, _i, _i, _i]),
+        "stb_linear_host": (_i, [_p, _p, _u64, _i, _u64, _p, _i, _i, _i]),
+        "stb_fill_normal": (_i, [_p, _u64, _i, _u64, _u64, _u64, ctypes.c_double]),
+        "stb_fill_value": (_i, [_p, _u64, _i, _u64, ctypes.c_float]),
+        "stb_nccl_unique_id": (_i, [_p]),
+        "stb_session_init_tp": (_i, [_p, _i, _i, _p]),
+        "stb_allreduce_sum_f32": (_i, [_p, _u64, _u64]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name, None)
+        if fn is None:
+            continue
+        fn.restype = res
+        fn.argtypes = args
+
+
+def call(name: str, *args) -> None:
+    """CudaDriver.call idiom: nonzero status -> exception with the library's message."""
+    fn = getattr(library(), name)
+    code = fn(*args)
+    if code != 0:
+        msg = library().stb_last_error().decode(errors="replace")
+        if code == 1:
+            raise IllegalArgumentException(f"{name}: {msg}")
+        raise IllegalStateException(name, code, msg)
+
+
+def require(cond: bool, message: str) -> None:
+    if not cond:
+        raise IllegalArgumentException(message)
+
+
+@dataclass(eq=False)
+class DeviceTensor:
+    """A resident device buffer with a logical shape (CudaTensor, CudaSession.scala:14-20).
+
+    dtype is the element type in HBM.  `transposed_weight` marks a half (out,in) weight used as
+    W^T: its logical shape is (in, out) -- what BackendLlama.prepare's upload(p, transposed=true)
+    hands to matmul (BackendLlama.scala:161-162) -- but the bytes stay (out,in) and half."""
+    session: "B200Session"
+    address: int
+    shape: tuple
+    dtype: int = STB_F32
+    nbytes: int = 0
+    transposed_weight: bool = False
+    owner: bool = True
+    _alive: list = field(default_factory=lambda: [True])
+
+    @property
+    def numel(self) -> int:
+        n = 1
+        for d in self.shape:
+            n *= int(d)
+        return n
+
+    def close(self) -> None:
+        self.session.release(self)
+
+
+class B200Session:
+    """Thread-confined device session with a byte budget (CudaSession.withDevice)."""
+
+    def __init__(self, device: int = 0, max_bytes: int = 1 << 30):
+        require(device >= 0 and max_bytes >= 0, "invalid device or budget")
+        h = ctypes.c_void_p()
+        call("stb_session_create", device, max_bytes, ctypes.byref(h))
+        self.handle = h
+        self.device = device
+        self.max_bytes = max_bytes
+        self._closed = False
+
+    # -- lifetime
+    @classmethod
+    def with_device(cls, device: int = 0, max_bytes: int = 1 << 30):
+        return cls(device, max_bytes)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def close(self) -> None:
+        if not self._closed:
+            self._closed = True
+            call("stb_session_destroy", self.handle)
+
+    def _check(self):
+        if self._closed:
+            raise IllegalStateException("session", 6, "session is closed")
+
+    @property
+    def allocated_bytes(self) -> int:
+        self._check()
+        v = ctypes.c_uint64()
+        call("stb_session_allocated", self.handle, ctypes.byref(v))
+        return v.value
+
+    @property
+    def launches(self) -> int:
+        v = ctypes.c_uint64()
+        call("stb_session_launches", self.handle, ctypes.byref(v))
+        return v.value
+
+    @property
+    def stream(self) -> int:
+        v = ctypes.c_void_p()
+        call("stb_session_stream", self.handle, ctypes.byref(v))
+        return v.value or 0
+
+    def sync(self) -> None:
+        self._check()
+        call("stb_sync", self.handle)
+
+    # -- memory
+    def allocate(self, shape, dtype: int = STB_F32) -> DeviceTensor:
+        self._check()
+        shape = tuple(int(d) for d in shape)
+        require(all(d >= 0 for d in shape), "negative dimension")
+        esz = 4 if dtype == STB_F32 else 2
+        n = 1
+        for d in shape:
+            n *= d
+        addr = ctypes.c_uint64()
+        call("stb_alloc", self.handle, n * esz, ctypes.byref(addr))
+        return DeviceTensor(self, addr.value, shape, dtype, n * esz)
+
+    def release(self, t: DeviceTensor) -> None:
+        """Idempotent release (CudaSession.scala:852-861)."""
+        self._check()
+        require(t.session is self, "tensor belongs to another session")
+        if t._alive[0]:
+            t._alive[0] = False
+            if t.owner:
+                call("stb_release", self.handle, t.address)
+
+    def _validate(self, t: DeviceTensor) -> None:
+        self._check()
+        require(isinstance(t, DeviceTensor) and t.session is self, "tensor belongs to another session")
+        if not t._alive[0]:
+            raise IllegalStateException("validate", 6, "tensor was released")
+
+    def shape(self, t: DeviceTensor) -> tuple:
+        self._validate(t)
+        return t.shape
+
+    # -- transfers
+    def upload(self, source: np.ndarray) -> DeviceTensor:
+        """FloatBackend.upload of a Float32 tensor (packed row-major)."""
+        a = np.ascontiguousarray(source, dtype=np.float32)
+        t = self.allocate(a.shape, STB_F32)
+        try:
+            if a.size:
+                call("stb_upload", self.handle, a.ctypes.data, a.nbytes, t.address)
+        except Exception:
+            self.release(t)
+            raise
+        return t
+
+    def upload_half(self, bits: np.ndarray, dtype: int, shape=None, transposed_weight: bool = False) -> DeviceTensor:
+        """Raw BF16/F16 payload straight into HBM, no F32 expansion (replaces SafeTensors.readFloat
+        + upload of the widened weight, SafeTensors.scala:63-77 / BackendLlama.scala:161-168)."""
+        require(dtype in (STB_BF16, STB_F16), "half upload requires BF16 or F16")
+        raw = np.ascontiguousarray(bits)
+        require(raw.dtype.itemsize == 2, "half payload must be 16-bit words")
+        shape = tuple(shape) if shape is not None else raw.shape
+        n = 1
+        for d in shape:
+            n *= int(d)
+        require(n == raw.size, "shape does not match payload")
+        t = self.allocate(shape, dtype)
+        try:
+            if raw.size:
+                call("stb_upload", self.handle, raw.ctypes.data, raw.nbytes, t.address)
+        except Exception:
+            self.release(t)
+            raise
+        if transposed_weight:
+            t.shape = (shape[1], shape[0])
+            t.transposed_weight = True
+        return t
+
+    def upload_weight(self, bits: np.ndarray, dtype: int) -> DeviceTensor:
+        """An (out,in) half weight used as W^T by matmul (BackendLlama.prepare's transposed upload)."""
+        require(np.ndim(bits) == 2, "Linear weight must have shape (out, in)")
+        return self.upload_half(bits, dtype, bits.shape, transposed_weight=True)
+
+    def download(self, t: DeviceTensor) -> np.ndarray:
+        self._validate(t)
+        require(t.dtype == STB_F32, "download returns Float32 tensors")
+        out = np.empty(t.shape, np.float32)
+        call("stb_download", self.handle, t.address, out.ctypes.data, out.nbytes)
+        return out
+
+    def download_raw(self, t: DeviceTensor) -> np.ndarray:
+        self._validate(t)
+        out = np.empty(t.nbytes, np.uint8)
+        call("stb_download", self.handle, t.address, out.ctypes.data, out.nbytes)
+        return out
+
+    # -- arithmetic on the hot path
+    def matmul(self, a: DeviceTensor, b: DeviceTensor) -> DeviceTensor:
+        """FloatBackend.matmul(x, W^T) where b is a resident (out,in) half weight
+        (CudaSession.matmul, CudaSession.scala:561-571 -> the B200 decode GEMV)."""
+        self._validate(a)
+        self._validate(b)
+        require(len(a.shape) == 2 and len(b.shape) == 2 and a.shape[1] == b.shape[0], "CUDA GEMM shape mismatch")
+        require(a.dtype == STB_F32, "activations must be Float32")
+        require(b.transposed_weight, "device matmul takes a resident (out,in) weight uploaded for W^T")
+        M, K = a.shape
+        N = b.shape[1]
+        require(max(M, N, K) <= 0x7fffffff, "CUDA GEMM dimension exceeds Int indexing")
+        y = self.allocate((M, N), STB_F32)
+        try:
+            call("stb_linear", self.handle, a.address, b.address, b.dtype, 0, y.address, M, N, K)
+        except Exception:
+            self.release(y)
+            raise
+        return y
+
+    def linear(self, x: DeviceTensor, weight: DeviceTensor, bias: DeviceTensor | None = None,
+               prefill: bool = False) -> DeviceTensor:
+        """y = x.W^T (+ bias) in one launch; prefill=True takes the tcgen05 path (x rounded to half)."""
+        self._validate(x)
+        self._validate(weight)
+        require(weight.transposed_weight, "weight must be a resident (out,in) weight")
+        M, K = x.shape
+        N = weight.shape[1]
+        require(weight.shape[0] == K, "Linear shape mismatch")
+        if bias is not None:
+            self._validate(bias)
+            require(bias.shape == (N,), "Linear bias shape mismatch")
+        y = self.allocate((M, N), STB_F32)
+        fn = "stb_linear_prefill" if prefill else "stb_linear"
+        try:
+            call(fn, self.handle, x.address, weight.address, weight.dtype,
+                 bias.address if bias is not None else 0, y.address, M, N, K)
+        except Exception:
+            self.release(y)
+            raise
+        return y
+
+    def fill_normal(self, t: DeviceTensor, seed: int, stream: int, std: float) -> None:
+        self._validate(t)
+        call("stb_fill_normal", self.handle, t.address, t.dtype, t.numel, seed, stream, std)
+
+    # -- tensor parallel
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = (ctypes.c_uint8 * 128)()
+        call("stb_nccl_unique_id", buf)
+        return bytes(buf)
+
+    def init_tp(self, nranks: int, rank: int, unique_id: bytes | None) -> None:
+        buf = (ctypes.c_uint8 * 128)(*(unique_id or bytes(128)))
+        call("stb_session_init_tp", self.handle, nranks, rank, buf)
+
+    def allreduce_sum(self, t: DeviceTensor) -> None:
+        self._validate(t)
+        call("stb_allreduce_sum_f32", self.handle, t.address, t.numel)

@@ -1,0 +1,320 @@
+"""Llama runtime mirror: LlamaConfig, BackendLlama and BackendLlamaCache over libstb200.so.
+
+Names, argument meaning and error behaviour follow the reference
+(models/src/main/scala/scalatorch/models/{LlamaConfig,BackendLlama,BackendLlamaCache}.scala):
+invalid requests raise IllegalArgumentException before any native call; the cache position
+advances only after a whole chunk succeeded; generation is greedy (temperature 0) with the
+reference's lowest-id tie rule and EOS stop.
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .ffm import (B200Session, IllegalArgumentException, IllegalStateException, STB_BF16, STB_F16, STB_F32,
+                  call, library, require)
+
+# stb_llama_weight
+W_EMBED, W_FINAL_NORM, W_LM_HEAD, W_IN_NORM, W_POST_NORM = 0, 1, 2, 3, 4
+W_Q, W_K, W_V, W_O, W_GATE, W_UP, W_DOWN = 5, 6, 7, 8, 9, 10, 11
+LAYER_WEIGHTS = {
+    "input_layernorm": W_IN_NORM, "post_attention_layernorm": W_POST_NORM,
+    "self_attn.q_proj": W_Q, "self_attn.k_proj": W_K, "self_attn.v_proj": W_V, "self_attn.o_proj": W_O,
+    "mlp.gate_proj": W_GATE, "mlp.up_proj": W_UP, "mlp.down_proj": W_DOWN,
+}
+GLOBAL_WEIGHTS = {"model.embed_tokens.weight": W_EMBED, "model.norm.weight": W_FINAL_NORM, "lm_head.weight": W_LM_HEAD}
+
+
+def weight_stream(which: int, layer: int = 0) -> int:
+    """Generator stream of a named tensor in stb_llama_init_random."""
+    return 4096 + which if which in (W_EMBED, W_FINAL_NORM, W_LM_HEAD) else layer * 16 + which
+
+
+@dataclass
+class LlamaConfig:
+    """LlamaConfig (LlamaConfig.scala:12-23) with the same validation."""
+    vocab_size: int
+    hidden_size: int
+    intermediate_size: int
+    num_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    max_positions: int = 2048
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    tie_word_embeddings: bool = False
+    bos_token_id: int | None = 1
+    eos_token_ids: tuple = (2,)
+    initializer_range: float = 0.02
+
+    def __post_init__(self):
+        require(self.vocab_size > 0 and self.hidden_size > 0 and self.intermediate_size > 0 and self.num_layers > 0
+                and self.max_positions > 0, "invalid Llama dimensions")
+        require(self.num_attention_heads > 0 and self.num_key_value_heads > 0
+                and self.hidden_size % self.num_attention_heads == 0
+                and self.num_attention_heads % self.num_key_value_heads == 0, "invalid Llama head dimensions")
+        require(self.head_dim % 2 == 0, "Llama rotary head width must be even")
+        require(np.isfinite(self.rms_norm_eps) and self.rms_norm_eps > 0 and np.isfinite(self.rope_theta)
+                and self.rope_theta > 0, "invalid Llama norm/rotary configuration")
+        require(all(0 <= i < self.vocab_size for i in ([self.bos_token_id] if self.bos_token_id is not None else [])
+                    + list(self.eos_token_ids)), "special token ID out of vocabulary")
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_attention_heads
+
+    @staticmethod
+    def from_json(text: str) -> "LlamaConfig":
+        """LlamaConfig.fromJson (LlamaConfig.scala:44-112): strict llama/SiLU subset."""
+        try:
+            f = json.loads(text, object_pairs_hook=_no_duplicates)
+        except ValueError as e:
+            raise IllegalArgumentException(f"invalid Llama config JSON: {e}") from e
+        require(isinstance(f, dict), "Llama config must be an object")
+        require(f.get("model_type") == "llama", "only model_type=llama is supported")
+        require(f.get("hidden_act", "silu") == "silu", "only SiLU Llama MLP is supported")
+        for key in ("rope_scaling", "rope_parameters", "sliding_window"):
+            require(f.get(key) is None, f"unsupported Llama option: {key}")
+        require(not f.get("attention_bias", False) and not f.get("mlp_bias", False), "Llama projection biases unsupported")
+        require(f.get("attention_dropout", 0.0) == 0 and f.get("pretraining_tp", 1) == 1,
+                "unsupported Llama dropout/tensor parallel setting")
+        require(f.get("partial_rotary_factor", 1.0) == 1.0, "partial rotary dimensions unsupported")
+
+        def integer(key, default=None):
+            v = f.get(key, default)
+            require(isinstance(v, int) and not isinstance(v, bool) and 0 <= v <= 0x7FFFFFFF,
+                    f"expected nonnegative integer config: {key}")
+            return v
+
+        heads = integer("num_attention_heads")
+        eos = f.get("eos_token_id", 2)
+        eos = () if eos is None else (tuple(eos) if isinstance(eos, list) else (eos,))
+        c = LlamaConfig(integer("vocab_size"), integer("hidden_size"), integer("intermediate_size"),
+                        integer("num_hidden_layers"), heads, integer("num_key_value_heads", heads),
+                        integer("max_position_embeddings", 2048), float(f.get("rms_norm_eps", 1e-6)),
+                        float(f.get("rope_theta", 10000.0)), bool(f.get("tie_word_embeddings", False)),
+                        f.get("bos_token_id", 1), eos, float(f.get("initializer_range", 0.02)))
+        require(integer("head_dim", c.head_dim) == c.head_dim, "custom Llama head_dim unsupported")
+        return c
+
+
+def _no_duplicates(pairs):
+    keys = [k for k, _ in pairs]
+    if len(keys) != len(set(keys)):
+        raise ValueError("duplicate key")
+    return dict(pairs)
+
+
+class _Config(ctypes.Structure):
+    _fields_ = [("vocab_size", ctypes.c_int), ("hidden_size", ctypes.c_int), ("intermediate_size", ctypes.c_int),
+                ("num_layers", ctypes.c_int), ("num_attention_heads", ctypes.c_int),
+                ("num_key_value_heads", ctypes.c_int), ("max_positions", ctypes.c_int),
+                ("tie_word_embeddings", ctypes.c_int), ("rms_norm_eps", ctypes.c_double),
+                ("rope_theta", ctypes.c_double), ("weight_dtype", ctypes.c_int), ("tp_rank", ctypes.c_int),
+                ("tp_size", ctypes.c_int)]
+
+
+def _declare_llama():
+    L = library()
+    P, I, U64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64
+    sig = {
+        "stb_llama_create": [P, P, ctypes.POINTER(P)],
+        "stb_llama_destroy": [P],
+        "stb_llama_weight_bytes": [P, ctypes.POINTER(U64)],
+        "stb_llama_set_weight": [P, I, I, P, U64, I],
+        "stb_llama_init_random": [P, U64, ctypes.c_double],
+        "stb_llama_cache_create": [P, I, I, ctypes.POINTER(P)],
+        "stb_llama_cache_destroy": [P],
+        "stb_llama_cache_position": [P, ctypes.POINTER(I)],
+        "stb_llama_cache_reset": [P],
+        "stb_llama_decode": [P, P, I, I, P, P],
+        "stb_llama_generate": [P, P, I, I, I, P, I, P, P, P],
+    }
+    for name, args in sig.items():
+        fn = getattr(L, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = args
+
+
+class BackendLlama:
+    """Prepared, thread-confined inference over resident half weights (BackendLlama.scala:27-174)."""
+
+    def __init__(self, session: B200Session, config: LlamaConfig, weight_dtype: int = STB_BF16,
+                 tp_rank: int = 0, tp_size: int = 1):
+        _declare_llama()
+        require(weight_dtype in (STB_BF16, STB_F16), "Llama weights must be BF16 or F16")
+        self.session = session
+        self.config = config
+        self.weight_dtype = weight_dtype
+        c = _Config(config.vocab_size, config.hidden_size, config.intermediate_size, config.num_layers,
+                    config.num_attention_heads, config.num_key_value_heads, config.max_positions,
+                    int(config.tie_word_embeddings), config.rms_norm_eps, config.rope_theta, weight_dtype,
+                    tp_rank, tp_size)
+        h = ctypes.c_void_p()
+        call("stb_llama_create", session.handle, ctypes.byref(c), ctypes.byref(h))
+        self.handle = h
+        self._closed = False
+        self._caches = []
+
+    # -- preparation
+    @classmethod
+    def prepare_random(cls, session, config, seed: int, weight_dtype: int = STB_BF16, tp_rank=0, tp_size=1):
+        """LlamaModel.init + BackendLlama.prepare in one step: N(0, initializer_range) matrices generated
+        on the device by the counter-based generator, norms = 1."""
+        m = cls(session, config, weight_dtype, tp_rank, tp_size)
+        try:
+            call("stb_llama_init_random", m.handle, seed, config.initializer_range)
+        except Exception:
+            m.close()
+            raise
+        return m
+
+    def set_weight(self, name: str, payload: np.ndarray, dtype: int) -> None:
+        """Upload one named tensor's raw payload (full tensor; this rank keeps its shard)."""
+        which, layer = _parse_name(name)
+        raw = np.ascontiguousarray(payload)
+        call("stb_llama_set_weight", self.handle, which, layer, raw.ctypes.data, raw.nbytes, dtype)
+
+    @property
+    def weight_bytes(self) -> int:
+        v = ctypes.c_uint64()
+        call("stb_llama_weight_bytes", self.handle, ctypes.byref(v))
+        return v.value
+
+    def close(self) -> None:
+        if not self._closed:
+            for c in list(self._caches):
+                c.close()
+            self._closed = True
+            call("stb_llama_destroy", self.handle)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _check(self):
+        if self._closed:
+            raise IllegalStateException("BackendLlama", 6, "prepared Llama is closed")
+
+    # -- inference
+    def new_cache(self, batch_size: int = 1, capacity: int | None = None) -> "BackendLlamaCache":
+        self._check()
+        cap = self.config.max_positions if capacity is None else capacity
+        require(batch_size > 0 and 0 < cap <= self.config.max_positions, "invalid model cache dimensions/budget")
+        c = BackendLlamaCache(self, batch_size, cap)
+        self._caches.append(c)
+        return c
+
+    def generate_ids(self, prompt, max_new_tokens: int, eos_token_ids=None, timings: list | None = None):
+        """Greedy BackendLlama.generateIds (BackendLlama.scala:126-141).  prompt: 1-D ids, or 2-D
+        (batch, tokens) for a batch of equal-length prompts; returns list(s) of ids."""
+        self._check()
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int64))
+        single = p.ndim == 1
+        if single:
+            p = p[None, :]
+        require(p.ndim == 2 and p.shape[1] > 0 and max_new_tokens >= 0
+                and p.shape[1] + max_new_tokens <= self.config.max_positions, "invalid generation length")
+        require(bool(np.all((p >= 0) & (p < self.config.vocab_size))), "generation token outside vocabulary")
+        eos = np.ascontiguousarray(np.asarray(self.config.eos_token_ids if eos_token_ids is None else eos_token_ids,
+                                              np.int64).reshape(-1))
+        b, t = p.shape
+        out = np.empty((b, t + max_new_tokens), np.int64)
+        gen = np.zeros(b, np.int32)
+        tm = np.zeros(2, np.float32)
+        call("stb_llama_generate", self.handle, p.ctypes.data, b, t, max_new_tokens,
+             eos.ctypes.data if eos.size else None, int(eos.size), out.ctypes.data, gen.ctypes.data, tm.ctypes.data)
+        if timings is not None:
+            timings[:] = [float(tm[0]), float(tm[1])]
+        rows = [out[i, :t + gen[i]].tolist() for i in range(b)]
+        return rows[0] if single else rows
+
+
+class BackendLlamaCache:
+    """Resident KV cache (BackendLlamaCache.scala:8-49)."""
+
+    def __init__(self, model: BackendLlama, batch_size: int, capacity: int):
+        self.model = model
+        self.batch_size = batch_size
+        self.capacity = capacity
+        h = ctypes.c_void_p()
+        call("stb_llama_cache_create", model.handle, batch_size, capacity, ctypes.byref(h))
+        self.handle = h
+        self._closed = False
+
+    @property
+    def position(self) -> int:
+        self._check()
+        v = ctypes.c_int()
+        call("stb_llama_cache_position", self.handle, ctypes.byref(v))
+        return v.value
+
+    def _check(self):
+        if self._closed:
+            raise IllegalStateException("BackendLlamaCache", 6, "model cache is closed")
+
+    def decode(self, tokens, want_logits: bool = True):
+        """tokens (batch, count) -> logits (batch, count, vocab) as float32, and the greedy next ids."""
+        self._check()
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int64))
+        require(t.ndim == 2 and t.shape[0] == self.batch_size and t.shape[1] > 0,
+                "cache tokens must match batch with positive chunk length")
+        require(self.position + t.shape[1] <= self.capacity, "model cache capacity exceeded")
+        require(bool(np.all((t >= 0) & (t < self.model.config.vocab_size))), "embedding token ID out of bounds")
+        logits = np.empty((t.shape[0], t.shape[1], self.model.config.vocab_size), np.float32) if want_logits else None
+        nxt = np.empty(t.shape[0], np.int64)
+        call("stb_llama_decode", self.handle, t.ctypes.data, t.shape[0], t.shape[1],
+             logits.ctypes.data if logits is not None else None, nxt.ctypes.data)
+        return logits, nxt.tolist()
+
+    def reset(self) -> None:
+        self._check()
+        call("stb_llama_cache_reset", self.handle)
+
+    def close(self) -> None:
+        if not self._closed:
+            self._closed = True
+            if self in self.model._caches:
+                self.model._caches.remove(self)
+            call("stb_llama_cache_destroy", self.handle)
+
+
+def _parse_name(name: str):
+    if name in GLOBAL_WEIGHTS:
+        return GLOBAL_WEIGHTS[name], 0
+    parts = name.split(".")
+    require(len(parts) >= 5 and parts[0] == "model" and parts[1] == "layers" and parts[-1] == "weight",
+            f"Llama weight names mismatch: {name}")
+    layer = int(parts[2])
+    key = ".".join(parts[3:-1])
+    require(key in LAYER_WEIGHTS, f"Llama weight names mismatch: {name}")
+    return LAYER_WEIGHTS[key], layer
+
+
+def load_safetensors(session: B200Session, directory: str, weight_dtype: int | None = None,
+                     tp_rank: int = 0, tp_size: int = 1) -> BackendLlama:
+    """LlamaModel.load + BackendLlama.prepare with raw half uploads (no F32 widening on the host)."""
+    import os
+
+    from .io import SafeTensorSet
+    with open(os.path.join(directory, "config.json")) as f:
+        config = LlamaConfig.from_json(f.read())
+    archive = SafeTensorSet.open(directory)
+    dtypes = {archive.info(n).dtype for n in archive.names() if archive.info(n).shape and len(archive.info(n).shape) == 2}
+    require(len(dtypes) == 1 and next(iter(dtypes)) in ("BF16", "F16"), "Llama matrices must share one BF16/F16 dtype")
+    wdt = STB_BF16 if next(iter(dtypes)) == "BF16" else STB_F16
+    m = BackendLlama(session, config, weight_dtype or wdt, tp_rank, tp_size)
+    try:
+        for name in archive.names():
+            info = archive.info(name)
+            raw = archive.read_raw(name)
+            m.set_weight(name, raw, {"F32": STB_F32, "BF16": STB_BF16, "F16": STB_F16}[info.dtype])
+    except Exception:
+        m.close()
+        raise
+    return m

@@ -1,0 +1,144 @@
+"""Device Llama runtime against the CPU oracle on the same synthetic BF16 weights.
+
+Tolerances: logits |a - e| <= 1e-5 * (1 + |e|) (the reference holds 3e-6*(1+|e|) between its
+own CUDA and CPU paths, BackendLlamaSuite.scala:18, for a 1-layer model; deeper models add
+per-layer Float32 reassociation); greedy token ids identical for the small models.
+"""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+from llama_fixtures import SMOL, TINY, named_bf16_weights, oracle_model
+from scalatorch import ffm
+from scalatorch.io import write_safetensors
+from scalatorch.models import BackendLlama, LlamaConfig, load_safetensors
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 1e-5
+
+
+def close(a, e, tol=LOGIT_TOL):
+    err = np.abs(a.astype(np.float64) - e.astype(np.float64))
+    lim = tol * (1 + np.abs(e.astype(np.float64)))
+    assert np.all(err <= lim), f"max err {err.max()}, worst ratio {np.max(err / lim)}"
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    return LlamaConfig(**TINY)
+
+
+def test_tiny_cached_decode_matches_oracle(session, tiny):
+    ref = oracle_model(tiny, seed=3)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, tiny.vocab_size, (2, 5))
+    with BackendLlama.prepare_random(session, tiny, seed=3) as m:
+        cache = m.new_cache(batch_size=2, capacity=12)
+        oc = ref.new_cache(2, 12)
+        got, nxt = cache.decode(prompt)
+        want = ref.decode(oc, prompt)
+        close(got, want)
+        assert cache.position == 5
+        for step in range(4):
+            tok = rng.integers(0, tiny.vocab_size, (2, 1))
+            got, nxt = cache.decode(tok)
+            want = ref.decode(oc, tok)
+            close(got, want)
+            assert nxt == [int(np.argmax(want[b, -1])) for b in range(2)]
+        assert cache.position == 9
+        ref.free_cache(oc)
+        cache.close()
+
+
+def test_tiny_generate_ids_match_oracle(session, tiny):
+    ref = oracle_model(tiny, seed=5)
+    prompt = [1, 17, 400, 999, 3]
+    with BackendLlama.prepare_random(session, tiny, seed=5) as m:
+        assert m.generate_ids(prompt, 20) == ref.generate(prompt, 20)
+        # EOS stop: stop at the 4th generated id of the unconstrained run
+        full = ref.generate(prompt, 20)
+        eos = full[len(prompt) + 3]
+        got = m.generate_ids(prompt, 20, eos_token_ids=[eos])
+        assert got == ref.generate(prompt, 20, eos=[eos])
+        assert got[-1] == eos and len(got) <= len(full)
+        assert m.generate_ids(prompt, 0) == prompt
+
+
+def test_batched_generation_rows_are_independent(session, tiny):
+    ref = oracle_model(tiny, seed=9)
+    prompts = np.array([[5, 6, 7, 8], [900, 1, 2, 3], [42, 42, 42, 42]])
+    with BackendLlama.prepare_random(session, tiny, seed=9) as m:
+        rows = m.generate_ids(prompts, 10)
+        for b in range(3):
+            assert rows[b] == ref.generate(prompts[b].tolist(), 10)
+
+
+def test_safetensors_raw_upload_equals_device_init(session, tiny):
+    named = named_bf16_weights(tiny, seed=11)
+    with tempfile.TemporaryDirectory() as d:
+        cfg = ('{"model_type":"llama","vocab_size":1000,"hidden_size":64,"intermediate_size":128,'
+               '"num_hidden_layers":2,"num_attention_heads":4,"num_key_value_heads":2,'
+               '"max_position_embeddings":64,"tie_word_embeddings":false,"eos_token_id":null}')
+        open(os.path.join(d, "config.json"), "w").write(cfg)
+        names = sorted(named)
+        half = len(names) // 2
+        for i, part in enumerate((names[:half], names[half:])):  # a two-shard set
+            write_safetensors(os.path.join(d, f"model-{i}.safetensors"),
+                              {n: ("BF16", named[n].shape, named[n]) for n in part})
+        loaded = load_safetensors(session, d)
+    prompt = [3, 1, 4, 1, 5, 9, 2, 6]
+    with loaded, BackendLlama.prepare_random(session, tiny, seed=11) as gen:
+        a = loaded.new_cache(1, 16)
+        b = gen.new_cache(1, 16)
+        la, _ = a.decode([prompt])
+        lb, _ = b.decode([prompt])
+        assert np.array_equal(la, lb)  # identical bits: raw upload == device generator
+        # resident bytes: half matrices (never widened), F32 norms, the double rotary table
+        H, V, I, L, hd, pos = 64, 1000, 128, 2, 16, 64
+        half_matrices = 2 * V * H + L * ((4 + 2 * 2) * hd * H + H * H + 2 * I * H + H * I)
+        assert loaded.weight_bytes == 2 * half_matrices + 4 * H * (2 * L + 1) + pos * (hd // 2) * 16
+
+
+def test_tied_head_is_stored_once(session):
+    cfg = LlamaConfig(**dict(TINY, tie_word_embeddings=True))
+    untied = LlamaConfig(**TINY)
+    with BackendLlama(session, cfg) as a, BackendLlama(session, untied) as b:
+        assert b.weight_bytes - a.weight_bytes == 2 * cfg.vocab_size * cfg.hidden_size
+
+
+def test_cache_rejects_and_keeps_position(session, tiny):
+    with BackendLlama.prepare_random(session, tiny, seed=1) as m:
+        c = m.new_cache(1, 6)
+        c.decode([[1, 2, 3, 4]])
+        with pytest.raises(ffm.IllegalArgumentException):
+            c.decode([[1, 2, 3]])  # capacity 6 exceeded
+        assert c.position == 4
+        with pytest.raises(ffm.IllegalArgumentException):
+            c.decode([[1000]])  # outside the vocabulary
+        assert c.position == 4
+        c.reset()
+        assert c.position == 0
+        with pytest.raises(ffm.IllegalArgumentException):
+            m.generate_ids([1], 64)  # prompt + new > max_positions
+        c.close()
+
+
+def test_smollm2_shaped_greedy_ids_and_logits(session):
+    """BASELINE config 2 shape (30 layers, vocab 49152, 9/3 heads) with a shortened prompt and
+    decode so the CPU oracle finishes in seconds; ids must be identical."""
+    cfg = LlamaConfig(**SMOL)
+    ref = oracle_model(cfg, seed=2024)
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, cfg.vocab_size, 12).tolist()
+    with BackendLlama.prepare_random(session, cfg, seed=2024) as m:
+        assert m.generate_ids(prompt, 12) == ref.generate(prompt, 12)
+        c = m.new_cache(1, 32)
+        oc = ref.new_cache(1, 32)
+        got, _ = c.decode([prompt])
+        close(got, ref.decode(oc, np.array([prompt])))
+        got, _ = c.decode([[17]])
+        close(got, ref.decode(oc, np.array([[17]])))
+        ref.free_cache(oc)
+        c.close()
