@@ -73,6 +73,8 @@ struct stb_session {
   void *nccl = nullptr;  // ncclComm_t
   int tp_rank = 0, tp_size = 1;
   std::atomic<uint64_t> launches{0};
+  uint64_t scratch = 0, scratch_bytes = 0;  // grow-only device scratch (charged to the budget)
+  uint64_t err_word = 0;                    // device int: nonzero when a bounded device wait expired
   bool closed = false;
 };
 
@@ -89,8 +91,47 @@ void download(stb_session *s, uint64_t src, void *host, uint64_t bytes);
 void fill_normal(stb_session *s, uint64_t dst, int dtype, uint64_t count, uint64_t seed, uint64_t stream,
                  double stddev);
 void fill_value(stb_session *s, uint64_t dst, int dtype, uint64_t count, float value);
+// Grow-only scratch buffer of at least `bytes` (contents undefined).
+uint64_t session_scratch(stb_session *s, uint64_t bytes);
+// Device error word kernels write when a bounded wait expires (allocated and zeroed on first use).
+int *session_error_word(stb_session *s);
+// After a stream synchronisation: throws (and clears the word) if a kernel recorded an error.
+void check_device_error(stb_session *s);
+
+// ---------------------------------------------------------------- launch helpers
+
+// Launches `kernel` on `stream`; with pdl the launch carries programmatic stream serialisation, so
+// it may start while the previous kernel drains -- the kernel must call pdl_wait() before it
+// touches anything the previous kernel writes.  Inside stream capture this becomes a
+// programmatic graph edge.
+template <typename... KArgs, typename... Args>
+void launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                   Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) throw Error(STB_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(e));
+}
 
 // ---------------------------------------------------------------- device helpers
+
+// Programmatic dependent launch: wait for the prerequisite grid's completion and memory, and let
+// the dependent grid begin launching.  Both are no-ops for launches without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// L2 prefetch of a byte range (16-byte aligned start, size a multiple of 16), issued by one thread.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
   uint4 v;

@@ -1,5 +1,366 @@
-// Prefill Linear on the tcgen05 tensor cores (placeholder until the TMA/TMEM kernel lands).
+// Prefill Linear on the tcgen05 tensor cores: y[M,N] = half(x)[M,K] . W[N,K]^T (+ bias), FP32
+// accumulation in TMEM.  The same Linear as stb_linear (nn.Linear.apply, nn/src/main/scala/
+// scalatorch/nn/Linear.scala:11-17) for prompt-sized M; the activations are rounded to the
+// weight's type (round-to-nearest-even, SafeTensorsWriter.bfloat's rule for BF16) because a
+// kind::f16 MMA takes both operands in one 16-bit type -- that rounding is the tolerance source.
+//
+// Kernel shape (one CTA per SM, persistent over 128x256 output tiles):
+//   warp 0      TMA producer: x tile 128x64 and W tile 256x64 per stage (SWIZZLE_128B, K-major),
+//               4-stage shared-memory ring guarded by full/empty mbarriers
+//   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16) into a TMEM accumulator and
+//               commits to the ring's empty barrier / the accumulator's full barrier
+//   warp 2      allocates and frees the 512 TMEM columns (two 256-column accumulators)
+//   warps 4..7  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, + bias, Float32 stores;
+//               accumulator double buffering overlaps a tile's epilogue with the next tile's MMAs
+// Every mbarrier wait is bounded by the global timer; on expiry the kernel records an error code,
+// stops issuing work, drains its MMAs (bounded) and frees TMEM before returning.
+// No cluster multicast is used anywhere: each CTA loads its own tiles.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
+
+namespace stb {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s per wait
+
+struct TcParams {
+  int M, N, K, ldy;
+  float *y;
+  const float *bias;
+  int *err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false (and the abort flag set) if the phase did not complete within WAIT_NS or
+// another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, int *err,
+                                          int code) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 0;; i++) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > WAIT_NS) {
+        *abort_flag = 1;
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor (sm_100 form): K-major, 128-byte swizzle, 8-row groups 1024 B
+// apart; start address and offsets in 16-byte units, descriptor version 1 at bit 46.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr & 0x3FFFF) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(256, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, TcParams p,
+                   uint32_t idesc) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES), tempty0 = smem_u32(bars + 2 * STAGES + 2);
+  const uint32_t drain = smem_u32(bars + 2 * STAGES + 4);
+  uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 5);
+  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mtiles = (p.M + BM - 1) / BM, ntiles = (p.N + BN - 1) / BN;
+  const int tiles = mtiles * ntiles, kblocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sa0 = smem_u32(smem), sb0 = sa0 + STAGES * A_BYTES;
+
+  if (warp == 0 && lane == 0) {
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      const int mb = tile % mtiles, nb = tile / mtiles;
+      for (int kb = 0; kb < kblocks; kb++) {
+        if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, p.err, 1)) break;
+        mbar_expect_tx(full0 + 8 * stage, STAGE_BYTES);
+        tma_load_2d(sa0 + stage * A_BYTES, &ta, kb * BK, mb * BM, full0 + 8 * stage);
+        tma_load_2d(sb0 + stage * B_BYTES, &tb, kb * BK, nb * BN, full0 + 8 * stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    int stage = 0, it = 0;
+    uint32_t phase = 0;
+    bool issued = false;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, it++) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, p.err, 2)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(acc * BN);
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; kb++) {
+        if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, p.err, 3)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t a = smem_desc(sa0 + stage * A_BYTES), b = smem_desc(sb0 + stage * B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; k++)  // +32 bytes of K per instruction inside the swizzle row
+          mma_f16(d, a + (uint64_t)(2 * k), b + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+        issued = true;
+        mma_commit(empty0 + 8 * stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      mma_commit(tfull0 + 8 * acc);
+    }
+    if (issued) {  // all issued MMAs complete before TMEM is released
+      mma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.err, 4);
+    }
+  } else if (warp >= 4) {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int it = 0;
+    for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, it++) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      const int mb = tile % mtiles, nb = tile / mtiles;
+      if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, p.err, 5)) break;
+      tc_fence_after();
+      const int row = mb * BM + q * 32 + lane;
+      float *yrow = p.y + (size_t)row * p.ldy;
+      for (int c = 0; c < BN / 32; c++) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        const int n0 = nb * BN + c * 32;
+        if (row < p.M && n0 < p.N) {
+          if (n0 + 32 <= p.N && (p.ldy & 3) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                     __uint_as_float(r[j + 3]));
+              if (p.bias) {
+                v.x = v.x + p.bias[n0 + j];
+                v.y = v.y + p.bias[n0 + j + 1];
+                v.z = v.z + p.bias[n0 + j + 2];
+                v.w = v.w + p.bias[n0 + j + 3];
+              }
+              *reinterpret_cast<float4 *>(yrow + n0 + j) = v;
+            }
+          } else {
+            for (int j = 0; j < 32 && n0 + j < p.N; j++) {
+              float v = __uint_as_float(r[j]);
+              yrow[n0 + j] = p.bias ? v + p.bias[n0 + j] : v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty0 + 8 * acc);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                              : "memory");
+}
+
+// x (Float32) -> weight type, round to nearest even, 8 elements per thread.
+template <bool BF16>
+__global__ void round_activations_kernel(const float *x, uint16_t *out, size_t count) {
+  const size_t i = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) * 8;
+  if (i + 8 <= count) {
+    const float4 a = *reinterpret_cast<const float4 *>(x + i), b = *reinterpret_cast<const float4 *>(x + i + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint16_t h[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) h[j] = BF16 ? f32_to_bf16_rne(v[j]) : __half_as_ushort(__float2half_rn(v[j]));
+    uint4 packed;
+    packed.x = h[0] | ((uint32_t)h[1] << 16);
+    packed.y = h[2] | ((uint32_t)h[3] << 16);
+    packed.z = h[4] | ((uint32_t)h[5] << 16);
+    packed.w = h[6] | ((uint32_t)h[7] << 16);
+    *reinterpret_cast<uint4 *>(out + i) = packed;
+  } else {
+    for (size_t j = i; j < count; j++) out[j] = BF16 ? f32_to_bf16_rne(x[j]) : __half_as_ushort(__float2half_rn(x[j]));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  });
+  if (!fn) throw Error(STB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+CUtensorMap make_map(const void *base, int dtype, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = encode_fn()(&m, dtype == STB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                           2, const_cast<void *>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(STB_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
+int sm_count(int device) {
+  int n = 0;
+  STB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
+  return n;
+}
+
+}  // namespace
+
+// Instruction descriptor of kind::f16: D = F32 (bits 4-5 = 1), A/B = BF16 (1) or F16 (0) at bits
+// 7-9 / 10-12, both K-major (bits 15/16 = 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+uint32_t tc_idesc(int dtype) {
+  const uint32_t ab = dtype == STB_BF16 ? 1u : 0u;
+  return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// Enqueues the prefill GEMM on `stream`.  xh: the activations already in the weight's type
+// (M x K, row-major); err: device int that receives a nonzero code if a wait expired.
+void gemm_tc_launch(const void *xh, const void *w, int dtype, const float *bias, float *y, int ldy, int M, int N,
+                    int K, int *err, int device, cudaStream_t stream) {
+  const CUtensorMap ta = make_map(xh, dtype, (uint64_t)M, (uint64_t)K, BM);
+  const CUtensorMap tb = make_map(w, dtype, (uint64_t)N, (uint64_t)K, BN);
+  TcParams p{M, N, K, ldy, y, bias, err};
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, sm_count(device));
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  gemm_tc_kernel<<<grid, 256, SMEM_BYTES, stream>>>(ta, tb, p, tc_idesc(dtype));
+  check_launch("gemm_tc");
+}
+
+void round_activations(const float *x, uint16_t *out, size_t count, int dtype, cudaStream_t stream) {
+  const size_t threads = (count + 7) / 8;
+  const unsigned blocks = (unsigned)((threads + 255) / 256);
+  if (dtype == STB_BF16) round_activations_kernel<true><<<blocks, 256, 0, stream>>>(x, out, count);
+  else round_activations_kernel<false><<<blocks, 256, 0, stream>>>(x, out, count);
+  check_launch("round_activations");
+}
+
+}  // namespace stb
 
 using namespace stb;
 
@@ -9,8 +370,19 @@ int stb_linear_prefill(stb_session *s, uint64_t x, uint64_t w, int w_dtype, uint
                        int K) {
   return guarded([&] {
     enter(s);
-    (void)x; (void)w; (void)w_dtype; (void)bias; (void)y; (void)M; (void)N; (void)K;
-    throw Error(STB_ERR_UNSUPPORTED, "tensor-core prefill Linear is not built yet");
+    STB_REQUIRE(M >= 0 && N >= 0 && K >= 0, "Linear dimensions must be nonnegative");
+    STB_REQUIRE(w_dtype == STB_BF16 || w_dtype == STB_F16, "tensor-core Linear needs BF16 or F16 weights");
+    if (M == 0 || N == 0) return;
+    STB_REQUIRE(K > 0 && K % 8 == 0, "tensor-core Linear needs K a positive multiple of 8");
+    STB_REQUIRE(x && w && y, "null buffer");
+    STB_REQUIRE(x % 16 == 0 && w % 16 == 0 && y % 16 == 0, "buffers must be 16-byte aligned");
+    const uint64_t xbytes = (uint64_t)M * K * 2;
+    int *err = session_error_word(s);
+    const uint64_t scratch = session_scratch(s, xbytes);
+    round_activations((const float *)x, (uint16_t *)scratch, (size_t)M * K, w_dtype, s->stream);
+    gemm_tc_launch((const void *)scratch, (const void *)w, w_dtype, (const float *)bias, (float *)y, N, M, N, K, err,
+                   s->device, s->stream);
+    count_launch(s, 2);
   });
 }
 

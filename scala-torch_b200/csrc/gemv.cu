@@ -56,7 +56,7 @@ static void launch_one(const GemvParams &p, cudaStream_t stream) {
   const int rpb = (256 / TPR) * ROWS;
   const long blocks = (long)((p.N + rpb - 1) / rpb) * mtiles;
   if (blocks > 0x7fffffffL) throw Error(STB_ERR_INVALID, "GEMV grid too large");
-  gemv_kernel<MT, ROWS, TPR, WT, EPI><<<(unsigned)blocks, 256, 0, stream>>>(p, mtiles);
+  launch_kernel(gemv_kernel<MT, ROWS, TPR, WT, EPI>, dim3((unsigned)blocks), dim3(256), 0, stream, p.pdl, p, mtiles);
 }
 
 template <int MT, int ROWS, typename WT, int EPI>
@@ -101,9 +101,23 @@ static void dispatch_mt(const GemvParams &p, GemvConfig cfg, cudaStream_t stream
   }
 }
 
+// The shape actually instantiated for an epilogue: fused epilogues exist for MT in {1, 8} and
+// ROWS in {2, 4}; the plain one for MT in {1, 2, 4, 8} and ROWS in {1, 2, 4}.  Row-block counts
+// (the lm_head candidate slots) must be computed from this, not from the request.
+GemvConfig normalize_gemv(GemvConfig cfg, int epi) {
+  if (epi != EPI_PLAIN) {
+    if (cfg.mt != 1) cfg.mt = 8;
+    cfg.rows = cfg.rows >= 4 ? 4 : 2;
+  } else {
+    cfg.mt = cfg.mt <= 1 ? 1 : (cfg.mt <= 2 ? 2 : (cfg.mt <= 4 ? 4 : 8));
+    cfg.rows = cfg.rows >= 4 ? 4 : (cfg.rows >= 2 ? 2 : 1);
+  }
+  return cfg;
+}
+
 template <int EPI>
 int launch_gemv(const GemvParams &p, int w_dtype, GemvConfig cfg, cudaStream_t stream) {
-  if (EPI != EPI_PLAIN && cfg.mt != 1) cfg.mt = 8;
+  cfg = normalize_gemv(cfg, EPI);
   if (w_dtype == STB_BF16) dispatch_mt<__nv_bfloat16, EPI>(p, cfg, stream);
   else if (w_dtype == STB_F16) dispatch_mt<__half, EPI>(p, cfg, stream);
   else throw Error(STB_ERR_INVALID, "GEMV weight dtype must be BF16 or F16");

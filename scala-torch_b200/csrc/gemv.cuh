@@ -49,6 +49,7 @@ struct GemvParams {
   int *part_idx = nullptr;
   int row_offset = 0;  // global index of row 0 (vocab shard offset)
   const int *stop = nullptr;  // device flag; nonzero makes the kernel a no-op
+  bool pdl = false;           // launched as a programmatic dependent of the previous kernel
 };
 
 struct GemvConfig {
@@ -93,8 +94,6 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
   __shared__ float s_out[G][ROWS][MT];
   __shared__ float s_red[TPR > 32 ? 8 : 1][ROWS * MT];
 
-  if (p.stop && *p.stop) return;
-
   const int tid = threadIdx.x;
   const int g = tid / TPR, lane = tid % TPR;
   const int mtile = blockIdx.x % mtiles, rblock = blockIdx.x / mtiles;
@@ -102,6 +101,23 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
   const int mcount = min(MT, p.M - m0);
   const int rowbase = (rblock * G + g) * ROWS;
   const int nchunk = p.K >> 3;
+
+  if (p.pdl) {
+    // The weights never depend on the previous kernel: start pulling this block's rows (one
+    // contiguous range) into L2 before waiting for the producer of x.
+    if (tid == 0 && mtile == 0) {
+      const int r0 = rblock * G * ROWS;
+      const int nrows = min(G * ROWS, p.N - r0);
+      if (nrows > 0) {
+        const char *base = (const char *)p.w + (size_t)r0 * p.K * 2;
+        size_t bytes = (size_t)nrows * p.K * 2;
+        for (size_t off = 0; off < bytes; off += 65536)
+          prefetch_l2(base + off, (uint32_t)(bytes - off < 65536 ? bytes - off : 65536));
+      }
+    }
+    pdl_wait();
+  }
+  if (p.stop && *p.stop) return;
 
   if (p.norm_w) {
     for (int m = 0; m < MT; m++) {
@@ -174,6 +190,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
       }
     }
   }
+
+  if (p.pdl) pdl_trigger();  // the next kernel may start its own weight prefetch now
 
   // Group reduction in a fixed order.
 #pragma unroll
@@ -327,5 +345,7 @@ GemvConfig choose_gemv(int M, int N, int K, bool paired);
 template <int EPI>
 int launch_gemv(const GemvParams &p, int w_dtype, GemvConfig cfg, cudaStream_t stream);
 int gemv_row_blocks(int N, GemvConfig cfg);
+// The launch shape launch_gemv<epi> really uses for a requested config.
+GemvConfig normalize_gemv(GemvConfig cfg, int epi);
 
 }  // namespace stb

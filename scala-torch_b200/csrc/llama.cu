@@ -101,6 +101,7 @@ size_t esize(int dtype) { return dtype == STB_F32 ? 4 : 2; }
 
 __global__ void embed_kernel(const int64_t *tokens, const uint16_t *table, int dtype, int H, int V, float *hidden,
                              int rows, const int *stop) {
+  pdl_wait();
   if (stop && *stop) return;
   const int m = blockIdx.x;
   if (m >= rows) return;
@@ -112,11 +113,19 @@ __global__ void embed_kernel(const int64_t *tokens, const uint16_t *table, int d
 }
 
 // Causal grouped-query attention of CpuAttention.causal (cpu/.../CpuAttention.scala:20-50):
-// scores, softmax and the weighted value sum in double; one block per (token row, query head).
-__global__ void attention_kernel(const float *q, int ldq, const float *kcache, const float *vcache, float *out,
-                                 int ldo, int rows, int count, int nh, int kvh, int hd, int capacity,
-                                 const int *pos_dev, int pos0, const int *stop) {
-  extern __shared__ double s_p[];  // [capacity] scores, then 32 reduction slots
+// scores, softmax and the weighted value sum in double (the reference's precision); one block of
+// ATT_THREADS per (token row, query head).  Keys are spread over warps four at a time so each lane
+// keeps several coalesced K loads in flight; the weighted V sum splits the keys over thread groups
+// (one thread per output dimension in each group) and combines the groups in a fixed order.
+constexpr int ATT_THREADS = 256;
+
+__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float *q, int ldq, const float *kcache,
+                                                                const float *vcache, float *out, int ldo, int rows,
+                                                                int count, int nh, int kvh, int hd, int capacity,
+                                                                const int *pos_dev, int pos0, const int *stop) {
+  extern __shared__ double s_p[];  // [capacity] probabilities, [32] reductions, [ATT_THREADS] partial sums
+  pdl_wait();
+  pdl_trigger();
   if (stop && *stop) return;
   const int m = blockIdx.x / nh, h = blockIdx.x % nh;
   if (m >= rows) return;
@@ -129,51 +138,84 @@ __global__ void attention_kernel(const float *q, int ldq, const float *kcache, c
   const float *K = kcache + base * hd;
   const float *Vc = vcache + base * hd;
   double *red = s_p + capacity;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  double *part = red + 32;
+  constexpr int NW = ATT_THREADS / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const double scale = 1.0 / sqrt((double)hd);
   double local_max = -(double)INFINITY;
-  for (int j = warp; j < keys; j += nwarps) {
-    double dot = 0.0;
-    for (int d = lane; d < hd; d += 32) dot += (double)qr[d] * (double)K[(size_t)j * hd + d];
+  for (int j0 = warp * 4; j0 < keys; j0 += NW * 4) {
+    double dot[4] = {0.0, 0.0, 0.0, 0.0};
+    for (int d = lane; d < hd; d += 32) {
+      const double qd = (double)qr[d];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-    const double sc = dot * scale;
-    if (lane == 0) s_p[j] = sc;
-    local_max = fmax(local_max, sc);
+      for (int u = 0; u < 4; u++)
+        if (j0 + u < keys) dot[u] += qd * (double)K[(size_t)(j0 + u) * hd + d];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], off);
+      if (j0 + u < keys) {
+        const double sc = dot[u] * scale;
+        if (lane == 0) s_p[j0 + u] = sc;
+        local_max = fmax(local_max, sc);
+      }
+    }
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) local_max = fmax(local_max, __shfl_xor_sync(0xffffffffu, local_max, off));
   if (lane == 0) red[warp] = local_max;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    double mx = red[0];
-    for (int i = 1; i < nwarps; i++) mx = fmax(mx, red[i]);
-    red[0] = mx;
+  double mx = red[0];
+  for (int i = 1; i < NW; i++) mx = fmax(mx, red[i]);
+  double local_sum = 0.0;
+  for (int j = threadIdx.x; j < keys; j += ATT_THREADS) {
+    const double e = exp(s_p[j] - mx);
+    s_p[j] = e;
+    local_sum += e;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) local_sum += __shfl_xor_sync(0xffffffffu, local_sum, off);
+  __syncthreads();  // every thread has read red[] for the max
+  if (lane == 0) red[warp] = local_sum;
+  __syncthreads();
+  double den = 0.0;
+  for (int i = 0; i < NW; i++) den += red[i];
+  for (int j = threadIdx.x; j < keys; j += ATT_THREADS) s_p[j] = s_p[j] / den;
+  __syncthreads();
+  // weighted value sum: `groups` key subsets x hd dimensions
+  const int groups = ATT_THREADS / hd;
+  const int d = threadIdx.x % hd, grp = threadIdx.x / hd;
+  if (grp < groups) {
+    double acc = 0.0;
+    int j = grp;
+    for (; j + 3 * groups < keys; j += 4 * groups) {
+      const double v0 = (double)Vc[(size_t)j * hd + d], v1 = (double)Vc[(size_t)(j + groups) * hd + d];
+      const double v2 = (double)Vc[(size_t)(j + 2 * groups) * hd + d], v3 = (double)Vc[(size_t)(j + 3 * groups) * hd + d];
+      acc += s_p[j] * v0;
+      acc += s_p[j + groups] * v1;
+      acc += s_p[j + 2 * groups] * v2;
+      acc += s_p[j + 3 * groups] * v3;
+    }
+    for (; j < keys; j += groups) acc += s_p[j] * (double)Vc[(size_t)j * hd + d];
+    part[grp * hd + d] = acc;
   }
   __syncthreads();
-  const double mx = red[0];
-  __syncthreads();
-  for (int j = threadIdx.x; j < keys; j += blockDim.x) s_p[j] = exp(s_p[j] - mx);
-  __syncthreads();
-  if (threadIdx.x == 0) {  // sequential denominator, as the reference
-    double den = 0.0;
-    for (int j = 0; j < keys; j++) den += s_p[j];
-    red[0] = den;
-  }
-  __syncthreads();
-  const double den = red[0];
-  for (int j = threadIdx.x; j < keys; j += blockDim.x) s_p[j] = s_p[j] / den;
-  __syncthreads();
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+  if (threadIdx.x < hd) {
     double sum = 0.0;
-    for (int j = 0; j < keys; j++) sum += s_p[j] * (double)Vc[(size_t)j * hd + d];
-    out[(size_t)m * ldo + (size_t)h * hd + d] = (float)sum;
+    for (int gi = 0; gi < groups; gi++) sum += part[gi * hd + threadIdx.x];
+    out[(size_t)m * ldo + (size_t)h * hd + threadIdx.x] = (float)sum;
   }
 }
+
+size_t attention_smem(int capacity) { return (size_t)(capacity + 32 + ATT_THREADS) * sizeof(double); }
 
 // Greedy pick over every rank's per-block candidates (strict '>' in increasing id order, i.e.
 // lowest id on ties), token feedback, output append, EOS stop and position advance.
 __global__ void finalize_kernel(const float *pval, const int *pidx, int nparts_total, int batch, int count,
                                 int64_t *tokens, int *state, int64_t *out_ids, int out_stride, const int64_t *eos,
                                 int eos_count, int64_t *next_ids, int advance) {
+  pdl_wait();
   if (state[1]) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   int *stopped = state + 2;
@@ -382,7 +424,8 @@ void ensure_rows(stb_llama_cache *c, int rows) {
   // candidate slots per row: the most row blocks any lm_head launch shape of <= rows rows uses
   c->parts = 0;
   for (int mm : {1, 2, 4, 8, c->batch, rows})
-    if (mm <= rows) c->parts = std::max(c->parts, gemv_row_blocks(m->V, choose_gemv(mm, m->V, m->H, false)));
+    if (mm <= rows)
+      c->parts = std::max(c->parts, gemv_row_blocks(m->V, normalize_gemv(choose_gemv(mm, m->V, m->H, false), EPI_LOGITS)));
   const int qw = m->NH * m->hd;
   c->hidden = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
   c->sum = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
@@ -390,8 +433,9 @@ void ensure_rows(stb_llama_cache *c, int rows) {
   c->att = alloc_owned(s, c->owned, (uint64_t)rows * qw * 4);
   c->act = alloc_owned(s, c->owned, (uint64_t)rows * m->I * 4);
   c->logits = alloc_owned(s, c->owned, (uint64_t)rows * m->V * 4);
-  c->pval = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4);
-  c->pidx = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4);
+  // candidates: [rows][parts] per rank, [batch][tp*parts] after the cross-rank re-layout
+  c->pval = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
+  c->pidx = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
   c->gval = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
   c->gidx = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
   c->tokens = alloc_owned(s, c->owned, (uint64_t)rows * 8);
@@ -420,12 +464,11 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
   int launches = 0;
   const int wdt = m->c.weight_dtype;
 
-  embed_kernel<<<rows, 128, 0, st>>>((const int64_t *)c->tokens, (const uint16_t *)m->embed, wdt, H,
-                                     m->c.vocab_size, (float *)c->hidden, rows, stop);
-  check_launch("embed");
+  // The first kernel follows host copies (or the previous graph replay): a plain launch.  Every
+  // later kernel is a programmatic dependent of its predecessor (see launch_kernel / pdl_wait).
+  launch_kernel(embed_kernel, dim3(rows), dim3(128), 0, st, false, (const int64_t *)c->tokens,
+                (const uint16_t *)m->embed, wdt, H, m->c.vocab_size, (float *)c->hidden, rows, stop);
   launches++;
-  const float eps = 0;  // unused
-  (void)eps;
   const size_t kv_layer = (size_t)2 * c->batch * m->KV * c->capacity * m->hd;
   const size_t kv_half = kv_layer / 2;
   const int qw = m->NH * m->hd;
@@ -442,15 +485,15 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.rope = (const double2 *)m->rope; p.pos_dev = posd; p.pos0 = c->used; p.count = a.count;
       p.nh = m->NH; p.kvh = m->KV; p.hd = m->hd; p.capacity = c->capacity; p.k_cache = kc; p.v_cache = vc;
       p.stop = stop;
+      p.pdl = true;
       launch_gemv<EPI_QKV>(p, wdt, choose_gemv(rows, p.N, p.K, true), st);
       launches++;
     }
     {  // 2. attention
-      const size_t smem = (size_t)(c->capacity + 32) * sizeof(double);
-      attention_kernel<<<rows * m->NH, 128, smem, st>>>((const float *)c->qbuf, qw, kc, vc, (float *)c->att, qw,
-                                                        rows, a.count, m->NH, m->KV, m->hd, c->capacity, posd,
-                                                        c->used, stop);
-      check_launch("attention");
+      const size_t smem = attention_smem(c->capacity);
+      launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), smem, st, true, (const float *)c->qbuf,
+                    qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows, a.count, m->NH, m->KV,
+                    m->hd, c->capacity, posd, c->used, stop);
       launches++;
     }
     for (int half = 0; half < 2; half++) {  // 3. O (+residual)   then   4./5. MLP (+residual)
@@ -461,6 +504,7 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
         p.y = (float *)c->act; p.ldy = m->I;
         p.norm_w = (const float *)L.post_norm; p.norm_eps = m->c.rms_norm_eps;
         p.stop = stop;
+        p.pdl = true;
         launch_gemv<EPI_SILU>(p, wdt, choose_gemv(rows, p.N, p.K, true), st);
         launches++;
       }
@@ -470,6 +514,7 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.w = (const void *)(half == 0 ? L.o : L.down);
       p.M = rows; p.N = H; p.K = half == 0 ? qw : m->I;
       p.stop = stop;
+      p.pdl = true;
       if (m->tp == 1) {
         p.y = (float *)c->hidden; p.ldy = H; p.residual = (const float *)c->hidden; p.ldr = H;
         launch_gemv<EPI_RESID>(p, wdt, choose_gemv(rows, p.N, p.K, false), st);
@@ -503,12 +548,10 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
     p.norm_w = (const float *)m->final_norm; p.norm_eps = m->c.rms_norm_eps;
     p.part_val = (float *)c->pval; p.part_idx = (int *)c->pidx; p.row_offset = m->v0;
     p.stop = stop;
+    p.pdl = true;
     GemvConfig cfg = choose_gemv(brows, p.N, p.K, false);
-    const int parts = launch_gemv<EPI_LOGITS>(p, wdt, cfg, st);
+    const int parts = launch_gemv<EPI_LOGITS>(p, wdt, cfg, st);  // <= c->parts slots per row
     launches++;
-    if (parts != c->parts && !a.all_logits) {
-      // candidate buffers are sized for c->parts per row; configs for fewer rows never exceed it
-    }
     const float *gv = (const float *)c->pval;
     const int *gi = (const int *)c->pidx;
     int nparts = parts;
@@ -537,11 +580,10 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
         gi = (const int *)c->pidx;
         nparts = parts * m->tp;
       }
-      finalize_kernel<<<1, 256, 0, st>>>(gv, gi, nparts, brows, a.all_logits ? 1 : a.count, (int64_t *)c->tokens,
-                                         (int *)c->state, a.append ? (int64_t *)c->out_ids : nullptr,
-                                         c->out_stride, (const int64_t *)c->eos, c->eos_count, a.next_ids,
-                                         a.advance);
-      check_launch("finalize");
+      launch_kernel(finalize_kernel, dim3(1), dim3(256), 0, st, m->tp == 1, gv, gi, nparts, brows,
+                    a.all_logits ? 1 : a.count, (int64_t *)c->tokens, (int *)c->state,
+                    a.append ? (int64_t *)c->out_ids : nullptr, c->out_stride, (const int64_t *)c->eos,
+                    c->eos_count, a.next_ids, a.advance);
       launches++;
     }
   }
@@ -798,7 +840,8 @@ int stb_llama_cache_create(stb_llama *m, int batch, int capacity, stb_llama_cach
     STB_REQUIRE(batch > 0 && capacity > 0 && capacity <= m->c.max_positions, "invalid model cache dimensions/budget");
     // attention keeps one row of double scores per block in shared memory
     STB_REQUIRE(capacity <= 28000, "model cache capacity exceeds the attention score workspace");
-    const size_t smem = (size_t)(capacity + 32) * sizeof(double);
+    STB_REQUIRE(m->hd <= ATT_THREADS, "head width exceeds the attention block");
+    const size_t smem = attention_smem(capacity);
     if (smem > 48 * 1024)
       STB_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     auto *c = new stb_llama_cache();

@@ -49,6 +49,37 @@ void session_free(stb_session *s, uint64_t ptr) {
   s->allocations.erase(it);
 }
 
+uint64_t session_scratch(stb_session *s, uint64_t bytes) {
+  if (bytes <= s->scratch_bytes && s->scratch) return s->scratch;
+  if (s->scratch) {
+    session_free(s, s->scratch);
+    s->scratch = 0;
+    s->scratch_bytes = 0;
+  }
+  const uint64_t want = bytes < (64ull << 20) ? (64ull << 20) : bytes;
+  s->scratch = session_alloc(s, want);
+  s->scratch_bytes = want;
+  return s->scratch;
+}
+
+int *session_error_word(stb_session *s) {
+  if (!s->err_word) {
+    s->err_word = session_alloc(s, 256);
+    STB_CUDA(cudaMemsetAsync((void *)s->err_word, 0, 256, s->stream));
+  }
+  return (int *)s->err_word;
+}
+
+void check_device_error(stb_session *s) {
+  if (!s->err_word) return;
+  int code = 0;
+  STB_CUDA(cudaMemcpy(&code, (const void *)s->err_word, 4, cudaMemcpyDeviceToHost));
+  if (code) {
+    STB_CUDA(cudaMemset((void *)s->err_word, 0, 4));
+    throw Error(STB_ERR_CUDA, "a device-side wait expired (code " + std::to_string(code) + "); results are invalid");
+  }
+}
+
 void check_launch(const char *what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw Error(STB_ERR_CUDA, std::string(what) + " launch failed: " + cudaGetErrorString(e));
@@ -145,12 +176,14 @@ void upload(stb_session *s, const void *host, uint64_t bytes, uint64_t dst) {
 void download(stb_session *s, uint64_t src, void *host, uint64_t bytes) {
   if (!bytes) {
     STB_CUDA(cudaStreamSynchronize(s->stream));
+    check_device_error(s);
     return;
   }
   STB_REQUIRE(host && src, "download requires host and device buffers");
   if (is_pinned(host)) {
     STB_CUDA(cudaMemcpyAsync(host, (const void *)src, bytes, cudaMemcpyDeviceToHost, s->stream));
     STB_CUDA(cudaStreamSynchronize(s->stream));
+    check_device_error(s);
     return;
   }
   ensure_staging(s);
@@ -162,6 +195,7 @@ void download(stb_session *s, uint64_t src, void *host, uint64_t bytes) {
     std::memcpy((char *)host + done, s->staging, n);
     done += n;
   }
+  check_device_error(s);
 }
 
 }  // namespace stb
@@ -282,6 +316,7 @@ int stb_sync(stb_session *s) {
   return guarded([&] {
     enter(s);
     STB_CUDA(cudaStreamSynchronize(s->stream));
+    check_device_error(s);
   });
 }
 
