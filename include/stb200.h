@@ -99,6 +99,17 @@ int stb_linear_ld(stb_session *s, uint64_t x, int ldx, uint64_t w, int w_dtype, 
  * accumulation in TMEM.  The activation rounding is the stated tolerance source. */
 int stb_linear_prefill(stb_session *s, uint64_t x, uint64_t w, int w_dtype, uint64_t bias,
                        uint64_t y, int M, int N, int K);
+/* No counterpart in the reference.  The prefill Linear above without any device allocation, for
+ * callers that may not allocate device memory themselves (a host framework that owns every device
+ * allocation through its own allocator or budget; a serving loop that forbids allocation after
+ * warm-up).  The rounded activations go to a fixed 16 MiB array compiled into the library instead
+ * of the session's scratch, so M * K must not exceed 8,388,608 (larger requests are rejected with
+ * STB_ERR_INVALID).  Runs on `stream` (a cudaStream_t, NULL for the legacy stream) of the current
+ * device and returns after the product is complete.  All calls share the array: calls that
+ * overlap on the GPU (other threads or streams) race.  The first call on a device looks up the
+ * array's address; make it before any stream capture. */
+int stb_linear_prefill_static(void *stream, uint64_t x, uint64_t w, int w_dtype, uint64_t bias, uint64_t y,
+                              int M, int N, int K);
 /* Host-buffer form used for end-to-end measurement: copies x from host, runs stb_linear against
  * the resident weight, copies y back.  Synchronous. */
 int stb_linear_host(stb_session *s, const float *x_host, uint64_t w, int w_dtype, uint64_t bias,

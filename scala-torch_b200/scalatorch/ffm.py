@@ -81,6 +81,7 @@ def _declare(L):
         "stb_linear_ld": (_i, [_p, _u64, _i, _u64, _i, _u64, _u64, _i, _i, _i, _i]),
         "stb_linear_prefill": (_i, [_p, _u64, _u64, _i, _u64, _u64, _i, _i, _i]),
         "stb_linear_host": (_i, [_p, _p, _u64, _i, _u64, _p, _i, _i, _i]),
+        "stb_linear_prefill_static": (_i, [_p, _u64, _u64, _i, _u64, _u64, _i, _i, _i]),
         "stb_fill_normal": (_i, [_p, _u64, _i, _u64, _u64, _u64, ctypes.c_double]),
         "stb_fill_value": (_i, [_p, _u64, _i, _u64, ctypes.c_float]),
         "stb_nccl_unique_id": (_i, [_p]),
