@@ -45,9 +45,8 @@ struct GemvParams {
   int nh = 0, kvh = 0, hd = 0, capacity = 0;
   float *k_cache = nullptr, *v_cache = nullptr;  // [batch][kvh][capacity][hd] of this layer
   // EPI_LOGITS
-  float *part_val = nullptr;  // [M][row blocks]
-  int *part_idx = nullptr;
-  int row_offset = 0;  // global index of row 0 (vocab shard offset)
+  unsigned long long *best = nullptr;  // [M] greedy candidate keys (argmax_key), or null
+  int row_offset = 0;                  // global index of row 0 (vocab shard offset)
   const int *stop = nullptr;  // device flag; nonzero makes the kernel a no-op
   bool pdl = false;           // launched as a programmatic dependent of the previous kernel
 };
@@ -71,6 +70,20 @@ __device__ __forceinline__ double block_sum_double(double v, double *scratch) {
   total = scratch[0];
   __syncthreads();
   return total;
+}
+
+// Greedy candidates as one 64-bit key: an order-preserving image of the logit in the high word
+// (-0 folded onto +0, since the reference compares numerically) and the complement of the token
+// id in the low word, so the unsigned maximum is the largest logit and, among equal logits, the
+// lowest id -- TokenSampler's strict '>' scan (TokenSampler.scala:32-38).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  if (v == 0.0f) v = 0.0f;
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)idx);
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long key) {
+  return (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
 }
 
 // SiLU of CpuFloatBackend.silu (CpuFloatBackend.scala:72-79), in double.
@@ -102,10 +115,25 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
   const int rowbase = (rblock * G + g) * ROWS;
   const int nchunk = p.K >> 3;
 
+  // The weights never depend on the previous kernel.  Load this thread's first PRE chunks into
+  // registers now and (under programmatic launch) pull the rest of the block's rows -- one
+  // contiguous range -- into L2, all before waiting for the producer of x.
+  constexpr int PRE = 2;  // the consumer loop below selects wpre[0] / wpre[1] with constant indices
+  static_assert(PRE == 2, "preload depth");
+  const uint16_t *W = (const uint16_t *)p.w;
+  uint4 wpre[PRE][ROWS];
+#pragma unroll
+  for (int i = 0; i < PRE; i++) {
+    const int c = lane + i * TPR;
+#pragma unroll
+    for (int r = 0; r < ROWS; r++) {
+      const int row = rowbase + r;
+      wpre[i][r] = (c < nchunk && row < p.N) ? ld_stream_u4(W + (size_t)row * p.K + (size_t)c * 8)
+                                             : make_uint4(0, 0, 0, 0);
+    }
+  }
   if (p.pdl) {
-    // The weights never depend on the previous kernel: start pulling this block's rows (one
-    // contiguous range) into L2 before waiting for the producer of x.
-    if (tid == 0 && mtile == 0) {
+    if (tid == 0 && mtile == 0 && nchunk > PRE * TPR) {
       const int r0 = rblock * G * ROWS;
       const int nrows = min(G * ROWS, p.N - r0);
       if (nrows > 0) {
@@ -141,13 +169,18 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
 #pragma unroll
     for (int m = 0; m < MT; m++) acc[r][m] = 0.0f;
 
-  const uint16_t *W = (const uint16_t *)p.w;
-  for (int c = lane; c < nchunk; c += TPR) {
+  // Chunks in increasing order: the PRE preloaded ones, then the rest streamed in the loop.
+  for (int i = 0, c = lane; c < nchunk; i++, c += TPR) {
     uint4 wv[ROWS];
+    if (i < PRE) {
 #pragma unroll
-    for (int r = 0; r < ROWS; r++) {
-      const int row = rowbase + r;
-      wv[r] = row < p.N ? ld_stream_u4(W + (size_t)row * p.K + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
+      for (int r = 0; r < ROWS; r++) wv[r] = i == 0 ? wpre[0][r] : wpre[PRE - 1][r];
+    } else {
+#pragma unroll
+      for (int r = 0; r < ROWS; r++) {
+        const int row = rowbase + r;
+        wv[r] = row < p.N ? ld_stream_u4(W + (size_t)row * p.K + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
+      }
     }
     float xv[MT][8];
 #pragma unroll
@@ -243,7 +276,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
       p.y[mm * p.ldy + row] = v;
     }
     if constexpr (EPI == EPI_LOGITS) {
-      if (tid < mcount) {
+      if (p.best && tid < mcount) {
         const int m = tid;
         float best = 0.0f;
         int besti = -1;
@@ -251,14 +284,12 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
           const int row = blockrow0 + rr;
           if (row >= p.N) break;
           const float v = s_out[rr / ROWS][rr % ROWS][m];
-          if (besti < 0 || v > best) {
+          if (besti < 0 || v > best) {  // strict '>': the lowest row wins inside the block
             best = v;
             besti = row;
           }
         }
-        const int nblocks = gridDim.x / mtiles;
-        p.part_val[(size_t)(m0 + m) * nblocks + rblock] = best;
-        p.part_idx[(size_t)(m0 + m) * nblocks + rblock] = besti + p.row_offset;
+        if (besti >= 0) atomicMax(&p.best[m0 + m], argmax_key(best, besti + p.row_offset));
       }
     }
   } else if constexpr (EPI == EPI_SILU) {

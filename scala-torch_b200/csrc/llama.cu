@@ -64,8 +64,10 @@ struct stb_llama_cache {
   int batch = 0, capacity = 0, used = 0;
   uint64_t kv = 0;  // [layers][2][batch][kvh][capacity][hd] f32
   // scratch sized for `rows` token rows
-  int rows = 0, parts = 0;
-  uint64_t hidden = 0, qbuf = 0, att = 0, act = 0, sum = 0, logits = 0, pval = 0, pidx = 0, gval = 0, gidx = 0;
+  int rows = 0;
+  uint64_t hidden = 0, qbuf = 0, att = 0, act = 0, sum = 0, logits = 0;
+  uint64_t best = 0;      // u64 [batch] greedy candidate keys of this rank (zero between steps)
+  uint64_t best_all = 0;  // u64 [tp][batch] after the cross-rank gather
   uint64_t tokens = 0;  // int64 [rows]
   uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
   uint64_t out_ids = 0;
@@ -114,16 +116,19 @@ __global__ void embed_kernel(const int64_t *tokens, const uint16_t *table, int d
 
 // Causal grouped-query attention of CpuAttention.causal (cpu/.../CpuAttention.scala:20-50):
 // scores, softmax and the weighted value sum in double (the reference's precision); one block of
-// ATT_THREADS per (token row, query head).  Keys are spread over warps four at a time so each lane
-// keeps several coalesced K loads in flight; the weighted V sum splits the keys over thread groups
-// (one thread per output dimension in each group) and combines the groups in a fixed order.
+// ATT_THREADS per (token row, query head).  Decode is latency-bound, so the kernel keeps memory
+// round trips few: one key per thread for the scores (its whole K row in flight as float4 loads),
+// and for the weighted sum each thread owns 4 output dimensions of a key subset with 8 V rows in
+// flight; the subsets are combined in a fixed order.  hd must be a multiple of 4 and <= 256.
 constexpr int ATT_THREADS = 256;
+constexpr int ATT_UNROLL = 8;
 
 __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float *q, int ldq, const float *kcache,
                                                                 const float *vcache, float *out, int ldo, int rows,
                                                                 int count, int nh, int kvh, int hd, int capacity,
                                                                 const int *pos_dev, int pos0, const int *stop) {
-  extern __shared__ double s_p[];  // [capacity] probabilities, [32] reductions, [ATT_THREADS] partial sums
+  // [capacity] probabilities | [32] reductions | [hd] q in double | [ATT_THREADS*4] partial sums
+  extern __shared__ double s_p[];
   pdl_wait();
   pdl_trigger();
   if (stop && *stop) return;
@@ -135,32 +140,39 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float *q, 
   const int g = h / (nh / kvh);
   const float *qr = q + (size_t)m * ldq + (size_t)h * hd;
   const size_t base = ((size_t)b * kvh + g) * capacity;
-  const float *K = kcache + base * hd;
-  const float *Vc = vcache + base * hd;
+  const float4 *K4 = reinterpret_cast<const float4 *>(kcache + base * hd);
+  const float4 *V4 = reinterpret_cast<const float4 *>(vcache + base * hd);
   double *red = s_p + capacity;
-  double *part = red + 32;
+  double *qs = red + 32;
+  double *part = qs + hd;
   constexpr int NW = ATT_THREADS / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int F = hd >> 2;  // float4 slots per row
+  for (int d = threadIdx.x; d < hd; d += ATT_THREADS) qs[d] = (double)qr[d];
+  __syncthreads();
   const double scale = 1.0 / sqrt((double)hd);
   double local_max = -(double)INFINITY;
-  for (int j0 = warp * 4; j0 < keys; j0 += NW * 4) {
-    double dot[4] = {0.0, 0.0, 0.0, 0.0};
-    for (int d = lane; d < hd; d += 32) {
-      const double qd = (double)qr[d];
+  for (int j = threadIdx.x; j < keys; j += ATT_THREADS) {
+    const float4 *kr = K4 + (size_t)j * F;
+    double dot = 0.0;
+    for (int f0 = 0; f0 < F; f0 += ATT_UNROLL) {
+      float4 kv[ATT_UNROLL];
 #pragma unroll
-      for (int u = 0; u < 4; u++)
-        if (j0 + u < keys) dot[u] += qd * (double)K[(size_t)(j0 + u) * hd + d];
-    }
+      for (int u = 0; u < ATT_UNROLL; u++) kv[u] = f0 + u < F ? kr[f0 + u] : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], off);
-      if (j0 + u < keys) {
-        const double sc = dot[u] * scale;
-        if (lane == 0) s_p[j0 + u] = sc;
-        local_max = fmax(local_max, sc);
+      for (int u = 0; u < ATT_UNROLL; u++) {
+        if (f0 + u < F) {
+          const double *qd = qs + 4 * (f0 + u);
+          dot += qd[0] * (double)kv[u].x;
+          dot += qd[1] * (double)kv[u].y;
+          dot += qd[2] * (double)kv[u].z;
+          dot += qd[3] * (double)kv[u].w;
+        }
       }
     }
+    const double sc = dot * scale;
+    s_p[j] = sc;
+    local_max = fmax(local_max, sc);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) local_max = fmax(local_max, __shfl_xor_sync(0xffffffffu, local_max, off));
@@ -183,74 +195,67 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float *q, 
   for (int i = 0; i < NW; i++) den += red[i];
   for (int j = threadIdx.x; j < keys; j += ATT_THREADS) s_p[j] = s_p[j] / den;
   __syncthreads();
-  // weighted value sum: `groups` key subsets x hd dimensions
-  const int groups = ATT_THREADS / hd;
-  const int d = threadIdx.x % hd, grp = threadIdx.x / hd;
+  // weighted value sum: thread (grp, f) owns dimensions 4f..4f+3 for keys j = grp (mod groups)
+  const int groups = ATT_THREADS / F;
+  const int f = threadIdx.x % F, grp = threadIdx.x / F;
   if (grp < groups) {
-    double acc = 0.0;
-    int j = grp;
-    for (; j + 3 * groups < keys; j += 4 * groups) {
-      const double v0 = (double)Vc[(size_t)j * hd + d], v1 = (double)Vc[(size_t)(j + groups) * hd + d];
-      const double v2 = (double)Vc[(size_t)(j + 2 * groups) * hd + d], v3 = (double)Vc[(size_t)(j + 3 * groups) * hd + d];
-      acc += s_p[j] * v0;
-      acc += s_p[j + groups] * v1;
-      acc += s_p[j + 2 * groups] * v2;
-      acc += s_p[j + 3 * groups] * v3;
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    for (int j0 = grp; j0 < keys; j0 += groups * ATT_UNROLL) {
+      float4 vv[ATT_UNROLL];
+#pragma unroll
+      for (int u = 0; u < ATT_UNROLL; u++) {
+        const int j = j0 + u * groups;
+        vv[u] = j < keys ? V4[(size_t)j * F + f] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < ATT_UNROLL; u++) {
+        const int j = j0 + u * groups;
+        if (j < keys) {
+          const double pj = s_p[j];
+          a0 += pj * (double)vv[u].x;
+          a1 += pj * (double)vv[u].y;
+          a2 += pj * (double)vv[u].z;
+          a3 += pj * (double)vv[u].w;
+        }
+      }
     }
-    for (; j < keys; j += groups) acc += s_p[j] * (double)Vc[(size_t)j * hd + d];
-    part[grp * hd + d] = acc;
+    double *pp = part + (size_t)(grp * F + f) * 4;
+    pp[0] = a0; pp[1] = a1; pp[2] = a2; pp[3] = a3;
   }
   __syncthreads();
-  if (threadIdx.x < hd) {
+  for (int d = threadIdx.x; d < hd; d += ATT_THREADS) {
     double sum = 0.0;
-    for (int gi = 0; gi < groups; gi++) sum += part[gi * hd + threadIdx.x];
-    out[(size_t)m * ldo + (size_t)h * hd + threadIdx.x] = (float)sum;
+    for (int gi = 0; gi < groups; gi++) sum += part[(size_t)(gi * F + (d >> 2)) * 4 + (d & 3)];
+    out[(size_t)m * ldo + (size_t)h * hd + d] = (float)sum;
   }
 }
 
-size_t attention_smem(int capacity) { return (size_t)(capacity + 32 + ATT_THREADS) * sizeof(double); }
+size_t attention_smem(int capacity, int hd) {
+  return (size_t)(capacity + 32 + hd + ATT_THREADS * 4) * sizeof(double);
+}
 
-// Greedy pick over every rank's per-block candidates (strict '>' in increasing id order, i.e.
-// lowest id on ties), token feedback, output append, EOS stop and position advance.
-__global__ void finalize_kernel(const float *pval, const int *pidx, int nparts_total, int batch, int count,
-                                int64_t *tokens, int *state, int64_t *out_ids, int out_stride, const int64_t *eos,
-                                int eos_count, int64_t *next_ids, int advance) {
+// Greedy pick from every rank's candidate key (argmax_key: largest logit, lowest id on ties --
+// TokenSampler's strict '>'), token feedback, output append, EOS stop and position advance.  The
+// local candidate slots are cleared for the next step.
+__global__ void finalize_kernel(const unsigned long long *best_all, unsigned long long *best_local, int nranks,
+                                int batch, int count, int64_t *tokens, int *state, int64_t *out_ids, int out_stride,
+                                const int64_t *eos, int eos_count, int advance) {
   pdl_wait();
   if (state[1]) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   int *stopped = state + 2;
   int *out_count = state + 2 + batch;
-  for (int b = warp; b < batch; b += nwarps) {
-    float best = 0.0f;
-    int besti = -1;
-    for (int i = lane; i < nparts_total; i += 32) {
-      const float v = pval[(size_t)b * nparts_total + i];
-      const int id = pidx[(size_t)b * nparts_total + i];
-      if (id < 0) continue;
-      if (besti < 0 || v > best || (v == best && id < besti)) {
-        best = v;
-        besti = id;
-      }
+  for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+    unsigned long long key = 0;
+    for (int r = 0; r < nranks; r++) key = max(key, best_all[(size_t)r * batch + b]);
+    const int besti = argmax_key_index(key);
+    best_local[b] = 0ull;
+    if (out_ids && !stopped[b]) {
+      out_ids[(size_t)b * out_stride + out_count[b]] = besti;
+      out_count[b] += 1;
+      for (int e = 0; e < eos_count; e++)
+        if (eos[e] == besti) stopped[b] = 1;
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, besti, off);
-      if (oi >= 0 && (besti < 0 || ov > best || (ov == best && oi < besti))) {
-        best = ov;
-        besti = oi;
-      }
-    }
-    if (lane == 0) {
-      if (next_ids) next_ids[b] = besti;
-      if (out_ids && !stopped[b]) {
-        out_ids[(size_t)b * out_stride + out_count[b]] = besti;
-        out_count[b] += 1;
-        for (int e = 0; e < eos_count; e++)
-          if (eos[e] == besti) stopped[b] = 1;
-      }
-      tokens[(size_t)b * count + (count - 1)] = besti;  // next step's input (count == 1 in decode)
-    }
+    tokens[(size_t)b * count + (count - 1)] = besti;  // next step's input (count == 1 in decode)
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -421,11 +426,6 @@ void ensure_rows(stb_llama_cache *c, int rows) {
     if (p == kv) keep.push_back(p);
     else session_free(s, p);
   c->owned = keep;
-  // candidate slots per row: the most row blocks any lm_head launch shape of <= rows rows uses
-  c->parts = 0;
-  for (int mm : {1, 2, 4, 8, c->batch, rows})
-    if (mm <= rows)
-      c->parts = std::max(c->parts, gemv_row_blocks(m->V, normalize_gemv(choose_gemv(mm, m->V, m->H, false), EPI_LOGITS)));
   const int qw = m->NH * m->hd;
   c->hidden = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
   c->sum = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
@@ -433,11 +433,9 @@ void ensure_rows(stb_llama_cache *c, int rows) {
   c->att = alloc_owned(s, c->owned, (uint64_t)rows * qw * 4);
   c->act = alloc_owned(s, c->owned, (uint64_t)rows * m->I * 4);
   c->logits = alloc_owned(s, c->owned, (uint64_t)rows * m->V * 4);
-  // candidates: [rows][parts] per rank, [batch][tp*parts] after the cross-rank re-layout
-  c->pval = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
-  c->pidx = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
-  c->gval = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
-  c->gidx = alloc_owned(s, c->owned, (uint64_t)rows * c->parts * 4 * m->tp);
+  c->best = alloc_owned(s, c->owned, (uint64_t)c->batch * 8);
+  c->best_all = alloc_owned(s, c->owned, (uint64_t)c->batch * 8 * m->tp);
+  STB_CUDA(cudaMemsetAsync((void *)c->best, 0, (size_t)c->batch * 8, s->stream));
   c->tokens = alloc_owned(s, c->owned, (uint64_t)rows * 8);
   c->state = alloc_owned(s, c->owned, (uint64_t)(2 + 2 * c->batch) * 4);
   c->rows = rows;
@@ -447,7 +445,6 @@ struct StepArgs {
   int rows, count;          // token rows in this chunk and tokens per batch row
   bool device_pos;          // read position from state[0] (graph) instead of c->used
   bool all_logits;          // logits for every row (decode API) or only each batch row's last token
-  int64_t *next_ids = nullptr;
   bool append = false;      // append picks to out_ids (generation)
   int advance = 0;          // position increment done on device
 };
@@ -490,7 +487,7 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       launches++;
     }
     {  // 2. attention
-      const size_t smem = attention_smem(c->capacity);
+      const size_t smem = attention_smem(c->capacity, m->hd);
       launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), smem, st, true, (const float *)c->qbuf,
                     qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows, a.count, m->NH, m->KV,
                     m->hd, c->capacity, posd, c->used, stop);
@@ -546,44 +543,22 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
     p.M = brows; p.N = m->V; p.K = H;
     p.y = (float *)c->logits; p.ldy = m->V;
     p.norm_w = (const float *)m->final_norm; p.norm_eps = m->c.rms_norm_eps;
-    p.part_val = (float *)c->pval; p.part_idx = (int *)c->pidx; p.row_offset = m->v0;
+    p.best = a.all_logits ? nullptr : (unsigned long long *)c->best;  // greedy candidates per batch row
+    p.row_offset = m->v0;
     p.stop = stop;
     p.pdl = true;
-    GemvConfig cfg = choose_gemv(brows, p.N, p.K, false);
-    const int parts = launch_gemv<EPI_LOGITS>(p, wdt, cfg, st);  // <= c->parts slots per row
+    launch_gemv<EPI_LOGITS>(p, wdt, choose_gemv(brows, p.N, p.K, false), st);
     launches++;
-    const float *gv = (const float *)c->pval;
-    const int *gi = (const int *)c->pidx;
-    int nparts = parts;
-    if (!a.all_logits && m->tp > 1) {
-      // [rank][batch][parts] after the gather; re-laid as [batch][rank*parts] by reading strided
-      allgather_bytes(s, (const void *)c->pval, (void *)c->gval, (uint64_t)brows * parts * 4);
-      allgather_bytes(s, (const void *)c->pidx, (void *)c->gidx, (uint64_t)brows * parts * 4);
-      gv = (const float *)c->gval;
-      gi = (const int *)c->gidx;
-      nparts = parts;  // handled by finalize via per-rank stride below
-    }
-    if (!a.all_logits || a.next_ids) {
-      if (m->tp > 1 && !a.all_logits) {
-        // finalize over rank-major candidates: treat [rank][batch][parts] as batch-major by running
-        // one finalize per rank would lose the cross-rank max, so transpose through a tiny copy.
-        // (For batch rows b, the candidates of all ranks are at r*brows*parts + b*parts + i.)
-        for (int r = 0; r < m->tp; r++)
-          STB_CUDA(cudaMemcpy2DAsync((void *)(c->pval + (uint64_t)r * parts * 4), (size_t)m->tp * parts * 4,
-                                     (const void *)((const char *)gv + (size_t)r * brows * parts * 4),
-                                     (size_t)parts * 4, (size_t)parts * 4, brows, cudaMemcpyDeviceToDevice, st));
-        for (int r = 0; r < m->tp; r++)
-          STB_CUDA(cudaMemcpy2DAsync((void *)(c->pidx + (uint64_t)r * parts * 4), (size_t)m->tp * parts * 4,
-                                     (const void *)((const char *)gi + (size_t)r * brows * parts * 4),
-                                     (size_t)parts * 4, (size_t)parts * 4, brows, cudaMemcpyDeviceToDevice, st));
-        gv = (const float *)c->pval;
-        gi = (const int *)c->pidx;
-        nparts = parts * m->tp;
+    if (!a.all_logits) {
+      const unsigned long long *all = (const unsigned long long *)c->best;
+      if (m->tp > 1) {  // every rank's best over its vocabulary shard, [rank][batch]
+        allgather_bytes(s, (const void *)c->best, (void *)c->best_all, (uint64_t)brows * 8);
+        all = (const unsigned long long *)c->best_all;
       }
-      launch_kernel(finalize_kernel, dim3(1), dim3(256), 0, st, m->tp == 1, gv, gi, nparts, brows,
-                    a.all_logits ? 1 : a.count, (int64_t *)c->tokens, (int *)c->state,
-                    a.append ? (int64_t *)c->out_ids : nullptr, c->out_stride, (const int64_t *)c->eos,
-                    c->eos_count, a.next_ids, a.advance);
+      launch_kernel(finalize_kernel, dim3(1), dim3(32), 0, st, m->tp == 1, all, (unsigned long long *)c->best, m->tp,
+                    brows, a.count, (int64_t *)c->tokens, (int *)c->state,
+                    a.append ? (int64_t *)c->out_ids : nullptr, c->out_stride, (const int64_t *)c->eos, c->eos_count,
+                    a.advance);
       launches++;
     }
   }
@@ -839,9 +814,9 @@ int stb_llama_cache_create(stb_llama *m, int batch, int capacity, stb_llama_cach
     *out = nullptr;
     STB_REQUIRE(batch > 0 && capacity > 0 && capacity <= m->c.max_positions, "invalid model cache dimensions/budget");
     // attention keeps one row of double scores per block in shared memory
-    STB_REQUIRE(capacity <= 28000, "model cache capacity exceeds the attention score workspace");
+    STB_REQUIRE(capacity <= 26000, "model cache capacity exceeds the attention score workspace");
     STB_REQUIRE(m->hd <= ATT_THREADS, "head width exceeds the attention block");
-    const size_t smem = attention_smem(capacity);
+    const size_t smem = attention_smem(capacity, m->hd);
     if (smem > 48 * 1024)
       STB_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     auto *c = new stb_llama_cache();
@@ -902,8 +877,6 @@ int stb_llama_decode(stb_llama_cache *c, const int64_t *tokens, int batch, int c
     ensure_rows(c, rows);
     upload(s, tokens, (uint64_t)rows * 8, c->tokens);
     STB_CUDA(cudaMemsetAsync((void *)c->state, 0, (size_t)(2 + 2 * batch) * 4, s->stream));
-    uint64_t dnext = 0;
-    if (next_ids) dnext = c->tokens;  // finalize writes picks into a device buffer we read below
     StepArgs a;
     a.rows = rows;
     a.count = count;
@@ -922,7 +895,9 @@ int stb_llama_decode(stb_llama_cache *c, const int64_t *tokens, int batch, int c
       }
     }
     if (next_ids) {
-      // greedy pick of each batch row's last token, from the full logits just computed
+      // greedy pick of each batch row's last token on the host, as BackendLlama samples the
+      // downloaded logits (BackendLlama.scala:126-141; TokenSampler strict '>')
+      STB_REQUIRE(m->tp == 1, "host-side greedy pick needs the full vocabulary on this rank");
       std::vector<float> last((size_t)batch * m->V);
       for (int b = 0; b < batch; b++) {
         const uint64_t src = c->logits + ((uint64_t)(b * count + count - 1) * m->V) * 4;
@@ -933,7 +908,6 @@ int stb_llama_decode(stb_llama_cache *c, const int64_t *tokens, int batch, int c
         next_ids[b] = best;
       }
     }
-    (void)dnext;
     STB_CUDA(cudaStreamSynchronize(s->stream));
     c->used += count;  // publish only after the whole chunk succeeded (BackendLlamaCache.scala:38-40)
   });
