@@ -88,6 +88,16 @@ class Clocks:
                 "samples": len(self.rows)}
 
 
+def max_over_ranks(values, device=None):
+    """Element-wise maximum over all ranks of the current process group (the slowest rank's
+    times); `device` None keeps the tensor on the CPU (gloo)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
 def cpu_baseline_smol(seconds_budget: float = 20.0):
     """The oracle restatement of the reference CPU path (all host threads) on a bounded sample of the
     same workload: same model and prompt length, as many generated tokens as fit the budget."""
@@ -189,9 +199,7 @@ def main():
     assert int(gen[0]) == NEW, "generation stopped early"
     dev_total = sum(dev_ms) / 1000.0
     if world > 1:
-        t = torch.tensor([dev_total, wall], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_total, wall = float(t[0]), float(t[1])
+        dev_total, wall = max_over_ranks([dev_total, wall], device="cuda")
         dist.barrier()
     tokens = NEW * args.steps * world
     value = tokens / dev_total

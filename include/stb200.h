@@ -179,6 +179,14 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
 
 /* ---------------------------------------------------------------- tensor parallel (NCCL) */
 
+/* The Megatron shard of `rank` in a tp-way split of config (host-only; no device is touched).
+ * out[0..13] = query heads [begin, end), KV heads [begin, end), intermediate rows [begin, end),
+ * vocabulary rows [begin, end), o_proj input columns [begin, end), down_proj input columns
+ * [begin, end), and the resident half-weight bytes of that rank, and 0.  Fails like
+ * stb_llama_create when the split is uneven.  No counterpart in the reference (it has no
+ * distributed path, LlamaConfig.scala:91). */
+int stb_llama_shard_plan(const stb_llama_config *config, int rank, int tp, int64_t out[14]);
+
 /* ncclGetUniqueId: 128 bytes to broadcast from rank 0 to the group. */
 int stb_nccl_unique_id(uint8_t id[128]);
 /* ncclCommInitRank on the session's device; one communicator per session. */

@@ -14,7 +14,7 @@
 //               accumulator double buffering overlaps a tile's epilogue with the next tile's MMAs
 // Every mbarrier wait is bounded by the global timer; on expiry the kernel records an error code,
 // stops issuing work, drains its MMAs (bounded) and frees TMEM before returning.
-// No cluster multicast is used anywhere: each CTA loads its own tiles.
+// Each CTA loads its own tiles from this GPU's memory; no load is shared across CTAs.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

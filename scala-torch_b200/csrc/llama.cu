@@ -590,6 +590,27 @@ void check_config(const stb_llama_config &c) {
 
 extern "C" {
 
+int stb_llama_shard_plan(const stb_llama_config *config, int rank, int tp, int64_t out[14]) {
+  return guarded([&] {
+    STB_REQUIRE(config && out, "null argument");
+    stb_llama_config c = *config;
+    c.tp_rank = rank;
+    c.tp_size = tp;
+    STB_REQUIRE(tp >= 1, "invalid tensor-parallel size");
+    check_config(c);
+    const int64_t hd = c.hidden_size / c.num_attention_heads, H = c.hidden_size;
+    const int64_t nh = c.num_attention_heads / tp, kv = c.num_key_value_heads / tp;
+    const int64_t I = c.intermediate_size / tp, V = c.vocab_size / tp;
+    const int64_t r = rank;
+    const int64_t v[14] = {r * nh, (r + 1) * nh, r * kv, (r + 1) * kv, r * I, (r + 1) * I, r * V, (r + 1) * V,
+                           r * nh * hd, (r + 1) * nh * hd, r * I, (r + 1) * I, 0, 0};
+    for (int i = 0; i < 14; i++) out[i] = v[i];
+    const int64_t layer = ((nh + 2 * kv) * hd * H + H * nh * hd + 2 * I * H + H * I) * 2;
+    const bool head_is_embed = c.tie_word_embeddings && tp == 1;
+    out[12] = layer * c.num_layers + (int64_t)c.vocab_size * H * 2 + (head_is_embed ? 0 : V * H * 2);
+  });
+}
+
 int stb_llama_create(stb_session *s, const stb_llama_config *config, stb_llama **out) {
   return guarded([&] {
     enter(s);

@@ -284,6 +284,32 @@ class BackendLlamaCache:
             call("stb_llama_cache_destroy", self.handle)
 
 
+@dataclass(frozen=True)
+class ShardPlan:
+    """What one rank of a tensor-parallel group holds (stb_llama_shard_plan)."""
+    heads: tuple
+    kv_heads: tuple
+    intermediate: tuple
+    vocab: tuple
+    o_cols: tuple
+    down_cols: tuple
+    weight_bytes: int
+
+
+def shard_plan(config: LlamaConfig, rank: int, tp: int, weight_dtype: int = STB_BF16) -> ShardPlan:
+    """Host-only Megatron split of `config` for `rank` of `tp` (no device is touched)."""
+    L = library()
+    L.stb_llama_shard_plan.restype = ctypes.c_int
+    L.stb_llama_shard_plan.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    c = _Config(config.vocab_size, config.hidden_size, config.intermediate_size, config.num_layers,
+                config.num_attention_heads, config.num_key_value_heads, config.max_positions,
+                int(config.tie_word_embeddings), config.rms_norm_eps, config.rope_theta, weight_dtype, rank, tp)
+    out = (ctypes.c_int64 * 14)()
+    call("stb_llama_shard_plan", ctypes.byref(c), rank, tp, out)
+    v = list(out)
+    return ShardPlan((v[0], v[1]), (v[2], v[3]), (v[4], v[5]), (v[6], v[7]), (v[8], v[9]), (v[10], v[11]), v[12])
+
+
 def _parse_name(name: str):
     if name in GLOBAL_WEIGHTS:
         return GLOBAL_WEIGHTS[name], 0
