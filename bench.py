@@ -48,6 +48,10 @@ class Clocks:
         self.device = device
         self.rows = []
         self.proc = None
+        self.window = []  # [start, end) sample indices of the timed region (mark() twice)
+
+    def mark(self):
+        self.window.append(len(self.rows))
 
     def __enter__(self):
         try:
@@ -78,14 +82,17 @@ class Clocks:
                 self.proc.kill()
 
     def summary(self):
-        if not self.rows:
+        rows = self.rows
+        if len(self.window) == 2 and self.window[1] > self.window[0]:
+            rows = rows[self.window[0]:self.window[1] + 1]  # samples taken during the timed region
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = sorted(float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit())
-        mx = max((float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()), default=None)
+        sm = sorted(float(r[0]) for r in rows if r[0].replace(".", "").isdigit())
+        mx = max((float(r[1]) for r in rows if r[1].replace(".", "").isdigit()), default=None)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 3 + i and r[3 + i] == "Active"})
+        reasons = sorted({names[i] for r in rows for i in range(4) if len(r) > 3 + i and r[3 + i] == "Active"})
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(self.rows)}
+                "samples": len(rows)}
 
 
 def max_over_ranks(values, device=None):
@@ -98,9 +105,10 @@ def max_over_ranks(values, device=None):
     return [float(v) for v in t.tolist()]
 
 
-def cpu_baseline_smol(seconds_budget: float = 20.0):
-    """The oracle restatement of the reference CPU path (all host threads) on a bounded sample of the
-    same workload: same model and prompt length, as many generated tokens as fit the budget."""
+def cpu_baseline_smol(seconds_budget: float = 20.0, model=None, with_model: bool = False):
+    """The oracle restatement of the reference CPU path (all host threads) on the same workload: the
+    full 128 + 128 generation when it fits the budget, else the prompt plus as many greedy tokens as
+    fit, with the remaining decode steps extrapolated at the measured per-token rate."""
     import numpy as np
 
     import oracle
@@ -108,24 +116,65 @@ def cpu_baseline_smol(seconds_budget: float = 20.0):
     from llama_fixtures import oracle_model
     from scalatorch.models import LlamaConfig
     cfg = LlamaConfig(**SMOL)
-    model = oracle_model(cfg, seed=SEED)
+    if model is None:
+        model = oracle_model(cfg, seed=SEED)
     threads = oracle.max_threads()
     prompt = np.random.default_rng(SEED).integers(0, cfg.vocab_size, PROMPT).tolist()
     t0 = time.perf_counter()
-    model.generate(prompt[:PROMPT], 1)
-    t_first = time.perf_counter() - t0
-    # tokens after the first cost one decode step each; estimate how many fit the budget
+    model.generate(prompt, 1)  # prefill of the 128-token prompt + the first pick
+    t_prefill = time.perf_counter() - t0
+    n = 8
     t0 = time.perf_counter()
-    model.generate(prompt[:8], 2)
-    t_small = time.perf_counter() - t0
-    per_token = max(t_small / 2, 1e-3)
-    n = int(max(1, min(NEW, (seconds_budget - t_first) / per_token)))
-    t0 = time.perf_counter()
-    out = model.generate(prompt, n)
-    dt = time.perf_counter() - t0
-    gen = len(out) - PROMPT
-    return {"value": gen / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{PROMPT}-token prompt + {gen} greedy tokens (of {NEW}) on the oracle, {dt:.1f} s"}
+    model.generate(prompt, 1 + n)
+    per_token = max((time.perf_counter() - t0 - t_prefill) / n, 1e-6)
+    if t_prefill + NEW * per_token <= seconds_budget:
+        t0 = time.perf_counter()
+        out = model.generate(prompt, NEW)
+        dt = time.perf_counter() - t0
+        r = {"value": (len(out) - PROMPT) / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+             "sample": f"full {PROMPT}-token prompt + {len(out) - PROMPT} greedy tokens on the oracle, {dt:.2f} s"}
+    else:
+        dt = t_prefill + (NEW - 1) * per_token
+        r = {"value": NEW / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+             "sample": f"{PROMPT}-token prefill {t_prefill:.2f} s + {per_token * 1000:.1f} ms/token measured over "
+                       f"{n} tokens, extrapolated to {NEW} tokens"}
+    return (r, model) if with_model else r
+
+
+LLAMA70B = dict(vocab_size=128256, hidden_size=8192, intermediate_size=28672, num_layers=80,
+                num_attention_heads=64, num_key_value_heads=8, max_positions=8192, tie_word_embeddings=False,
+                rope_theta=500000.0, rms_norm_eps=1e-5, eos_token_ids=())
+
+
+class Generator:
+    """One generate call through the C ABI with pinned host prompt/output buffers (the e2e path)."""
+
+    def __init__(self, model, prompts, new):
+        import ctypes
+
+        import numpy as np
+        from scalatorch import ffm
+        self.ffm, self.model, self.new = ffm, model, new
+        self.batch, self.plen = prompts.shape
+        n_in, n_out = prompts.size, self.batch * (self.plen + new)
+        self.hp, self.ho = ctypes.c_void_p(), ctypes.c_void_p()
+        ffm.call("stb_host_alloc", n_in * 8, ctypes.byref(self.hp))
+        ffm.call("stb_host_alloc", n_out * 8, ctypes.byref(self.ho))
+        self.prompt = np.ctypeslib.as_array((ctypes.c_int64 * n_in).from_address(self.hp.value))
+        self.prompt[:] = prompts.ravel()
+        self.out = np.ctypeslib.as_array((ctypes.c_int64 * n_out).from_address(self.ho.value))
+        self.gen = np.zeros(self.batch, np.int32)
+        self.tm = np.zeros(2, np.float32)
+        self.h2d, self.d2h = n_in * 8, self.batch * new * 8 + 8 * (2 + 2 * self.batch)
+
+    def __call__(self):
+        self.ffm.call("stb_llama_generate", self.model.handle, self.prompt.ctypes.data, self.batch, self.plen,
+                      self.new, None, 0, self.out.ctypes.data, self.gen.ctypes.data, self.tm.ctypes.data)
+        return float(self.tm[0]), float(self.tm[1])
+
+    def close(self):
+        self.ffm.call("stb_host_free", self.hp)
+        self.ffm.call("stb_host_free", self.ho)
 
 
 def main():
@@ -134,6 +183,10 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="smollm2", choices=["smollm2", "llama70b"])
+    ap.add_argument("--batch", type=int, default=1, help="llama70b: decode batch (1, 8, 32)")
+    ap.add_argument("--prompt", type=int, default=512, help="llama70b: prompt tokens")
+    ap.add_argument("--new", type=int, default=32, help="llama70b: generated tokens per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -154,88 +207,146 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=__import__("datetime").timedelta(seconds=300))
     hbm_peak, tc_peak, peak_kind = peaks()
-    session = ffm.B200Session(local, 170 << 30)
-    cfg = LlamaConfig(**SMOL)
-    model = BackendLlama.prepare_random(session, cfg, seed=SEED)
-    rng = np.random.default_rng(SEED + rank)
-    prompt = rng.integers(0, cfg.vocab_size, PROMPT).astype(np.int64)
-    # pinned host buffers for the end-to-end path
-    lib = ffm.library()
-    import ctypes
-    hp = ctypes.c_void_p()
-    ffm.call("stb_host_alloc", PROMPT * 8, ctypes.byref(hp))
-    pin_prompt = np.ctypeslib.as_array((ctypes.c_int64 * PROMPT).from_address(hp.value))
-    pin_prompt[:] = prompt
-    ho = ctypes.c_void_p()
-    ffm.call("stb_host_alloc", (PROMPT + NEW) * 8, ctypes.byref(ho))
-    pin_out = np.ctypeslib.as_array((ctypes.c_int64 * (PROMPT + NEW)).from_address(ho.value))
-    gen = np.zeros(1, np.int32)
-    tm = np.zeros(2, np.float32)
+    session = ffm.B200Session(local, 178 << 30)
+    tp = args.workload == "llama70b"
+    if tp:
+        cfg = LlamaConfig(**LLAMA70B)
+        batch, plen, new = args.batch, args.prompt, args.new
+        if world > 1:  # one communicator for the tensor-parallel group
+            uid = [ffm.B200Session.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            session.init_tp(world, rank, uid[0])
+        model = BackendLlama.prepare_random(session, cfg, seed=SEED, tp_rank=rank, tp_size=world)
+        prompts = np.random.default_rng(SEED).integers(0, cfg.vocab_size, (batch, plen)).astype(np.int64)
+    else:
+        cfg = LlamaConfig(**SMOL)
+        batch, plen, new = 1, PROMPT, NEW
+        model = BackendLlama.prepare_random(session, cfg, seed=SEED)
+        prompts = np.random.default_rng(SEED + rank).integers(0, cfg.vocab_size, (1, PROMPT)).astype(np.int64)
+    step = Generator(model, prompts, new)
 
-    def step():
-        ffm.call("stb_llama_generate", model.handle, pin_prompt.ctypes.data, 1, PROMPT, NEW, None, 0,
-                 pin_out.ctypes.data, gen.ctypes.data, tm.ctypes.data)
-        return float(tm[0]) + float(tm[1]), float(tm[0]), float(tm[1])
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    session.sync()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    launches0 = session.launches
-    dev_ms, pre_ms, dec_ms = [], [], []
-    with Clocks(local) as clocks:
+    with Clocks(local) as clocks:  # started before the warm-up so its start-up never overlaps the timing
+        for _ in range(max(args.warmup, 3)):
+            step()
+        session.sync()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        clocks.mark()
+        launches0 = session.launches
+        pre_ms, dec_ms = [], []
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            d, p, q = step()
-            dev_ms.append(d)
+            p, q = step()
             pre_ms.append(p)
             dec_ms.append(q)
         session.sync()
         wall = time.perf_counter() - t0
+        clocks.mark()
     torch.cuda.synchronize()
     launches = session.launches - launches0
-    assert int(gen[0]) == NEW, "generation stopped early"
-    dev_total = sum(dev_ms) / 1000.0
+    assert int(step.gen.min()) == new, "generation stopped early"
+    pre_s, dec_s = sum(pre_ms) / 1000.0, sum(dec_ms) / 1000.0
     if world > 1:
-        dev_total, wall = max_over_ranks([dev_total, wall], device="cuda")
+        pre_s, dec_s, wall = max_over_ranks([pre_s, dec_s, wall], device="cuda")
         dist.barrier()
-    tokens = NEW * args.steps * world
-    value = tokens / dev_total
-    e2e = tokens / wall
 
-    roof = roofline_lm_head(session, cfg, hbm_peak, peak_kind)
-    line = {
-        "metric": "greedy decode tokens/s (SmolLM2-135M-shaped, BF16 weights, batch 1, 128-token prompt + 128 new)",
-        "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dev_total * 1000 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16-weights/f32-compute", "data": "synthetic (device counter-RNG weights, random prompt ids)",
-        "config": {"workload": "smollm2-135m-shaped greedy decode", "batch": 1, "prompt": PROMPT, "new_tokens": NEW,
-                   "layers": 30, "hidden": 576, "vocab": 49152, "parallelism": f"replicas x{world}",
-                   "prefill_ms": round(sum(pre_ms) / len(pre_ms), 3), "decode_ms": round(sum(dec_ms) / len(dec_ms), 3),
-                   "decode_tok_s": round(NEW * 1000 / (sum(dec_ms) / len(dec_ms)), 1),
-                   "weight_bytes_per_token": 268959744,
-                   "l2": "inputs larger than L2: 269 MB of weights streamed per token vs 126 MB L2"},
-        "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": PROMPT * 8,
-                "d2h_bytes_per_step": (NEW * 8 + 8 * 3)},
-        "gpu_launches": int(launches),
-        "roofline": roof,
-        "clocks": clocks.summary(),
-    }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            line["cpu_baseline"] = cpu_baseline_smol()
-        except Exception as e:  # reported, never silently replaced
-            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    ffm.call("stb_host_free", hp)
-    ffm.call("stb_host_free", ho)
+    if tp:
+        # tensor parallel: the ranks produce one sequence batch together; metric = decode tokens/s
+        tokens = batch * new * args.steps
+        value = tokens / dec_s
+        e2e = tokens / wall
+        line = {
+            "metric": "greedy decode tokens/s (Llama-3-70B-shaped, BF16 weights, tensor parallel)",
+            "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round((pre_s + dec_s) * 1000 / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16-weights/f32-compute",
+            "data": "synthetic (device counter-RNG weights, random prompt ids)",
+            "config": {"workload": "llama3-70b-shaped greedy decode", "batch": batch, "prompt": plen,
+                       "new_tokens": new, "layers": 80, "hidden": 8192, "vocab": 128256,
+                       "parallelism": f"tp{world}", "prefill_ms": round(pre_s * 1000 / args.steps, 3),
+                       "decode_ms": round(dec_s * 1000 / args.steps, 3),
+                       "decode_ms_per_token": round(dec_s * 1000 / args.steps / max(new - 1, 1), 3),
+                       "weight_bytes_per_rank": model.weight_bytes,
+                       "l2": "inputs larger than L2: 141 GB of weights"},
+            "e2e": {"value": round(e2e, 3), "unit": "tokens/s", "h2d_bytes_per_step": step.h2d,
+                    "d2h_bytes_per_step": step.d2h},
+            "gpu_launches": int(launches), "clocks": clocks.summary(),
+        }
+        # HBM roofline of the decode step: every rank streams its weight shard once per token
+        per_tok = dec_s / args.steps / max(new - 1, 1)
+        achieved = model.weight_bytes / per_tok / 1e9
+        line["roofline"] = {"kernel": "decode step (all kernels, per rank)", "bound": "hbm",
+                            "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                            "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                            "algorithmic_bytes": model.weight_bytes, "traffic": None}
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline_70b_layer()
+            except Exception as e:
+                line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    else:
+        tokens = new * args.steps * world
+        value = tokens / (pre_s + dec_s)
+        e2e = tokens / wall
+        line = {
+            "metric": "greedy decode tokens/s (SmolLM2-135M-shaped, BF16 weights, batch 1, 128-token prompt + 128 new)",
+            "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round((pre_s + dec_s) * 1000 / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16-weights/f32-compute",
+            "data": "synthetic (device counter-RNG weights, random prompt ids)",
+            "config": {"workload": "smollm2-135m-shaped greedy decode", "batch": 1, "prompt": PROMPT, "new_tokens": NEW,
+                       "layers": 30, "hidden": 576, "vocab": 49152, "parallelism": f"replicas x{world}",
+                       "prefill_ms": round(pre_s * 1000 / args.steps, 3),
+                       "decode_ms": round(dec_s * 1000 / args.steps, 3),
+                       "decode_tok_s": round(NEW * args.steps / dec_s, 1),
+                       "weight_bytes_per_token": 268959744,
+                       "l2": "inputs larger than L2: 269 MB of weights streamed per token vs 126 MB L2"},
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": step.h2d,
+                    "d2h_bytes_per_step": step.d2h},
+            "gpu_launches": int(launches),
+            "roofline": roofline_lm_head(session, cfg, hbm_peak, peak_kind),
+            "clocks": clocks.summary(),
+        }
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            try:
+                line["cpu_baseline"] = cpu_baseline_smol()
+            except Exception as e:  # reported, never silently replaced
+                line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    step.close()
     model.close()
     session.close()
     if world > 1:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_70b_layer():
+    """The reference CPU path on ONE Llama-3-70B-shaped decoder layer (weights generated by the same
+    counter-based streams, widened to F32 as SafeTensors.readFloat does), decode at batch 1 after a
+    16-token context, scaled to 80 layers.  The tiny vocabulary of the probe model keeps the
+    lm_head out of the measurement."""
+    import numpy as np
+
+    import oracle
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from llama_fixtures import oracle_model
+    from scalatorch.models import LlamaConfig
+    cfg = LlamaConfig(**dict(LLAMA70B, num_layers=1, vocab_size=256))
+    model = oracle_model(cfg, seed=SEED)
+    ctx = list(range(1, 17))
+    cache = model.new_cache(1, 64)
+    model.decode(cache, np.array([ctx]))
+    t0 = time.perf_counter()
+    n = 3
+    for i in range(n):
+        model.decode(cache, np.array([[i + 20]]))
+    per_layer = (time.perf_counter() - t0) / n
+    model.free_cache(cache)
+    return {"value": round(1.0 / (per_layer * 80), 5), "unit": "tokens/s", "cores": oracle.max_threads(),
+            "kind": "port", "sample": f"1 of 80 decoder layers, batch 1, {n} decode steps after a 16-token context: "
+                                      f"{per_layer * 1000:.0f} ms/layer/token x 80 layers"}
 
 
 def roofline_lm_head(session, cfg, hbm_peak, peak_kind):
@@ -283,19 +394,32 @@ def reference_arm(args, world, rank):
         return
     import oracle
     samples = []
-    for i in range(max(args.warmup, 0) + args.steps):
-        r = cpu_baseline_smol(seconds_budget=15.0)
-        if i >= args.warmup:
-            samples.append(r)
+    if args.workload == "llama70b":
+        for i in range(max(args.warmup, 0) + args.steps):
+            r = cpu_baseline_70b_layer()
+            if i >= args.warmup:
+                samples.append(r)
+        metric = "greedy decode tokens/s (Llama-3-70B-shaped, BF16 weights, tensor parallel)"
+        config = {"workload": "llama3-70b-shaped greedy decode", "batch": args.batch, "prompt": args.prompt,
+                  "new_tokens": args.new}
+        scaling = "strong"
+    else:
+        model = None
+        for i in range(max(args.warmup, 0) + args.steps):
+            r, model = cpu_baseline_smol(seconds_budget=10.0, model=model, with_model=True)
+            if i >= args.warmup:
+                samples.append(r)
+        metric = "greedy decode tokens/s (SmolLM2-135M-shaped, BF16 weights, batch 1, 128-token prompt + 128 new)"
+        config = {"workload": "smollm2-135m-shaped greedy decode", "batch": 1, "prompt": PROMPT, "new_tokens": NEW}
+        scaling = "weak"
     v = sum(s["value"] for s in samples) / len(samples)
-    line = {"impl": "reference", "metric": "greedy decode tokens/s (SmolLM2-135M-shaped, BF16 weights, batch 1, 128-token prompt + 128 new)",
-            "value": round(v, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "smollm2-135m-shaped greedy decode", "batch": 1,
-                                            "prompt": PROMPT, "new_tokens": NEW},
-            "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": oracle.max_threads(), "kind": "port",
+    line = {"impl": "reference", "metric": metric,
+            "value": round(v, 5), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": round(v, 5), "unit": "tokens/s", "cores": oracle.max_threads(), "kind": "port",
                              "sample": samples[-1]["sample"]},
-            "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(v, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 

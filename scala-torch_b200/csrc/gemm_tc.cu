@@ -37,6 +37,8 @@ struct TcParams {
   float *y;
   const float *bias;
   int *err;
+  const float *residual;  // optional: y = residual + (acc + bias); may alias y
+  int ldr;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -234,12 +236,14 @@ __global__ void __launch_bounds__(256, 1)
       tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
       float *yrow = p.y + (size_t)row * p.ldy;
+      const float *rrow = p.residual ? p.residual + (size_t)row * p.ldr : nullptr;
       for (int c = 0; c < BN / 32; c++) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         const int n0 = nb * BN + c * 32;
         if (row < p.M && n0 < p.N) {
-          if (n0 + 32 <= p.N && (p.ldy & 3) == 0) {
+          // y = acc (+ bias) ; then y = residual + y (LlamaBlock's x + f(x), LlamaModel.scala:49-52)
+          if (n0 + 32 <= p.N && (p.ldy & 3) == 0 && (!rrow || (p.ldr & 3) == 0)) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
               float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
@@ -250,12 +254,21 @@ __global__ void __launch_bounds__(256, 1)
                 v.z = v.z + p.bias[n0 + j + 2];
                 v.w = v.w + p.bias[n0 + j + 3];
               }
+              if (rrow) {
+                const float4 res = *reinterpret_cast<const float4 *>(rrow + n0 + j);
+                v.x = res.x + v.x;
+                v.y = res.y + v.y;
+                v.z = res.z + v.z;
+                v.w = res.w + v.w;
+              }
               *reinterpret_cast<float4 *>(yrow + n0 + j) = v;
             }
           } else {
             for (int j = 0; j < 32 && n0 + j < p.N; j++) {
               float v = __uint_as_float(r[j]);
-              yrow[n0 + j] = p.bias ? v + p.bias[n0 + j] : v;
+              if (p.bias) v = v + p.bias[n0 + j];
+              if (rrow) v = rrow[n0 + j] + v;
+              yrow[n0 + j] = v;
             }
           }
         }
@@ -337,19 +350,30 @@ uint32_t tc_idesc(int dtype) {
 
 // Enqueues the prefill GEMM on `stream`.  xh: the activations already in the weight's type
 // (M x K, row-major); err: device int that receives a nonzero code if a wait expired.
+// residual (optional, may alias y): y = residual + (x.W^T + bias), the residual add of a Llama block.
 void gemm_tc_launch(const void *xh, const void *w, int dtype, const float *bias, float *y, int ldy, int M, int N,
-                    int K, int *err, int device, cudaStream_t stream) {
+                    int K, int *err, int device, cudaStream_t stream, const float *residual, int ldr) {
   const CUtensorMap ta = make_map(xh, dtype, (uint64_t)M, (uint64_t)K, BM);
   const CUtensorMap tb = make_map(w, dtype, (uint64_t)N, (uint64_t)K, BN);
-  TcParams p{M, N, K, ldy, y, bias, err};
+  TcParams p{M, N, K, ldy, y, bias, err, residual, ldr};
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = std::min(tiles, sm_count(device));
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  });
+  static std::mutex mu;
+  static bool configured[64] = {};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0 || device >= 64 || !configured[device]) {
+      STB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+      if (device >= 0 && device < 64) configured[device] = true;
+    }
+  }
   gemm_tc_kernel<<<grid, 256, SMEM_BYTES, stream>>>(ta, tb, p, tc_idesc(dtype));
   check_launch("gemm_tc");
+}
+
+void gemm_tc_launch(const void *xh, const void *w, int dtype, const float *bias, float *y, int ldy, int M, int N,
+                    int K, int *err, int device, cudaStream_t stream) {
+  gemm_tc_launch(xh, w, dtype, bias, y, ldy, M, N, K, err, device, stream, nullptr, 0);
 }
 
 void round_activations(const float *x, uint16_t *out, size_t count, int dtype, cudaStream_t stream) {

@@ -18,6 +18,7 @@
 // o/down by input columns; each row-split projection's partial sums are joined by one NCCL
 // allreduce which also carries the residual (rank 0 adds it before the reduction).  lm_head is
 // split by vocabulary; ranks exchange their (value, index) candidates with one allgather.
+#include <climits>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -28,6 +29,9 @@
 namespace stb {
 void allreduce_sum_f32(stb_session *s, void *buf, uint64_t count);
 void allgather_bytes(stb_session *s, const void *send, void *recv, uint64_t bytes);
+void gemm_tc_launch(const void *xh, const void *w, int dtype, const float *bias, float *y, int ldy, int M, int N,
+                    int K, int *err, int device, cudaStream_t stream, const float *residual, int ldr);
+void round_activations(const float *x, uint16_t *out, size_t count, int dtype, cudaStream_t stream);
 }  // namespace stb
 
 using namespace stb;
@@ -56,7 +60,7 @@ struct stb_llama {
   uint64_t rope = 0;  // double2 [max_positions][hd/2]
   std::vector<uint64_t> owned;
   uint64_t weight_bytes = 0;
-  bool weights_ready[16] = {};
+  int tc_rows = 512;  // chunks of >= tc_rows token rows use the tensor-core prefill (INT_MAX: never)
 };
 
 struct stb_llama_cache {
@@ -68,6 +72,9 @@ struct stb_llama_cache {
   uint64_t hidden = 0, qbuf = 0, att = 0, act = 0, sum = 0, logits = 0;
   uint64_t best = 0;      // u64 [batch] greedy candidate keys of this rank (zero between steps)
   uint64_t best_all = 0;  // u64 [tp][batch] after the cross-rank gather
+  // tensor-core prefill buffers (allocated when rows >= tc_rows): normalised x, half activations,
+  // paired q/k/v projection, interleaved gate/up projection
+  uint64_t xn = 0, xh = 0, qkvbuf = 0, gubuf = 0;
   uint64_t tokens = 0;  // int64 [rows]
   uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
   uint64_t out_ids = 0;
@@ -268,6 +275,73 @@ __global__ void finalize_kernel(const unsigned long long *best_all, unsigned lon
   }
 }
 
+// ---- tensor-core prefill helpers (chunks of >= tc_rows token rows)
+
+// CpuFloatBackend.rmsNorm per row (CpuFloatBackend.scala:80-93), double accumulation; one block per row.
+__global__ void rmsnorm_rows_kernel(const float *x, const float *w, double eps, float *out, int H) {
+  __shared__ double s_red[8];
+  pdl_wait();
+  pdl_trigger();
+  const float *xr = x + (size_t)blockIdx.x * H;
+  double sq = 0.0;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    const double v = (double)xr[k];
+    sq = __dadd_rn(sq, __dmul_rn(v, v));
+  }
+  const double total = block_sum_double(sq, s_red);
+  const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(total, (double)H), eps)));
+  for (int k = threadIdx.x; k < H; k += blockDim.x)
+    out[(size_t)blockIdx.x * H + k] = __double2float_rn(__dmul_rn(__dmul_rn((double)xr[k], inv), (double)w[k]));
+}
+
+// RoPE + KV append from a paired q/k/v projection row (the QKV GEMV epilogue's arithmetic, applied
+// to a tensor-core GEMM output): one thread per (row, pair).
+__global__ void rope_append_kernel(const float *qkv, int ldq, const double2 *rope, const int *pos_dev, int pos0,
+                                   int count, int nh, int kvh, int hd, int capacity, float *q_out, int ldo,
+                                   float *k_cache, float *v_cache, int rows) {
+  pdl_wait();
+  pdl_trigger();
+  const int half = hd >> 1;
+  const int pairs = (nh + 2 * kvh) * half;
+  const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i >= (long)rows * pairs) return;
+  const int mm = (int)(i / pairs), pi = (int)(i % pairs);
+  const float fa = qkv[(size_t)mm * ldq + 2 * pi], fb = qkv[(size_t)mm * ldq + 2 * pi + 1];
+  const int qpairs = nh * half, kpairs = kvh * half;
+  const int bb = mm / count, t = mm % count;
+  const int pos = (pos_dev ? *pos_dev : pos0) + t;
+  if (pi < qpairs + kpairs) {
+    const int local = pi < qpairs ? pi : pi - qpairs;
+    const int h = local / half, d = local % half;
+    const double2 cs = rope[(size_t)pos * half + d];
+    const double a = (double)fa, b = (double)fb;
+    const float oa = __double2float_rn(__dsub_rn(__dmul_rn(a, cs.x), __dmul_rn(b, cs.y)));
+    const float ob = __double2float_rn(__dadd_rn(__dmul_rn(b, cs.x), __dmul_rn(a, cs.y)));
+    float *dst = pi < qpairs ? q_out + (size_t)mm * ldo + (size_t)h * hd
+                             : k_cache + (((size_t)bb * kvh + h) * capacity + pos) * hd;
+    dst[d] = oa;
+    dst[d + half] = ob;
+  } else {
+    const int local = pi - qpairs - kpairs;
+    const int h = local / half, d = local % half;
+    float *vc = v_cache + (((size_t)bb * kvh + h) * capacity + pos) * hd;
+    vc[d] = fa;
+    vc[d + half] = fb;
+  }
+}
+
+// act[m][i] = silu(gate) * up from the interleaved gate/up projection row.
+__global__ void silu_mul_kernel(const float *gu, float *act, int I, long total) {
+  pdl_wait();
+  pdl_trigger();
+  const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const long m = i / I, j = i % I;
+  act[i] = silu_ref(gu[(size_t)m * 2 * I + 2 * j]) * gu[(size_t)m * 2 * I + 2 * j + 1];
+}
+
+__global__ void set_position_kernel(int *state, int position) { state[0] = position; }
+
 // dst[i][j] = widen/copy of src[rowmap[i]][col0 + j] (half -> half).  Packs a full (out,in) tensor
 // into this rank's fused layout (paired q/k/v rows, interleaved gate/up rows, column shards).
 __global__ void pack_rows_kernel(uint16_t *dst, const uint16_t *src, const uint32_t *rowmap, int rows, int cols,
@@ -411,6 +485,13 @@ uint64_t logical_cols(const stb_llama *m, int which) {
 
 // ---------------------------------------------------------------- cache scratch & steps
 
+// Logit rows a cache keeps: every token row up to the reference's logits limit
+// (LlamaLimits.maxLogitsElements = 16,777,216, LlamaModel.scala:10-12), at least one per batch row.
+int logits_rows(const stb_llama_cache *c, int rows) {
+  const long cap = std::max<long>(1, 16777216L / c->m->V);
+  return (int)std::max<long>(c->batch, std::min<long>(rows, cap));
+}
+
 void ensure_rows(stb_llama_cache *c, int rows) {
   stb_llama *m = c->m;
   stb_session *s = m->s;
@@ -432,12 +513,20 @@ void ensure_rows(stb_llama_cache *c, int rows) {
   c->qbuf = alloc_owned(s, c->owned, (uint64_t)rows * qw * 4);
   c->att = alloc_owned(s, c->owned, (uint64_t)rows * qw * 4);
   c->act = alloc_owned(s, c->owned, (uint64_t)rows * m->I * 4);
-  c->logits = alloc_owned(s, c->owned, (uint64_t)rows * m->V * 4);
+  c->logits = alloc_owned(s, c->owned, (uint64_t)logits_rows(c, rows) * m->V * 4);
   c->best = alloc_owned(s, c->owned, (uint64_t)c->batch * 8);
   c->best_all = alloc_owned(s, c->owned, (uint64_t)c->batch * 8 * m->tp);
   STB_CUDA(cudaMemsetAsync((void *)c->best, 0, (size_t)c->batch * 8, s->stream));
   c->tokens = alloc_owned(s, c->owned, (uint64_t)rows * 8);
   c->state = alloc_owned(s, c->owned, (uint64_t)(2 + 2 * c->batch) * 4);
+  c->xn = c->xh = c->qkvbuf = c->gubuf = 0;
+  if (rows >= m->tc_rows) {
+    const uint64_t widest = std::max<uint64_t>(std::max<uint64_t>(m->H, qw), m->I);
+    c->xn = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
+    c->xh = alloc_owned(s, c->owned, (uint64_t)rows * widest * 2);
+    c->qkvbuf = alloc_owned(s, c->owned, (uint64_t)rows * (m->NH + 2 * m->KV) * m->hd * 4);
+    c->gubuf = alloc_owned(s, c->owned, (uint64_t)rows * 2 * m->I * 4);
+  }
   c->rows = rows;
 }
 
@@ -445,9 +534,59 @@ struct StepArgs {
   int rows, count;          // token rows in this chunk and tokens per batch row
   bool device_pos;          // read position from state[0] (graph) instead of c->used
   bool all_logits;          // logits for every row (decode API) or only each batch row's last token
+  bool logits = true;       // false: a non-final prefill chunk (no lm_head, no pick)
   bool append = false;      // append picks to out_ids (generation)
   int advance = 0;          // position increment done on device
 };
+
+// Tensor-core form of one layer for a chunk of rows >= tc_rows: RMSNorm -> round -> tcgen05 GEMM
+// -> RoPE/KV append; attention; round -> GEMM (+residual); RMSNorm -> round -> GEMM -> SiLU*up;
+// round -> GEMM (+residual).  Row-split projections under TP write partial sums and reduce.
+int enqueue_layer_tc(stb_llama_cache *c, size_t l, int rows, int count, const int *posd, float *kc, float *vc) {
+  stb_llama *m = c->m;
+  stb_session *s = m->s;
+  cudaStream_t st = s->stream;
+  const Layer &L = m->layers[l];
+  const int H = m->H, qw = m->NH * m->hd, nqkv = (m->NH + 2 * m->KV) * m->hd, wdt = m->c.weight_dtype;
+  int *err = session_error_word(s);
+  int launches = 0;
+  auto gemm = [&](const float *x, int K, uint64_t w, int N, float *y, const float *residual) {
+    round_activations(x, (uint16_t *)c->xh, (size_t)rows * K, wdt, st);
+    gemm_tc_launch((const void *)c->xh, (const void *)w, wdt, nullptr, y, N, rows, N, K, err, s->device, st, residual,
+                   residual ? N : 0);
+    launches += 2;
+  };
+  auto row_split = [&](const float *x, int K, uint64_t w) {  // o_proj / down_proj
+    if (m->tp == 1) {
+      gemm(x, K, w, H, (float *)c->hidden, (const float *)c->hidden);
+    } else {
+      gemm(x, K, w, H, (float *)c->sum, m->rank == 0 ? (const float *)c->hidden : nullptr);
+      allreduce_sum_f32(s, (void *)c->sum, (uint64_t)rows * H);
+      std::swap(c->hidden, c->sum);
+    }
+  };
+  launch_kernel(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, st, false, (const float *)c->hidden,
+                (const float *)L.in_norm, m->c.rms_norm_eps, (float *)c->xn, H);
+  gemm((const float *)c->xn, H, L.qkv, nqkv, (float *)c->qkvbuf, nullptr);
+  const long pairs = (long)rows * (nqkv / 2);
+  launch_kernel(rope_append_kernel, dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, st, false,
+                (const float *)c->qkvbuf, nqkv, (const double2 *)m->rope, posd, c->used, count, m->NH, m->KV, m->hd,
+                c->capacity, (float *)c->qbuf, qw, kc, vc, rows);
+  launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), attention_smem(c->capacity, m->hd), st,
+                false, (const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows,
+                count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, (const int *)nullptr);
+  launches += 3;
+  row_split((const float *)c->att, qw, L.o);
+  launch_kernel(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, st, false, (const float *)c->hidden,
+                (const float *)L.post_norm, m->c.rms_norm_eps, (float *)c->xn, H);
+  gemm((const float *)c->xn, H, L.gu, 2 * m->I, (float *)c->gubuf, nullptr);
+  const long acts = (long)rows * m->I;
+  launch_kernel(silu_mul_kernel, dim3((unsigned)((acts + 255) / 256)), dim3(256), 0, st, false,
+                (const float *)c->gubuf, (float *)c->act, m->I, acts);
+  launches += 2;
+  row_split((const float *)c->act, m->I, L.down);
+  return launches;
+}
 
 // Enqueues one forward chunk on the session stream.
 int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
@@ -469,10 +608,15 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
   const size_t kv_layer = (size_t)2 * c->batch * m->KV * c->capacity * m->hd;
   const size_t kv_half = kv_layer / 2;
   const int qw = m->NH * m->hd;
+  const bool tensor_cores = rows >= m->tc_rows && c->xh != 0;
   for (size_t l = 0; l < m->layers.size(); l++) {
     const Layer &L = m->layers[l];
     float *kc = (float *)c->kv + l * kv_layer;
     float *vc = kc + kv_half;
+    if (tensor_cores) {
+      launches += enqueue_layer_tc(c, l, rows, a.count, posd, kc, vc);
+      continue;
+    }
     {  // 1. QKV + RoPE + cache append
       GemvParams p;
       p.x = (const float *)c->hidden; p.ldx = H; p.w = (const void *)L.qkv;
@@ -532,7 +676,7 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
   }
   // final norm + lm_head (+ greedy candidates)
   const int brows = a.all_logits ? rows : c->batch;
-  {
+  if (a.logits) {
     GemvParams p;
     if (a.all_logits) {
       p.x = (const float *)c->hidden; p.ldx = H;
@@ -625,6 +769,7 @@ int stb_llama_create(stb_session *s, const stb_llama_config *config, stb_llama *
     m->c = *config;
     m->c.tp_size = tp;
     m->tp = tp;
+    m->tc_rows = config->tc_prefill_rows == 0 ? 512 : (config->tc_prefill_rows < 0 ? INT_MAX : config->tc_prefill_rows);
     m->rank = config->tp_rank;
     m->H = config->hidden_size;
     m->hd = config->hidden_size / config->num_attention_heads;
@@ -893,6 +1038,8 @@ int stb_llama_decode(stb_llama_cache *c, const int64_t *tokens, int batch, int c
     STB_REQUIRE(tokens && batch == c->batch && count > 0, "cache tokens must match batch with positive chunk length");
     STB_REQUIRE((long)c->used + count <= c->capacity, "model cache capacity exceeded");
     const int rows = batch * count;
+    // LlamaCache.decode's logits limit (LlamaLimits.maxLogitsElements, LlamaCache.scala:31-32)
+    STB_REQUIRE((long)rows * m->c.vocab_size <= 16777216L, "cached logits allocation limit exceeded");
     for (int i = 0; i < rows; i++)
       STB_REQUIRE(tokens[i] >= 0 && tokens[i] < m->c.vocab_size, "embedding token ID out of bounds");
     ensure_rows(c, rows);
@@ -961,8 +1108,12 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     try {
       for (auto &e : ev) STB_CUDA(cudaEventCreate(&e));
-      const int rows = batch * prompt_len;
-      ensure_rows(c, rows);
+      // The prompt is prefilled in chunks of at most kChunkRows token rows (all batch rows advance
+      // together), bounding the activation buffers for long or wide prompts.
+      const char *env = std::getenv("STB_PREFILL_CHUNK_ROWS");
+      const int chunk_rows = env && *env ? std::max(1, std::atoi(env)) : 4096;
+      const int chunk = std::max(1, std::min(prompt_len, chunk_rows / batch));
+      ensure_rows(c, batch * chunk);
       c->out_stride = max_new;
       c->out_ids = alloc_owned(s, c->owned, (uint64_t)batch * max_new * 8);
       if (eos_count) {
@@ -970,25 +1121,40 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
         upload(s, eos, (uint64_t)eos_count * 8, c->eos);
       }
       c->eos_count = eos_count;
+      std::vector<int64_t> part((size_t)batch * chunk);
       STB_CUDA(cudaEventRecord(ev[0], s->stream));
-      upload(s, prompt, (uint64_t)rows * 8, c->tokens);
       STB_CUDA(cudaMemsetAsync((void *)c->state, 0, (size_t)(2 + 2 * batch) * 4, s->stream));
-      // prefill: logits of each row's last token only; pick appended; position += prompt_len
-      StepArgs a;
-      a.rows = rows;
-      a.count = prompt_len;
-      a.device_pos = true;
-      a.all_logits = false;
-      a.append = true;
-      a.advance = prompt_len;
-      int launches = enqueue_step(c, a);
-      count_launch(s, launches);
+      int last = 0;
+      for (int t0 = 0; t0 < prompt_len; t0 += chunk) {
+        const int count = std::min(chunk, prompt_len - t0);
+        const bool final_chunk = t0 + count == prompt_len;
+        for (int b = 0; b < batch; b++)
+          std::memcpy(part.data() + (size_t)b * count, prompt + (size_t)b * prompt_len + t0, (size_t)count * 8);
+        upload(s, part.data(), (uint64_t)batch * count * 8, c->tokens);
+        StepArgs a;
+        a.rows = batch * count;
+        a.count = count;
+        a.all_logits = false;
+        if (final_chunk) {
+          // the last chunk picks each row's first token; from here the position lives on the device
+          launch_kernel(set_position_kernel, dim3(1), dim3(1), 0, s->stream, false, (int *)c->state, c->used);
+          a.device_pos = true;
+          a.append = true;
+          a.advance = count;
+        } else {
+          a.device_pos = false;
+          a.logits = false;
+        }
+        count_launch(s, enqueue_step(c, a));
+        if (!final_chunk) c->used += count;
+        last = count;
+      }
       STB_CUDA(cudaEventRecord(ev[1], s->stream));
       if (max_new > 1) {
         // decode: tokens[b*count + count-1] was rewritten in place; compact them to rows 0..batch
-        if (prompt_len > 1) {
-          STB_CUDA(cudaMemcpy2DAsync((void *)c->tokens, 8, (const void *)(c->tokens + (uint64_t)(prompt_len - 1) * 8),
-                                     (size_t)prompt_len * 8, 8, batch, cudaMemcpyDeviceToDevice, s->stream));
+        if (last > 1) {
+          STB_CUDA(cudaMemcpy2DAsync((void *)c->tokens, 8, (const void *)(c->tokens + (uint64_t)(last - 1) * 8),
+                                     (size_t)last * 8, 8, batch, cudaMemcpyDeviceToDevice, s->stream));
         }
         StepArgs d;
         d.rows = batch;

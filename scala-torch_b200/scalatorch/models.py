@@ -114,7 +114,7 @@ class _Config(ctypes.Structure):
                 ("num_key_value_heads", ctypes.c_int), ("max_positions", ctypes.c_int),
                 ("tie_word_embeddings", ctypes.c_int), ("rms_norm_eps", ctypes.c_double),
                 ("rope_theta", ctypes.c_double), ("weight_dtype", ctypes.c_int), ("tp_rank", ctypes.c_int),
-                ("tp_size", ctypes.c_int)]
+                ("tp_size", ctypes.c_int), ("tc_prefill_rows", ctypes.c_int)]
 
 
 def _declare_llama():
@@ -143,7 +143,9 @@ class BackendLlama:
     """Prepared, thread-confined inference over resident half weights (BackendLlama.scala:27-174)."""
 
     def __init__(self, session: B200Session, config: LlamaConfig, weight_dtype: int = STB_BF16,
-                 tp_rank: int = 0, tp_size: int = 1):
+                 tp_rank: int = 0, tp_size: int = 1, tc_prefill_rows: int = 0):
+        """tc_prefill_rows: chunks with at least this many token rows use the tensor-core prefill
+        (activations rounded to the weight type); 0 = library default (512), < 0 = never."""
         _declare_llama()
         require(weight_dtype in (STB_BF16, STB_F16), "Llama weights must be BF16 or F16")
         self.session = session
@@ -152,7 +154,7 @@ class BackendLlama:
         c = _Config(config.vocab_size, config.hidden_size, config.intermediate_size, config.num_layers,
                     config.num_attention_heads, config.num_key_value_heads, config.max_positions,
                     int(config.tie_word_embeddings), config.rms_norm_eps, config.rope_theta, weight_dtype,
-                    tp_rank, tp_size)
+                    tp_rank, tp_size, tc_prefill_rows)
         h = ctypes.c_void_p()
         call("stb_llama_create", session.handle, ctypes.byref(c), ctypes.byref(h))
         self.handle = h
@@ -161,10 +163,11 @@ class BackendLlama:
 
     # -- preparation
     @classmethod
-    def prepare_random(cls, session, config, seed: int, weight_dtype: int = STB_BF16, tp_rank=0, tp_size=1):
+    def prepare_random(cls, session, config, seed: int, weight_dtype: int = STB_BF16, tp_rank=0, tp_size=1,
+                       tc_prefill_rows: int = 0):
         """LlamaModel.init + BackendLlama.prepare in one step: N(0, initializer_range) matrices generated
         on the device by the counter-based generator, norms = 1."""
-        m = cls(session, config, weight_dtype, tp_rank, tp_size)
+        m = cls(session, config, weight_dtype, tp_rank, tp_size, tc_prefill_rows)
         try:
             call("stb_llama_init_random", m.handle, seed, config.initializer_range)
         except Exception:

@@ -108,6 +108,42 @@ def test_tied_head_is_stored_once(session):
         assert b.weight_bytes - a.weight_bytes == 2 * cfg.vocab_size * cfg.hidden_size
 
 
+def test_chunked_prefill_matches_oracle(session, tiny, monkeypatch):
+    """Prompts prefilled in several chunks (STB_PREFILL_CHUNK_ROWS) give the same greedy ids."""
+    ref = oracle_model(tiny, seed=13)
+    prompts = np.array([[3, 1, 4, 1, 5, 9, 2], [6, 5, 3, 5, 8, 9, 7]])
+    monkeypatch.setenv("STB_PREFILL_CHUNK_ROWS", "4")  # 2 tokens per chunk for batch 2
+    with BackendLlama.prepare_random(session, tiny, seed=13) as m:
+        rows = m.generate_ids(prompts, 8)
+    for b in range(2):
+        assert rows[b] == ref.generate(prompts[b].tolist(), 8)
+
+
+def test_tensor_core_prefill_within_prefill_tolerance(session, tiny):
+    """Chunks of >= tc_prefill_rows rows run the projections on tcgen05 with activations rounded to
+    BF16.  Each rounded GEMM is within 2e-3 normwise (test_prefill_gpu.py); a model chains four of
+    them per layer, so the model-level logits tolerance is 1e-2 normwise per row (observed ~3e-3 for
+    two layers).  The single-token decode steps after it keep Float32 activations."""
+    ref = oracle_model(tiny, seed=17)
+    rng = np.random.default_rng(17)
+    prompt = rng.integers(0, tiny.vocab_size, (2, 6))
+    with BackendLlama.prepare_random(session, tiny, seed=17, tc_prefill_rows=4) as m:
+        c = m.new_cache(2, 12)
+        oc = ref.new_cache(2, 12)
+        got, _ = c.decode(prompt)  # 12 rows -> tensor cores
+        want = ref.decode(oc, prompt)
+        for b in range(2):
+            for t in range(6):
+                rel = np.linalg.norm(got[b, t] - want[b, t]) / np.linalg.norm(want[b, t])
+                assert rel <= 1e-2, (b, t, rel)
+        got, _ = c.decode([[7], [8]])  # 2 rows -> Float32 GEMV path over the tensor-core-built cache
+        want = ref.decode(oc, np.array([[7], [8]]))
+        rel = np.linalg.norm(got - want) / np.linalg.norm(want)
+        assert rel <= 1e-2, rel
+        ref.free_cache(oc)
+        c.close()
+
+
 def test_cache_rejects_and_keeps_position(session, tiny):
     with BackendLlama.prepare_random(session, tiny, seed=1) as m:
         c = m.new_cache(1, 6)
