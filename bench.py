@@ -183,7 +183,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="smollm2", choices=["smollm2", "llama70b"])
+    ap.add_argument("--workload", default="smollm2", choices=["smollm2", "llama70b", "linear", "prefill"])
+    ap.add_argument("--shapes", default="", help="linear/prefill: comma list of shape names to run (default all)")
     ap.add_argument("--batch", type=int, default=1, help="llama70b: decode batch (1, 8, 32)")
     ap.add_argument("--prompt", type=int, default=512, help="llama70b: prompt tokens")
     ap.add_argument("--new", type=int, default=32, help="llama70b: generated tokens per step")
@@ -195,6 +196,8 @@ def main():
 
     if args.impl == "reference":
         return reference_arm(args, world, rank)
+    if args.workload in ("linear", "prefill"):
+        return linear_sweep(args, world, rank, local)
 
     import numpy as np
     import torch
@@ -320,6 +323,127 @@ def main():
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+LLAMA8B_SHAPES = {"q": (4096, 4096), "k": (1024, 4096), "v": (1024, 4096), "o": (4096, 4096),
+                  "gate": (14336, 4096), "up": (14336, 4096), "down": (4096, 14336), "lm_head": (128256, 4096)}
+
+
+def linear_sweep(args, world, rank, local):
+    """BASELINE configs 1/3 (--workload linear: decode GEMV, FP32 activations, M = 1/4/16/32) and
+    config 4 (--workload prefill: tcgen05 GEMM, M = 2048/8192) on Llama-3-8B projection shapes with
+    device-generated BF16 weights ~N(0,0.02).  Each launch is timed alone with CUDA events on the
+    session stream after a 256 MB L2 flush; the median of the timed launches is reported."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    from scalatorch import ffm
+    torch.cuda.set_device(local)
+    hbm_peak, tc_peak, peak_kind = peaks()
+    s = ffm.B200Session(local, 100 << 30)
+    stream = torch.cuda.ExternalStream(s.stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    prefill = args.workload == "prefill"
+    ms = (2048, 8192) if prefill else (1, 4, 16, 32)
+    names = [n for n in LLAMA8B_SHAPES if not args.shapes or n in args.shapes.split(",")]
+    fn = "stb_linear_prefill" if prefill else "stb_linear"
+    L = ffm.library()
+    results, clocks = [], Clocks(local)
+    launches0 = s.launches
+    with clocks:
+        clocks.mark()
+        for si, name in enumerate(names):
+            n, k = LLAMA8B_SHAPES[name]
+            w = torch.empty(n * k, dtype=torch.bfloat16, device="cuda")
+            wt = ffm.DeviceTensor(s, w.data_ptr(), (k, n), ffm.STB_BF16, n * k * 2, transposed_weight=True, owner=False)
+            s.fill_normal(wt, SEED, 100 + si, 0.02)
+            for m in ms:
+                x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(m))
+                y = torch.empty(m, n, device="cuda")
+                torch.cuda.synchronize()
+                s.sync()
+                times = []
+                for it in range(args.warmup + args.steps):
+                    with torch.cuda.stream(stream):
+                        flush.zero_()
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record(stream)
+                    ffm.call(fn, s.handle, x.data_ptr(), w.data_ptr(), ffm.STB_BF16, 0, y.data_ptr(), m, n, k)
+                    e1.record(stream)
+                    e1.synchronize()
+                    if it >= args.warmup:
+                        times.append(e0.elapsed_time(e1) / 1000.0)
+                t = sorted(times)[len(times) // 2]
+                algo = n * k * 2 + m * k * 4 + m * n * 4
+                results.append({"shape": name, "M": m, "N": n, "K": k, "us": round(t * 1e6, 2),
+                                "GB_s": round(algo / t / 1e9, 1), "TFLOP_s": round(2 * m * n * k / t / 1e12, 2),
+                                "hbm_frac": round(algo / t / 1e9 / hbm_peak, 4),
+                                "tensor_frac": round(2 * m * n * k / t / 1e12 / tc_peak, 4)})
+                del x, y
+            del w
+            torch.cuda.empty_cache()
+        clocks.mark()
+    launches = s.launches - launches0
+    # end-to-end through the host-buffer C ABI on the first shape at the smallest M
+    n, k = LLAMA8B_SHAPES[names[0]]
+    m = ms[0]
+    w = torch.empty(n * k, dtype=torch.bfloat16, device="cuda")
+    wt = ffm.DeviceTensor(s, w.data_ptr(), (k, n), ffm.STB_BF16, n * k * 2, transposed_weight=True, owner=False)
+    s.fill_normal(wt, SEED, 100, 0.02)
+    s.sync()
+    hx = np.random.default_rng(0).standard_normal((m, k)).astype(np.float32)
+    hy = np.empty((m, n), np.float32)
+    e2e_t = None
+    if not prefill:
+        for it in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            ffm.call("stb_linear_host", s.handle, hx.ctypes.data, w.data_ptr(), ffm.STB_BF16, 0, hy.ctypes.data, m, n, k)
+            dt = time.perf_counter() - t0
+            e2e_t = dt if e2e_t is None or it < args.warmup else min(e2e_t, dt)
+    s.close()
+    if prefill:
+        flops = sum(2 * r["M"] * r["N"] * r["K"] for r in results)
+        secs = sum(r["us"] for r in results) / 1e6
+        value, unit = flops / secs / 1e12, "TFLOP/s"
+        top = max(results, key=lambda r: r["us"])
+        roof = {"kernel": f"gemm_tc_kernel ({top['shape']} M={top['M']})", "bound": "tensor",
+                "achieved": top["TFLOP_s"], "peak": tc_peak, "unit": "TFLOP/s", "frac": top["tensor_frac"],
+                "peak_source": f"{peak_kind} bf16_tflops (burst)", "traffic": None}
+        metric = "prefill GEMM TFLOP/s (Llama-3-8B projections, BF16 weights, activations rounded to BF16)"
+    else:
+        m1 = [r for r in results if r["M"] == 1]
+        byts = sum(r["N"] * r["K"] * 2 + r["K"] * 4 + r["N"] * 4 for r in m1)
+        secs = sum(r["us"] for r in m1) / 1e6
+        value, unit = byts / secs / 1e9, "GB/s"
+        top = max(m1, key=lambda r: r["us"])
+        roof = {"kernel": f"gemv_kernel ({top['shape']} M=1)", "bound": "hbm", "achieved": top["GB_s"],
+                "peak": hbm_peak, "unit": "GB/s", "frac": top["hbm_frac"], "peak_source": f"{peak_kind} hbm_gbs",
+                "algorithmic_bytes": top["N"] * top["K"] * 2 + top["K"] * 4 + top["N"] * 4, "traffic": None}
+        metric = "decode GEMV GB/s at M=1 (Llama-3-8B projections, BF16 weights, FP32 activations)"
+    line = {"metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(secs * 1000 / max(len(results), 1), 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16-weights/f32-accumulate",
+            "data": "synthetic (device counter-RNG weights, N(0,1) activations)",
+            "config": {"workload": f"llama3-8b {args.workload} sweep", "l2": "flushed (256 MB write) before every launch",
+                       "shapes": results},
+            "gpu_launches": int(launches), "roofline": roof, "clocks": clocks.summary()}
+    if e2e_t:
+        line["e2e"] = {"value": round((n * k * 2 + m * k * 4 + m * n * 4) / e2e_t / 1e9, 2), "unit": "GB/s",
+                       "h2d_bytes_per_step": m * k * 4, "d2h_bytes_per_step": m * n * 4,
+                       "note": f"stb_linear_host on {names[0]} M={m} (host x in, host y out)"}
+    if not args.no_cpu_baseline and not prefill:
+        import oracle
+        x = np.random.default_rng(1).standard_normal((16, 576)).astype(np.float32)
+        wf = oracle.widen(oracle.normal_bf16(1536 * 576, 1, 1, 0.02), oracle.BF16).reshape(1536, 576)
+        t0, reps = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 2.0:  # weights widened once, as SafeTensors.readFloat at load
+            oracle.matmul_tr(x, wf)
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        line["cpu_baseline"] = {"value": round(1904640 / dt / 1e9, 3), "unit": "GB/s", "cores": oracle.max_threads(),
+                                "kind": "port", "sample": f"BASELINE config 1 Linear x[16,576].W[1536,576]^T, {reps} calls"}
+    print(json.dumps(line), flush=True)
 
 
 def cpu_baseline_70b_layer():

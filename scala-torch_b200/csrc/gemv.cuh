@@ -147,6 +147,20 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
   }
   if (p.stop && *p.stop) return;
 
+  // The residual values this thread's epilogue adds, loaded now so the load overlaps the product
+  // (epilogue item i = tid + 256 j covers (token m, row) = (i / (G*ROWS), i % (G*ROWS))).
+  const int blockrow0 = rblock * G * ROWS;
+  float resid_pre[2] = {0.0f, 0.0f};
+  if constexpr (EPI == EPI_RESID) {
+    static_assert(G * ROWS * MT <= 512, "residual prefetch covers two epilogue items per thread");
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int i = tid + 256 * j;
+      const int m = i / (G * ROWS), row = blockrow0 + i % (G * ROWS);
+      if (i < G * ROWS * MT && m < mcount && row < p.N) resid_pre[j] = p.residual[(size_t)(m0 + m) * p.ldr + row];
+    }
+  }
+
   if (p.norm_w) {
     for (int m = 0; m < MT; m++) {
       double sq = 0.0;
@@ -260,9 +274,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
   }
   __syncthreads();
 
-  const int blockrow0 = rblock * G * ROWS;
   if constexpr (EPI == EPI_PLAIN || EPI == EPI_RESID || EPI == EPI_LOGITS) {
-    for (int i = tid; i < G * ROWS * MT; i += 256) {
+    for (int i = tid, j = 0; i < G * ROWS * MT; i += 256, j++) {
       const int m = i / (G * ROWS), rr = i % (G * ROWS);
       const int row = blockrow0 + rr;
       if (m >= mcount || row >= p.N) continue;
@@ -271,7 +284,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
       if constexpr (EPI == EPI_PLAIN) {
         if (p.bias) v = v + p.bias[row];
       } else if constexpr (EPI == EPI_RESID) {
-        v = p.residual[mm * p.ldr + row] + v;
+        v = (j == 0 ? resid_pre[0] : resid_pre[1]) + v;
       }
       p.y[mm * p.ldy + row] = v;
     }

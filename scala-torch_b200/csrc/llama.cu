@@ -595,7 +595,10 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
   cudaStream_t st = s->stream;
   const int H = m->H, rows = a.rows;
   const int *state = (const int *)c->state;
-  const int *stop = a.append ? state + 1 : nullptr;
+  // Once every row has stopped, finalize appends nothing and no longer advances the position, so
+  // the remaining replays only recompute; the kernels themselves need not read the stop flag
+  // (it would sit on each kernel's critical path).
+  const int *stop = nullptr;
   const int *posd = a.device_pos ? state : nullptr;
   int launches = 0;
   const int wdt = m->c.weight_dtype;
