@@ -197,6 +197,15 @@ int stb_nccl_unique_id(uint8_t id[128]);
 int stb_session_init_tp(stb_session *s, int nranks, int rank, const uint8_t id[128]);
 /* In-place Float32 sum allreduce on the session stream (the one exchange per row-split projection). */
 int stb_allreduce_sum_f32(stb_session *s, uint64_t buf, uint64_t count);
+/* Whether stb_session_init_tp mapped the group's NVLink receive buffers (CUDA IPC) that let the
+ * decode step's row-split projections store their partial sums straight into every rank and reduce
+ * them in rank order (set STB_TP_PEER=0 to keep NCCL); slot_elems = Float32 values one projection may
+ * exchange per rank.  No counterpart in the reference. */
+int stb_session_tp_peer(stb_session *s, int *enabled, uint64_t *slot_elems);
+/* Failure detection without a fault: runs the device-side bounded wait used by the peer exchange on
+ * a counter nothing increments, for wait_ns (<= 5 s), and returns the error code the kernel recorded
+ * (99) -- the context stays usable.  No counterpart in the reference. */
+int stb_check_bounded_wait(stb_session *s, uint64_t wait_ns, int *code);
 
 /* ---------------------------------------------------------------- measurement */
 

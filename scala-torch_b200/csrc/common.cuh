@@ -71,6 +71,7 @@ struct stb_session {
   uint64_t staging_bytes = 0;
   cudaEvent_t staging_done[2] = {nullptr, nullptr};
   void *nccl = nullptr;  // ncclComm_t
+  void *peer = nullptr;  // PeerComm (peer.cu): IPC-mapped receive buffers of the TP group
   int tp_rank = 0, tp_size = 1;
   std::atomic<uint64_t> launches{0};
   uint64_t scratch = 0, scratch_bytes = 0;  // grow-only device scratch (charged to the budget)

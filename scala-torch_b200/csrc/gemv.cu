@@ -130,6 +130,12 @@ template int launch_gemv<EPI_RESID>(const GemvParams &, int, GemvConfig, cudaStr
 template int launch_gemv<EPI_SILU>(const GemvParams &, int, GemvConfig, cudaStream_t);
 template int launch_gemv<EPI_QKV>(const GemvParams &, int, GemvConfig, cudaStream_t);
 template int launch_gemv<EPI_LOGITS>(const GemvParams &, int, GemvConfig, cudaStream_t);
+template int launch_gemv<EPI_PEER>(const GemvParams &, int, GemvConfig, cudaStream_t);
+
+int gemv_grid_blocks(int M, int N, GemvConfig cfg, int epi) {
+  cfg = normalize_gemv(cfg, epi);
+  return gemv_row_blocks(N, cfg) * ((M + cfg.mt - 1) / cfg.mt);
+}
 
 __global__ void fill_bias_kernel(float *y, int ldy, const float *bias, int M, int N) {
   const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;

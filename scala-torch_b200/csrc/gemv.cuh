@@ -20,10 +20,13 @@
 #pragma once
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace stb {
 
-enum GemvEpi { EPI_PLAIN = 0, EPI_RESID = 1, EPI_SILU = 2, EPI_QKV = 3, EPI_LOGITS = 4 };
+// EPI_PEER: the partial sums of a row-split projection go to every tensor-parallel rank's receive
+// slots (peer.cuh) instead of y.
+enum GemvEpi { EPI_PLAIN = 0, EPI_RESID = 1, EPI_SILU = 2, EPI_QKV = 3, EPI_LOGITS = 4, EPI_PEER = 5 };
 
 struct GemvParams {
   const float *x = nullptr;
@@ -49,6 +52,7 @@ struct GemvParams {
   int row_offset = 0;                  // global index of row 0 (vocab shard offset)
   const int *stop = nullptr;  // device flag; nonzero makes the kernel a no-op
   bool pdl = false;           // launched as a programmatic dependent of the previous kernel
+  PeerArgs peer{};            // EPI_PEER: receive slots of every rank (slot row stride = ldy)
 };
 
 struct GemvConfig {
@@ -305,6 +309,19 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
         if (besti >= 0) atomicMax(&p.best[m0 + m], argmax_key(best, besti + p.row_offset));
       }
     }
+  } else if constexpr (EPI == EPI_PEER) {
+    const size_t slot = ((size_t)p.peer.region * p.peer.tp + p.peer.rank) * p.peer.slot_elems;
+    for (int i = tid; i < G * ROWS * MT; i += 256) {
+      const int m = i / (G * ROWS), rr = i % (G * ROWS);
+      const int row = blockrow0 + rr;
+      if (m >= mcount || row >= p.N) continue;
+      const float v = s_out[rr / ROWS][rr % ROWS][m];
+      const size_t off = slot + (size_t)(m0 + m) * p.ldy + row;
+      for (int r = 0; r < p.peer.tp; r++) p.peer.slots[r][off] = v;  // NVLink stores to each rank
+    }
+    __threadfence_system();  // this thread's stores are visible system-wide before the signal
+    __syncthreads();
+    if (tid == 0) peer_signal(p.peer);
   } else if constexpr (EPI == EPI_SILU) {
     // Rows are interleaved gate/up: row 2i = gate_i, row 2i+1 = up_i; output width N/2.
     constexpr int PAIRS = ROWS / 2;
@@ -391,5 +408,7 @@ int launch_gemv(const GemvParams &p, int w_dtype, GemvConfig cfg, cudaStream_t s
 int gemv_row_blocks(int N, GemvConfig cfg);
 // The launch shape launch_gemv<epi> really uses for a requested config.
 GemvConfig normalize_gemv(GemvConfig cfg, int epi);
+// Thread blocks one launch_gemv<epi> of (M, N) with cfg runs.
+int gemv_grid_blocks(int M, int N, GemvConfig cfg, int epi);
 
 }  // namespace stb

@@ -32,6 +32,11 @@ void allgather_bytes(stb_session *s, const void *send, void *recv, uint64_t byte
 void gemm_tc_launch(const void *xh, const void *w, int dtype, const float *bias, float *y, int ldy, int M, int N,
                     int K, int *err, int device, cudaStream_t stream, const float *residual, int ldr);
 void round_activations(const float *x, uint16_t *out, size_t count, int dtype, cudaStream_t stream);
+bool peer_usable(stb_session *s, uint64_t elems);
+PeerArgs peer_args(stb_session *s, int region);
+void peer_reduce_launch(stb_session *s, int region, long total, const float *residual, float *out,
+                        unsigned long long blocks_per_rank);
+void peer_reset(stb_session *s);
 }  // namespace stb
 
 using namespace stb;
@@ -663,6 +668,16 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
         p.y = (float *)c->hidden; p.ldy = H; p.residual = (const float *)c->hidden; p.ldr = H;
         launch_gemv<EPI_RESID>(p, wdt, choose_gemv(rows, p.N, p.K, false), st);
         launches++;
+      } else if (peer_usable(s, (uint64_t)rows * H)) {
+        // fused row-split projection: partial sums stored into every rank's slots over NVLink,
+        // then summed in rank order with the residual on each rank
+        p.ldy = H;
+        p.peer = peer_args(s, half);
+        const GemvConfig cfg = choose_gemv(rows, p.N, p.K, false);
+        launch_gemv<EPI_PEER>(p, wdt, cfg, st);
+        peer_reduce_launch(s, half, (long)rows * H, (const float *)c->hidden, (float *)c->hidden,
+                           (unsigned long long)gemv_grid_blocks(rows, p.N, cfg, EPI_PEER));
+        launches += 2;
       } else {
         p.y = (float *)c->sum; p.ldy = H;
         if (m->rank == 0) {
@@ -1046,6 +1061,7 @@ int stb_llama_decode(stb_llama_cache *c, const int64_t *tokens, int batch, int c
     for (int i = 0; i < rows; i++)
       STB_REQUIRE(tokens[i] >= 0 && tokens[i] < m->c.vocab_size, "embedding token ID out of bounds");
     ensure_rows(c, rows);
+    if (m->tp > 1) peer_reset(s);  // collective, as every rank decodes the same chunk
     upload(s, tokens, (uint64_t)rows * 8, c->tokens);
     STB_CUDA(cudaMemsetAsync((void *)c->state, 0, (size_t)(2 + 2 * batch) * 4, s->stream));
     StepArgs a;
@@ -1108,6 +1124,7 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
       int rc = stb_llama_cache_create(m, batch, total, &c);
       if (rc != STB_OK) throw Error(rc, stb_last_error());
     }
+    if (m->tp > 1) peer_reset(s);  // collective: every rank starts the exchange counters at zero
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     try {
       for (auto &e : ev) STB_CUDA(cudaEventCreate(&e));

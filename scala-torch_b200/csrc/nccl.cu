@@ -10,6 +10,9 @@
 
 namespace stb {
 
+void peer_setup(stb_session *s);
+void peer_teardown(stb_session *s);
+
 #define STB_NCCL(call)                                                                            \
   do {                                                                                            \
     ncclResult_t r_ = (call);                                                                     \
@@ -38,6 +41,7 @@ using namespace stb;
 extern "C" {
 
 void stb_session_close_tp(stb_session *s) {
+  if (s && s->peer) peer_teardown(s);
   if (s && s->nccl) {
     ncclCommDestroy((ncclComm_t)s->nccl);
     s->nccl = nullptr;
@@ -68,6 +72,7 @@ int stb_session_init_tp(stb_session *s, int nranks, int rank, const uint8_t id[1
     ncclComm_t comm;
     STB_NCCL(ncclCommInitRank(&comm, nranks, u, rank));
     s->nccl = comm;
+    peer_setup(s);  // NVLink receive buffers for the fused row-split projections
   });
 }
 

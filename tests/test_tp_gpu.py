@@ -18,8 +18,10 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _rank_main(rank, world, id_q, res_q, prompts, max_new, seed):
+def _rank_main(rank, world, id_q, res_q, prompts, max_new, seed, peer):
     sys.path[:0] = [ROOT, os.path.join(ROOT, "scala-torch_b200"), os.path.join(ROOT, "tests")]
+    os.environ["STB_TP_PEER"] = "1" if peer else "0"
+    os.environ["STB_PEER_WAIT_MS"] = "20000"
     try:
         from llama_fixtures import TINY
         from scalatorch import ffm
@@ -32,6 +34,11 @@ def _rank_main(rank, world, id_q, res_q, prompts, max_new, seed):
             uid = id_q.get(timeout=120)
         s = ffm.B200Session(rank, 1 << 30)
         s.init_tp(world, rank, uid)
+        import ctypes
+        enabled, elems = ctypes.c_int(), ctypes.c_uint64()
+        ffm.library().stb_session_tp_peer.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        ffm.call("stb_session_tp_peer", s.handle, ctypes.byref(enabled), ctypes.byref(elems))
+        assert bool(enabled.value) == peer, (enabled.value, peer)
         m = BackendLlama.prepare_random(s, LlamaConfig(**TINY), seed=seed, tp_rank=rank, tp_size=world)
         out = m.generate_ids(np.array(prompts), max_new)
         single = m.generate_ids(prompts[0], max_new)
@@ -48,13 +55,14 @@ def _gpus():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-def test_tp2_generation_matches_oracle():
+@pytest.mark.parametrize("peer", [True, False], ids=["nvlink-peer-exchange", "nccl-allreduce"])
+def test_tp2_generation_matches_oracle(peer):
     from llama_fixtures import TINY, oracle_model
     from scalatorch.models import LlamaConfig
     ctx = mp.get_context("spawn")
     id_q, res_q = ctx.Queue(), ctx.Queue()
     prompts = [[5, 6, 7, 8], [900, 1, 2, 3]]
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, id_q, res_q, prompts, 12, 9)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, id_q, res_q, prompts, 12, 9, peer)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}

@@ -64,3 +64,34 @@ def test_uneven_splits_are_rejected_before_any_device_work():
     assert shard_plan(smol, 0, 1).heads == (0, 9)
     with pytest.raises(ffm.IllegalArgumentException):
         shard_plan(smol, 0, 2)  # 9 heads / 3 KV heads do not split over 2 ranks
+
+
+def _dying_worker(rank, world, port, results):
+    sys.path[:0] = [ROOT, os.path.join(ROOT, "scala-torch_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # a rank that leaves between steps, with nothing in flight
+    try:
+        import bench
+        bench.max_over_ranks([1.0], device=None)
+        results[rank] = "no error"
+    except Exception as e:  # the survivor learns of it through the collective's error
+        results[rank] = type(e).__name__
+
+
+def test_a_rank_that_leaves_makes_the_next_collective_fail_not_hang():
+    mgr = tmp.Manager()
+    results = mgr.dict()
+    port = 30500 + os.getpid() % 1000
+    ctx = tmp.get_context("spawn")
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert results.get(0) not in (None, "no error")
