@@ -310,18 +310,17 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
       }
     }
   } else if constexpr (EPI == EPI_PEER) {
+    // one 8-byte (use, value) word per output to every rank, this rank's slot (peer.cuh)
+    const uint32_t use = (uint32_t)(p.peer.my_epoch[p.peer.region] + 1ull);
     const size_t slot = ((size_t)p.peer.region * p.peer.tp + p.peer.rank) * p.peer.slot_elems;
     for (int i = tid; i < G * ROWS * MT; i += 256) {
       const int m = i / (G * ROWS), rr = i % (G * ROWS);
       const int row = blockrow0 + rr;
       if (m >= mcount || row >= p.N) continue;
-      const float v = s_out[rr / ROWS][rr % ROWS][m];
+      const unsigned long long w = peer_word(s_out[rr / ROWS][rr % ROWS][m], use);
       const size_t off = slot + (size_t)(m0 + m) * p.ldy + row;
-      for (int r = 0; r < p.peer.tp; r++) p.peer.slots[r][off] = v;  // NVLink stores to each rank
+      for (int r = 0; r < p.peer.tp; r++) peer_store(p.peer.slots[r] + off, w);
     }
-    __threadfence_system();  // this thread's stores are visible system-wide before the signal
-    __syncthreads();
-    if (tid == 0) peer_signal(p.peer);
   } else if constexpr (EPI == EPI_SILU) {
     // Rows are interleaved gate/up: row 2i = gate_i, row 2i+1 = up_i; output width N/2.
     constexpr int PAIRS = ROWS / 2;

@@ -34,8 +34,7 @@ void gemm_tc_launch(const void *xh, const void *w, int dtype, const float *bias,
 void round_activations(const float *x, uint16_t *out, size_t count, int dtype, cudaStream_t stream);
 bool peer_usable(stb_session *s, uint64_t elems);
 PeerArgs peer_args(stb_session *s, int region);
-void peer_reduce_launch(stb_session *s, int region, long total, const float *residual, float *out,
-                        unsigned long long blocks_per_rank);
+void peer_reduce_launch(stb_session *s, int region, long total, const float *residual, float *out);
 void peer_reset(stb_session *s);
 }  // namespace stb
 
@@ -675,8 +674,7 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
         p.peer = peer_args(s, half);
         const GemvConfig cfg = choose_gemv(rows, p.N, p.K, false);
         launch_gemv<EPI_PEER>(p, wdt, cfg, st);
-        peer_reduce_launch(s, half, (long)rows * H, (const float *)c->hidden, (float *)c->hidden,
-                           (unsigned long long)gemv_grid_blocks(rows, p.N, cfg, EPI_PEER));
+        peer_reduce_launch(s, half, (long)rows * H, (const float *)c->hidden, (float *)c->hidden);
         launches += 2;
       } else {
         p.y = (float *)c->sum; p.ldy = H;

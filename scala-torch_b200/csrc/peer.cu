@@ -63,7 +63,7 @@ void peer_setup(stb_session *s) {
       STB_CUDA(cudaIpcOpenMemHandle(&pc->remote[r], all[r], cudaIpcMemLazyEnablePeerAccess));
       pc->base[r] = (uint64_t)pc->remote[r];
     }
-    pc->slot_elems = ((pc->bytes - kPeerControlBytes) / (2ull * pc->tp * 4)) & ~3ull;
+    pc->slot_elems = ((pc->bytes - kPeerControlBytes) / (2ull * pc->tp * 8)) & ~3ull;
     s->peer = pc;
     peer_barrier(s);  // every rank has mapped every buffer before first use
   } catch (...) {
@@ -98,7 +98,8 @@ void peer_reset(stb_session *s) {
   auto *pc = (PeerComm *)s->peer;
   if (!pc) return;
   peer_barrier(s);
-  STB_CUDA(cudaMemsetAsync((void *)pc->local, 0, kPeerControlBytes, s->stream));
+  // epochs restart at 0, so every slot word must lose its old use number too
+  STB_CUDA(cudaMemsetAsync((void *)pc->local, 0, pc->bytes, s->stream));
   peer_barrier(s);
 }
 
@@ -110,14 +111,10 @@ bool peer_usable(stb_session *s, uint64_t elems) {
 PeerArgs peer_args(stb_session *s, int region) {
   auto *pc = (PeerComm *)s->peer;
   PeerArgs a{};
-  for (int r = 0; r < pc->tp; r++) {
-    a.slots[r] = (float *)(pc->base[r] + kPeerControlBytes);
-    a.counters[r] = (unsigned long long *)pc->base[r];
-  }
-  a.my_counter = (unsigned long long *)pc->local;
-  a.my_epoch = (unsigned long long *)(pc->local + 64);
-  a.my_done = (unsigned int *)(pc->local + 128);
-  a.my_slots = (const float *)(pc->local + kPeerControlBytes);
+  for (int r = 0; r < pc->tp; r++) a.slots[r] = (unsigned long long *)(pc->base[r] + kPeerControlBytes);
+  a.my_epoch = (unsigned long long *)pc->local;
+  a.my_done = (unsigned int *)(pc->local + 64);
+  a.my_slots = (const unsigned long long *)(pc->local + kPeerControlBytes);
   a.slot_elems = pc->slot_elems;
   a.tp = pc->tp;
   a.rank = pc->rank;
@@ -127,26 +124,19 @@ PeerArgs peer_args(stb_session *s, int region) {
   return a;
 }
 
-// out[i] = residual[i] + (((slot_0[i] + slot_1[i]) + slot_2[i]) + ...) once every block of every rank
-// has signalled this use of the region; the last block to finish advances the region's epoch.
-__global__ void peer_reduce_kernel(PeerArgs pa, long total, const float *residual, float *out,
-                                   unsigned long long per_use) {
-  __shared__ int ok;
+// out[i] = residual[i] + (((slot_0[i] + slot_1[i]) + slot_2[i]) + ...), each slot word taken once it
+// carries this use of the region; the last block to finish advances the region's epoch.
+__global__ void peer_reduce_kernel(PeerArgs pa, long total, const float *residual, float *out) {
   pdl_wait();
-  if (threadIdx.x == 0) {
-    const unsigned long long target = (pa.my_epoch[pa.region] + 1ull) * per_use;
-    ok = peer_wait_geq(pa.my_counter + pa.region, target, pa.wait_ns, pa.err, 16 + pa.region);
-    __threadfence_system();
-  }
-  __syncthreads();
   pdl_trigger();
-  if (ok) {
-    const float *base = pa.my_slots + (size_t)pa.region * pa.tp * pa.slot_elems;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-      float acc = __ldcg(base + i);
-      for (int r = 1; r < pa.tp; r++) acc += __ldcg(base + (size_t)r * pa.slot_elems + i);
-      out[i] = residual[i] + acc;
-    }
+  const uint32_t use = (uint32_t)(pa.my_epoch[pa.region] + 1ull);
+  const unsigned long long *base = pa.my_slots + (size_t)pa.region * pa.tp * pa.slot_elems;
+  bool ok = true;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total && ok; i += (long)gridDim.x * blockDim.x) {
+    float acc = peer_take(base + i, use, pa.wait_ns, pa.err, 16 + pa.region, &ok);
+    for (int r = 1; r < pa.tp; r++)
+      acc += peer_take(base + (size_t)r * pa.slot_elems + i, use, pa.wait_ns, pa.err, 16 + pa.region, &ok);
+    if (ok) out[i] = residual[i] + acc;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -160,14 +150,11 @@ __global__ void peer_reduce_kernel(PeerArgs pa, long total, const float *residua
   }
 }
 
-void peer_reduce_launch(stb_session *s, int region, long total, const float *residual, float *out,
-                        unsigned long long blocks_per_rank) {
+void peer_reduce_launch(stb_session *s, int region, long total, const float *residual, float *out) {
   PeerArgs pa = peer_args(s, region);
-  const unsigned long long per_use = blocks_per_rank * (unsigned long long)pa.tp;
   long blocks = (total + 255) / 256;
-  if (blocks > 64) blocks = 64;
-  launch_kernel(peer_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, s->stream, true, pa, total, residual, out,
-                per_use);
+  if (blocks > 148) blocks = 148;
+  launch_kernel(peer_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, s->stream, true, pa, total, residual, out);
 }
 
 __global__ void wait_probe_kernel(const unsigned long long *counter, unsigned long long wait_ns, int *err) {
