@@ -178,6 +178,16 @@ void linear(stb_session *s, uint64_t x, int ldx, uint64_t w, int w_dtype, uint64
     count_launch(s);
     return;
   }
+  if (skinny_eligible(M, N, K, w_dtype)) {
+    // 8..64 token rows: tensor cores with the activations split into three BF16 terms
+    const uint64_t bytes = skinny_scratch_bytes(M, N, K, nullptr, s->device);
+    int *err = session_error_word(s);
+    void *scratch = (void *)session_scratch(s, bytes);
+    skinny_launch((const float *)x, ldx, (const void *)w, (const float *)bias, nullptr, 0, (float *)y, ldy, M, N, K,
+                  scratch, err, s->device, s->stream, false);
+    count_launch(s, 3);
+    return;
+  }
   GemvParams p;
   p.x = (const float *)x;
   p.ldx = ldx;
@@ -190,6 +200,11 @@ void linear(stb_session *s, uint64_t x, int ldx, uint64_t w, int w_dtype, uint64
   p.bias = (const float *)bias;
   launch_gemv<EPI_PLAIN>(p, w_dtype, choose_gemv(M, N, K, false), s->stream);
   count_launch(s);
+}
+
+bool skinny_eligible(int M, int N, int K, int w_dtype) {
+  static const int enabled = env_int("STB_SKINNY", 1);
+  return enabled && w_dtype == STB_BF16 && M >= 8 && M <= 64 && K % 8 == 0 && N >= 128;
 }
 
 }  // namespace stb

@@ -410,4 +410,12 @@ GemvConfig normalize_gemv(GemvConfig cfg, int epi);
 // Thread blocks one launch_gemv<epi> of (M, N) with cfg runs.
 int gemv_grid_blocks(int M, int N, GemvConfig cfg, int epi);
 
+// Tensor-core skinny form (gemm_skinny.cu) for 8 <= M <= 64 rows and BF16 weights, activations
+// split into three BF16 terms (FP32-accurate); STB_SKINNY=0 keeps the SIMT kernel.
+bool skinny_eligible(int M, int N, int K, int w_dtype);
+uint64_t skinny_scratch_bytes(int M, int N, int K, int *splits_out, int device);
+void skinny_launch(const float *x, int ldx, const void *w, const float *bias, const float *residual, int ldr,
+                   float *y, int ldy, int M, int N, int K, void *scratch, int *err, int device, cudaStream_t stream,
+                   bool pdl);
+
 }  // namespace stb
