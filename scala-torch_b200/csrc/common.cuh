@@ -8,6 +8,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <map>
 #include <stdexcept>
 #include <string>
@@ -86,6 +87,12 @@ void enter(stb_session *s);
 uint64_t session_alloc(stb_session *s, uint64_t bytes);
 void session_free(stb_session *s, uint64_t ptr);
 inline void count_launch(stb_session *s, uint64_t n = 1) { s->launches += n; }
+
+// Integer tuning switch from the environment, or `fallback` when unset.
+inline int env_int(const char *name, int fallback) {
+  const char *v = std::getenv(name);
+  return v && *v ? std::atoi(v) : fallback;
+}
 void check_launch(const char *what);
 void upload(stb_session *s, const void *host, uint64_t bytes, uint64_t dst);
 void download(stb_session *s, uint64_t src, void *host, uint64_t bytes);

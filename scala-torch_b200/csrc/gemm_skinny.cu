@@ -1,22 +1,34 @@
 // Decode-sized Linear on the tcgen05 tensor cores with Float32-accurate activations:
-//   y[M,N] = x[M,K] . W[N,K]^T (+ bias) (+ residual),  8 <= M <= 64 token rows, BF16 weights.
+//   y[M,N] = epilogue(x[M,K] . W[N,K]^T),  1 <= M <= 64 token rows, BF16 weights,
+// with the vector GEMV's optional RMSNorm prologue and its epilogues (gemv.cuh).
 //
 // The SIMT decode GEMV keeps FP32 activations with FP32 FMA, which is bound by FP32 issue once M
 // reaches ~10 (2M flop per weight byte).  Here each activation is split into three BF16 terms
 //   x0 = rne(x), x1 = rne(x - x0), x2 = rne(x - x0 - x1)   (x - x0 and x - x0 - x1 are exact),
 // which together carry x's 24-bit significand (the remainder is ~2^-27 |x|).  BF16 x BF16 products
-// are exact in FP32.  The tensor core's FP32 accumulation is not round-to-nearest (a chain of
-// ~200 MMAs drifted by ~3e-5 relative here), so each 64-wide K block gets a fresh TMEM accumulator
-// (12 MMAs: x2, x1, x0 terms x 4 K steps) from a ring of four, and the epilogue warps add the block
-// partials in FP32 in K order.  The result keeps Float32-activation accuracy (within the decode
-// GEMV's 1e-5 * (1 + |e|)) at tensor-core throughput: the kernel is bound by streaming W from HBM.
+// are exact in FP32.  The B operand of one MMA is the whole [x0; x1; x2] tile (N = 3 NT rows), so a
+// 64-wide K block takes 4 MMAs (M = 128, N = 3 NT, K = 16) rather than 12 dependent small ones, and
+// the three term products land in separate TMEM column groups.  The tensor core's FP32
+// accumulation is not round-to-nearest (a chain of ~200 MMAs drifted by ~3e-5 relative), so each
+// K block gets a fresh accumulator from a ring, and the epilogue warps combine the terms
+// ((x2 + x1) + x0) and add the block partials in FP32 in K order.  The result keeps
+// Float32-activation accuracy (within the decode GEMV's 1e-5 * (1 + |e|)) at tensor-core
+// throughput: the kernel is bound by streaming W from HBM.
 //
-// Grid: (N / 128 weight-row tiles) x KSPLIT.  Each CTA streams a 128 x (K / KSPLIT) slice of W
-// through a 4-stage TMA ring (SWIZZLE_128B, K-major) together with the matching 3 x NT x 64 slice
-// of the split activations (NT = M rounded up to 32 or 64), one thread issues
-// tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = NT), four warps read and sum TMEM and store the
-// CTA's partial sums.  A second kernel adds the KSPLIT partials in split order (deterministic) and applies the
-// epilogue.  Every mbarrier wait is bounded; each CTA loads its own tiles.
+// Three kernels:
+//   1. prologue: RMSNorm (the GEMV's expression) and the split into x3[3][NT][K] (NT = M rounded up
+//      to 16, 32 or 64; rows M..NT-1 zero), one block per 1024 elements of a row;
+//   2. stream-K GEMM: one persistent CTA per SM.  The iterations (128-row weight tile t, 64-wide
+//      K block kb), t-major, are cut into gridDim.x equal contiguous ranges, so every SM streams
+//      the same number of weight bytes whatever the tile count.  Warp 0 issues TMA loads of the
+//      W tile and the matching 3 x NT x 64 slice of x3 through a 5-9 stage ring (SWIZZLE_128B,
+//      K-major; the first stages' W loads go out before the programmatic-dependency wait, since
+//      weights never depend on the previous kernel), warp 1 issues
+//      tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = 3 NT), warps 2-5 sum the accumulators and
+//      store one partial per (tile, piece): the part of a tile's K range this CTA covered;
+//   3. fixup: adds each tile's pieces in piece (= K) order and applies the epilogue.
+// Deterministic for a given SM count.  Every mbarrier wait is bounded; each CTA loads its own tiles.
+#include "gemv.cuh"
 #include "tc_common.cuh"
 
 namespace stb {
@@ -25,25 +37,84 @@ namespace {
 
 using namespace tc;
 
-constexpr int SK_BM = 128, SK_STAGES = 4, SK_ACC = 4;
+constexpr int SK_BM = 128, SK_ACC_MAX = 4;
 
 template <int NT>
 struct SkinnyShape {
+  static constexpr int STAGES = NT == 16 ? 9 : (NT == 32 ? 7 : 5);
   static constexpr int A_BYTES = SK_BM * BK * 2;
-  static constexpr int B_BYTES = 3 * NT * BK * 2;
+  static constexpr int B_BYTES = 3 * NT * BK * 2;  // multiple of 1024: the tile stays swizzle-aligned
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int SMEM = SK_STAGES * STAGE + 1024 + 256;
-  static constexpr int TMEM_COLS = SK_ACC * NT;  // 128 or 256 columns, a power of two
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+  static constexpr int ACC_STRIDE = NT == 16 ? 64 : (NT == 32 ? 128 : 256);  // >= 3 NT TMEM columns
+  static constexpr int ACC = NT == 64 ? 2 : 4;                                // accumulators in the ring
+  static constexpr int TMEM_COLS = ACC * ACC_STRIDE;                          // 256 or 512
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert(TMEM_COLS <= 512 && ACC <= SK_ACC_MAX, "tensor memory");
+  static_assert((2 * STAGES + 2 * SK_ACC_MAX + 1) * 8 + 8 <= 256, "barrier area");
 };
 
-// x [M][K] (row stride ldx) -> x3 [3][NT][K] BF16 terms; rows M..NT-1 are zero.
-__global__ void split3_kernel(const float *x, int ldx, uint16_t *x3, int M, int NT, int K) {
+template <int W>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&out)[W]) {
+  static_assert(W == 16 || W == 32, "load width");
+  uint32_t r[32];
+  if constexpr (W == 16) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  } else {
+    tmem_ld32(taddr, r);
+  }
+#pragma unroll
+  for (int j = 0; j < W; j++) out[j] = __uint_as_float(r[j]);
+}
+
+// First iteration of CTA c when T iterations are cut into G ranges.
+__host__ __device__ __forceinline__ long long sk_start(int c, long long T, int G) { return (long long)c * T / G; }
+
+// The CTA whose range holds iteration i.
+__device__ __forceinline__ int sk_cta_of(long long i, long long T, int G) {
+  int c = (int)(i * G / T);
+  while (c + 1 < G && sk_start(c + 1, T, G) <= i) c++;
+  return c;
+}
+
+// x [M][K] (row stride ldx), optionally RMS-normalised as the vector GEMV does it, -> x3 [3][NT][K].
+// Block (kb, m) converts elements [kb * 1024, kb * 1024 + 1024) of row m, four per thread; with
+// RMSNorm every block of a row recomputes the row's inverse RMS with the GEMV's exact loop and
+// reduction order, so all blocks (and the GEMV) agree bit for bit.
+__global__ void __launch_bounds__(256) skinny_prep_kernel(const float *x, int ldx, const float *norm_w,
+                                                          double eps, uint16_t *x3, int M, int NT, int K) {
+  __shared__ double s_scratch[8];
   pdl_wait();
   pdl_trigger();
-  const long total = (long)NT * K;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const int m = (int)(i / K), k = (int)(i % K);
-    const float v = m < M ? x[(size_t)m * ldx + k] : 0.0f;
+  const int m = blockIdx.y;
+  double inv = 1.0;
+  if (m < M && norm_w) {
+    const float *xr = x + (size_t)m * ldx;
+    double sq = 0.0;
+#pragma unroll 8
+    for (int k = threadIdx.x; k < K; k += 256) {
+      const double v = (double)xr[k];
+      sq = __dadd_rn(sq, __dmul_rn(v, v));
+    }
+    const double total = block_sum_double(sq, s_scratch);
+    inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(total, (double)K), eps)));
+  }
+  const int k0 = blockIdx.x * 1024 + threadIdx.x * 4;
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const int k = k0 + e;
+    if (k >= K) break;
+    float v = 0.0f;
+    if (m < M) {
+      v = x[(size_t)m * ldx + k];
+      if (norm_w) v = __double2float_rn(__dmul_rn(__dmul_rn((double)v, inv), (double)norm_w[k]));
+    }
     const uint16_t h0 = f32_to_bf16_rne(v);
     const float r1 = v - __uint_as_float((uint32_t)h0 << 16);  // exact
     const uint16_t h1 = f32_to_bf16_rne(r1);
@@ -58,28 +129,27 @@ __global__ void split3_kernel(const float *x, int ldx, uint16_t *x3, int M, int 
 template <int NT>
 __global__ void __launch_bounds__(192, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, float *part,
-                       int M, int N, int K, int kb_per_split, uint32_t idesc, int *err) {
+                       int M, int N, int kbs, long long T, int pmax, uint32_t idesc, int *err) {
   using S = SkinnyShape<NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t *bars = (uint64_t *)(smem + SK_STAGES * S::STAGE);
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + SK_STAGES);
-  const uint32_t accf0 = smem_u32(bars + 2 * SK_STAGES), acce0 = smem_u32(bars + 2 * SK_STAGES + SK_ACC);
-  const uint32_t drain = smem_u32(bars + 2 * SK_STAGES + 2 * SK_ACC);
-  uint32_t *tmem_slot = (uint32_t *)(bars + 2 * SK_STAGES + 2 * SK_ACC + 1);
+  uint64_t *bars = (uint64_t *)(smem + S::STAGES * S::STAGE);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S::STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * S::STAGES), acce0 = smem_u32(bars + 2 * S::STAGES + SK_ACC_MAX);
+  const uint32_t drain = smem_u32(bars + 2 * S::STAGES + 2 * SK_ACC_MAX);
+  uint32_t *tmem_slot = (uint32_t *)(bars + 2 * S::STAGES + 2 * SK_ACC_MAX + 1);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nb = blockIdx.x, ks = blockIdx.y;
-  const int kblocks = (K + BK - 1) / BK;
-  const int kb0 = ks * kb_per_split, kb1 = min(kblocks, kb0 + kb_per_split);
+  const int cta = blockIdx.x, G = gridDim.x;
+  const long long i0 = sk_start(cta, T, G), i1 = sk_start(cta + 1, T, G);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SK_STAGES; s++) {
+    for (int s = 0; s < S::STAGES; s++) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    for (int r = 0; r < SK_ACC; r++) {
+    for (int r = 0; r < S::ACC; r++) {
       mbar_init(accf0 + 8 * r, 1);
       mbar_init(acce0 + 8 * r, 4);  // one arrival per epilogue warp
     }
@@ -97,87 +167,106 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t sa0 = smem_u32(smem), sb0 = sa0 + SK_STAGES * S::A_BYTES;
-  pdl_wait();  // the split activations come from the previous kernel
+  const uint32_t sa0 = smem_u32(smem), sb0 = sa0 + S::STAGES * S::A_BYTES;
 
-  if (warp == 0 && lane == 0) {
-    int stage = 0;
-    uint32_t phase = 0;
-    for (int kb = kb0; kb < kb1; kb++) {
-      if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, 31)) break;
-      mbar_expect_tx(full0 + 8 * stage, S::STAGE);
-      tma_load_2d(sa0 + stage * S::A_BYTES, &tw, kb * BK, nb * SK_BM, full0 + 8 * stage);
-      tma_load_2d(sb0 + stage * S::B_BYTES, &tx, kb * BK, 0, full0 + 8 * stage);
-      if (++stage == SK_STAGES) {
-        stage = 0;
-        phase ^= 1;
+  if (warp == 0) {
+    if (lane == 0) {
+      // Weights never depend on the previous kernel: the first ring's W tiles load before the wait
+      // for the split activations.
+      const int pre = (int)min((long long)S::STAGES, i1 - i0);
+      for (int j = 0; j < pre; j++) {
+        const long long i = i0 + j;
+        mbar_expect_tx(full0 + 8 * j, S::STAGE);
+        tma_load_2d(sa0 + j * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * j);
+      }
+      pdl_wait();
+      for (int j = 0; j < pre; j++)
+        tma_load_2d(sb0 + j * S::B_BYTES, &tx, (int)((i0 + j) % kbs) * BK, 0, full0 + 8 * j);
+      int stage = pre % S::STAGES;
+      uint32_t phase = pre == S::STAGES ? 1u : 0u;
+      for (long long i = i0 + pre; i < i1; i++) {
+        if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, 31)) break;
+        mbar_expect_tx(full0 + 8 * stage, S::STAGE);
+        tma_load_2d(sa0 + stage * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * stage);
+        tma_load_2d(sb0 + stage * S::B_BYTES, &tx, (int)(i % kbs) * BK, 0, full0 + 8 * stage);
+        if (++stage == S::STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // One K block (64 x 3 terms = 12 MMAs) per accumulator: short tensor-core chains, the block
-    // partials are added in FP32 by the epilogue warps.
-    int stage = 0;
-    uint32_t phase = 0;
-    bool issued = false;
-    for (int kb = kb0, j = 0; kb < kb1; kb++, j++) {
-      const int r = j % SK_ACC;
-      if (!mbar_wait(acce0 + 8 * r, ((uint32_t)(j / SK_ACC) & 1u) ^ 1u, abort_flag, err, 35)) break;
-      if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, err, 32)) break;
-      tc_fence_after();
-      const uint64_t a = smem_desc(sa0 + stage * S::A_BYTES);
-      const uint32_t d = tmem + (uint32_t)(r * NT);
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool issued = false;
+      int j = 0;
+      for (long long i = i0; i < i1; i++, j++) {
+        const int r = j % S::ACC;
+        if (!mbar_wait(acce0 + 8 * r, ((uint32_t)(j / S::ACC) & 1u) ^ 1u, abort_flag, err, 35)) break;
+        if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, err, 32)) break;
+        tc_fence_after();
+        const uint64_t a = smem_desc(sa0 + stage * S::A_BYTES);
+        const uint64_t b = smem_desc(sb0 + stage * S::B_BYTES);  // [x0; x1; x2]: N = 3 NT rows
+        const uint32_t d = tmem + (uint32_t)(r * S::ACC_STRIDE);
 #pragma unroll
-      for (int t = 2; t >= 0; t--) {  // smallest term first: x2, x1, x0, each NT rows of the B tile
-        const uint64_t b = smem_desc(sb0 + stage * S::B_BYTES + t * NT * BK * 2);
-#pragma unroll
-        for (int k = 0; k < BK / 16; k++)
-          mma_f16(d, a + (uint64_t)(2 * k), b + (uint64_t)(2 * k), idesc, (t != 2 || k != 0));
+        for (int k = 0; k < BK / 16; k++) mma_f16(d, a + (uint64_t)(2 * k), b + (uint64_t)(2 * k), idesc, k != 0);
+        issued = true;
+        mma_commit(empty0 + 8 * stage);
+        mma_commit(accf0 + 8 * r);
+        if (++stage == S::STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
       }
-      issued = true;
-      mma_commit(empty0 + 8 * stage);
-      mma_commit(accf0 + 8 * r);
-      if (++stage == SK_STAGES) {
-        stage = 0;
-        phase ^= 1;
+      if (issued) {
+        mma_commit(drain);
+        volatile int no_abort = 0;
+        mbar_wait(drain, 0, &no_abort, err, 33);
       }
     }
-    if (issued) {
-      mma_commit(drain);
-      volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort, err, 33);
-    }
-  } else if (warp >= 2) {
+  } else {
+    pdl_wait();  // the previous fixup may still read `part`
     const int q = warp & 3;  // TMEM lane quarter of this warp
-    const int row = nb * SK_BM + q * 32 + lane;
     float acc[NT];
 #pragma unroll
     for (int m = 0; m < NT; m++) acc[m] = 0.0f;
-    bool ok = true;
-    for (int kb = kb0, j = 0; kb < kb1; kb++, j++) {
-      const int r = j % SK_ACC;
+    int j = 0;
+    for (long long i = i0; i < i1; i++, j++) {
+      const int r = j % S::ACC;
       int got = 0;
-      if (lane == 0) got = mbar_wait(accf0 + 8 * r, (uint32_t)(j / SK_ACC) & 1u, abort_flag, err, 34);
-      if (!__shfl_sync(0xffffffffu, got, 0)) {
-        ok = false;
-        break;
-      }
+      if (lane == 0) got = mbar_wait(accf0 + 8 * r, (uint32_t)(j / S::ACC) & 1u, abort_flag, err, 34);
+      if (!__shfl_sync(0xffffffffu, got, 0)) break;
       tc_fence_after();
+      constexpr int W = NT == 16 ? 16 : 32;
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(r * S::ACC_STRIDE);
 #pragma unroll
-      for (int c = 0; c < NT / 32; c++) {
-        uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(r * NT + c * 32), v);
+      for (int c = 0; c < NT / W; c++) {  // columns t * NT + m hold term t of token row m
+        float lo[W], mid[W];
+        tmem_ld_cols<W>(base + (uint32_t)(2 * NT + c * W), lo);
+        tmem_ld_cols<W>(base + (uint32_t)(NT + c * W), mid);
 #pragma unroll
-        for (int jj = 0; jj < 32; jj++) acc[c * 32 + jj] += __uint_as_float(v[jj]);
+        for (int jj = 0; jj < W; jj++) lo[jj] = lo[jj] + mid[jj];
+        tmem_ld_cols<W>(base + (uint32_t)(c * W), mid);
+#pragma unroll
+        for (int jj = 0; jj < W; jj++) acc[c * W + jj] += lo[jj] + mid[jj];
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce0 + 8 * r);
-    }
-    if (ok && row < N) {
-      float *pp = part + (size_t)ks * M * N;
+      if (i + 1 == i1 || (i + 1) % kbs == 0) {  // end of this CTA's piece of tile t
+        const int t = (int)(i / kbs);
+        const int piece = cta - sk_cta_of((long long)t * kbs, T, G);
+        const int row = t * SK_BM + q * 32 + lane;
+        if (row < N) {
+          float *pp = part + ((size_t)t * pmax + piece) * M * SK_BM + q * 32 + lane;
 #pragma unroll
-      for (int m = 0; m < NT; m++)
-        if (m < M) pp[(size_t)m * N + row] = acc[m];
+          for (int m = 0; m < NT; m++)
+            if (m < M) pp[(size_t)m * SK_BM] = acc[m];
+        }
+#pragma unroll
+        for (int m = 0; m < NT; m++) acc[m] = 0.0f;
+      }
     }
   }
   pdl_trigger();
@@ -188,84 +277,172 @@ __global__ void __launch_bounds__(192, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
 }
 
-// y[m][n] = residual + ((part_0 + part_1) + ... + bias): split-K partials in split order.
-__global__ void skinny_reduce_kernel(const float *part, int splits, int M, int N, const float *bias,
-                                     const float *residual, int ldr, float *y, int ldy) {
+// Sum of the pieces of output (m, row) in piece order.
+__device__ __forceinline__ float sk_gather(const float *part, int m, int row, int M, int kbs, long long T, int G,
+                                           int pmax) {
+  const int t = row / SK_BM;
+  const int first = sk_cta_of((long long)t * kbs, T, G), last = sk_cta_of((long long)(t + 1) * kbs - 1, T, G);
+  const float *pp = part + ((size_t)t * pmax * M + m) * SK_BM + (row % SK_BM);
+  float s = pp[0];
+  for (int pc = 1; pc <= last - first; pc++) s += pp[(size_t)pc * M * SK_BM];
+  return s;
+}
+
+// One thread per (token row m = blockIdx.y, output row) -- per row pair for SiLU / QKV -- with the
+// vector GEMV's epilogue expressions.
+template <int EPI>
+__global__ void __launch_bounds__(256) skinny_fixup_kernel(const GemvParams p, const float *part, int kbs,
+                                                           long long T, int G, int pmax) {
   pdl_wait();
   pdl_trigger();
-  const long total = (long)M * N;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    float acc = part[i];
-    for (int s = 1; s < splits; s++) acc += part[(size_t)s * total + i];
-    const int m = (int)(i / N), n = (int)(i % N);
-    if (bias) acc = acc + bias[n];
-    if (residual) acc = residual[(size_t)m * ldr + n] + acc;
-    y[(size_t)m * ldy + n] = acc;
+  constexpr bool paired = EPI == EPI_SILU || EPI == EPI_QKV;
+  const int m = blockIdx.y;
+  const int units = paired ? p.N / 2 : p.N;
+  const int u = blockIdx.x * 256 + threadIdx.x;
+  if constexpr (EPI == EPI_LOGITS) {
+    __shared__ unsigned long long s_best[8];
+    unsigned long long key = 0ull;
+    if (u < units) {
+      const float v = sk_gather(part, m, u, p.M, kbs, T, G, pmax);
+      p.y[(size_t)m * p.ldy + u] = v;
+      key = argmax_key(v, u + p.row_offset);
+    }
+    if (p.best) {  // uniform: every thread of the block reaches the reduction
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
+        key = o > key ? o : key;
+      }
+      if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = key;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        unsigned long long b = s_best[0];
+        for (int w = 1; w < 8; w++) b = s_best[w] > b ? s_best[w] : b;
+        if (b) atomicMax(&p.best[m], b);
+      }
+    }
+    return;
+  }
+  if (u >= units) return;
+  if constexpr (EPI == EPI_PLAIN) {
+    float v = sk_gather(part, m, u, p.M, kbs, T, G, pmax);
+    if (p.bias) v = v + p.bias[u];
+    p.y[(size_t)m * p.ldy + u] = v;
+  } else if constexpr (EPI == EPI_RESID) {
+    const float v = sk_gather(part, m, u, p.M, kbs, T, G, pmax);
+    p.y[(size_t)m * p.ldy + u] = p.residual[(size_t)m * p.ldr + u] + v;
+  } else if constexpr (EPI == EPI_PEER) {
+    const float v = sk_gather(part, m, u, p.M, kbs, T, G, pmax);
+    const uint32_t use = (uint32_t)(p.peer.my_epoch[p.peer.region] + 1ull);
+    const size_t off = ((size_t)p.peer.region * p.peer.tp + p.peer.rank) * p.peer.slot_elems + (size_t)m * p.ldy + u;
+    const unsigned long long w = peer_word(v, use);
+    for (int r = 0; r < p.peer.tp; r++) peer_store(p.peer.slots[r] + off, w);
+  } else if constexpr (EPI == EPI_SILU) {
+    const float gate = sk_gather(part, m, 2 * u, p.M, kbs, T, G, pmax);
+    const float up = sk_gather(part, m, 2 * u + 1, p.M, kbs, T, G, pmax);
+    p.y[(size_t)m * p.ldy + u] = silu_ref(gate) * up;
+  } else if constexpr (EPI == EPI_QKV) {
+    const float fa = sk_gather(part, m, 2 * u, p.M, kbs, T, G, pmax);
+    const float fb = sk_gather(part, m, 2 * u + 1, p.M, kbs, T, G, pmax);
+    qkv_store_pair(p, m, u, fa, fb, p.pos_dev ? *p.pos_dev : p.pos0);
   }
 }
 
 uint32_t skinny_idesc(int nt) {
-  // D = F32, A = B = BF16, both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(SK_BM >> 4) << 24);
+  // D = F32, A = B = BF16, both K-major, N = 3 NT (>> 3 at bits 17-22), M = 128 (>> 4 at bits 24-28)
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)((3 * nt) >> 3) << 17) | ((uint32_t)(SK_BM >> 4) << 24);
+}
+
+struct SkinnyPlan {
+  int nt, tiles, kbs, grid, pmax;
+  long long iters;
+  uint64_t x3_bytes, part_bytes;
+};
+
+SkinnyPlan skinny_plan(int M, int N, int K, int device) {
+  SkinnyPlan q;
+  q.nt = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  q.tiles = (N + SK_BM - 1) / SK_BM;
+  q.kbs = (K + BK - 1) / BK;
+  q.iters = (long long)q.tiles * q.kbs;
+  q.grid = (int)std::min<long long>(sm_count(device), q.iters);
+  const long long per = q.iters / q.grid;  // every range holds per or per + 1 iterations
+  q.pmax = (int)std::min<long long>(q.grid, (q.kbs + per - 1) / per + 1);
+  q.x3_bytes = ((uint64_t)3 * q.nt * K * 2 + 255) & ~255ull;
+  q.part_bytes = (uint64_t)q.tiles * q.pmax * M * SK_BM * 4;
+  return q;
+}
+
+template <int NT>
+void configure(int device) {
+  static std::mutex mu;
+  static bool configured[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= 64 || !configured[device]) {
+    STB_CUDA(cudaFuncSetAttribute(gemm_skinny_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  SkinnyShape<NT>::SMEM));
+    if (device >= 0 && device < 64) configured[device] = true;
+  }
+}
+
+template <int NT>
+void launch_gemm(const SkinnyPlan &q, const CUtensorMap &tw, const CUtensorMap &tx, float *part, int M, int N,
+                 int *err, int device, cudaStream_t stream) {
+  configure<NT>(device);
+  launch_kernel(gemm_skinny_kernel<NT>, dim3(q.grid), dim3(192), (size_t)SkinnyShape<NT>::SMEM, stream, true, tw, tx,
+                part, M, N, q.kbs, q.iters, q.pmax, skinny_idesc(NT), err);
 }
 
 }  // namespace
 
-// Scratch bytes the skinny path needs for (M, N, K): split activations + split-K partials.
-uint64_t skinny_scratch_bytes(int M, int N, int K, int *splits_out, int device) {
-  const int nt = M <= 32 ? 32 : 64;
-  const int tiles = (N + SK_BM - 1) / SK_BM;
-  const int kblocks = (K + BK - 1) / BK;
-  const int sms = sm_count(device);
-  int splits = std::max(1, std::min(kblocks, (2 * sms + tiles - 1) / tiles));  // cover the SMs twice
-  const int kbps = (kblocks + splits - 1) / splits;
-  splits = (kblocks + kbps - 1) / kbps;
-  if (splits_out) *splits_out = splits;
-  const uint64_t x3 = ((uint64_t)3 * nt * K * 2 + 255) & ~255ull;
-  return x3 + (uint64_t)splits * M * N * 4;
+bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w) {
+  static const int enabled = env_int("STB_SKINNY", 1);
+  static const int min_rows = env_int("STB_SKINNY_MIN_ROWS", 2);
+  return enabled && w_dtype == STB_BF16 && M >= std::max(1, min_rows) && M <= 64 && K % 8 == 0 && K >= BK &&
+         N >= SK_BM && ((uintptr_t)w % 16) == 0;
 }
 
-// Enqueues split -> skinny GEMM -> reduce on `stream`.  scratch: skinny_scratch_bytes() bytes.
-void skinny_launch(const float *x, int ldx, const void *w, const float *bias, const float *residual, int ldr,
-                   float *y, int ldy, int M, int N, int K, void *scratch, int *err, int device, cudaStream_t stream,
-                   bool pdl) {
-  int splits = 1;
-  skinny_scratch_bytes(M, N, K, &splits, device);
-  const int nt = M <= 32 ? 32 : 64;
-  const int kblocks = (K + BK - 1) / BK;
-  const int kbps = (kblocks + splits - 1) / splits;
-  uint16_t *x3 = (uint16_t *)scratch;
-  float *part = (float *)((char *)scratch + (((uint64_t)3 * nt * K * 2 + 255) & ~255ull));
-  const long total = (long)nt * K;
-  launch_kernel(split3_kernel, dim3((unsigned)std::min<long>((total + 255) / 256, 148 * 8)), dim3(256), 0, stream,
-                pdl, x, ldx, x3, M, nt, K);
-  const CUtensorMap tw = make_map(w, STB_BF16, (uint64_t)N, (uint64_t)K, SK_BM);
-  const CUtensorMap tx = make_map(x3, STB_BF16, (uint64_t)3 * nt, (uint64_t)K, 3 * nt);
-  const dim3 grid((N + SK_BM - 1) / SK_BM, splits);
-  static std::mutex mu;
-  static bool configured[64][2] = {};
-  const int which = nt == 32 ? 0 : 1;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (device < 0 || device >= 64 || !configured[device][which]) {
-      if (nt == 32)
-        STB_CUDA(cudaFuncSetAttribute(gemm_skinny_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      SkinnyShape<32>::SMEM));
-      else
-        STB_CUDA(cudaFuncSetAttribute(gemm_skinny_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      SkinnyShape<64>::SMEM));
-      if (device >= 0 && device < 64) configured[device][which] = true;
-    }
-  }
-  if (nt == 32)
-    launch_kernel(gemm_skinny_kernel<32>, grid, dim3(192), (size_t)SkinnyShape<32>::SMEM, stream, true, tw, tx, part,
-                  M, N, K, kbps, skinny_idesc(32), err);
-  else
-    launch_kernel(gemm_skinny_kernel<64>, grid, dim3(192), (size_t)SkinnyShape<64>::SMEM, stream, true, tw, tx, part,
-                  M, N, K, kbps, skinny_idesc(64), err);
-  const long outs = (long)M * N;
-  launch_kernel(skinny_reduce_kernel, dim3((unsigned)std::min<long>((outs + 255) / 256, 148 * 4)), dim3(256), 0,
-                stream, true, (const float *)part, splits, M, N, bias, residual, ldr, y, ldy);
+void skinny_prepare(int device) {
+  configure<16>(device);
+  configure<32>(device);
+  configure<64>(device);
 }
+
+uint64_t skinny_scratch_bytes(int M, int N, int K, int device) {
+  const SkinnyPlan q = skinny_plan(M, N, K, device);
+  return q.x3_bytes + q.part_bytes;
+}
+
+template <int EPI>
+int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
+                  cudaStream_t stream) {
+  STB_REQUIRE(p.M >= 1 && p.M <= 64 && p.K % 8 == 0 && p.K >= BK && p.N >= SK_BM, "skinny Linear shape");
+  STB_REQUIRE(p.stop == nullptr, "skinny Linear takes no stop flag");
+  const SkinnyPlan q = skinny_plan(p.M, p.N, p.K, device);
+  STB_REQUIRE(scratch && ((uintptr_t)scratch % 256) == 0 && scratch_bytes >= q.x3_bytes + q.part_bytes,
+              "skinny Linear scratch too small");
+  uint16_t *x3 = (uint16_t *)scratch;
+  float *part = (float *)((char *)scratch + q.x3_bytes);
+  launch_kernel(skinny_prep_kernel, dim3((p.K + 1023) / 1024, q.nt), dim3(256), 0, stream, p.pdl, p.x, p.ldx,
+                p.norm_w, p.norm_eps, x3, p.M, q.nt, p.K);
+  const CUtensorMap tw = make_map(p.w, STB_BF16, (uint64_t)p.N, (uint64_t)p.K, SK_BM);
+  const CUtensorMap tx = make_map(x3, STB_BF16, (uint64_t)3 * q.nt, (uint64_t)p.K, 3 * q.nt);
+  if (q.nt == 16) launch_gemm<16>(q, tw, tx, part, p.M, p.N, err, device, stream);
+  else if (q.nt == 32) launch_gemm<32>(q, tw, tx, part, p.M, p.N, err, device, stream);
+  else launch_gemm<64>(q, tw, tx, part, p.M, p.N, err, device, stream);
+  constexpr bool paired = EPI == EPI_SILU || EPI == EPI_QKV;
+  const int units = paired ? p.N / 2 : p.N;
+  launch_kernel(skinny_fixup_kernel<EPI>, dim3((units + 255) / 256, p.M), dim3(256), 0, stream, true, p,
+                (const float *)part, q.kbs, q.iters, q.grid, q.pmax);
+  check_launch("skinny");
+  return 3;
+}
+
+template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_RESID>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_SILU>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_QKV>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_LOGITS>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_PEER>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
 
 }  // namespace stb

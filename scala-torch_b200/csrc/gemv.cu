@@ -6,11 +6,6 @@
 
 namespace stb {
 
-static int env_int(const char *name, int fallback) {
-  const char *v = std::getenv(name);
-  return v && *v ? std::atoi(v) : fallback;
-}
-
 int gemv_row_blocks(int N, GemvConfig cfg) {
   const int rows_per_block = (256 / cfg.tpr) * cfg.rows;
   return (N + rows_per_block - 1) / rows_per_block;
@@ -178,16 +173,6 @@ void linear(stb_session *s, uint64_t x, int ldx, uint64_t w, int w_dtype, uint64
     count_launch(s);
     return;
   }
-  if (skinny_eligible(M, N, K, w_dtype)) {
-    // 8..64 token rows: tensor cores with the activations split into three BF16 terms
-    const uint64_t bytes = skinny_scratch_bytes(M, N, K, nullptr, s->device);
-    int *err = session_error_word(s);
-    void *scratch = (void *)session_scratch(s, bytes);
-    skinny_launch((const float *)x, ldx, (const void *)w, (const float *)bias, nullptr, 0, (float *)y, ldy, M, N, K,
-                  scratch, err, s->device, s->stream, false);
-    count_launch(s, 3);
-    return;
-  }
   GemvParams p;
   p.x = (const float *)x;
   p.ldx = ldx;
@@ -198,13 +183,15 @@ void linear(stb_session *s, uint64_t x, int ldx, uint64_t w, int w_dtype, uint64
   p.y = (float *)y;
   p.ldy = ldy;
   p.bias = (const float *)bias;
+  if (skinny_eligible(M, N, K, w_dtype, (const void *)w)) {
+    // 2..64 token rows: tensor cores with the activations split into three BF16 terms
+    const uint64_t bytes = skinny_scratch_bytes(M, N, K, s->device);
+    void *scratch = (void *)session_scratch(s, bytes);
+    count_launch(s, skinny_launch<EPI_PLAIN>(p, scratch, bytes, session_error_word(s), s->device, s->stream));
+    return;
+  }
   launch_gemv<EPI_PLAIN>(p, w_dtype, choose_gemv(M, N, K, false), s->stream);
   count_launch(s);
-}
-
-bool skinny_eligible(int M, int N, int K, int w_dtype) {
-  static const int enabled = env_int("STB_SKINNY", 1);
-  return enabled && w_dtype == STB_BF16 && M >= 8 && M <= 64 && K % 8 == 0 && N >= 128;
 }
 
 }  // namespace stb

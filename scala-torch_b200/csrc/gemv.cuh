@@ -102,6 +102,42 @@ __device__ __forceinline__ float silu_ref(float x) {
   return (isinf(v) && v < 0.0) ? -0.0f : __double2float_rn(__dmul_rn(v, sigmoid));
 }
 
+// EPI_QKV for one pair of projection rows: pair pi enumerates q heads, then k heads, then v
+// heads, each head contributing hd/2 pairs (d, d + hd/2).  q and k pairs are rotated
+// (CpuAttention.rope: (a*c - b*s).toFloat, (b*c + a*s).toFloat in double, no contraction) and q
+// goes to y, k to the key cache; v pairs go to the value cache unrotated.  Token row mm is batch
+// row mm / count at position pos_base + mm % count.
+__device__ __forceinline__ void qkv_store_pair(const GemvParams &p, int mm, int pi, float fa, float fb,
+                                               int pos_base) {
+  const int half = p.hd >> 1;
+  const int qpairs = p.nh * half, kpairs = p.kvh * half;
+  const int bb = mm / p.count, t = mm % p.count;
+  const int pos = pos_base + t;
+  if (pi < qpairs + kpairs) {
+    const int local = pi < qpairs ? pi : pi - qpairs;
+    const int h = local / half, d = local % half;
+    const double2 cs = p.rope[(size_t)pos * half + d];
+    const double a = (double)fa, b = (double)fb;
+    const float oa = __double2float_rn(__dsub_rn(__dmul_rn(a, cs.x), __dmul_rn(b, cs.y)));
+    const float ob = __double2float_rn(__dadd_rn(__dmul_rn(b, cs.x), __dmul_rn(a, cs.y)));
+    if (pi < qpairs) {
+      float *q = p.y + (size_t)mm * p.ldy + (size_t)h * p.hd;
+      q[d] = oa;
+      q[d + half] = ob;
+    } else {
+      float *kc = p.k_cache + (((size_t)bb * p.kvh + h) * p.capacity + pos) * p.hd;
+      kc[d] = oa;
+      kc[d + half] = ob;
+    }
+  } else {
+    const int local = pi - qpairs - kpairs;
+    const int h = local / half, d = local % half;
+    float *vc = p.v_cache + (((size_t)bb * p.kvh + h) * p.capacity + pos) * p.hd;
+    vc[d] = fa;
+    vc[d + half] = fb;
+  }
+}
+
 template <int MT, int ROWS, int TPR, typename WT, int EPI>
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtiles) {
   constexpr int G = 256 / TPR;
@@ -334,46 +370,15 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
       p.y[(size_t)(m0 + m) * p.ldy + (row >> 1)] = silu_ref(gate) * up;
     }
   } else if constexpr (EPI == EPI_QKV) {
-    // Rows are pairs (d, d + hd/2) of one head: pair index pi enumerates q heads, then k heads,
-    // then v heads, each head contributing hd/2 pairs.
+    // Rows are pairs (d, d + hd/2) of one head (qkv_store_pair).
     constexpr int PAIRS = ROWS / 2;
-    const int half = p.hd >> 1;
-    const int qpairs = p.nh * half, kpairs = p.kvh * half;
     const int pos_base = p.pos_dev ? *p.pos_dev : p.pos0;
     for (int i = tid; i < G * PAIRS * MT; i += 256) {
       const int m = i / (G * PAIRS), pr = i % (G * PAIRS);
       const int gg = pr / PAIRS, r = (pr % PAIRS) * 2;
       const int row = blockrow0 + gg * ROWS + r;
       if (m >= mcount || row >= p.N) continue;
-      const float fa = s_out[gg][r][m], fb = s_out[gg][r + 1][m];
-      const int pi = row >> 1;
-      const int mm = m0 + m;
-      const int bb = mm / p.count, t = mm % p.count;
-      const int pos = pos_base + t;
-      if (pi < qpairs + kpairs) {
-        const int local = pi < qpairs ? pi : pi - qpairs;
-        const int h = local / half, d = local % half;
-        const double2 cs = p.rope[(size_t)pos * half + d];
-        const double a = (double)fa, b = (double)fb;
-        // CpuAttention.rope: (a*c - b*s).toFloat, (b*c + a*s).toFloat, no contraction.
-        const float oa = __double2float_rn(__dsub_rn(__dmul_rn(a, cs.x), __dmul_rn(b, cs.y)));
-        const float ob = __double2float_rn(__dadd_rn(__dmul_rn(b, cs.x), __dmul_rn(a, cs.y)));
-        if (pi < qpairs) {
-          float *q = p.y + (size_t)mm * p.ldy + (size_t)h * p.hd;
-          q[d] = oa;
-          q[d + half] = ob;
-        } else {
-          float *kc = p.k_cache + (((size_t)bb * p.kvh + h) * p.capacity + pos) * p.hd;
-          kc[d] = oa;
-          kc[d + half] = ob;
-        }
-      } else {
-        const int local = pi - qpairs - kpairs;
-        const int h = local / half, d = local % half;
-        float *vc = p.v_cache + (((size_t)bb * p.kvh + h) * p.capacity + pos) * p.hd;
-        vc[d] = fa;
-        vc[d + half] = fb;
-      }
+      qkv_store_pair(p, m0 + m, row >> 1, s_out[gg][r][m], s_out[gg][r + 1][m], pos_base);
     }
   }
 }
@@ -410,12 +415,19 @@ GemvConfig normalize_gemv(GemvConfig cfg, int epi);
 // Thread blocks one launch_gemv<epi> of (M, N) with cfg runs.
 int gemv_grid_blocks(int M, int N, GemvConfig cfg, int epi);
 
-// Tensor-core skinny form (gemm_skinny.cu) for 8 <= M <= 64 rows and BF16 weights, activations
-// split into three BF16 terms (FP32-accurate); STB_SKINNY=0 keeps the SIMT kernel.
-bool skinny_eligible(int M, int N, int K, int w_dtype);
-uint64_t skinny_scratch_bytes(int M, int N, int K, int *splits_out, int device);
-void skinny_launch(const float *x, int ldx, const void *w, const float *bias, const float *residual, int ldr,
-                   float *y, int ldy, int M, int N, int K, void *scratch, int *err, int device, cudaStream_t stream,
-                   bool pdl);
+// Tensor-core skinny form (gemm_skinny.cu) for 1 <= M <= 64 token rows and BF16 weights, the
+// activations split into three BF16 terms (FP32-accurate), with the same prologue (RMSNorm) and
+// epilogues as the vector kernel.  p.stop must be null.  skinny_eligible() says whether a
+// problem takes it (STB_SKINNY=0 keeps the vector kernel; STB_SKINNY_MIN_ROWS sets the smallest
+// M, default 2); skinny_scratch_bytes() is the scratch one launch of (M, N, K) needs.
+bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w);
+uint64_t skinny_scratch_bytes(int M, int N, int K, int device);
+// Sets the kernels' shared-memory limits on `device` (before a graph capture that launches them).
+void skinny_prepare(int device);
+// Enqueues prologue -> stream-K GEMM -> fixup/epilogue (3 kernels, all programmatic dependents
+// except the first when !p.pdl).  Returns the number of kernels launched.
+template <int EPI>
+int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
+                  cudaStream_t stream);
 
 }  // namespace stb

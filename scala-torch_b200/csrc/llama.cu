@@ -79,6 +79,7 @@ struct stb_llama_cache {
   // tensor-core prefill buffers (allocated when rows >= tc_rows): normalised x, half activations,
   // paired q/k/v projection, interleaved gate/up projection
   uint64_t xn = 0, xh = 0, qkvbuf = 0, gubuf = 0;
+  uint64_t skin = 0, skin_bytes = 0;  // tensor-core skinny path scratch (chunks of 1..64 rows)
   uint64_t tokens = 0;  // int64 [rows]
   uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
   uint64_t out_ids = 0;
@@ -524,6 +525,24 @@ void ensure_rows(stb_llama_cache *c, int rows) {
   c->tokens = alloc_owned(s, c->owned, (uint64_t)rows * 8);
   c->state = alloc_owned(s, c->owned, (uint64_t)(2 + 2 * c->batch) * 4);
   c->xn = c->xh = c->qkvbuf = c->gubuf = 0;
+  c->skin = c->skin_bytes = 0;
+  {  // the largest scratch any projection of a chunk of up to min(rows, 64) rows takes
+    const int sm = std::min(rows, 64);
+    const int wdt = m->c.weight_dtype;
+    const int qkv_n = (m->NH + 2 * m->KV) * m->hd;
+    const int shapes[5][3] = {{sm, qkv_n, m->H}, {sm, m->H, qw}, {sm, 2 * m->I, m->H}, {sm, m->H, m->I},
+                              {std::min(logits_rows(c, rows), 64), m->V, m->H}};
+    uint64_t need = 0;
+    for (const auto &sh : shapes)
+      if (skinny_eligible(sh[0], sh[1], sh[2], wdt, (const void *)256))
+        need = std::max(need, skinny_scratch_bytes(sh[0], sh[1], sh[2], s->device));
+    if (need) {
+      c->skin = alloc_owned(s, c->owned, need);
+      c->skin_bytes = need;
+      skinny_prepare(s->device);
+      session_error_word(s);  // allocated now, not inside a graph capture
+    }
+  }
   if (rows >= m->tc_rows) {
     const uint64_t widest = std::max<uint64_t>(std::max<uint64_t>(m->H, qw), m->I);
     c->xn = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
@@ -593,6 +612,19 @@ int enqueue_layer_tc(stb_llama_cache *c, size_t l, int rows, int count, const in
 }
 
 // Enqueues one forward chunk on the session stream.
+// One projection of a chunk: the tensor-core skinny form (three-term BF16 activations, FP32
+// accurate) when it applies to the shape and the cache holds its scratch, else the vector GEMV.
+// Returns the kernels launched.
+template <int EPI>
+int project(stb_llama_cache *c, const GemvParams &p, int wdt, GemvConfig cfg, cudaStream_t st) {
+  stb_session *s = c->m->s;
+  if (c->skin && skinny_eligible(p.M, p.N, p.K, wdt, p.w) &&
+      skinny_scratch_bytes(p.M, p.N, p.K, s->device) <= c->skin_bytes)
+    return skinny_launch<EPI>(p, (void *)c->skin, c->skin_bytes, session_error_word(s), s->device, st);
+  launch_gemv<EPI>(p, wdt, cfg, st);
+  return 1;
+}
+
 int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
   stb_llama *m = c->m;
   stb_session *s = m->s;
@@ -634,8 +666,7 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.nh = m->NH; p.kvh = m->KV; p.hd = m->hd; p.capacity = c->capacity; p.k_cache = kc; p.v_cache = vc;
       p.stop = stop;
       p.pdl = true;
-      launch_gemv<EPI_QKV>(p, wdt, choose_gemv(rows, p.N, p.K, true), st);
-      launches++;
+      launches += project<EPI_QKV>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st);
     }
     {  // 2. attention
       const size_t smem = attention_smem(c->capacity, m->hd);
@@ -653,8 +684,7 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
         p.norm_w = (const float *)L.post_norm; p.norm_eps = m->c.rms_norm_eps;
         p.stop = stop;
         p.pdl = true;
-        launch_gemv<EPI_SILU>(p, wdt, choose_gemv(rows, p.N, p.K, true), st);
-        launches++;
+        launches += project<EPI_SILU>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st);
       }
       GemvParams p;
       p.x = (const float *)(half == 0 ? c->att : c->act);
@@ -665,26 +695,24 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.pdl = true;
       if (m->tp == 1) {
         p.y = (float *)c->hidden; p.ldy = H; p.residual = (const float *)c->hidden; p.ldr = H;
-        launch_gemv<EPI_RESID>(p, wdt, choose_gemv(rows, p.N, p.K, false), st);
-        launches++;
+        launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st);
       } else if (peer_usable(s, (uint64_t)rows * H)) {
         // fused row-split projection: partial sums stored into every rank's slots over NVLink,
         // then summed in rank order with the residual on each rank
         p.ldy = H;
         p.peer = peer_args(s, half);
         const GemvConfig cfg = choose_gemv(rows, p.N, p.K, false);
-        launch_gemv<EPI_PEER>(p, wdt, cfg, st);
+        launches += project<EPI_PEER>(c, p, wdt, cfg, st);
         peer_reduce_launch(s, half, (long)rows * H, (const float *)c->hidden, (float *)c->hidden);
-        launches += 2;
+        launches++;
       } else {
         p.y = (float *)c->sum; p.ldy = H;
         if (m->rank == 0) {
           p.residual = (const float *)c->hidden; p.ldr = H;
-          launch_gemv<EPI_RESID>(p, wdt, choose_gemv(rows, p.N, p.K, false), st);
+          launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st);
         } else {
-          launch_gemv<EPI_PLAIN>(p, wdt, choose_gemv(rows, p.N, p.K, false), st);
+          launches += project<EPI_PLAIN>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st);
         }
-        launches++;
         allreduce_sum_f32(s, (void *)c->sum, (uint64_t)rows * H);
         std::swap(c->hidden, c->sum);
       }
@@ -707,8 +735,7 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
     p.row_offset = m->v0;
     p.stop = stop;
     p.pdl = true;
-    launch_gemv<EPI_LOGITS>(p, wdt, choose_gemv(brows, p.N, p.K, false), st);
-    launches++;
+    launches += project<EPI_LOGITS>(c, p, wdt, choose_gemv(brows, p.N, p.K, false), st);
     if (!a.all_logits) {
       const unsigned long long *all = (const unsigned long long *)c->best;
       if (m->tp > 1) {  // every rank's best over its vocabulary shard, [rank][batch]

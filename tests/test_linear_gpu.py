@@ -72,6 +72,29 @@ def test_decode_batches(session, m):
     close(run_linear(session, x, w, ffm.STB_BF16), oracle.linear(x, w, oracle.BF16))
 
 
+@pytest.mark.parametrize("m,n,k", [(2, 1000, 1000), (9, 128, 64), (16, 1000, 4104), (17, 300, 2048),
+                                   (40, 1536, 576), (64, 2500, 1000)])
+def test_skinny_tensor_core_form(session, m, n, k):
+    """Rows 2..64 with BF16 weights run on the tensor cores (prologue, stream-K GEMM, fixup: three
+    launches), activations split into three BF16 terms: still within the FP32 GEMV tolerance.
+    Ragged N (tile tails), K tails below one 64-wide block, bias; repeated calls are identical.
+    Magnitudes as BASELINE config 1 (x ~ N(0,1), W ~ N(0, 0.02)): the bound is relative to |y| ~ 1."""
+    rng = np.random.default_rng(m * 7 + n)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = oracle.normal_bf16(n * k, seed=m, stream=9, std=0.02).reshape(n, k)
+    b = rng.standard_normal(n).astype(np.float32)
+    xd, wd, bd = session.upload(x), session.upload_weight(w, ffm.STB_BF16), session.upload(b)
+    l0 = session.launches
+    y1 = session.linear(xd, wd, bd)
+    assert session.launches - l0 == 3
+    y2 = session.linear(xd, wd, bd)
+    a1, a2 = session.download(y1), session.download(y2)
+    for t in (xd, wd, bd, y1, y2):
+        session.release(t)
+    assert np.array_equal(a1.view(np.uint32), a2.view(np.uint32))
+    close(a1, oracle.linear(x, w, oracle.BF16, b))
+
+
 def test_f16_weights_and_bias(session):
     rng = np.random.default_rng(3)
     x = rng.standard_normal((4, 4096)).astype(np.float32)
