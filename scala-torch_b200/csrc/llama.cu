@@ -21,6 +21,7 @@
 #include <climits>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "gemv.cuh"
@@ -244,6 +245,212 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const float *q, 
 
 size_t attention_smem(int capacity, int hd) {
   return (size_t)(capacity + 32 + hd + ATT_THREADS * 4) * sizeof(double);
+}
+
+// Causal grouped-query attention of a long prefill chunk in Float32 (the tensor-core prefill path,
+// whose projections already round activations to BF16): flash-style tiles instead of one block
+// per query row, so each K/V row is read once per 64 queries rather than once per query.
+// Block (query tile, head, batch row) holds 64 queries; per 64-key tile it forms the 64 x 64
+// scores (thread (ty, tx): queries 4ty..4ty+3 x keys 4tx..4tx+3, FP32 FMA over hd from shared
+// memory), applies the causal mask, updates the running row max / sum (online softmax: earlier
+// tiles rescaled by exp(m_old - m_new)) and accumulates P.V (queries 4ty.. x hd/16 dimensions).
+// Keys are positions 0..base+t of this batch row's cache; the chunk's own keys were appended
+// before the launch.
+constexpr int FA_BQ = 64, FA_BK = 64, FA_PAD = 4;
+
+template <int HD>
+constexpr size_t flash_smem() {
+  return (size_t)(HD * FA_BQ + HD * (FA_BK + FA_PAD) + FA_BK * HD + FA_BK * (FA_BQ + FA_PAD)) * sizeof(float);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) flash_attention_kernel(const float *q, int ldq, const float *kcache,
+                                                              const float *vcache, float *out, int ldo, int count,
+                                                              int nh, int kvh, int capacity, const int *pos_dev,
+                                                              int pos0) {
+  static_assert(HD == 16 || HD == 32 || HD == 64 || HD == 128, "head size");
+  constexpr int DPT = HD / 16;  // output dimensions per thread
+  extern __shared__ float fsm[];
+  float *Qs = fsm;                           // [HD][BQ]        d-major
+  float *Ks = Qs + HD * FA_BQ;               // [HD][BK + PAD]  d-major
+  float *Vs = Ks + HD * (FA_BK + FA_PAD);    // [BK][HD]
+  float *Ps = Vs + FA_BK * HD;               // [BK][BQ + PAD]  key-major
+  pdl_wait();
+  pdl_trigger();
+  const int t0 = blockIdx.x * FA_BQ, h = blockIdx.y, b = blockIdx.z;
+  const int g = h / (nh / kvh);
+  const int base = pos_dev ? *pos_dev : pos0;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int nq = min(FA_BQ, count - t0);
+  const int nkeys = base + t0 + nq;  // keys 0 .. position of the tile's last query
+  const float scale = (float)(1.0 / sqrt((double)HD));
+  const float *kb = kcache + ((size_t)b * kvh + g) * capacity * HD;
+  const float *vb = vcache + ((size_t)b * kvh + g) * capacity * HD;
+
+  for (int idx = tid; idx < FA_BQ * (HD / 4); idx += 256) {
+    const int i = idx / (HD / 4), d = (idx % (HD / 4)) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < nq) v = *reinterpret_cast<const float4 *>(q + (size_t)(b * count + t0 + i) * ldq + (size_t)h * HD + d);
+    Qs[(d + 0) * FA_BQ + i] = v.x;
+    Qs[(d + 1) * FA_BQ + i] = v.y;
+    Qs[(d + 2) * FA_BQ + i] = v.z;
+    Qs[(d + 3) * FA_BQ + i] = v.w;
+  }
+
+  float o[4][DPT];
+  float mrow[4], lrow[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    mrow[i] = -INFINITY;
+    lrow[i] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < DPT; e++) o[i][e] = 0.0f;
+  }
+
+  for (int j0 = 0; j0 < nkeys; j0 += FA_BK) {
+    __syncthreads();  // previous tile's K, V and P are no longer read
+    for (int idx = tid; idx < FA_BK * (HD / 4); idx += 256) {
+      const int jj = idx / (HD / 4), d = (idx % (HD / 4)) * 4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (j0 + jj < nkeys) {
+        kv = *reinterpret_cast<const float4 *>(kb + (size_t)(j0 + jj) * HD + d);
+        vv = *reinterpret_cast<const float4 *>(vb + (size_t)(j0 + jj) * HD + d);
+      }
+      Ks[(d + 0) * (FA_BK + FA_PAD) + jj] = kv.x;
+      Ks[(d + 1) * (FA_BK + FA_PAD) + jj] = kv.y;
+      Ks[(d + 2) * (FA_BK + FA_PAD) + jj] = kv.z;
+      Ks[(d + 3) * (FA_BK + FA_PAD) + jj] = kv.w;
+      *reinterpret_cast<float4 *>(Vs + jj * HD + d) = vv;
+    }
+    __syncthreads();
+
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) s[i][jj] = 0.0f;
+#pragma unroll 8
+    for (int d = 0; d < HD; d++) {
+      const float4 qv = *reinterpret_cast<const float4 *>(Qs + d * FA_BQ + 4 * ty);
+      const float4 kv = *reinterpret_cast<const float4 *>(Ks + d * (FA_BK + FA_PAD) + 4 * tx);
+      const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) s[i][jj] = fmaf(qa[i], ka[jj], s[i][jj]);
+    }
+
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int qpos = base + t0 + 4 * ty + i;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        const int key = j0 + 4 * tx + jj;
+        s[i][jj] = key <= qpos ? s[i][jj] * scale : -INFINITY;
+        mt = fmaxf(mt, s[i][jj]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float mnew = fmaxf(mrow[i], mt);
+      const float alpha = mnew == -INFINITY ? 1.0f : expf(mrow[i] - mnew);
+      float rs = 0.0f;
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        const float p = mnew == -INFINITY ? 0.0f : expf(s[i][jj] - mnew);
+        s[i][jj] = p;
+        rs += p;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+      lrow[i] = lrow[i] * alpha + rs;
+      mrow[i] = mnew;
+#pragma unroll
+      for (int e = 0; e < DPT; e++) o[i][e] *= alpha;
+    }
+#pragma unroll
+    for (int jj = 0; jj < 4; jj++)
+      *reinterpret_cast<float4 *>(Ps + (4 * tx + jj) * (FA_BQ + FA_PAD) + 4 * ty) =
+          make_float4(s[0][jj], s[1][jj], s[2][jj], s[3][jj]);
+    __syncthreads();
+
+    const int kmax = min(FA_BK, nkeys - j0);
+    for (int jj = 0; jj < kmax; jj++) {
+      const float4 pv = *reinterpret_cast<const float4 *>(Ps + jj * (FA_BQ + FA_PAD) + 4 * ty);
+      const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+      float va[DPT];
+      if constexpr (DPT >= 4) {
+#pragma unroll
+        for (int c = 0; c < DPT / 4; c++) {
+          const float4 v = *reinterpret_cast<const float4 *>(Vs + jj * HD + 64 * c + 4 * tx);
+          va[4 * c + 0] = v.x;
+          va[4 * c + 1] = v.y;
+          va[4 * c + 2] = v.z;
+          va[4 * c + 3] = v.w;
+        }
+      } else if constexpr (DPT == 2) {
+        const float2 v = *reinterpret_cast<const float2 *>(Vs + jj * HD + 2 * tx);
+        va[0] = v.x;
+        va[1] = v.y;
+      } else {
+        va[0] = Vs[jj * HD + tx];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int e = 0; e < DPT; e++) o[i][e] = fmaf(pa[i], va[e], o[i][e]);
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int t = t0 + 4 * ty + i;
+    if (4 * ty + i >= nq) continue;
+    float *orow = out + (size_t)(b * count + t) * ldo + (size_t)h * HD;
+    const float inv = 1.0f / lrow[i];
+#pragma unroll
+    for (int e = 0; e < DPT; e++) {
+      const int d = DPT >= 4 ? 64 * (e / 4) + 4 * tx + (e % 4) : (DPT == 2 ? 2 * tx + e : tx);
+      orow[d] = o[i][e] * inv;
+    }
+  }
+}
+
+template <int HD>
+void flash_launch(dim3 grid, const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
+                  int count, int nh, int kvh, int capacity, const int *posd, int pos0, int device, cudaStream_t st) {
+  static std::mutex mu;
+  static bool configured[64] = {};  // per head size: one static set per instantiation
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0 || device >= 64 || !configured[device]) {
+      STB_CUDA(cudaFuncSetAttribute(flash_attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)flash_smem<HD>()));
+      if (device >= 0 && device < 64) configured[device] = true;
+    }
+  }
+  launch_kernel(flash_attention_kernel<HD>, grid, dim3(256), flash_smem<HD>(), st, false, q, ldq, kc, vc, out, ldo,
+                count, nh, kvh, capacity, posd, pos0);
+}
+
+// Launches the tiled prefill attention when the head size has an instantiation (16, 32, 64, 128)
+// and STB_FLASH_ATTENTION is not 0; returns false otherwise.
+bool launch_flash_attention(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
+                            int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
+                            int device, cudaStream_t st) {
+  static const int enabled = env_int("STB_FLASH_ATTENTION", 1);
+  if (!enabled || rows % count != 0) return false;
+  const dim3 grid((count + FA_BQ - 1) / FA_BQ, nh, rows / count);
+  switch (hd) {
+    case 16: flash_launch<16>(grid, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, device, st); break;
+    case 32: flash_launch<32>(grid, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, device, st); break;
+    case 64: flash_launch<64>(grid, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, device, st); break;
+    case 128:
+      flash_launch<128>(grid, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, device, st);
+      break;
+    default: return false;
+  }
+  return true;
 }
 
 // Greedy pick from every rank's candidate key (argmax_key: largest logit, lowest id on ties --
@@ -595,9 +802,11 @@ int enqueue_layer_tc(stb_llama_cache *c, size_t l, int rows, int count, const in
   launch_kernel(rope_append_kernel, dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, st, false,
                 (const float *)c->qkvbuf, nqkv, (const double2 *)m->rope, posd, c->used, count, m->NH, m->KV, m->hd,
                 c->capacity, (float *)c->qbuf, qw, kc, vc, rows);
-  launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), attention_smem(c->capacity, m->hd), st,
-                false, (const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows,
-                count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, (const int *)nullptr);
+  if (!launch_flash_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw,
+                              rows, count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, s->device, st))
+    launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), attention_smem(c->capacity, m->hd), st,
+                  false, (const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows,
+                  count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, (const int *)nullptr);
   launches += 3;
   row_split((const float *)c->att, qw, L.o);
   launch_kernel(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, st, false, (const float *)c->hidden,
@@ -611,7 +820,6 @@ int enqueue_layer_tc(stb_llama_cache *c, size_t l, int rows, int count, const in
   return launches;
 }
 
-// Enqueues one forward chunk on the session stream.
 // One projection of a chunk: the tensor-core skinny form (three-term BF16 activations, FP32
 // accurate) when it applies to the shape and the cache holds its scratch, else the vector GEMV.
 // Returns the kernels launched.
@@ -625,6 +833,7 @@ int project(stb_llama_cache *c, const GemvParams &p, int wdt, GemvConfig cfg, cu
   return 1;
 }
 
+// Enqueues one forward chunk on the session stream.
 int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
   stb_llama *m = c->m;
   stb_session *s = m->s;
