@@ -81,6 +81,8 @@ struct stb_llama_cache {
   // paired q/k/v projection, interleaved gate/up projection
   uint64_t xn = 0, xh = 0, qkvbuf = 0, gubuf = 0;
   uint64_t skin = 0, skin_bytes = 0;  // tensor-core skinny path scratch (chunks of 1..64 rows)
+  uint64_t att_part = 0, att_count = 0;  // split decode attention records and counters (batch rows)
+  int att_rows = 0;
   uint64_t tokens = 0;  // int64 [rows]
   uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
   uint64_t out_ids = 0;
@@ -416,6 +418,194 @@ __global__ void __launch_bounds__(256) flash_attention_kernel(const float *q, in
   }
 }
 
+// Decode attention (one query token per batch row) in Float32, split over keys and shared by the
+// query heads of a KV group: block (split s, KV head, token row) takes keys [128 s, 128 s + 128) of
+// the visible range for all G = nh / kvh query heads of the group, so each K and V row is read once
+// per group.  Decode is latency-bound, so every thread issues its K half-row and its V rows into
+// registers at the start (one memory round trip for the whole block), then: scores by two threads
+// per key (FMA over half of hd, one xor shuffle), per head max and sum of exp over the split (a warp
+// per head), the weighted V sum by (key group, dimension quad) threads with the key groups added in
+// order through shared memory.  A single split writes the normalised output; otherwise each split
+// stores (max, sum, unnormalised sum) and the last split to finish (a per-(row, KV head) counter,
+// reset by that block) merges them in split order, rescaling by exp(max_s - max).
+constexpr int DA_KPS = 128, DA_GMAX = 8, DA_THREADS = 256;
+
+template <int HD>
+__global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
+    const float *q, int ldq, const float *kcache, const float *vcache, float *out, int ldo, int count, int nh,
+    int kvh, int capacity, const int *pos_dev, int pos0, float *part, int *counters, int smax) {
+  static_assert(HD == 16 || HD == 32 || HD == 64 || HD == 128, "head size");
+  constexpr int HALF = HD / 2, NK4 = HALF / 4, F = HD / 4, KG = DA_THREADS / F, VPT = DA_KPS / KG;
+  __shared__ __align__(16) float qs[DA_GMAX][HD];
+  __shared__ float sp[DA_GMAX][DA_KPS];
+  __shared__ float red[DA_GMAX][2];
+  __shared__ __align__(16) float opart[KG][DA_GMAX][HD];
+  __shared__ int s_last;
+  pdl_wait();
+  pdl_trigger();
+  const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
+  const int G = nh / kvh;
+  const int b = m / count, t = m % count;
+  const int keys = (pos_dev ? *pos_dev : pos0) + t + 1;
+  const int S = (keys + DA_KPS - 1) / DA_KPS;
+  if (split >= S) return;  // the grid covers the longest visible range
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int j0 = split * DA_KPS, nk = min(DA_KPS, keys - j0);
+  const size_t kvrow0 = ((size_t)b * kvh + g0) * capacity + j0;
+  const float scale = (float)(1.0 / sqrt((double)HD));
+
+  // every load of the block in flight at once
+  const int jj = tid >> 1, hf = tid & 1;  // score role: key jj, half hf of the dimensions
+  const int f = tid % F, kg = tid / F;    // value role: dimensions 4f..4f+3 of keys kg, kg + KG, ...
+  float4 kreg[NK4], vreg[VPT];
+#pragma unroll
+  for (int i = 0; i < NK4; i++)
+    kreg[i] = jj < nk ? *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * HALF + 4 * i)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int j = kg + i * KG;
+    vreg[i] = j < nk ? *reinterpret_cast<const float4 *>(vcache + (kvrow0 + j) * HD + 4 * f)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int i = tid; i < G * HD; i += DA_THREADS)
+    qs[i / HD][i % HD] = q[(size_t)m * ldq + (size_t)(g0 * G) * HD + i];
+  __syncthreads();
+
+  {  // scores
+    float dots[DA_GMAX];
+#pragma unroll
+    for (int g = 0; g < DA_GMAX; g++) {
+      dots[g] = 0.0f;
+      if (g < G) {
+#pragma unroll
+        for (int i = 0; i < NK4; i++) {
+          const float4 qv = *reinterpret_cast<const float4 *>(&qs[g][hf * HALF + 4 * i]);
+          dots[g] = fmaf(qv.x, kreg[i].x, dots[g]);
+          dots[g] = fmaf(qv.y, kreg[i].y, dots[g]);
+          dots[g] = fmaf(qv.z, kreg[i].z, dots[g]);
+          dots[g] = fmaf(qv.w, kreg[i].w, dots[g]);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < DA_GMAX; g++) dots[g] += __shfl_xor_sync(0xffffffffu, dots[g], 1);
+    if (hf == 0 && jj < nk) {
+#pragma unroll
+      for (int g = 0; g < DA_GMAX; g++)
+        if (g < G) sp[g][jj] = dots[g] * scale;
+    }
+  }
+  __syncthreads();
+  for (int g = warp; g < G; g += DA_THREADS / 32) {  // per head: max and sum of exp over the split
+    float mx = -INFINITY;
+    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sp[g][j]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.0f;
+    for (int j = lane; j < nk; j += 32) {
+      const float e = expf(sp[g][j] - mx);
+      sp[g][j] = e;
+      sum += e;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) {
+      red[g][0] = mx;
+      red[g][1] = sum;
+    }
+  }
+  __syncthreads();
+  {  // unnormalised weighted V sum
+#pragma unroll
+    for (int g = 0; g < DA_GMAX; g++) {
+      if (g < G) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPT; i++) {
+          const int j = kg + i * KG;
+          const float p = j < nk ? sp[g][j] : 0.0f;
+          a0 = fmaf(p, vreg[i].x, a0);
+          a1 = fmaf(p, vreg[i].y, a1);
+          a2 = fmaf(p, vreg[i].z, a2);
+          a3 = fmaf(p, vreg[i].w, a3);
+        }
+        *reinterpret_cast<float4 *>(&opart[kg][g][4 * f]) = make_float4(a0, a1, a2, a3);
+      }
+    }
+  }
+  __syncthreads();
+  const size_t slot = ((size_t)m * kvh + g0) * smax;  // this (row, KV head)'s split records
+  float *po = part, *pml = part + (size_t)gridDim.z * kvh * smax * DA_GMAX * HD;
+  for (int i = tid; i < G * HD; i += DA_THREADS) {
+    const int g = i / HD, d = i % HD;
+    float o = 0.0f;
+    for (int k = 0; k < KG; k++) o += opart[k][g][d];
+    if (S == 1) out[(size_t)m * ldo + (size_t)(g0 * G + g) * HD + d] = o / red[g][1];
+    else po[((slot + split) * DA_GMAX + g) * HD + d] = o;
+  }
+  if (S == 1) return;
+  if (tid < G) {
+    pml[((slot + split) * DA_GMAX + tid) * 2 + 0] = red[tid][0];
+    pml[((slot + split) * DA_GMAX + tid) * 2 + 1] = red[tid][1];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&counters[(size_t)m * kvh + g0], 1) == S - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = tid; i < G * HD; i += DA_THREADS) {
+    const int g = i / HD, d = i % HD;
+    float M = -INFINITY;
+    for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(&pml[((slot + s) * DA_GMAX + g) * 2]));
+    float num = 0.0f, den = 0.0f;
+    for (int s = 0; s < S; s++) {
+      const float w = expf(__ldcg(&pml[((slot + s) * DA_GMAX + g) * 2]) - M);
+      num = fmaf(w, __ldcg(&po[((slot + s) * DA_GMAX + g) * HD + d]), num);
+      den = fmaf(w, __ldcg(&pml[((slot + s) * DA_GMAX + g) * 2 + 1]), den);
+    }
+    out[(size_t)m * ldo + (size_t)(g0 * G + g) * HD + d] = num / den;
+  }
+  if (tid == 0) counters[(size_t)m * kvh + g0] = 0;
+}
+
+// Floats of split records decode_attention_kernel needs for `rows` token rows.
+size_t decode_attention_part_floats(int rows, int kvh, int capacity, int hd) {
+  const size_t smax = (size_t)(capacity + DA_KPS - 1) / DA_KPS;
+  return (size_t)rows * kvh * smax * DA_GMAX * ((size_t)hd + 2);
+}
+
+// Launches the split decode attention when the head size and group size have a form (hd in
+// {16, 32, 64, 128}, nh / kvh <= 8) and STB_DECODE_ATTENTION is not 0; returns false otherwise.
+bool launch_decode_attention(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
+                             int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
+                             float *part, int *counters, bool pdl, cudaStream_t st) {
+  static const int enabled = env_int("STB_DECODE_ATTENTION", 1);
+  if (!enabled || !part || !counters || nh % kvh != 0 || nh / kvh > DA_GMAX) return false;
+  const int smax = (capacity + DA_KPS - 1) / DA_KPS;
+  const dim3 grid(smax, kvh, rows);
+  switch (hd) {
+    case 16:
+      launch_kernel(decode_attention_kernel<16>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo, count,
+                    nh, kvh, capacity, posd, pos0, part, counters, smax);
+      return true;
+    case 32:
+      launch_kernel(decode_attention_kernel<32>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo, count,
+                    nh, kvh, capacity, posd, pos0, part, counters, smax);
+      return true;
+    case 64:
+      launch_kernel(decode_attention_kernel<64>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo, count,
+                    nh, kvh, capacity, posd, pos0, part, counters, smax);
+      return true;
+    case 128:
+      launch_kernel(decode_attention_kernel<128>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo, count,
+                    nh, kvh, capacity, posd, pos0, part, counters, smax);
+      return true;
+    default: return false;
+  }
+}
+
 template <int HD>
 void flash_launch(dim3 grid, const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
                   int count, int nh, int kvh, int capacity, const int *posd, int pos0, int device, cudaStream_t st) {
@@ -732,6 +922,11 @@ void ensure_rows(stb_llama_cache *c, int rows) {
   c->tokens = alloc_owned(s, c->owned, (uint64_t)rows * 8);
   c->state = alloc_owned(s, c->owned, (uint64_t)(2 + 2 * c->batch) * 4);
   c->xn = c->xh = c->qkvbuf = c->gubuf = 0;
+  c->att_rows = c->batch;
+  c->att_part = alloc_owned(s, c->owned,
+                            decode_attention_part_floats(c->batch, m->KV, c->capacity, m->hd) * sizeof(float));
+  c->att_count = alloc_owned(s, c->owned, (uint64_t)c->batch * m->KV * sizeof(int));
+  STB_CUDA(cudaMemsetAsync((void *)c->att_count, 0, (size_t)c->batch * m->KV * sizeof(int), s->stream));
   c->skin = c->skin_bytes = 0;
   {  // the largest scratch any projection of a chunk of up to min(rows, 64) rows takes
     const int sm = std::min(rows, 64);
@@ -877,11 +1072,22 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.pdl = true;
       launches += project<EPI_QKV>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st);
     }
-    {  // 2. attention
-      const size_t smem = attention_smem(c->capacity, m->hd);
-      launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), smem, st, true, (const float *)c->qbuf,
-                    qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows, a.count, m->NH, m->KV,
-                    m->hd, c->capacity, posd, c->used, stop);
+    {  // 2. attention: split GQA kernel for single-token steps, tiled kernel for chunks
+      bool done = false;
+      if (a.count == 1 && rows <= c->att_rows)
+        done = launch_decode_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc,
+                                       (float *)c->att, qw, rows, 1, m->NH, m->KV, m->hd, c->capacity, posd, c->used,
+                                       (float *)c->att_part, (int *)c->att_count, true, st);
+      else if (a.count > 1)
+        done = launch_flash_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc,
+                                      (float *)c->att, qw, rows, a.count, m->NH, m->KV, m->hd, c->capacity, posd,
+                                      c->used, s->device, st);
+      if (!done) {
+        const size_t smem = attention_smem(c->capacity, m->hd);
+        launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), smem, st, true,
+                      (const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows,
+                      a.count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, stop);
+      }
       launches++;
     }
     for (int half = 0; half < 2; half++) {  // 3. O (+residual)   then   4./5. MLP (+residual)
