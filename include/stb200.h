@@ -110,6 +110,28 @@ int stb_linear_prefill(stb_session *s, uint64_t x, uint64_t w, int w_dtype, uint
  * array's address; make it before any stream capture. */
 int stb_linear_prefill_static(void *stream, uint64_t x, uint64_t w, int w_dtype, uint64_t bias, uint64_t y,
                               int M, int N, int K);
+/* One low-rank adapter term of nn.Linear.apply (nn/src/main/scala/scalatorch/nn/Linear.scala:11-17;
+ * LowRankAdapter.apply, LowRankAdapter.scala:12-14; LinearAdapterScope.forWeight,
+ * LinearAdapterScope.scala:14-21).  a: Float32 [rank, K] device buffer, b: Float32 [N, rank];
+ * scale = LowRankAdapter.scale, (alpha / rank) rounded to Float32.  scoped = 0 is the Linear's own
+ * adapter (`base + a(x)`), scoped = 1 a LinearAdapterScope entry (`sum + a(x) * multiplier`). */
+typedef struct stb_adapter {
+  uint64_t a;
+  uint64_t b;
+  int rank;
+  float scale;
+  int scoped;
+  float multiplier;
+} stb_adapter;
+
+/* nn.Linear.apply with adapters (Linear.scala:11-17), each operation rounded to Float32 in the
+ * reference's order: base = x.W^T; for each term in array order (the Linear's own adapter, if any,
+ * first): t = x.A^T, u = t.B^T, v = u * scale (* multiplier when scoped), sum = sum + v; finally
+ * sum + bias.  count = 0 is stb_linear.  Rejects (STB_ERR_INVALID) a null or non-positive factor,
+ * a non-finite or non-positive scale, a non-finite multiplier, and an unscoped term that is not
+ * first. */
+int stb_linear_adapted(stb_session *s, uint64_t x, uint64_t w, int w_dtype, uint64_t bias,
+                       const stb_adapter *adapters, int count, uint64_t y, int M, int N, int K);
 /* Host-buffer form used for end-to-end measurement: copies x from host, runs stb_linear against
  * the resident weight, copies y back.  Synchronous. */
 int stb_linear_host(stb_session *s, const float *x_host, uint64_t w, int w_dtype, uint64_t bias,

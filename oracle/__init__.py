@@ -61,6 +61,7 @@ def _declare(L):
         "oracle_matmul_tr": (None, [_p, _p, _p, _i, _i, _i, _i]),
         "oracle_matmul_seq": (None, [_p, _p, _p, _i, _i, _i]),
         "oracle_linear": (None, [_p, _p, _i, _p, _p, _i, _i, _i, _i, _i]),
+        "oracle_linear_adapted": (None, [_p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _i, _i, _i]),
         "oracle_rmsnorm": (None, [_p, _p, _p, _i, _i, _d]),
         "oracle_silu": (ctypes.c_float, [ctypes.c_float]),
         "oracle_rope": (None, [_p, _p, _i, _i, _i, _i, _i, _d]),
@@ -152,6 +153,49 @@ def linear(x: np.ndarray, w_bits: np.ndarray, w_dtype: int, bias: np.ndarray | N
     b = None if bias is None else np.ascontiguousarray(bias, np.float32)
     lib().oracle_linear(_ptr(x), _ptr(w), w_dtype, _ptr(b), _ptr(y), M, N, K, order,
                         threads or max_threads())
+    return y
+
+
+def adapter_scale(alpha: float, rank: int) -> np.float32:
+    """LowRankAdapter.scale (LowRankAdapter.scala:24-27): (alpha / rank) rounded to Float32."""
+    value = np.float32(alpha / rank)
+    if not (np.isfinite(alpha) and alpha > 0 and np.isfinite(value) and value > 0):
+        raise ValueError("invalid adapter scale")
+    return value
+
+
+def linear_adapted(x: np.ndarray, w_bits: np.ndarray, w_dtype: int, bias: np.ndarray | None = None,
+                   lora=None, scoped=(), threads: int = 0) -> np.ndarray:
+    """nn.Linear.apply with its low-rank adapter and LinearAdapterScope entries (Linear.scala:11-17).
+    lora = (A[rank,K], B[N,rank], alpha) or None; scoped = [((A, B, alpha), multiplier), ...]."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w_bits)
+    M, K = x.shape
+    N = w.shape[0]
+    terms = ([(lora, 0, 1.0)] if lora is not None else []) + [(a, 1, m) for a, m in scoped]
+    keep, a_ptrs, b_ptrs, ranks, scales, flags, mults = [], [], [], [], [], [], []
+    for (A, B, alpha), flag, mult in terms:
+        A = np.ascontiguousarray(A, np.float32)
+        B = np.ascontiguousarray(B, np.float32)
+        keep += [A, B]
+        a_ptrs.append(A.ctypes.data)
+        b_ptrs.append(B.ctypes.data)
+        ranks.append(A.shape[0])
+        scales.append(adapter_scale(alpha, A.shape[0]))
+        flags.append(flag)
+        mults.append(mult)
+    n = len(terms)
+    pa = (ctypes.c_void_p * max(n, 1))(*a_ptrs)
+    pb = (ctypes.c_void_p * max(n, 1))(*b_ptrs)
+    pr = np.array(ranks or [0], np.int32)
+    ps = np.array(scales or [0], np.float32)
+    pf = np.array(flags or [0], np.int32)
+    pm = np.array(mults or [0], np.float32)
+    y = np.empty((M, N), np.float32)
+    bb = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().oracle_linear_adapted(_ptr(x), _ptr(w), w_dtype, _ptr(bb), ctypes.cast(pa, ctypes.c_void_p),
+                                ctypes.cast(pb, ctypes.c_void_p), _ptr(pr), _ptr(ps), _ptr(pf), _ptr(pm), n,
+                                _ptr(y), M, N, K, threads or max_threads())
     return y
 
 

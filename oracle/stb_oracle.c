@@ -168,6 +168,37 @@ void oracle_linear(const float *x, const void *w, int w_dtype, const float *bias
       for (int n = 0; n < N; n++) y[(size_t)m * N + n] = y[(size_t)m * N + n] + bias[n];
 }
 
+/* nn.Linear.apply with its low-rank adapter and the LinearAdapterScope adapters
+ * (nn/src/main/scala/scalatorch/nn/Linear.scala:11-17; LowRankAdapter.scala:12-14):
+ *   base = x.W^T;  attached (scoped == 0, first only): sum = base + ((x.A^T).B^T) * scale;
+ *   each scoped entry: sum = sum + (((x.A^T).B^T) * scale) * multiplier;  then + bias.
+ * A is [rank, K], B is [N, rank] (Float32 parameters); scale is LowRankAdapter.scale, (alpha / rank)
+ * rounded to Float32.  Every product in numscala's transposed-right order, every elementwise
+ * operation rounded to Float32 (Variable arithmetic). */
+void oracle_linear_adapted(const float *x, const void *w, int w_dtype, const float *bias,
+                           const float *const *a, const float *const *b, const int *rank,
+                           const float *scale, const int *scoped, const float *multiplier, int count,
+                           float *y, int M, int N, int K, int threads) {
+  oracle_linear(x, w, w_dtype, NULL, y, M, N, K, ORACLE_ORDER_NUMSCALA, threads);
+  for (int i = 0; i < count; i++) {
+    int r = rank[i];
+    float *t = (float *)malloc((size_t)M * r * 4 + 4);
+    float *u = (float *)malloc((size_t)M * N * 4 + 4);
+    oracle_matmul_tr(x, a[i], t, M, r, K, threads);   /* input.matmul(a.transpose(0, 1)) */
+    oracle_matmul_tr(t, b[i], u, M, N, r, threads);   /* .matmul(b.transpose(0, 1)) */
+    for (size_t e = 0; e < (size_t)M * N; e++) {
+      float v = u[e] * scale[i];                       /* * scale */
+      if (scoped[i]) v = v * multiplier[i];            /* adapter(input) * multiplier */
+      y[e] = y[e] + v;
+    }
+    free(t);
+    free(u);
+  }
+  if (bias)
+    for (int m = 0; m < M; m++)
+      for (int n = 0; n < N; n++) y[(size_t)m * N + n] = y[(size_t)m * N + n] + bias[n];
+}
+
 /* ---------------------------------------------------------------- decode-step ops */
 
 void oracle_rmsnorm(const float *x, const float *w, float *y, int rows, int width, double eps) {

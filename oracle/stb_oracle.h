@@ -56,6 +56,10 @@ void oracle_matmul_seq(const float *a, const float *b, float *c, int M, int N, i
  * (out,in) weight that SafeTensors.readFloat widens first: y = x.W^T [+ bias]. */
 void oracle_linear(const float *x, const void *w, int w_dtype, const float *bias, float *y,
                    int M, int N, int K, int order, int threads);
+void oracle_linear_adapted(const float *x, const void *w, int w_dtype, const float *bias,
+                           const float *const *a, const float *const *b, const int *rank,
+                           const float *scale, const int *scoped, const float *multiplier, int count,
+                           float *y, int M, int N, int K, int threads);
 
 /* CpuFloatBackend.rmsNorm, cpu/src/main/scala/scalatorch/cpu/CpuFloatBackend.scala:80-93 */
 void oracle_rmsnorm(const float *x, const float *w, float *y, int rows, int width, double eps);

@@ -16,6 +16,7 @@ There is no fallback: if libstb200.so is missing or fails to load, every entry p
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 from dataclasses import dataclass, field
 
@@ -82,6 +83,7 @@ def _declare(L):
         "stb_linear_prefill": (_i, [_p, _u64, _u64, _i, _u64, _u64, _i, _i, _i]),
         "stb_linear_host": (_i, [_p, _p, _u64, _i, _u64, _p, _i, _i, _i]),
         "stb_linear_prefill_static": (_i, [_p, _u64, _u64, _i, _u64, _u64, _i, _i, _i]),
+        "stb_linear_adapted": (_i, [_p, _u64, _u64, _i, _u64, _p, _i, _u64, _i, _i, _i]),
         "stb_fill_normal": (_i, [_p, _u64, _i, _u64, _u64, _u64, ctypes.c_double]),
         "stb_fill_value": (_i, [_p, _u64, _i, _u64, ctypes.c_float]),
         "stb_nccl_unique_id": (_i, [_p]),
@@ -137,6 +139,25 @@ class DeviceTensor:
 
     def close(self) -> None:
         self.session.release(self)
+
+
+class StbAdapter(ctypes.Structure):
+    """stb_adapter (include/stb200.h)."""
+    _fields_ = [("a", ctypes.c_uint64), ("b", ctypes.c_uint64), ("rank", ctypes.c_int), ("scale", ctypes.c_float),
+                ("scoped", ctypes.c_int), ("multiplier", ctypes.c_float)]
+
+
+class LowRankAdapter:
+    """nn.LowRankAdapter (nn/src/main/scala/scalatorch/nn/LowRankAdapter.scala:7-27) over resident
+    Float32 factors: a [rank, in], b [out, rank]; scale = (alpha / rank) rounded to Float32."""
+
+    def __init__(self, a: "DeviceTensor", b: "DeviceTensor", alpha: float):
+        require(len(a.shape) == 2 and len(b.shape) == 2 and a.dtype == STB_F32 and b.dtype == STB_F32,
+                "adapter factors must both be Float32 matrices")
+        require(min(a.shape + b.shape) > 0 and a.shape[0] == b.shape[1], "invalid adapter factor dimensions")
+        value = float(np.float32(alpha / a.shape[0])) if math.isfinite(alpha) and alpha > 0 else float("nan")
+        require(math.isfinite(value) and value > 0, "invalid adapter scale")
+        self.a, self.b, self.alpha, self.rank, self.scale = a, b, alpha, a.shape[0], value
 
 
 class B200Session:
@@ -301,8 +322,11 @@ class B200Session:
         return y
 
     def linear(self, x: DeviceTensor, weight: DeviceTensor, bias: DeviceTensor | None = None,
-               prefill: bool = False) -> DeviceTensor:
-        """y = x.W^T (+ bias) in one launch; prefill=True takes the tcgen05 path (x rounded to half)."""
+               prefill: bool = False, lora: LowRankAdapter | None = None,
+               scoped: tuple = ()) -> DeviceTensor:
+        """nn.Linear.apply (Linear.scala:11-17): y = x.W^T (+ the Linear's own adapter)
+        (+ LinearAdapterScope entries, each (LowRankAdapter, multiplier)) (+ bias).  prefill=True takes
+        the tcgen05 path (x rounded to half; no adapters)."""
         self._validate(x)
         self._validate(weight)
         require(weight.transposed_weight, "weight must be a resident (out,in) weight")
@@ -312,11 +336,25 @@ class B200Session:
         if bias is not None:
             self._validate(bias)
             require(bias.shape == (N,), "Linear bias shape mismatch")
+        terms = ([(lora, 0, 1.0)] if lora is not None else []) + [(a, 1, float(m)) for a, m in scoped]
+        for adapter, _, mult in terms:
+            self._validate(adapter.a)
+            self._validate(adapter.b)
+            require(adapter.a.shape[1] == K and adapter.b.shape[0] == N, "Linear adapter shape mismatch")
+            require(math.isfinite(mult), "adapter multiplier must be finite")
+        require(not (prefill and terms), "the prefill form takes no adapters")
         y = self.allocate((M, N), STB_F32)
-        fn = "stb_linear_prefill" if prefill else "stb_linear"
         try:
-            call(fn, self.handle, x.address, weight.address, weight.dtype,
-                 bias.address if bias is not None else 0, y.address, M, N, K)
+            if terms:
+                arr = (StbAdapter * len(terms))(*[StbAdapter(a.a.address, a.b.address, a.rank, a.scale, sc, m)
+                                                  for a, sc, m in terms])
+                call("stb_linear_adapted", self.handle, x.address, weight.address, weight.dtype,
+                     bias.address if bias is not None else 0, ctypes.cast(arr, ctypes.c_void_p), len(terms),
+                     y.address, M, N, K)
+            else:
+                fn = "stb_linear_prefill" if prefill else "stb_linear"
+                call(fn, self.handle, x.address, weight.address, weight.dtype,
+                     bias.address if bias is not None else 0, y.address, M, N, K)
         except Exception:
             self.release(y)
             raise

@@ -174,3 +174,49 @@ def test_budget_rejects_before_allocation():
         with pytest.raises(ffm.IllegalStateException):
             s.allocate((1 << 20,), ffm.STB_F32)
         assert s.allocated_bytes == 0
+
+
+def _adapter(session, rng, n, k, rank, alpha, zero_b=False):
+    a = (rng.uniform(-1, 1, (rank, k)) / np.sqrt(k)).astype(np.float32)
+    b = np.zeros((n, rank), np.float32) if zero_b else (rng.standard_normal((n, rank)) * 0.1).astype(np.float32)
+    dev = ffm.LowRankAdapter(session.upload(a), session.upload(b), alpha)
+    return (a, b, alpha), dev
+
+
+@pytest.mark.parametrize("m", [1, 3, 16, 40])
+def test_linear_with_adapters_matches_oracle(session, m):
+    """nn.Linear.apply with its own LoRA adapter, two LinearAdapterScope entries (one with a negative
+    multiplier) and a bias (Linear.scala:11-17), in the reference's operation order; the base
+    product takes the GEMV (M = 1) or the skinny tensor-core form (M >= 2)."""
+    rng = np.random.default_rng(m)
+    n, k = 1536, 576
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = oracle.normal_bf16(n * k, seed=m, stream=5, std=0.02).reshape(n, k)
+    b = rng.standard_normal(n).astype(np.float32)
+    own, own_d = _adapter(session, rng, n, k, 8, 16.0)
+    s1, s1_d = _adapter(session, rng, n, k, 4, 4.0)
+    s2, s2_d = _adapter(session, rng, n, k, 16, 8.0)
+    xd, wd, bd = session.upload(x), session.upload_weight(w, ffm.STB_BF16), session.upload(b)
+    y = session.linear(xd, wd, bd, lora=own_d, scoped=[(s1_d, 0.75), (s2_d, -1.5)])
+    got = session.download(y)
+    close(got, oracle.linear_adapted(x, w, oracle.BF16, b, lora=own, scoped=[(s1, 0.75), (s2, -1.5)]))
+    for t in (xd, wd, bd, y, own_d.a, own_d.b, s1_d.a, s1_d.b, s2_d.a, s2_d.b):
+        session.release(t)
+
+
+def test_fresh_adapter_leaves_the_linear_unchanged(session):
+    """LowRankAdapter.init zero-fills B (LowRankAdapter.scala:37): the adapted device Linear equals
+    the plain device Linear bit for bit."""
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal((5, 576)).astype(np.float32)
+    w = oracle.normal_bf16(1536 * 576, seed=9, stream=6, std=0.02).reshape(1536, 576)
+    b = rng.standard_normal(1536).astype(np.float32)
+    _, own_d = _adapter(session, rng, 1536, 576, 8, 16.0, zero_b=True)
+    xd, wd, bd = session.upload(x), session.upload_weight(w, ffm.STB_BF16), session.upload(b)
+    plain, adapted = session.linear(xd, wd, bd), session.linear(xd, wd, bd, lora=own_d)
+    assert np.array_equal(session.download(plain).view(np.uint32), session.download(adapted).view(np.uint32))
+    with pytest.raises(ffm.IllegalArgumentException):
+        bad = ffm.LowRankAdapter(own_d.a, session.upload(np.zeros((10, 8), np.float32)), 16.0)
+        session.linear(xd, wd, bd, lora=bad)
+    with pytest.raises(ffm.IllegalArgumentException):
+        ffm.LowRankAdapter(own_d.a, own_d.b, 0.0)

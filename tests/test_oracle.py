@@ -173,3 +173,31 @@ def test_rng_is_normal_and_counter_addressed():
 def test_log_restatement_is_accurate():
     for x in [1e-300, 1e-20, 0.001, 0.25, 0.5, 0.70710678, 0.75, 0.999999, 1.0 - 2.0 ** -52]:
         assert abs(oracle.lib().oracle_log(x) - math.log(x)) <= 4e-16 * max(1.0, abs(math.log(x)))
+
+
+def test_linear_adapters_known_answer():
+    """Linear.apply with its adapter, two LinearAdapterScope entries and a bias (Linear.scala:11-17),
+    small integers so every step is exact: base [1,2]; own adapter adds ((x.A^T).B^T)*1 = [3,6];
+    scoped (scale 2, multiplier 0.5) adds [1,1]; scoped (scale 1, multiplier -1) adds [-2,-2]."""
+    x = np.array([[1.0, 2.0]], np.float32)
+    w = oracle.round_bf16(np.eye(2, dtype=np.float32))
+    own = (np.array([[1.0, 1.0]]), np.array([[1.0], [2.0]]), 1.0)
+    half = (np.array([[1.0, 0.0]]), np.array([[1.0], [1.0]]), 2.0)
+    neg = (np.array([[0.0, 1.0]]), np.array([[1.0], [1.0]]), 1.0)
+    y = oracle.linear_adapted(x, w, oracle.BF16, np.array([0.5, -1.0], np.float32), lora=own,
+                              scoped=[(half, 0.5), (neg, -1.0)])
+    assert y.tolist() == [[1 + 3 + 1 - 2 + 0.5, 2 + 6 + 1 - 2 - 1.0]]
+
+
+def test_linear_adapter_with_zero_up_factor_is_the_base_product():
+    """LowRankAdapter.init zero-fills B (LowRankAdapter.scala:37): the adapted Linear equals the
+    plain Linear bit for bit."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((3, 40)).astype(np.float32)
+    w = oracle.round_bf16(rng.standard_normal((7, 40)).astype(np.float32))
+    b = rng.standard_normal(7).astype(np.float32)
+    own = (rng.standard_normal((4, 40)).astype(np.float32), np.zeros((7, 4), np.float32), 8.0)
+    assert np.array_equal(oracle.linear_adapted(x, w, oracle.BF16, b, lora=own), oracle.linear(x, w, oracle.BF16, b))
+    assert oracle.adapter_scale(8.0, 4) == np.float32(2.0)
+    with pytest.raises(ValueError):
+        oracle.adapter_scale(0.0, 4)
