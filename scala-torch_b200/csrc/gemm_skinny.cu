@@ -1,5 +1,5 @@
 // Decode-sized Linear on the tcgen05 tensor cores with Float32-accurate activations:
-//   y[M,N] = epilogue(x[M,K] . W[N,K]^T),  1 <= M <= 64 token rows, BF16 weights,
+//   y[M,N] = epilogue(x[M,K] . W[N,K]^T),  M >= 1 token rows (blocks of 64), BF16 weights,
 // with the vector GEMV's optional RMSNorm prologue and its epilogues (gemv.cuh).
 //
 // The SIMT decode GEMV keeps FP32 activations with FP32 FMA, which is bound by FP32 issue once M
@@ -288,23 +288,24 @@ __device__ __forceinline__ float sk_gather(const float *part, int m, int row, in
   return s;
 }
 
-// One thread per (token row m = blockIdx.y, output row) -- per row pair for SiLU / QKV -- with the
-// vector GEMV's epilogue expressions.
+// One thread per (token row, output row) -- per row pair for SiLU / QKV -- with the vector GEMV's
+// epilogue expressions.  This launch covers rows m0 .. m0 + mb - 1 of the problem (blockIdx.y = row
+// within the block; `part` holds mb rows); mg is the row in the problem's own indexing.
 template <int EPI>
 __global__ void __launch_bounds__(256) skinny_fixup_kernel(const GemvParams p, const float *part, int kbs,
-                                                           long long T, int G, int pmax) {
+                                                           long long T, int G, int pmax, int m0, int mb) {
   pdl_wait();
   pdl_trigger();
   constexpr bool paired = EPI == EPI_SILU || EPI == EPI_QKV;
-  const int m = blockIdx.y;
+  const int m = blockIdx.y, mg = m0 + m;
   const int units = paired ? p.N / 2 : p.N;
   const int u = blockIdx.x * 256 + threadIdx.x;
   if constexpr (EPI == EPI_LOGITS) {
     __shared__ unsigned long long s_best[8];
     unsigned long long key = 0ull;
     if (u < units) {
-      const float v = sk_gather(part, m, u, p.M, kbs, T, G, pmax);
-      p.y[(size_t)m * p.ldy + u] = v;
+      const float v = sk_gather(part, m, u, mb, kbs, T, G, pmax);
+      p.y[(size_t)mg * p.ldy + u] = v;
       key = argmax_key(v, u + p.row_offset);
     }
     if (p.best) {  // uniform: every thread of the block reaches the reduction
@@ -318,33 +319,33 @@ __global__ void __launch_bounds__(256) skinny_fixup_kernel(const GemvParams p, c
       if (threadIdx.x == 0) {
         unsigned long long b = s_best[0];
         for (int w = 1; w < 8; w++) b = s_best[w] > b ? s_best[w] : b;
-        if (b) atomicMax(&p.best[m], b);
+        if (b) atomicMax(&p.best[mg], b);
       }
     }
     return;
   }
   if (u >= units) return;
   if constexpr (EPI == EPI_PLAIN) {
-    float v = sk_gather(part, m, u, p.M, kbs, T, G, pmax);
+    float v = sk_gather(part, m, u, mb, kbs, T, G, pmax);
     if (p.bias) v = v + p.bias[u];
-    p.y[(size_t)m * p.ldy + u] = v;
+    p.y[(size_t)mg * p.ldy + u] = v;
   } else if constexpr (EPI == EPI_RESID) {
-    const float v = sk_gather(part, m, u, p.M, kbs, T, G, pmax);
-    p.y[(size_t)m * p.ldy + u] = p.residual[(size_t)m * p.ldr + u] + v;
+    const float v = sk_gather(part, m, u, mb, kbs, T, G, pmax);
+    p.y[(size_t)mg * p.ldy + u] = p.residual[(size_t)mg * p.ldr + u] + v;
   } else if constexpr (EPI == EPI_PEER) {
-    const float v = sk_gather(part, m, u, p.M, kbs, T, G, pmax);
+    const float v = sk_gather(part, m, u, mb, kbs, T, G, pmax);
     const uint32_t use = (uint32_t)(p.peer.my_epoch[p.peer.region] + 1ull);
-    const size_t off = ((size_t)p.peer.region * p.peer.tp + p.peer.rank) * p.peer.slot_elems + (size_t)m * p.ldy + u;
+    const size_t off = ((size_t)p.peer.region * p.peer.tp + p.peer.rank) * p.peer.slot_elems + (size_t)mg * p.ldy + u;
     const unsigned long long w = peer_word(v, use);
     for (int r = 0; r < p.peer.tp; r++) peer_store(p.peer.slots[r] + off, w);
   } else if constexpr (EPI == EPI_SILU) {
-    const float gate = sk_gather(part, m, 2 * u, p.M, kbs, T, G, pmax);
-    const float up = sk_gather(part, m, 2 * u + 1, p.M, kbs, T, G, pmax);
-    p.y[(size_t)m * p.ldy + u] = silu_ref(gate) * up;
+    const float gate = sk_gather(part, m, 2 * u, mb, kbs, T, G, pmax);
+    const float up = sk_gather(part, m, 2 * u + 1, mb, kbs, T, G, pmax);
+    p.y[(size_t)mg * p.ldy + u] = silu_ref(gate) * up;
   } else if constexpr (EPI == EPI_QKV) {
-    const float fa = sk_gather(part, m, 2 * u, p.M, kbs, T, G, pmax);
-    const float fb = sk_gather(part, m, 2 * u + 1, p.M, kbs, T, G, pmax);
-    qkv_store_pair(p, m, u, fa, fb, p.pos_dev ? *p.pos_dev : p.pos0);
+    const float fa = sk_gather(part, m, 2 * u, mb, kbs, T, G, pmax);
+    const float fb = sk_gather(part, m, 2 * u + 1, mb, kbs, T, G, pmax);
+    qkv_store_pair(p, mg, u, fa, fb, p.pos_dev ? *p.pos_dev : p.pos0);
   }
 }
 
@@ -398,7 +399,8 @@ void launch_gemm(const SkinnyPlan &q, const CUtensorMap &tw, const CUtensorMap &
 bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w) {
   static const int enabled = env_int("STB_SKINNY", 1);
   static const int min_rows = env_int("STB_SKINNY_MIN_ROWS", 2);
-  return enabled && w_dtype == STB_BF16 && M >= std::max(1, min_rows) && M <= 64 && K % 8 == 0 && K >= BK &&
+  static const int max_rows = env_int("STB_SKINNY_MAX_ROWS", 1 << 30);
+  return enabled && w_dtype == STB_BF16 && M >= std::max(1, min_rows) && M <= max_rows && K % 8 == 0 && K >= BK &&
          N >= SK_BM && ((uintptr_t)w % 16) == 0;
 }
 
@@ -409,33 +411,40 @@ void skinny_prepare(int device) {
 }
 
 uint64_t skinny_scratch_bytes(int M, int N, int K, int device) {
-  const SkinnyPlan q = skinny_plan(M, N, K, device);
+  const SkinnyPlan q = skinny_plan(std::min(M, 64), N, K, device);  // one 64-row block at a time
   return q.x3_bytes + q.part_bytes;
 }
 
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
                   cudaStream_t stream) {
-  STB_REQUIRE(p.M >= 1 && p.M <= 64 && p.K % 8 == 0 && p.K >= BK && p.N >= SK_BM, "skinny Linear shape");
+  STB_REQUIRE(p.M >= 1 && p.K % 8 == 0 && p.K >= BK && p.N >= SK_BM, "skinny Linear shape");
   STB_REQUIRE(p.stop == nullptr, "skinny Linear takes no stop flag");
-  const SkinnyPlan q = skinny_plan(p.M, p.N, p.K, device);
-  STB_REQUIRE(scratch && ((uintptr_t)scratch % 256) == 0 && scratch_bytes >= q.x3_bytes + q.part_bytes,
+  STB_REQUIRE(scratch && ((uintptr_t)scratch % 256) == 0 && scratch_bytes >= skinny_scratch_bytes(p.M, p.N, p.K, device),
               "skinny Linear scratch too small");
-  uint16_t *x3 = (uint16_t *)scratch;
-  float *part = (float *)((char *)scratch + q.x3_bytes);
-  launch_kernel(skinny_prep_kernel, dim3((p.K + 1023) / 1024, q.nt), dim3(256), 0, stream, p.pdl, p.x, p.ldx,
-                p.norm_w, p.norm_eps, x3, p.M, q.nt, p.K);
   const CUtensorMap tw = make_map(p.w, STB_BF16, (uint64_t)p.N, (uint64_t)p.K, SK_BM);
-  const CUtensorMap tx = make_map(x3, STB_BF16, (uint64_t)3 * q.nt, (uint64_t)p.K, 3 * q.nt);
-  if (q.nt == 16) launch_gemm<16>(q, tw, tx, part, p.M, p.N, err, device, stream);
-  else if (q.nt == 32) launch_gemm<32>(q, tw, tx, part, p.M, p.N, err, device, stream);
-  else launch_gemm<64>(q, tw, tx, part, p.M, p.N, err, device, stream);
   constexpr bool paired = EPI == EPI_SILU || EPI == EPI_QKV;
   const int units = paired ? p.N / 2 : p.N;
-  launch_kernel(skinny_fixup_kernel<EPI>, dim3((units + 255) / 256, p.M), dim3(256), 0, stream, true, p,
-                (const float *)part, q.kbs, q.iters, q.grid, q.pmax);
+  int launches = 0;
+  // blocks of up to 64 token rows, in order, through the same scratch (each block's prologue waits
+  // for the previous block's fixup)
+  for (int m0 = 0; m0 < p.M; m0 += 64) {
+    const int mb = std::min(64, p.M - m0);
+    const SkinnyPlan q = skinny_plan(mb, p.N, p.K, device);
+    uint16_t *x3 = (uint16_t *)scratch;
+    float *part = (float *)((char *)scratch + q.x3_bytes);
+    launch_kernel(skinny_prep_kernel, dim3((p.K + 1023) / 1024, q.nt), dim3(256), 0, stream, m0 > 0 || p.pdl,
+                  p.x + (size_t)m0 * p.ldx, p.ldx, p.norm_w, p.norm_eps, x3, mb, q.nt, p.K);
+    const CUtensorMap tx = make_map(x3, STB_BF16, (uint64_t)3 * q.nt, (uint64_t)p.K, 3 * q.nt);
+    if (q.nt == 16) launch_gemm<16>(q, tw, tx, part, mb, p.N, err, device, stream);
+    else if (q.nt == 32) launch_gemm<32>(q, tw, tx, part, mb, p.N, err, device, stream);
+    else launch_gemm<64>(q, tw, tx, part, mb, p.N, err, device, stream);
+    launch_kernel(skinny_fixup_kernel<EPI>, dim3((units + 255) / 256, mb), dim3(256), 0, stream, true, p,
+                  (const float *)part, q.kbs, q.iters, q.grid, q.pmax, m0, mb);
+    launches += 3;
+  }
   check_launch("skinny");
-  return 3;
+  return launches;
 }
 
 template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);

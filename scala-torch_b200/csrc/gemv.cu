@@ -184,7 +184,7 @@ void linear(stb_session *s, uint64_t x, int ldx, uint64_t w, int w_dtype, uint64
   p.ldy = ldy;
   p.bias = (const float *)bias;
   if (skinny_eligible(M, N, K, w_dtype, (const void *)w)) {
-    // 2..64 token rows: tensor cores with the activations split into three BF16 terms
+    // 2+ token rows: tensor cores with the activations split into three BF16 terms, 64-row blocks
     const uint64_t bytes = skinny_scratch_bytes(M, N, K, s->device);
     void *scratch = (void *)session_scratch(s, bytes);
     count_launch(s, skinny_launch<EPI_PLAIN>(p, scratch, bytes, session_error_word(s), s->device, s->stream));

@@ -415,17 +415,17 @@ GemvConfig normalize_gemv(GemvConfig cfg, int epi);
 // Thread blocks one launch_gemv<epi> of (M, N) with cfg runs.
 int gemv_grid_blocks(int M, int N, GemvConfig cfg, int epi);
 
-// Tensor-core skinny form (gemm_skinny.cu) for 1 <= M <= 64 token rows and BF16 weights, the
+// Tensor-core skinny form (gemm_skinny.cu) for BF16 weights, token rows in blocks of up to 64, the
 // activations split into three BF16 terms (FP32-accurate), with the same prologue (RMSNorm) and
 // epilogues as the vector kernel.  p.stop must be null.  skinny_eligible() says whether a
-// problem takes it (STB_SKINNY=0 keeps the vector kernel; STB_SKINNY_MIN_ROWS sets the smallest
-// M, default 2); skinny_scratch_bytes() is the scratch one launch of (M, N, K) needs.
+// problem takes it (STB_SKINNY=0 keeps the vector kernel; STB_SKINNY_MIN_ROWS / _MAX_ROWS bound
+// M, default 2 .. unbounded); skinny_scratch_bytes() is the scratch one call of (M, N, K) needs.
 bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w);
 uint64_t skinny_scratch_bytes(int M, int N, int K, int device);
 // Sets the kernels' shared-memory limits on `device` (before a graph capture that launches them).
 void skinny_prepare(int device);
-// Enqueues prologue -> stream-K GEMM -> fixup/epilogue (3 kernels, all programmatic dependents
-// except the first when !p.pdl).  Returns the number of kernels launched.
+// Enqueues prologue -> stream-K GEMM -> fixup/epilogue per 64-row block (3 kernels each, all
+// programmatic dependents except the first when !p.pdl).  Returns the number of kernels launched.
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
                   cudaStream_t stream);

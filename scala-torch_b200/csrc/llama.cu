@@ -66,6 +66,10 @@ struct stb_llama {
   std::vector<uint64_t> owned;
   uint64_t weight_bytes = 0;
   int tc_rows = 512;  // chunks of >= tc_rows token rows use the tensor-core prefill (INT_MAX: never)
+  // the last stb_llama_generate call's cache and decode graph, reused by the next call of the same
+  // shape (batch, prompt + new, new, EOS count, prefill chunk)
+  stb_llama_cache *gen = nullptr;
+  int gen_key[5] = {};
 };
 
 struct stb_llama_cache {
@@ -80,9 +84,10 @@ struct stb_llama_cache {
   // tensor-core prefill buffers (allocated when rows >= tc_rows): normalised x, half activations,
   // paired q/k/v projection, interleaved gate/up projection
   uint64_t xn = 0, xh = 0, qkvbuf = 0, gubuf = 0;
-  uint64_t skin = 0, skin_bytes = 0;  // tensor-core skinny path scratch (chunks of 1..64 rows)
+  uint64_t skin = 0, skin_bytes = 0;  // tensor-core skinny path scratch (one 64-row block)
   uint64_t att_part = 0, att_count = 0;  // split decode attention records and counters (batch rows)
   int att_rows = 0;
+  int graph_launches = 0;  // kernels in one replay of `graph`
   uint64_t tokens = 0;  // int64 [rows]
   uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
   uint64_t out_ids = 0;
@@ -1283,6 +1288,10 @@ int stb_llama_destroy(stb_llama *m) {
   if (!m) return STB_OK;
   return guarded([&] {
     enter(m->s);
+    if (m->gen) {
+      stb_llama_cache_destroy(m->gen);
+      m->gen = nullptr;
+    }
     free_owned(m->s, m->owned);
     delete m;
   });
@@ -1559,8 +1568,22 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
       for (int b = 0; b < batch; b++) generated[b] = 0;
     if (timings_ms) timings_ms[0] = timings_ms[1] = 0.0f;
     if (max_new == 0) return;
+    // The prompt is prefilled in chunks of at most STB_PREFILL_CHUNK_ROWS token rows (all batch
+    // rows advance together), bounding the activation buffers for long or wide prompts.
+    const char *env = std::getenv("STB_PREFILL_CHUNK_ROWS");
+    const int chunk_rows = env && *env ? std::max(1, std::atoi(env)) : 4096;
+    const int chunk = std::max(1, std::min(prompt_len, chunk_rows / batch));
+    // A call of the same shape as the previous one reuses its cache, buffers and decode graph
+    // (STB_GENERATE_REUSE=0: every call builds and frees its own).
+    static const int reuse_enabled = env_int("STB_GENERATE_REUSE", 1);
+    const int key[5] = {batch, total, max_new, eos_count, chunk};
     stb_llama_cache *c = nullptr;
-    {
+    if (m->gen) {
+      if (reuse_enabled && std::equal(key, key + 5, m->gen_key)) c = m->gen;
+      else stb_llama_cache_destroy(m->gen);
+      m->gen = nullptr;  // owned by this call until it completes
+    }
+    if (!c) {
       int rc = stb_llama_cache_create(m, batch, total, &c);
       if (rc != STB_OK) throw Error(rc, stb_last_error());
     }
@@ -1568,16 +1591,12 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     try {
       for (auto &e : ev) STB_CUDA(cudaEventCreate(&e));
-      // The prompt is prefilled in chunks of at most kChunkRows token rows (all batch rows advance
-      // together), bounding the activation buffers for long or wide prompts.
-      const char *env = std::getenv("STB_PREFILL_CHUNK_ROWS");
-      const int chunk_rows = env && *env ? std::max(1, std::atoi(env)) : 4096;
-      const int chunk = std::max(1, std::min(prompt_len, chunk_rows / batch));
       ensure_rows(c, batch * chunk);
+      c->used = 0;
       c->out_stride = max_new;
-      c->out_ids = alloc_owned(s, c->owned, (uint64_t)batch * max_new * 8);
+      if (!c->out_ids) c->out_ids = alloc_owned(s, c->owned, (uint64_t)batch * max_new * 8);
       if (eos_count) {
-        c->eos = alloc_owned(s, c->owned, (uint64_t)eos_count * 8);
+        if (!c->eos) c->eos = alloc_owned(s, c->owned, (uint64_t)eos_count * 8);
         upload(s, eos, (uint64_t)eos_count * 8, c->eos);
       }
       c->eos_count = eos_count;
@@ -1623,22 +1642,27 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
         d.all_logits = false;
         d.append = true;
         d.advance = 1;
-        cudaGraph_t g = nullptr;
-        STB_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
-        int step_launches = 0;
-        try {
-          step_launches = enqueue_step(c, d);
-        } catch (...) {
-          cudaStreamEndCapture(s->stream, &g);
-          if (g) cudaGraphDestroy(g);
-          throw;
+        if (!c->graph) {
+          cudaGraph_t g = nullptr;
+          STB_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+          int step_launches = 0;
+          try {
+            step_launches = enqueue_step(c, d);
+          } catch (...) {
+            cudaStreamEndCapture(s->stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+          }
+          STB_CUDA(cudaStreamEndCapture(s->stream, &g));
+          cudaGraphExec_t made = nullptr;
+          cudaError_t e = cudaGraphInstantiate(&made, g, 0);
+          cudaGraphDestroy(g);
+          STB_CUDA(e);
+          c->graph = made;
+          c->graph_launches = step_launches;
         }
-        STB_CUDA(cudaStreamEndCapture(s->stream, &g));
-        cudaGraphExec_t exec = nullptr;
-        cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
-        cudaGraphDestroy(g);
-        STB_CUDA(e);
-        c->graph = exec;
+        cudaGraphExec_t exec = c->graph;
+        const int step_launches = c->graph_launches;
         for (int i = 1; i < max_new; i++) STB_CUDA(cudaGraphLaunch(exec, s->stream));
         count_launch(s, (uint64_t)step_launches * (max_new - 1));
       }
@@ -1664,8 +1688,13 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
     }
     for (auto &e : ev)
       if (e) cudaEventDestroy(e);
-    int rc = stb_llama_cache_destroy(c);
-    if (rc != STB_OK) throw Error(rc, stb_last_error());
+    if (reuse_enabled) {
+      m->gen = c;
+      std::copy(key, key + 5, m->gen_key);
+    } else {
+      int rc = stb_llama_cache_destroy(c);
+      if (rc != STB_OK) throw Error(rc, stb_last_error());
+    }
   });
 }
 

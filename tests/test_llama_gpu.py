@@ -66,6 +66,23 @@ def test_tiny_generate_ids_match_oracle(session, tiny):
         assert m.generate_ids(prompt, 0) == prompt
 
 
+def test_repeated_generation_reuses_the_cache_and_graph(session, tiny):
+    """A generate call of the same shape as the previous one reuses its cache, buffers and decode
+    graph: identical ids, no growth of the session's allocations; a different shape rebuilds."""
+    ref = oracle_model(tiny, seed=21)
+    prompts = np.array([[5, 6, 7, 8], [900, 1, 2, 3]])
+    with BackendLlama.prepare_random(session, tiny, seed=21) as m:
+        first = m.generate_ids(prompts, 9)
+        held = session.allocated_bytes
+        for _ in range(3):
+            assert m.generate_ids(prompts, 9) == first
+            assert session.allocated_bytes == held
+        assert m.generate_ids(prompts[:1], 5) == [ref.generate(prompts[0].tolist(), 5)]
+        assert m.generate_ids(prompts, 9) == first
+    for b in range(2):
+        assert first[b] == ref.generate(prompts[b].tolist(), 9)
+
+
 def test_batched_generation_rows_are_independent(session, tiny):
     ref = oracle_model(tiny, seed=9)
     prompts = np.array([[5, 6, 7, 8], [900, 1, 2, 3], [42, 42, 42, 42]])
