@@ -24,6 +24,7 @@
 #include <mutex>
 #include <vector>
 
+#include "decode_mega.cuh"
 #include "gemv.cuh"
 #include "rng.cuh"
 
@@ -70,6 +71,7 @@ struct stb_llama {
   // shape (batch, prompt + new, new, EOS count, prefill chunk)
   stb_llama_cache *gen = nullptr;
   int gen_key[5] = {};
+  uint64_t mega_layers = 0;  // MegaLayer [layers] for the persistent decode
 };
 
 struct stb_llama_cache {
@@ -88,6 +90,7 @@ struct stb_llama_cache {
   uint64_t att_part = 0, att_count = 0;  // split decode attention records and counters (batch rows)
   int att_rows = 0;
   int graph_launches = 0;  // kernels in one replay of `graph`
+  uint64_t mopart = 0, mbar = 0;  // persistent decode: per-head o partials, grid barrier words
   uint64_t tokens = 0;  // int64 [rows]
   uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
   uint64_t out_ids = 0;
@@ -1635,6 +1638,58 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
           STB_CUDA(cudaMemcpy2DAsync((void *)c->tokens, 8, (const void *)(c->tokens + (uint64_t)(last - 1) * 8),
                                      (size_t)last * 8, 8, batch, cudaMemcpyDeviceToDevice, s->stream));
         }
+        const bool persistent = mega_eligible(m->H, m->NH, m->KV, m->hd, m->I, m->V, c->capacity, batch, m->tp,
+                                              m->c.weight_dtype, s->device);
+        if (persistent) {
+          if (!m->mega_layers) {
+            std::vector<MegaLayer> hl(m->layers.size());
+            for (size_t l = 0; l < hl.size(); l++) {
+              const Layer &L = m->layers[l];
+              hl[l] = MegaLayer{(const uint16_t *)L.qkv, (const uint16_t *)L.o, (const uint16_t *)L.gu,
+                                (const uint16_t *)L.down, (const float *)L.in_norm, (const float *)L.post_norm};
+            }
+            const uint64_t bytes = hl.size() * sizeof(MegaLayer);
+            m->mega_layers = alloc_owned(s, m->owned, bytes);
+            upload(s, hl.data(), bytes, m->mega_layers);
+          }
+          if (!c->mopart) {
+            c->mopart = alloc_owned(s, c->owned, (uint64_t)m->NH * m->H * sizeof(float));
+            c->mbar = alloc_owned(s, c->owned, 64);
+          }
+          STB_CUDA(cudaMemsetAsync((void *)c->mbar, 0, 8, s->stream));
+          MegaArgs ma{};
+          ma.layers = (const MegaLayer *)m->mega_layers;
+          ma.L = (int)m->layers.size();
+          ma.H = m->H;
+          ma.NH = m->NH;
+          ma.KV = m->KV;
+          ma.hd = m->hd;
+          ma.I = m->I;
+          ma.V = m->V;
+          ma.capacity = c->capacity;
+          ma.eps = m->c.rms_norm_eps;
+          ma.embed = (const uint16_t *)m->embed;
+          ma.lm_head = (const uint16_t *)m->lm_head;
+          ma.final_norm = (const float *)m->final_norm;
+          ma.rope = (const double2 *)m->rope;
+          ma.kv = (float *)c->kv;
+          ma.qbuf = (float *)c->qbuf;
+          ma.opart = (float *)c->mopart;
+          ma.act = (float *)c->act;
+          ma.hid = (float *)c->sum;
+          ma.tokens = (int64_t *)c->tokens;
+          ma.state = (int *)c->state;
+          ma.out_ids = (int64_t *)c->out_ids;
+          ma.out_stride = c->out_stride;
+          ma.eos = (const int64_t *)c->eos;
+          ma.eos_count = c->eos_count;
+          ma.best = (unsigned long long *)c->best;
+          ma.bar = (unsigned *)c->mbar;
+          ma.err = session_error_word(s);
+          ma.steps = max_new - 1;
+          mega_launch(ma, s->device, s->stream);
+          count_launch(s, 1);
+        }
         StepArgs d;
         d.rows = batch;
         d.count = 1;
@@ -1642,7 +1697,7 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
         d.all_logits = false;
         d.append = true;
         d.advance = 1;
-        if (!c->graph) {
+        if (!persistent && !c->graph) {
           cudaGraph_t g = nullptr;
           STB_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
           int step_launches = 0;
@@ -1661,10 +1716,12 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
           c->graph = made;
           c->graph_launches = step_launches;
         }
-        cudaGraphExec_t exec = c->graph;
-        const int step_launches = c->graph_launches;
-        for (int i = 1; i < max_new; i++) STB_CUDA(cudaGraphLaunch(exec, s->stream));
-        count_launch(s, (uint64_t)step_launches * (max_new - 1));
+        if (!persistent) {
+          cudaGraphExec_t exec = c->graph;
+          const int step_launches = c->graph_launches;
+          for (int i = 1; i < max_new; i++) STB_CUDA(cudaGraphLaunch(exec, s->stream));
+          count_launch(s, (uint64_t)step_launches * (max_new - 1));
+        }
       }
       STB_CUDA(cudaEventRecord(ev[2], s->stream));
       std::vector<int64_t> picks((size_t)batch * max_new);

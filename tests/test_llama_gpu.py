@@ -220,3 +220,30 @@ def test_smollm2_shaped_greedy_ids_and_logits(session):
         close(got, ref.decode(oc, np.array([[17]])))
         ref.free_cache(oc)
         c.close()
+
+
+def test_persistent_decode_option_matches_oracle():
+    """The opt-in persistent decode (STB_DECODE_PERSISTENT=1: every decode step in one cooperative
+    launch with grid barriers) gives the oracle's greedy ids; run in a child process because the
+    switch is read once per process."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = [{root!r}, {os.path.join(root, 'scala-torch_b200')!r}, {os.path.join(root, 'tests')!r}]\n"
+        "from llama_fixtures import TINY, SMOL, oracle_model\n"
+        "from scalatorch import ffm\n"
+        "from scalatorch.models import BackendLlama, LlamaConfig\n"
+        "s = ffm.B200Session(0, 8 << 30)\n"
+        "for cfg, prompt, n in ((TINY, [1, 17, 400, 999, 3], 20), (SMOL, [5, 9, 700, 12, 44, 3000], 6)):\n"
+        "    c = LlamaConfig(**cfg)\n"
+        "    with BackendLlama.prepare_random(s, c, seed=5) as m:\n"
+        "        got = m.generate_ids(prompt, n)\n"
+        "        assert m.generate_ids(prompt, n) == got\n"
+        "    assert got == oracle_model(c, seed=5).generate(prompt, n), (got,)\n"
+        "s.close()\n"
+        "print('ok')\n")
+    env = dict(os.environ, STB_DECODE_PERSISTENT="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
