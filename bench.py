@@ -183,13 +183,15 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="smollm2", choices=["smollm2", "llama70b", "linear", "prefill"])
+    ap.add_argument("--workload", default="smollm2", choices=["smollm2", "llama70b", "linear", "prefill", "roofline"],
+                    help="roofline: only the SmolLM2 lm_head roofline leg of the default line (for profiling)")
     ap.add_argument("--shapes", default="", help="linear/prefill: comma list of shape names to run (default all)")
     ap.add_argument("--ms", default="", help="linear/prefill: comma list of token-row counts M (default 1,4,16,32 "
                     "for linear, 2048,8192 for prefill)")
     ap.add_argument("--batch", type=int, default=1, help="llama70b: decode batch (1, 8, 32)")
     ap.add_argument("--prompt", type=int, default=512, help="llama70b: prompt tokens")
     ap.add_argument("--new", type=int, default=32, help="llama70b: generated tokens per step")
+    ap.add_argument("--layers", type=int, default=0, help="llama70b: fewer layers (small profiling cases only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -200,6 +202,16 @@ def main():
         return reference_arm(args, world, rank)
     if args.workload in ("linear", "prefill"):
         return linear_sweep(args, world, rank, local)
+    if args.workload == "roofline":
+        import torch
+        from scalatorch import ffm
+        from scalatorch.models import LlamaConfig
+        torch.cuda.set_device(local)
+        hbm_peak, _, peak_kind = peaks()
+        session = ffm.B200Session(local, 8 << 30)
+        print(json.dumps(roofline_lm_head(session, LlamaConfig(**SMOL), hbm_peak, peak_kind)), flush=True)
+        session.close()
+        return 0
 
     import numpy as np
     import torch
@@ -215,7 +227,7 @@ def main():
     session = ffm.B200Session(local, 178 << 30)
     tp = args.workload == "llama70b"
     if tp:
-        cfg = LlamaConfig(**LLAMA70B)
+        cfg = LlamaConfig(**(dict(LLAMA70B, num_layers=args.layers) if args.layers else LLAMA70B))
         batch, plen, new = args.batch, args.prompt, args.new
         if world > 1:  # one communicator for the tensor-parallel group
             uid = [ffm.B200Session.nccl_unique_id() if rank == 0 else None]
@@ -268,7 +280,7 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16-weights/f32-compute",
             "data": "synthetic (device counter-RNG weights, random prompt ids)",
             "config": {"workload": "llama3-70b-shaped greedy decode", "batch": batch, "prompt": plen,
-                       "new_tokens": new, "layers": 80, "hidden": 8192, "vocab": 128256,
+                       "new_tokens": new, "layers": cfg.num_layers, "hidden": 8192, "vocab": 128256,
                        "parallelism": f"tp{world}", "prefill_ms": round(pre_s * 1000 / args.steps, 3),
                        "decode_ms": round(dec_s * 1000 / args.steps, 3),
                        "decode_ms_per_token": round(dec_s * 1000 / args.steps / max(new - 1, 1), 3),
@@ -310,7 +322,8 @@ def main():
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": step.h2d,
                     "d2h_bytes_per_step": step.d2h},
             "gpu_launches": int(launches),
-            "roofline": roofline_lm_head(session, cfg, hbm_peak, peak_kind),
+            "roofline": decode_step_roofline(NEW * args.steps / dec_s, hbm_peak, peak_kind,
+                                             roofline_lm_head(session, cfg, hbm_peak, peak_kind)),
             "clocks": clocks.summary(),
         }
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -477,6 +490,23 @@ def cpu_baseline_70b_layer():
                                       f"{per_layer * 1000:.0f} ms/layer/token x 80 layers"}
 
 
+LM_HEAD_TRAFFIC_BYTES = 56_646_400
+SMOL_WEIGHT_BYTES_PER_TOKEN = 268_959_744  # 30 x 3,538,944 x 2 + 49,152 x 576 x 2
+
+
+def decode_step_roofline(decode_tok_s, hbm_peak, peak_kind, lm_head):
+    """The SmolLM2 line's roofline in the benchmark's own unit: weight bytes per decode token x
+    decode tokens/s (CUDA events around the decode phase of the timed steps) against the measured
+    HBM copy bandwidth.  The step is a graph of ~150 short kernels and is latency-bound; the
+    largest single kernel (the lm_head GEMV, timed alone) is attached for the kernel-level view."""
+    achieved = SMOL_WEIGHT_BYTES_PER_TOKEN * decode_tok_s / 1e9
+    return {"kernel": "decode step (graph of per-layer GEMV / attention kernels, 153 launches per token)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+            "algorithmic_bytes": SMOL_WEIGHT_BYTES_PER_TOKEN, "units": "weight bytes per decode token",
+            "traffic": None, "lm_head_gemv": lm_head}
+
+
 def roofline_lm_head(session, cfg, hbm_peak, peak_kind):
     """The lm_head GEMV (49152 x 576 BF16, M = 1; the largest per-token kernel) timed alone with
     CUDA events on the session stream, L2 flushed (256 MB write) before every launch."""
@@ -512,7 +542,9 @@ def roofline_lm_head(session, cfg, hbm_peak, peak_kind):
     return {"kernel": "gemv_kernel (lm_head 49152x576 BF16, M=1)", "bound": "hbm", "achieved": round(achieved, 1),
             "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
             "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes": algo, "launch_us": round(t * 1e6, 2),
-            "traffic": None}
+            # dram__bytes_read.sum + dram__bytes_write.sum per launch of this kernel, one ncu capture
+            # (profiles/gemv_kernel_smollm2_lm_head_m1.md)
+            "traffic": LM_HEAD_TRAFFIC_BYTES, "traffic_unit": "B"}
 
 
 def reference_arm(args, world, rank):
