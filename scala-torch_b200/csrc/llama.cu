@@ -438,14 +438,18 @@ __global__ void __launch_bounds__(256) flash_attention_kernel(const float *q, in
 // reset by that block) merges them in split order, rescaling by exp(max_s - max).
 constexpr int DA_KPS = 128, DA_GMAX = 8, DA_THREADS = 256;
 
-template <int HD>
+// KPS keys per split: 128 (two threads per key) or, for head sizes up to 64 when the 128-key grid
+// would leave SMs idle, 256 (one thread per key, one split for contexts up to 256 keys).
+template <int HD, int KPS>
 __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
     const float *q, int ldq, const float *kcache, const float *vcache, float *out, int ldo, int count, int nh,
     int kvh, int capacity, const int *pos_dev, int pos0, float *part, int *counters, int smax) {
   static_assert(HD == 16 || HD == 32 || HD == 64 || HD == 128, "head size");
-  constexpr int HALF = HD / 2, NK4 = HALF / 4, F = HD / 4, KG = DA_THREADS / F, VPT = DA_KPS / KG;
+  static_assert(KPS == 128 || KPS == 256, "keys per split");
+  constexpr int TPK = DA_THREADS / KPS, SEG = HD / TPK, NK4 = SEG / 4;
+  constexpr int F = HD / 4, KG = DA_THREADS / F, VPT = KPS / KG;
   __shared__ __align__(16) float qs[DA_GMAX][HD];
-  __shared__ float sp[DA_GMAX][DA_KPS];
+  __shared__ float sp[DA_GMAX][KPS];
   __shared__ float red[DA_GMAX][2];
   __shared__ __align__(16) float opart[KG][DA_GMAX][HD];
   __shared__ int s_last;
@@ -455,20 +459,20 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   const int G = nh / kvh;
   const int b = m / count, t = m % count;
   const int keys = (pos_dev ? *pos_dev : pos0) + t + 1;
-  const int S = (keys + DA_KPS - 1) / DA_KPS;
+  const int S = (keys + KPS - 1) / KPS;
   if (split >= S) return;  // the grid covers the longest visible range
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int j0 = split * DA_KPS, nk = min(DA_KPS, keys - j0);
+  const int j0 = split * KPS, nk = min(KPS, keys - j0);
   const size_t kvrow0 = ((size_t)b * kvh + g0) * capacity + j0;
   const float scale = (float)(1.0 / sqrt((double)HD));
 
   // every load of the block in flight at once
-  const int jj = tid >> 1, hf = tid & 1;  // score role: key jj, half hf of the dimensions
+  const int jj = tid / TPK, hf = tid % TPK;  // score role: key jj, dimension segment hf
   const int f = tid % F, kg = tid / F;    // value role: dimensions 4f..4f+3 of keys kg, kg + KG, ...
   float4 kreg[NK4], vreg[VPT];
 #pragma unroll
   for (int i = 0; i < NK4; i++)
-    kreg[i] = jj < nk ? *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * HALF + 4 * i)
+    kreg[i] = jj < nk ? *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * SEG + 4 * i)
                       : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < VPT; i++) {
@@ -488,7 +492,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
       if (g < G) {
 #pragma unroll
         for (int i = 0; i < NK4; i++) {
-          const float4 qv = *reinterpret_cast<const float4 *>(&qs[g][hf * HALF + 4 * i]);
+          const float4 qv = *reinterpret_cast<const float4 *>(&qs[g][hf * SEG + 4 * i]);
           dots[g] = fmaf(qv.x, kreg[i].x, dots[g]);
           dots[g] = fmaf(qv.y, kreg[i].y, dots[g]);
           dots[g] = fmaf(qv.z, kreg[i].z, dots[g]);
@@ -496,8 +500,10 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
         }
       }
     }
+    if constexpr (TPK == 2) {
 #pragma unroll
-    for (int g = 0; g < DA_GMAX; g++) dots[g] += __shfl_xor_sync(0xffffffffu, dots[g], 1);
+      for (int g = 0; g < DA_GMAX; g++) dots[g] += __shfl_xor_sync(0xffffffffu, dots[g], 1);
+    }
     if (hf == 0 && jj < nk) {
 #pragma unroll
       for (int g = 0; g < DA_GMAX; g++)
@@ -591,27 +597,31 @@ bool launch_decode_attention(const float *q, int ldq, const float *kc, const flo
                              float *part, int *counters, bool pdl, cudaStream_t st) {
   static const int enabled = env_int("STB_DECODE_ATTENTION", 1);
   if (!enabled || !part || !counters || nh % kvh != 0 || nh / kvh > DA_GMAX) return false;
-  const int smax = (capacity + DA_KPS - 1) / DA_KPS;
+  const int smax128 = (capacity + DA_KPS - 1) / DA_KPS;
+  // 256-key splits when 128-key splits would not fill the SMs anyway (small batch, few KV heads)
+  const bool wide = hd <= 64 && (long)rows * kvh * smax128 < 148;
+  const int smax = wide ? (capacity + 255) / 256 : smax128;
   const dim3 grid(smax, kvh, rows);
+#define STB_DA_LAUNCH(HDV, KPSV)                                                                                   \
+  launch_kernel(decode_attention_kernel<HDV, KPSV>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo,   \
+                count, nh, kvh, capacity, posd, pos0, part, counters, smax)
   switch (hd) {
     case 16:
-      launch_kernel(decode_attention_kernel<16>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo, count,
-                    nh, kvh, capacity, posd, pos0, part, counters, smax);
+      if (wide) STB_DA_LAUNCH(16, 256);
+      else STB_DA_LAUNCH(16, 128);
       return true;
     case 32:
-      launch_kernel(decode_attention_kernel<32>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo, count,
-                    nh, kvh, capacity, posd, pos0, part, counters, smax);
+      if (wide) STB_DA_LAUNCH(32, 256);
+      else STB_DA_LAUNCH(32, 128);
       return true;
     case 64:
-      launch_kernel(decode_attention_kernel<64>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo, count,
-                    nh, kvh, capacity, posd, pos0, part, counters, smax);
+      if (wide) STB_DA_LAUNCH(64, 256);
+      else STB_DA_LAUNCH(64, 128);
       return true;
-    case 128:
-      launch_kernel(decode_attention_kernel<128>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo, count,
-                    nh, kvh, capacity, posd, pos0, part, counters, smax);
-      return true;
+    case 128: STB_DA_LAUNCH(128, 128); return true;
     default: return false;
   }
+#undef STB_DA_LAUNCH
 }
 
 template <int HD>
