@@ -492,6 +492,9 @@ def cpu_baseline_70b_layer():
 
 LM_HEAD_TRAFFIC_BYTES = 56_646_400
 SMOL_WEIGHT_BYTES_PER_TOKEN = 268_959_744  # 30 x 3,538,944 x 2 + 49,152 x 576 x 2
+# DRAM read + write of one decode step (all 153 kernels) in one ncu capture
+# (profiles/decode_step_smollm2_launch_list.md)
+SMOL_STEP_TRAFFIC_BYTES = 279_862_272
 
 
 def decode_step_roofline(decode_tok_s, hbm_peak, peak_kind, lm_head):
@@ -504,7 +507,7 @@ def decode_step_roofline(decode_tok_s, hbm_peak, peak_kind, lm_head):
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
             "algorithmic_bytes": SMOL_WEIGHT_BYTES_PER_TOKEN, "units": "weight bytes per decode token",
-            "traffic": None, "lm_head_gemv": lm_head}
+            "traffic": SMOL_STEP_TRAFFIC_BYTES, "traffic_unit": "B per decode token", "lm_head_gemv": lm_head}
 
 
 def roofline_lm_head(session, cfg, hbm_peak, peak_kind):
