@@ -198,6 +198,32 @@ __device__ __forceinline__ float mg_block_sum(float v, float *red) {
   return r;
 }
 
+// qkv_store_pair for one token row at `pos` with the position's (cos, sin) already in shared
+// memory: q and k pairs rotated (double, no contraction), v pairs stored as they are.
+template <int HD>
+__device__ __forceinline__ void mg_qkv_store(float *qbuf, float *kc, float *vc, int NH, int KV, int cap, int pos,
+                                             int pi, float fa, float fb, const double2 *rs) {
+  constexpr int half = HD / 2;
+  const int qpairs = NH * half, kpairs = KV * half;
+  if (pi < qpairs + kpairs) {
+    const int local = pi < qpairs ? pi : pi - qpairs;
+    const int h = local / half, d = local % half;
+    const double2 cs = rs[d];
+    const double x0 = (double)fa, x1 = (double)fb;
+    const float oa = __double2float_rn(__dsub_rn(__dmul_rn(x0, cs.x), __dmul_rn(x1, cs.y)));
+    const float ob = __double2float_rn(__dadd_rn(__dmul_rn(x1, cs.x), __dmul_rn(x0, cs.y)));
+    float *dst = pi < qpairs ? qbuf + (size_t)h * HD : kc + ((size_t)h * cap + pos) * HD;
+    dst[d] = oa;
+    dst[d + half] = ob;
+  } else {
+    const int local = pi - qpairs - kpairs;
+    const int h = local / half, d = local % half;
+    float *dst = vc + ((size_t)h * cap + pos) * HD;
+    dst[d] = fa;
+    dst[d + half] = fb;
+  }
+}
+
 // Per-block staged weight slices (elements): the largest share any block takes of q/k/v row
 // pairs, gate/up pairs and down rows, and the o projection's column slice of one head.
 struct MgShares {
@@ -212,14 +238,14 @@ template <int HD>
 __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaArgs a) {
   static_assert(HD == 16 || HD == 32 || HD == 64 || HD == 128, "head size");
   constexpr int F = HD / 4, KG = MG_THREADS / F;  // weighted sum: quads x key groups
-  constexpr int KB = F < 16 ? F : 16;             // K-row float4 loads in flight per batch
   extern __shared__ __align__(16) float mg_sm[];
   __shared__ double s_dscr[8];
   __shared__ float s_red[MG_WARPS];
   __shared__ int s_ok, s_pos, s_stop;
   __shared__ long long s_tok;
   __shared__ unsigned long long s_best[MG_WARPS];
-  __shared__ __align__(8) uint64_t s_bar[4];  // staging barriers: q/k/v, o slice, gate/up, down
+  __shared__ __align__(8) uint64_t s_bar[6];  // staging barriers: q/k/v, o slice, gate/up, down, 2 norms
+  __shared__ double2 s_rope[64];               // (cos, sin) of this step's position, hd / 2 pairs
   const int H = a.H, I = a.I, NH = a.NH, KV = a.KV, cap = a.capacity;
   const int G = gridDim.x, b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int XW = H > I ? H : I;
@@ -235,6 +261,9 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
   uint16_t *wo = wq + (size_t)2 * sh.qp * H;                // [H][HD]       o columns of head b
   uint16_t *wg = wo + (size_t)H * HD;                       // [2 sh.gp][H]  gate/up rows
   uint16_t *wd = wg + (size_t)2 * sh.gp * H;                // [sh.dn][I]    down rows
+  float *nin = reinterpret_cast<float *>(wd + (size_t)sh.dn * I);  // [H] input RMSNorm weight
+  float *npost = nin + H;                                           // [H] post-attention RMSNorm weight
+  MegaLayer *lt = reinterpret_cast<MegaLayer *>(npost + H);         // [L] layer table
   const int qkv_pairs = (NH + 2 * KV) * HD / 2;
   const int qp0 = (int)((long)b * qkv_pairs / G), qp1 = (int)((long)(b + 1) * qkv_pairs / G);
   const int gp0 = (int)((long)b * I / G), gp1 = (int)((long)(b + 1) * I / G);  // gate/up pairs
@@ -245,14 +274,25 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
   const float scale = (float)(1.0 / sqrt((double)HD));
   const uint32_t bq = tc::smem_u32(&s_bar[0]), bo = tc::smem_u32(&s_bar[1]);
   const uint32_t bg = tc::smem_u32(&s_bar[2]), bd = tc::smem_u32(&s_bar[3]);
-  const bool has_q = qp1 > qp0, has_o = b < NH, has_g = gp1 > gp0, has_d = dn1 > dn0;
+  const uint32_t bni = tc::smem_u32(&s_bar[4]), bnp = tc::smem_u32(&s_bar[5]);
+  const bool has_q = qp1 > qp0, has_g = gp1 > gp0, has_d = dn1 > dn0;
+  const int smax = (cap + 63) / 64;  // split records per head
+  // attention roles, fixed per step: block h * S + s takes key range s of head h; s == 0 merges
+  int S = 1, KS = 64, ah = 0, as = 0;
+  bool att_block = false, has_o = false;
   unsigned target = 0;            // grid_sync threshold
-  uint32_t uq = 0, uo = 0, ug = 0, ud = 0;  // completed uses of each staging barrier (phase parity)
-  bool pq = false, po = false, pg = false, pd = false;  // copies in flight
+  uint32_t uq = 0, uo = 0, ug = 0, ud = 0, uni = 0, unp = 0;  // completed uses per staging barrier
+  bool pq = false, po = false, pg = false, pd = false, pni = false, pnp = false;  // copies in flight
 
   if (tid == 0) {
-    for (int i = 0; i < 4; i++) tc::mbar_init(tc::smem_u32(&s_bar[i]), 1);
+    for (int i = 0; i < 6; i++) tc::mbar_init(tc::smem_u32(&s_bar[i]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  {  // the layer table, once
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(a.layers);
+    uint32_t *dst = reinterpret_cast<uint32_t *>(lt);
+    const int words = a.L * (int)(sizeof(MegaLayer) / 4);
+    for (int i = tid; i < words; i += MG_THREADS) dst[i] = src[i];
   }
   __syncthreads();
 
@@ -260,13 +300,13 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
     if (!has_q) return;
     const uint32_t bytes = (uint32_t)(2 * (qp1 - qp0)) * H * 2;
     mg_stage_begin(bq, bytes);
-    mg_copy(wq, a.layers[l].qkv + (size_t)2 * qp0 * H, bytes, bq);
+    mg_copy(wq, lt[l].qkv + (size_t)2 * qp0 * H, bytes, bq);
     pq = true;
   };
   auto stage_o = [&](int l) {
     if (!has_o) return;
     mg_stage_begin(bo, (uint32_t)H * HD * 2);
-    const uint16_t *src = a.layers[l].o + (size_t)b * HD;
+    const uint16_t *src = lt[l].o + (size_t)ah * HD;
     for (int n = tid; n < H; n += MG_THREADS) mg_bulk(wo + (size_t)n * HD, src + (size_t)n * qw, HD * 2, bo);
     po = true;
   };
@@ -274,15 +314,25 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
     if (!has_g) return;
     const uint32_t bytes = (uint32_t)(2 * (gp1 - gp0)) * H * 2;
     mg_stage_begin(bg, bytes);
-    mg_copy(wg, a.layers[l].gu + (size_t)2 * gp0 * H, bytes, bg);
+    mg_copy(wg, lt[l].gu + (size_t)2 * gp0 * H, bytes, bg);
     pg = true;
   };
   auto stage_d = [&](int l) {
     if (!has_d) return;
     const uint32_t bytes = (uint32_t)(dn1 - dn0) * I * 2;
     mg_stage_begin(bd, bytes);
-    mg_copy(wd, a.layers[l].down + (size_t)dn0 * I, bytes, bd);
+    mg_copy(wd, lt[l].down + (size_t)dn0 * I, bytes, bd);
     pd = true;
+  };
+  auto stage_ni = [&](int l) {
+    mg_stage_begin(bni, (uint32_t)H * 4);
+    mg_copy(nin, lt[l].in_norm, (uint32_t)H * 4, bni);
+    pni = true;
+  };
+  auto stage_np = [&](int l) {
+    mg_stage_begin(bnp, (uint32_t)H * 4);
+    mg_copy(npost, lt[l].post_norm, (uint32_t)H * 4, bnp);
+    pnp = true;
   };
   // on an early exit: no bulk copy may still be writing this block's shared memory
   auto drain = [&]() {
@@ -292,6 +342,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
       if (po) tc::mbar_wait(bo, uo & 1, &no_abort, a.err, 43);
       if (pg) tc::mbar_wait(bg, ug & 1, &no_abort, a.err, 43);
       if (pd) tc::mbar_wait(bd, ud & 1, &no_abort, a.err, 43);
+      if (pni) tc::mbar_wait(bni, uni & 1, &no_abort, a.err, 43);
+      if (pnp) tc::mbar_wait(bnp, unp & 1, &no_abort, a.err, 43);
     }
     __syncthreads();
   };
@@ -305,6 +357,17 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
     __syncthreads();
     if (s_stop) break;  // read after a barrier: every block sees the same flag
     const int pos = s_pos;
+    const int keys = pos + 1;
+    S = (keys + 63) / 64;
+    if (S > G / NH) S = G / NH;
+    KS = (keys + S - 1) / S;
+    ah = b / S;
+    as = b % S;
+    att_block = b < NH * S;
+    has_o = att_block && as == 0;
+    if (tid < HD / 2) s_rope[tid] = a.rope[(size_t)pos * (HD / 2) + tid];
+    stage_ni(0);
+    stage_np(0);
     stage_q(0);
     stage_o(0);
     stage_g(0);
@@ -313,11 +376,17 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
     __syncthreads();
 
     for (int l = 0; l < a.L; l++) {
-      const MegaLayer W = a.layers[l];
       float *kc = a.kv + (size_t)l * kv_layer;
       const bool more = l + 1 < a.L;
       // A: RMSNorm -> q/k/v pairs of this block -> RoPE, cache append
-      mg_rmsnorm(hs, W.in_norm, xs, H, a.eps, s_dscr);
+      if (!mg_stage_wait(bni, uni & 1, a.err, &s_ok)) {
+        drain();
+        return;
+      }
+      uni++;
+      pni = false;
+      mg_rmsnorm(hs, nin, xs, H, a.eps, s_dscr);  // ends with __syncthreads: nin is free again
+      if (more) stage_ni(l + 1);
       if (has_q) {
         if (!mg_stage_wait(bq, uq & 1, a.err, &s_ok)) {
           drain();
@@ -325,22 +394,11 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
         }
         uq++;
         pq = false;
-        GemvParams gp;
-        gp.y = a.qbuf;
-        gp.ldy = qw;
-        gp.rope = a.rope;
-        gp.count = 1;
-        gp.nh = NH;
-        gp.kvh = KV;
-        gp.hd = HD;
-        gp.capacity = cap;
-        gp.k_cache = kc;
-        gp.v_cache = kc + (size_t)KV * cap * HD;
         for (int p = qp0 + warp; p < qp1; p += MG_WARPS) {
           const uint16_t *rows[2] = {wq + (size_t)(2 * (p - qp0)) * H, wq + (size_t)(2 * (p - qp0) + 1) * H};
           float r[2];
           mg_dots<2, true>(rows, xs, H, lane, r);
-          if (lane == 0) qkv_store_pair(gp, 0, p, r[0], r[1], pos);
+          if (lane == 0) mg_qkv_store<HD>(a.qbuf, kc, kc + (size_t)KV * cap * HD, NH, KV, cap, pos, p, r[0], r[1], s_rope);
         }
         __syncthreads();
         if (more) stage_q(l + 1);
@@ -350,58 +408,74 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
         return;
       }
 
-      // B: attention of head b and its slice of the o projection
-      if (has_o) {
-        const int g = b / (NH / KV);
+      // B: attention split over (head, key range) blocks; the head's range-0 block merges the
+      // splits and applies the head's slice of the o projection
+      if (att_block) {
+        const int h = ah, g = h / (NH / KV);
         const float *kr = kc + (size_t)g * cap * HD;
         const float *vr = kc + (size_t)KV * cap * HD + (size_t)g * cap * HD;
-        if (tid < HD) qs[tid] = __ldcg(a.qbuf + (size_t)b * HD + tid);
-        __syncthreads();
-        const int keys = pos + 1;
-        float mx = -INFINITY;
-        for (int j = tid; j < keys; j += MG_THREADS) {
-          const float4 *k4 = reinterpret_cast<const float4 *>(kr + (size_t)j * HD);
-          float dot = 0.0f;
+        const int j0 = as * KS, j1 = min(keys, j0 + KS), nk = j1 - j0;
+        const int f = tid % F, kg = tid / F;  // weighted-sum role: quad f of keys kg, kg + KG, ...
+        float4 v0[8];                          // the first eight of them, loaded with the K rows
 #pragma unroll
-          for (int f0 = 0; f0 < F; f0 += KB) {
-            float4 kv[KB];
-#pragma unroll
-            for (int u = 0; u < KB; u++) kv[u] = __ldcg(k4 + f0 + u);
-#pragma unroll
-            for (int u = 0; u < KB; u++) {
-              const float *q4 = qs + 4 * (f0 + u);
-              dot = fmaf(q4[0], kv[u].x, dot);
-              dot = fmaf(q4[1], kv[u].y, dot);
-              dot = fmaf(q4[2], kv[u].z, dot);
-              dot = fmaf(q4[3], kv[u].w, dot);
-            }
-          }
-          sc[j] = dot * scale;
-          mx = fmaxf(mx, sc[j]);
+        for (int u = 0; u < 8; u++) {
+          const int j = kg + u * KG;
+          v0[u] = j < nk ? __ldcg(reinterpret_cast<const float4 *>(vr + (size_t)(j0 + j) * HD) + f)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        if (tid < HD) qs[tid] = __ldcg(a.qbuf + (size_t)h * HD + tid);
+        __syncthreads();
+        {  // scores: four threads per key, hd / 4 dimensions each
+          constexpr int QD = HD / 4;
+          const int qt = tid & 3;
+          for (int base = 0; base < nk; base += MG_THREADS / 4) {  // uniform trip count: all lanes shuffle
+            const int j = j0 + base + (tid >> 2);
+            float dot = 0.0f;
+            if (j < j1) {
+              const float4 *k4 = reinterpret_cast<const float4 *>(kr + (size_t)j * HD + qt * QD);
+              float4 kv[QD / 4];
+#pragma unroll
+              for (int u = 0; u < QD / 4; u++) kv[u] = __ldcg(k4 + u);
+#pragma unroll
+              for (int u = 0; u < QD / 4; u++) {
+                const float *q4 = qs + qt * QD + 4 * u;
+                dot = fmaf(q4[0], kv[u].x, dot);
+                dot = fmaf(q4[1], kv[u].y, dot);
+                dot = fmaf(q4[2], kv[u].z, dot);
+                dot = fmaf(q4[3], kv[u].w, dot);
+              }
+            }
+            dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+            dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+            if (qt == 0 && j < j1) sc[j - j0] = dot * scale;
+          }
+        }
+        __syncthreads();
+        float mx = -INFINITY;
+        for (int j = tid; j < nk; j += MG_THREADS) mx = fmaxf(mx, sc[j]);
         mx = mg_block_max(mx, s_red);
         float sum = 0.0f;
-        for (int j = tid; j < keys; j += MG_THREADS) {
+        for (int j = tid; j < nk; j += MG_THREADS) {
           const float e = expf(sc[j] - mx);
           sc[j] = e;
           sum += e;
         }
         sum = mg_block_sum(sum, s_red);
-        {  // weighted V sum: thread (key group kg, quad f), eight V rows in flight, groups added in order
-          const int f = tid % F, kg = tid / F;
+        {  // unnormalised weighted V sum of the range: thread (key group kg, quad f), groups in order
           float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-          for (int j0 = kg; j0 < keys; j0 += 8 * KG) {
+          for (int jb = kg; jb < nk; jb += 8 * KG) {
             float4 v[8];
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-              const int j = j0 + u * KG;
-              v[u] = j < keys ? __ldcg(reinterpret_cast<const float4 *>(vr + (size_t)j * HD) + f)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+              const int j = jb + u * KG;
+              v[u] = jb == kg ? v0[u]
+                              : (j < nk ? __ldcg(reinterpret_cast<const float4 *>(vr + (size_t)(j0 + j) * HD) + f)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f));
             }
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-              const int j = j0 + u * KG;
-              const float p = j < keys ? sc[j] : 0.0f;
+              const int j = jb + u * KG;
+              const float p = j < nk ? sc[j] : 0.0f;
               o0 = fmaf(p, v[u].x, o0);
               o1 = fmaf(p, v[u].y, o1);
               o2 = fmaf(p, v[u].z, o2);
@@ -409,29 +483,80 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
             }
           }
           *reinterpret_cast<float4 *>(pv + kg * HD + 4 * f) = make_float4(o0, o1, o2, o3);
-          __syncthreads();
-          if (tid < HD) {
-            float o = 0.0f;
-#pragma unroll
-            for (int k = 0; k < KG; k++) o += pv[k * HD + tid];
-            att[tid] = o / sum;
-          }
-        }
-        if (!mg_stage_wait(bo, uo & 1, a.err, &s_ok)) {  // (its __syncthreads also publishes att)
-          drain();
-          return;
-        }
-        uo++;
-        po = false;
-        for (int n = tid; n < H; n += MG_THREADS) {
-          const uint16_t *wr = wo + (size_t)n * HD;
-          float acc = 0.0f;
-#pragma unroll
-          for (int c = 0; c < HD / 8; c++) mg_fma8(*reinterpret_cast<const uint4 *>(wr + c * 8), att + c * 8, acc);
-          a.opart[(size_t)b * H + n] = acc;
         }
         __syncthreads();
-        if (more) stage_o(l + 1);
+        float *rec = a.apart + ((size_t)h * smax + as) * (HD + 2);
+        if (tid < HD) {
+          float o = 0.0f;
+#pragma unroll
+          for (int k = 0; k < KG; k++) o += pv[k * HD + tid];
+          if (S == 1) att[tid] = o / sum;
+          else rec[2 + tid] = o;
+        }
+        if (S > 1) {
+          if (tid == 0) {
+            rec[0] = mx;
+            rec[1] = sum;
+          }
+          __threadfence();
+          __syncthreads();
+          unsigned *done = a.bar + 16 + h;
+          if (tid == 0) atomicAdd(done, 1u);
+          if (has_o) {  // merge the head's S ranges in range order
+            if (tid == 0) {
+              int ok = 1;
+              const unsigned long long t0 = mg_now();
+              for (unsigned i = 1; mg_ld_acquire(done) < (unsigned)S; i++) {
+                if ((i & 63) == 0 && (*(volatile int *)a.err || mg_now() - t0 > MG_WAIT_NS)) {
+                  atomicCAS(a.err, 0, 44);
+                  ok = 0;
+                  break;
+                }
+              }
+              *done = 0u;  // every range has arrived: ready for the next layer
+              s_ok = ok;
+            }
+            __syncthreads();
+            if (!s_ok) {
+              drain();
+              return;
+            }
+            const float *hrec = a.apart + (size_t)h * smax * (HD + 2);
+            if (tid < HD) {
+              float M = -INFINITY;
+              for (int r = 0; r < S; r++) M = fmaxf(M, __ldcg(hrec + (size_t)r * (HD + 2)));
+              float num = 0.0f, den = 0.0f;
+              for (int r = 0; r < S; r++) {
+                const float w = expf(__ldcg(hrec + (size_t)r * (HD + 2)) - M);
+                num = fmaf(w, __ldcg(hrec + (size_t)r * (HD + 2) + 2 + tid), num);
+                den = fmaf(w, __ldcg(hrec + (size_t)r * (HD + 2) + 1), den);
+              }
+              att[tid] = num / den;
+            }
+          }
+        }
+        if (has_o) {
+          if (!mg_stage_wait(bo, uo & 1, a.err, &s_ok)) {  // (its __syncthreads also publishes att)
+            drain();
+            return;
+          }
+          uo++;
+          po = false;
+          {  // CH lanes per row (one 16-byte chunk each), 32 / CH rows per warp: conflict-free rows
+            constexpr int CH = HD / 8, RPW = 32 / CH;
+            const int rr = lane / CH, cc = lane % CH;
+            for (int n0 = warp * RPW; n0 < H; n0 += MG_WARPS * RPW) {
+              const int n = n0 + rr;
+              float acc = 0.0f;
+              if (n < H) mg_fma8(*reinterpret_cast<const uint4 *>(wo + (size_t)n * HD + cc * 8), att + cc * 8, acc);
+#pragma unroll
+              for (int off = CH / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+              if (cc == 0 && n < H) a.opart[(size_t)h * H + n] = acc;
+            }
+          }
+          __syncthreads();
+          if (more) stage_o(l + 1);
+        }
       }
       if (!grid_sync(a.bar, target, a.err, &s_ok)) {
         drain();
@@ -463,7 +588,14 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
         }
       }
       __syncthreads();
-      mg_rmsnorm(hs, W.post_norm, xs, H, a.eps, s_dscr);
+      if (!mg_stage_wait(bnp, unp & 1, a.err, &s_ok)) {
+        drain();
+        return;
+      }
+      unp++;
+      pnp = false;
+      mg_rmsnorm(hs, npost, xs, H, a.eps, s_dscr);
+      if (more) stage_np(l + 1);
       if (has_g) {
         if (!mg_stage_wait(bg, ug & 1, a.err, &s_ok)) {
           drain();
@@ -564,13 +696,14 @@ __global__ void __launch_bounds__(MG_THREADS, 1) decode_mega_kernel(const MegaAr
 
 // Shared memory of one block: hs [H], xs [max(H, I)], scores [capacity rounded up to 32], q [hd],
 // att [hd], weighted-sum partials [1024] (floats), then the staged BF16 weight slices (q/k/v pairs,
-// the o columns of one head, gate/up pairs, down rows) for a grid of G blocks.  H % 8 == 0,
+// the o columns of one head, gate/up pairs, down rows) for a grid of G blocks, the two staged RMSNorm
+// weights [H] each and the layer table [L].  H % 8 == 0,
 // I % 8 == 0 and hd % 16 == 0 keep each array 16-byte aligned.
-size_t mega_smem(int H, int I, int capacity, int hd, int NH, int KV, int G) {
+size_t mega_smem(int H, int I, int capacity, int hd, int NH, int KV, int G, int L) {
   const MgShares sh = mg_shares(NH, KV, hd, H, I, G);
   const size_t floats = (size_t)H + (H > I ? H : I) + ((capacity + 31) & ~31) + 2 * hd + 1024;
   const size_t halves = (size_t)2 * sh.qp * H + (size_t)H * hd + (size_t)2 * sh.gp * H + (size_t)sh.dn * I;
-  return floats * sizeof(float) + halves * 2;
+  return floats * sizeof(float) + halves * 2 + (size_t)2 * H * sizeof(float) + (size_t)L * sizeof(MegaLayer);
 }
 
 int mega_sms(int device) {
@@ -581,8 +714,8 @@ int mega_sms(int device) {
 
 }  // namespace
 
-bool mega_eligible(int H, int NH, int KV, int hd, int I, int V, int capacity, int batch, int tp, int w_dtype,
-                   int device) {
+bool mega_eligible(int H, int NH, int KV, int hd, int I, int V, int L, int capacity, int batch, int tp,
+                   int w_dtype, int device) {
   // Opt-in: measured on the SmolLM2-shaped bench it decodes at ~1270 tok/s against ~1600 for the
   // graph-replayed step (each of its 4 phases per layer still holds several dependent L2 round trips
   // plus a ~1.4 us grid barrier), so the graph path stays the default.
@@ -592,7 +725,7 @@ bool mega_eligible(int H, int NH, int KV, int hd, int I, int V, int capacity, in
   if (V <= 0 || NH > mega_sms(device)) return false;
   int coop = 0;
   STB_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
-  return coop && mega_smem(H, I, capacity, hd, NH, KV, mega_sms(device)) <= 200 * 1024;
+  return coop && mega_smem(H, I, capacity, hd, NH, KV, mega_sms(device), L) <= 200 * 1024;
 }
 
 namespace {
@@ -628,7 +761,7 @@ void mega_launch_hd(const MegaArgs &a, size_t smem, int device, cudaStream_t st)
 }  // namespace
 
 void mega_launch(const MegaArgs &a, int device, cudaStream_t st) {
-  const size_t smem = mega_smem(a.H, a.I, a.capacity, a.hd, a.NH, a.KV, mega_sms(device));
+  const size_t smem = mega_smem(a.H, a.I, a.capacity, a.hd, a.NH, a.KV, mega_sms(device), a.L);
   switch (a.hd) {
     case 16: mega_launch_hd<16>(a, smem, device, st); break;
     case 32: mega_launch_hd<32>(a, smem, device, st); break;

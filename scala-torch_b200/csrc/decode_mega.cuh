@@ -7,7 +7,8 @@
 // weights issued before each barrier.  Per layer:
 //   A  RMSNorm (every block, the GEMV's expression) -> q/k/v row pairs of this block -> RoPE,
 //      q to qbuf, k/v appended to the cache;
-//   B  blocks h < nh: causal attention of query head h (FP32, as decode_attention_kernel) and that
+//   B  causal attention split over (query head, key range) blocks (FP32); the block holding a
+//      head's first range waits for the head's other splits, merges them and multiplies by that
 //      head's slice of the o projection, opart[h][n] = att_h . W_o[n, h*hd : h*hd + hd];
 //   C  every block: hidden += sum over heads of opart (head order), post-attention RMSNorm,
 //      gate/up row pairs of this block -> act = SiLU(gate) * up;
@@ -40,6 +41,7 @@ struct MegaArgs {
   float *opart;  // [NH][H]
   float *act;    // [I]
   float *hid;    // [H]
+  float *apart;  // [NH][ceil(capacity / 64)][hd + 2] attention split records (max, sum, partial sums)
   int64_t *tokens;  // [1]
   int *state;       // [0] position, [1] all stopped, [2] stopped, [3] output count
   int64_t *out_ids;
@@ -47,14 +49,14 @@ struct MegaArgs {
   const int64_t *eos;
   int eos_count;
   unsigned long long *best;  // [1]
-  unsigned *bar;             // [2] barrier count, generation (zeroed before each launch)
+  unsigned *bar;             // [16 + NH]: [0] barrier count, [16 + h] head h's finished splits (zeroed before each launch)
   int *err;
   int steps;
 };
 
 // Whether a model / cache shape has the persistent form (see the conditions in decode_mega.cu).
-bool mega_eligible(int H, int NH, int KV, int hd, int I, int V, int capacity, int batch, int tp, int w_dtype,
-                   int device);
+bool mega_eligible(int H, int NH, int KV, int hd, int I, int V, int L, int capacity, int batch, int tp,
+                   int w_dtype, int device);
 // Launches the persistent decode (cooperative, one block per SM).  bar must be zero.
 void mega_launch(const MegaArgs &a, int device, cudaStream_t st);
 

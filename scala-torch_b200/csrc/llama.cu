@@ -90,7 +90,7 @@ struct stb_llama_cache {
   uint64_t att_part = 0, att_count = 0;  // split decode attention records and counters (batch rows)
   int att_rows = 0;
   int graph_launches = 0;  // kernels in one replay of `graph`
-  uint64_t mopart = 0, mbar = 0;  // persistent decode: per-head o partials, grid barrier words
+  uint64_t mopart = 0, mbar = 0, mapart = 0;  // persistent decode: o partials, barrier words, split records
   uint64_t tokens = 0;  // int64 [rows]
   uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
   uint64_t out_ids = 0;
@@ -1648,8 +1648,8 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
           STB_CUDA(cudaMemcpy2DAsync((void *)c->tokens, 8, (const void *)(c->tokens + (uint64_t)(last - 1) * 8),
                                      (size_t)last * 8, 8, batch, cudaMemcpyDeviceToDevice, s->stream));
         }
-        const bool persistent = mega_eligible(m->H, m->NH, m->KV, m->hd, m->I, m->V, c->capacity, batch, m->tp,
-                                              m->c.weight_dtype, s->device);
+        const bool persistent = mega_eligible(m->H, m->NH, m->KV, m->hd, m->I, m->V, (int)m->layers.size(),
+                                              c->capacity, batch, m->tp, m->c.weight_dtype, s->device);
         if (persistent) {
           if (!m->mega_layers) {
             std::vector<MegaLayer> hl(m->layers.size());
@@ -1662,11 +1662,14 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
             m->mega_layers = alloc_owned(s, m->owned, bytes);
             upload(s, hl.data(), bytes, m->mega_layers);
           }
+          const uint64_t bar_bytes = (uint64_t)(16 + m->NH) * sizeof(unsigned);
           if (!c->mopart) {
             c->mopart = alloc_owned(s, c->owned, (uint64_t)m->NH * m->H * sizeof(float));
-            c->mbar = alloc_owned(s, c->owned, 64);
+            c->mbar = alloc_owned(s, c->owned, bar_bytes);
+            c->mapart = alloc_owned(s, c->owned, (uint64_t)m->NH * ((c->capacity + 63) / 64) * (m->hd + 2) *
+                                                     sizeof(float));
           }
-          STB_CUDA(cudaMemsetAsync((void *)c->mbar, 0, 8, s->stream));
+          STB_CUDA(cudaMemsetAsync((void *)c->mbar, 0, bar_bytes, s->stream));
           MegaArgs ma{};
           ma.layers = (const MegaLayer *)m->mega_layers;
           ma.L = (int)m->layers.size();
@@ -1687,6 +1690,7 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
           ma.opart = (float *)c->mopart;
           ma.act = (float *)c->act;
           ma.hid = (float *)c->sum;
+          ma.apart = (float *)c->mapart;
           ma.tokens = (int64_t *)c->tokens;
           ma.state = (int *)c->state;
           ma.out_ids = (int64_t *)c->out_ids;
