@@ -716,9 +716,9 @@ int mega_sms(int device) {
 
 bool mega_eligible(int H, int NH, int KV, int hd, int I, int V, int L, int capacity, int batch, int tp,
                    int w_dtype, int device) {
-  // Opt-in: measured on the SmolLM2-shaped bench it decodes at ~1270 tok/s against ~1600 for the
-  // graph-replayed step (each of its 4 phases per layer still holds several dependent L2 round trips
-  // plus a ~1.4 us grid barrier), so the graph path stays the default.
+  // Opt-in: measured on the SmolLM2-shaped bench it decodes at ~1320 tok/s against ~1720 for the
+  // graph-replayed step (a grid barrier costs ~1.4 us and the o slice waits on one small strided
+  // bulk copy per row), so the graph path stays the default.
   static const int enabled = env_int("STB_DECODE_PERSISTENT", 0);
   if (!enabled || batch != 1 || tp != 1 || w_dtype != STB_BF16) return false;
   if (H % 8 || I % 8 || (hd != 16 && hd != 32 && hd != 64 && hd != 128) || KV <= 0 || NH % KV) return false;
