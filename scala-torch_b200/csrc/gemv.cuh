@@ -139,17 +139,24 @@ __device__ __forceinline__ void qkv_store_pair(const GemvParams &p, int mm, int 
 }
 
 template <int MT, int ROWS, int TPR, typename WT, int EPI>
-__global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtiles) {
+__global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtiles, int items) {
   constexpr int G = 256 / TPR;
   constexpr int LW = TPR < 32 ? TPR : 32;
   __shared__ double s_inv[MT];
   __shared__ double s_scratch[8];
   __shared__ float s_out[G][ROWS][MT];
   __shared__ float s_red[TPR > 32 ? 8 : 1][ROWS * MT];
+  __shared__ int s_inv_tile;  // m-tile whose inverse RMS s_inv holds
 
   const int tid = threadIdx.x;
   const int g = tid / TPR, lane = tid % TPR;
-  const int mtile = blockIdx.x % mtiles, rblock = blockIdx.x / mtiles;
+  if (tid == 0) s_inv_tile = -1;
+  __syncthreads();
+  // Grid-stride over (m-tile, row block) items: the grid holds at most what is resident at once,
+  // so no partial last wave.  Each item is produced by one block in a fixed order.
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+  const bool first = item == (int)blockIdx.x;
+  const int mtile = item % mtiles, rblock = item / mtiles;
   const int m0 = mtile * MT;
   const int mcount = min(MT, p.M - m0);
   const int rowbase = (rblock * G + g) * ROWS;
@@ -172,7 +179,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
                                              : make_uint4(0, 0, 0, 0);
     }
   }
-  if (p.pdl) {
+  if (p.pdl && first) {
     if (tid == 0 && mtile == 0 && nchunk > PRE * TPR) {
       const int r0 = rblock * G * ROWS;
       const int nrows = min(G * ROWS, p.N - r0);
@@ -201,7 +208,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
     }
   }
 
-  if (p.norm_w) {
+  if (p.norm_w && s_inv_tile != mtile) {
+    __syncthreads();  // every thread has compared s_inv_tile before thread 0 updates it
     for (int m = 0; m < MT; m++) {
       double sq = 0.0;
       if (m < mcount) {
@@ -214,6 +222,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
       double total = block_sum_double(sq, s_scratch);
       if (tid == 0) s_inv[m] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(total, (double)p.K), p.norm_eps)));
     }
+    if (tid == 0) s_inv_tile = mtile;
     __syncthreads();
   }
 
@@ -223,18 +232,25 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
 #pragma unroll
     for (int m = 0; m < MT; m++) acc[r][m] = 0.0f;
 
-  // Chunks in increasing order: the PRE preloaded ones, then the rest streamed in the loop.
-  for (int i = 0, c = lane; c < nchunk; i++, c += TPR) {
-    uint4 wv[ROWS];
-    if (i < PRE) {
+  // Chunks in increasing order; the weight loads run PRE chunk-steps ahead of the FMAs (the PRE
+  // preloaded ones first), so each thread keeps (PRE + 1) x ROWS 16-byte loads in flight.
+  uint4 cur[ROWS], nxt[ROWS];
 #pragma unroll
-      for (int r = 0; r < ROWS; r++) wv[r] = i == 0 ? wpre[0][r] : wpre[PRE - 1][r];
-    } else {
+  for (int r = 0; r < ROWS; r++) {
+    cur[r] = wpre[0][r];
+    nxt[r] = wpre[PRE - 1][r];
+  }
+  for (int c = lane; c < nchunk; c += TPR) {
+    uint4 wv[ROWS], fut[ROWS];
+    const int cf = c + PRE * TPR;
 #pragma unroll
-      for (int r = 0; r < ROWS; r++) {
-        const int row = rowbase + r;
-        wv[r] = row < p.N ? ld_stream_u4(W + (size_t)row * p.K + (size_t)c * 8) : make_uint4(0, 0, 0, 0);
-      }
+    for (int r = 0; r < ROWS; r++) {
+      const int row = rowbase + r;
+      fut[r] = (cf < nchunk && row < p.N) ? ld_stream_u4(W + (size_t)row * p.K + (size_t)cf * 8)
+                                          : make_uint4(0, 0, 0, 0);
+      wv[r] = cur[r];
+      cur[r] = nxt[r];
+      nxt[r] = fut[r];
     }
     float xv[MT][8];
 #pragma unroll
@@ -278,7 +294,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
     }
   }
 
-  if (p.pdl) pdl_trigger();  // the next kernel may start its own weight prefetch now
+  if (p.pdl && first) pdl_trigger();  // the next kernel may start its own weight prefetch now
 
   // Group reduction in a fixed order.
 #pragma unroll
@@ -380,6 +396,8 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvParams p, int mtile
       if (m >= mcount || row >= p.N) continue;
       qkv_store_pair(p, m0 + m, row >> 1, s_out[gg][r][m], s_out[gg][r + 1][m], pos_base);
     }
+  }
+  __syncthreads();  // the shared arrays are reused by the block's next item
   }
 }
 
