@@ -10,8 +10,10 @@
 // 64-wide K block takes 4 MMAs (M = 128, N = 3 NT, K = 16) rather than 12 dependent small ones, and
 // the three term products land in separate TMEM column groups.  The tensor core's FP32
 // accumulation is not round-to-nearest (a chain of ~200 MMAs drifted by ~3e-5 relative), so each
-// K block gets a fresh accumulator from a ring, and the epilogue warps combine the terms
-// ((x2 + x1) + x0) and add the block partials in FP32 in K order.  The result keeps
+// group of 1 / 4 / 8 K blocks (NT = 16 / 32 / 64; chains of at most 32 MMAs) gets a fresh
+// accumulator from a ring, and the epilogue warps combine the terms ((x2 + x1) + x0) and add the
+// group partials in FP32 in K order.  Larger groups give the epilogue, which reads 3 NT columns per
+// group, fewer turns where NT is wide.  The result keeps
 // Float32-activation accuracy (within the decode GEMV's 1e-5 * (1 + |e|)) at tensor-core
 // throughput: the kernel is bound by streaming W from HBM.
 //
@@ -48,29 +50,45 @@ struct SkinnyShape {
   static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
   static constexpr int ACC_STRIDE = NT == 16 ? 64 : (NT == 32 ? 128 : 256);  // >= 3 NT TMEM columns
   static constexpr int ACC = NT == 64 ? 2 : 4;                                // accumulators in the ring
+  static constexpr int GK = NT == 16 ? 1 : (NT == 32 ? 4 : 8);  // K blocks per accumulator (4 GK MMAs per chain)
   static constexpr int TMEM_COLS = ACC * ACC_STRIDE;                          // 256 or 512
   static_assert(SMEM <= 232448, "shared memory per CTA");
   static_assert(TMEM_COLS <= 512 && ACC <= SK_ACC_MAX, "tensor memory");
   static_assert((2 * STAGES + 2 * SK_ACC_MAX + 1) * 8 + 8 <= 256, "barrier area");
 };
 
+// Three W-column TMEM loads (the x2, x1 and x0 term columns of one chunk) and one wait, in a
+// single asm statement so no use of the registers can be scheduled before the wait.
 template <int W>
-__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&out)[W]) {
+__device__ __forceinline__ void tmem_ld3(uint32_t a2, uint32_t a1, uint32_t a0, float (&t2)[W], float (&t1)[W],
+                                         float (&t0)[W]) {
   static_assert(W == 16 || W == 32, "load width");
-  uint32_t r[32];
+  uint32_t r[3 * W];
   if constexpr (W == 16) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-        "%14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%48];\n"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%49];\n"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47}, [%50];\n"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47])
+        : "r"(a2), "r"(a1), "r"(a0)
+        : "memory");
   } else {
-    tmem_ld32(taddr, r);
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%96];\n"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%97];\n"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95}, [%98];\n"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95])
+        : "r"(a2), "r"(a1), "r"(a0)
+        : "memory");
   }
 #pragma unroll
-  for (int j = 0; j < W; j++) out[j] = __uint_as_float(r[j]);
+  for (int j = 0; j < W; j++) {
+    t2[j] = __uint_as_float(r[j]);
+    t1[j] = __uint_as_float(r[W + j]);
+    t0[j] = __uint_as_float(r[2 * W + j]);
+  }
 }
 
 // First iteration of CTA c when T iterations are cut into G ranges.
@@ -197,23 +215,30 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // Accumulator groups: up to GK consecutive K blocks of one tile; a group also ends at the end of
+      // a tile or of this CTA's range (the epilogue walks the same groups).
       int stage = 0;
       uint32_t phase = 0;
       bool issued = false;
-      int j = 0;
-      for (long long i = i0; i < i1; i++, j++) {
-        const int r = j % S::ACC;
-        if (!mbar_wait(acce0 + 8 * r, ((uint32_t)(j / S::ACC) & 1u) ^ 1u, abort_flag, err, 35)) break;
+      int grp = 0, cnt = 0;
+      for (long long i = i0; i < i1; i++) {
+        const int r = grp % S::ACC;
+        if (cnt == 0 && !mbar_wait(acce0 + 8 * r, ((uint32_t)(grp / S::ACC) & 1u) ^ 1u, abort_flag, err, 35)) break;
         if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, err, 32)) break;
         tc_fence_after();
         const uint64_t a = smem_desc(sa0 + stage * S::A_BYTES);
         const uint64_t b = smem_desc(sb0 + stage * S::B_BYTES);  // [x0; x1; x2]: N = 3 NT rows
         const uint32_t d = tmem + (uint32_t)(r * S::ACC_STRIDE);
 #pragma unroll
-        for (int k = 0; k < BK / 16; k++) mma_f16(d, a + (uint64_t)(2 * k), b + (uint64_t)(2 * k), idesc, k != 0);
+        for (int k = 0; k < BK / 16; k++)
+          mma_f16(d, a + (uint64_t)(2 * k), b + (uint64_t)(2 * k), idesc, cnt != 0 || k != 0);
         issued = true;
         mma_commit(empty0 + 8 * stage);
-        mma_commit(accf0 + 8 * r);
+        if (++cnt == S::GK || (i + 1) % kbs == 0 || i + 1 == i1) {
+          mma_commit(accf0 + 8 * r);
+          grp++;
+          cnt = 0;
+        }
         if (++stage == S::STAGES) {
           stage = 0;
           phase ^= 1;
@@ -231,29 +256,29 @@ __global__ void __launch_bounds__(192, 1)
     float acc[NT];
 #pragma unroll
     for (int m = 0; m < NT; m++) acc[m] = 0.0f;
-    int j = 0;
-    for (long long i = i0; i < i1; i++, j++) {
-      const int r = j % S::ACC;
+    int grp = 0, cnt = 0;
+    for (long long i = i0; i < i1; i++) {
+      if (!(++cnt == S::GK || (i + 1) % kbs == 0 || i + 1 == i1)) continue;  // inside an accumulator group
+      cnt = 0;
+      const int r = grp % S::ACC;
       int got = 0;
-      if (lane == 0) got = mbar_wait(accf0 + 8 * r, (uint32_t)(j / S::ACC) & 1u, abort_flag, err, 34);
+      if (lane == 0) got = mbar_wait(accf0 + 8 * r, (uint32_t)(grp / S::ACC) & 1u, abort_flag, err, 34);
       if (!__shfl_sync(0xffffffffu, got, 0)) break;
       tc_fence_after();
       constexpr int W = NT == 16 ? 16 : 32;
       const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(r * S::ACC_STRIDE);
 #pragma unroll
       for (int c = 0; c < NT / W; c++) {  // columns t * NT + m hold term t of token row m
-        float lo[W], mid[W];
-        tmem_ld_cols<W>(base + (uint32_t)(2 * NT + c * W), lo);
-        tmem_ld_cols<W>(base + (uint32_t)(NT + c * W), mid);
+        float lo[W], mid[W], hi[W];
+        tmem_ld3<W>(base + (uint32_t)(2 * NT + c * W), base + (uint32_t)(NT + c * W), base + (uint32_t)(c * W), lo,
+                    mid, hi);
 #pragma unroll
-        for (int jj = 0; jj < W; jj++) lo[jj] = lo[jj] + mid[jj];
-        tmem_ld_cols<W>(base + (uint32_t)(c * W), mid);
-#pragma unroll
-        for (int jj = 0; jj < W; jj++) acc[c * W + jj] += lo[jj] + mid[jj];
+        for (int jj = 0; jj < W; jj++) acc[c * W + jj] += (lo[jj] + mid[jj]) + hi[jj];
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce0 + 8 * r);
+      grp++;
       if (i + 1 == i1 || (i + 1) % kbs == 0) {  // end of this CTA's piece of tile t
         const int t = (int)(i / kbs);
         const int piece = cta - sk_cta_of((long long)t * kbs, T, G);
