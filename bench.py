@@ -269,10 +269,10 @@ def main():
         dist.barrier()
 
     if tp:
-        # tensor parallel: the ranks produce one sequence batch together; metric = decode tokens/s
-        tokens = batch * new * args.steps
-        value = tokens / dec_s
-        e2e = tokens / wall
+        # tensor parallel: the ranks produce one sequence batch together; metric = decode tokens/s,
+        # the new - 1 tokens per row of the decode phase (the first comes out of the prefill)
+        value = batch * max(new - 1, 1) * args.steps / dec_s
+        e2e = batch * new * args.steps / wall  # whole generate calls, host buffers
         line = {
             "metric": "greedy decode tokens/s (Llama-3-70B-shaped, BF16 weights, tensor parallel)",
             "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
