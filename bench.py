@@ -316,13 +316,13 @@ def main():
                        "layers": 30, "hidden": 576, "vocab": 49152, "parallelism": f"replicas x{world}",
                        "prefill_ms": round(pre_s * 1000 / args.steps, 3),
                        "decode_ms": round(dec_s * 1000 / args.steps, 3),
-                       "decode_tok_s": round(NEW * args.steps / dec_s, 1),
+                       "decode_tok_s": round((NEW - 1) * args.steps / dec_s, 1),
                        "weight_bytes_per_token": 268959744,
                        "l2": "inputs larger than L2: 269 MB of weights streamed per token vs 126 MB L2"},
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": step.h2d,
                     "d2h_bytes_per_step": step.d2h},
             "gpu_launches": int(launches),
-            "roofline": decode_step_roofline(NEW * args.steps / dec_s, hbm_peak, peak_kind,
+            "roofline": decode_step_roofline((NEW - 1) * args.steps / dec_s, hbm_peak, peak_kind,
                                              roofline_lm_head(session, cfg, hbm_peak, peak_kind)),
             "clocks": clocks.summary(),
         }
