@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
-Default workload (BASELINE config 2): SmolLM2-135M-shaped Llama, random-init BF16 weights
+Default workload: SmolLM2-135M-shaped Llama, random-init BF16 weights
 ~N(0,0.02) generated on the device, RMSNorm weights 1, batch 1, a 128-token prompt of ids uniform
 in [0,49152), greedy decode of 128 tokens with the KV cache resident in HBM.  One step = one
 generate call (prefill + 128 decode tokens).  Metric: generated tokens per second of the whole
@@ -345,8 +345,8 @@ LLAMA8B_SHAPES = {"q": (4096, 4096), "k": (1024, 4096), "v": (1024, 4096), "o": 
 
 
 def linear_sweep(args, world, rank, local):
-    """BASELINE configs 1/3 (--workload linear: decode GEMV, FP32 activations, M = 1/4/16/32) and
-    config 4 (--workload prefill: tcgen05 GEMM, M = 2048/8192) on Llama-3-8B projection shapes with
+    """The Linear sweeps (--workload linear: decode GEMV, FP32 activations, M = 1/4/16/32; --workload
+    prefill: tcgen05 GEMM, M = 2048/8192) on Llama-3-8B projection shapes with
     device-generated BF16 weights ~N(0,0.02).  Each launch is timed alone with CUDA events on the
     session stream after a 256 MB L2 flush; the median of the timed launches is reported."""
     import ctypes
@@ -459,7 +459,7 @@ def linear_sweep(args, world, rank, local):
             reps += 1
         dt = (time.perf_counter() - t0) / reps
         line["cpu_baseline"] = {"value": round(1904640 / dt / 1e9, 3), "unit": "GB/s", "cores": oracle.max_threads(),
-                                "kind": "port", "sample": f"BASELINE config 1 Linear x[16,576].W[1536,576]^T, {reps} calls"}
+                                "kind": "port", "sample": f"single-Linear config x[16,576].W[1536,576]^T, {reps} calls"}
     print(json.dumps(line), flush=True)
 
 

@@ -1,6 +1,6 @@
 """Parity of the device Linear (stb_linear, decode GEMV family) with the CPU oracle.
 
-Tolerance (BASELINE north_star): |y - ref| <= 1e-5 * (1 + |ref|) for BF16/F16-weight GEMV with
+Tolerance: |y - ref| <= 1e-5 * (1 + |ref|) for BF16/F16-weight GEMV with
 Float32 activations and FP32 accumulation; the reference's own form |a-e| <= tol*(1+|e|)
 (models/src/test/scala/scalatorch/models/BackendLlamaSuite.scala:18).
 """
@@ -40,7 +40,7 @@ def run_linear(session, x, w_bits, dtype, bias=None):
 
 
 def test_config1_single_linear(session):
-    """x F32 [16,576] ~N(0,1); W BF16 [1536,576] N(0,0.02) RNE; no bias."""
+    """The single-Linear configuration: x F32 [16,576] ~N(0,1); W BF16 [1536,576] N(0,0.02) RNE; no bias."""
     rng = np.random.default_rng(1)
     x = rng.standard_normal((16, 576)).astype(np.float32)
     w = oracle.normal_bf16(1536 * 576, seed=1, stream=1, std=0.02).reshape(1536, 576)
@@ -79,7 +79,8 @@ def test_skinny_tensor_core_form(session, m, n, k):
     stream-K GEMM, fixup), activations split into three BF16 terms: still within the FP32 GEMV
     tolerance.
     Ragged N (tile tails), K tails below one 64-wide block, bias; repeated calls are identical.
-    Magnitudes as BASELINE config 1 (x ~ N(0,1), W ~ N(0, 0.02)): the bound is relative to |y| ~ 1."""
+    Magnitudes as the single-Linear configuration (x ~ N(0,1), W ~ N(0, 0.02)): the bound is relative
+    to |y| ~ 1."""
     rng = np.random.default_rng(m * 7 + n)
     x = rng.standard_normal((m, k)).astype(np.float32)
     w = oracle.normal_bf16(n * k, seed=m, stream=9, std=0.02).reshape(n, k)
@@ -133,7 +134,7 @@ def test_empty_shapes(session):
 
 
 def test_llama8b_projection_shapes_against_fp32(session):
-    """BASELINE config 3 shapes at M = 1, 4, 16, 32 against a float64 product of the same widened
+    """Llama-3-8B projection shapes at M = 1, 4, 16, 32 against a float64 product of the same widened
     weights (an fp32 cuBLAS reference carries its own rounding at the 1e-5 level)."""
     import torch
     shapes = {"q": (4096, 4096), "k": (1024, 4096), "gate": (14336, 4096), "down": (4096, 14336),

@@ -204,7 +204,7 @@ def test_cache_rejects_and_keeps_position(session, tiny):
 
 
 def test_smollm2_shaped_greedy_ids_and_logits(session):
-    """BASELINE config 2 shape (30 layers, vocab 49152, 9/3 heads) with a shortened prompt and
+    """SmolLM2-135M shape (30 layers, vocab 49152, 9/3 heads) with a shortened prompt and
     decode so the CPU oracle finishes in seconds; ids must be identical."""
     cfg = LlamaConfig(**SMOL)
     ref = oracle_model(cfg, seed=2024)

@@ -1,6 +1,6 @@
 """The tcgen05 prefill Linear (stb_linear_prefill) against the CPU oracle.
 
-Tolerance source (BASELINE north_star): the activations are rounded to the weight's 16-bit type
+Tolerance source: the activations are rounded to the weight's 16-bit type
 for the tensor cores.  Checked two ways:
 * against the oracle on the *rounded* activations (exact products, only the accumulation order
   differs): |y - e| <= 1e-4 * (1 + |e|) elementwise;
@@ -63,7 +63,7 @@ def test_prefill_rejects_bad_k(session):
 
 
 def test_llama8b_prefill_shapes_sampled_rows(session):
-    """BASELINE config 4 shapes at M = 2048 against a float64 product on sampled output rows."""
+    """Llama-3-8B prefill shapes at M = 2048 against a float64 product on sampled output rows."""
     import torch
     shapes = {"q": (4096, 4096), "k": (1024, 4096), "gate": (14336, 4096), "down": (4096, 14336),
               "lm_head": (128256, 4096)}
