@@ -453,7 +453,9 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   __shared__ float red[DA_GMAX][2];
   __shared__ __align__(16) float opart[KG][DA_GMAX][HD];
   __shared__ int s_last;
-  pdl_wait();
+  // Before the programmatic-dependency wait: the position (written by the previous step's finalize,
+  // a graph launch earlier) and every K/V row but the newest (written by earlier steps).  The newest
+  // row and q come from the projection kernel just before this one: loaded after the wait.
   pdl_trigger();
   const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
   const int G = nh / kvh;
@@ -463,6 +465,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   if (split >= S) return;  // the grid covers the longest visible range
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int j0 = split * KPS, nk = min(KPS, keys - j0);
+  const int fresh = keys - 1 - j0;  // this split's index of the newest key (may be outside [0, nk))
   const size_t kvrow0 = ((size_t)b * kvh + g0) * capacity + j0;
   const float scale = (float)(1.0 / sqrt((double)HD));
 
@@ -472,13 +475,25 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   float4 kreg[NK4], vreg[VPT];
 #pragma unroll
   for (int i = 0; i < NK4; i++)
-    kreg[i] = jj < nk ? *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * SEG + 4 * i)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    kreg[i] = jj < nk && jj != fresh
+                  ? *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * SEG + 4 * i)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < VPT; i++) {
     const int j = kg + i * KG;
-    vreg[i] = j < nk ? *reinterpret_cast<const float4 *>(vcache + (kvrow0 + j) * HD + 4 * f)
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    vreg[i] = j < nk && j != fresh ? *reinterpret_cast<const float4 *>(vcache + (kvrow0 + j) * HD + 4 * f)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  pdl_wait();
+  if (jj == fresh) {
+#pragma unroll
+    for (int i = 0; i < NK4; i++)
+      kreg[i] = *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * SEG + 4 * i);
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int j = kg + i * KG;
+    if (j == fresh) vreg[i] = *reinterpret_cast<const float4 *>(vcache + (kvrow0 + j) * HD + 4 * f);
   }
   for (int i = tid; i < G * HD; i += DA_THREADS)
     qs[i / HD][i % HD] = q[(size_t)m * ldq + (size_t)(g0 * G) * HD + i];
