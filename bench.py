@@ -183,8 +183,10 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="smollm2", choices=["smollm2", "llama70b", "linear", "prefill", "roofline"],
-                    help="roofline: only the SmolLM2 lm_head roofline leg of the default line (for profiling)")
+    ap.add_argument("--workload", default="smollm2",
+                    choices=["smollm2", "llama70b", "linear", "prefill", "single", "roofline"],
+                    help="single: the single-Linear configuration [16,576]x[1536,576]; roofline: only the "
+                    "SmolLM2 lm_head roofline leg of the default line (for profiling)")
     ap.add_argument("--shapes", default="", help="linear/prefill: comma list of shape names to run (default all)")
     ap.add_argument("--ms", default="", help="linear/prefill: comma list of token-row counts M (default 1,4,16,32 "
                     "for linear, 2048,8192 for prefill)")
@@ -202,6 +204,8 @@ def main():
         return reference_arm(args, world, rank)
     if args.workload in ("linear", "prefill"):
         return linear_sweep(args, world, rank, local)
+    if args.workload == "single":
+        return single_linear(args, local)
     if args.workload == "roofline":
         import torch
         from scalatorch import ffm
@@ -463,6 +467,120 @@ def linear_sweep(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+SINGLE_M, SINGLE_N, SINGLE_K = 16, 1536, 576
+SINGLE_BYTES = SINGLE_N * SINGLE_K * 2 + SINGLE_M * SINGLE_K * 4 + SINGLE_M * SINGLE_N * 4  # 1,904,640 B
+
+
+def cpu_single_linear(seconds: float = 3.0):
+    """The reference CPU nn.Linear on the single-Linear configuration (weights widened to F32 once, as
+    SafeTensors.readFloat does at load; numscala's transposed-right order) on all host threads."""
+    import numpy as np
+
+    import oracle
+    x = np.random.default_rng(1).standard_normal((SINGLE_M, SINGLE_K)).astype(np.float32)
+    wf = oracle.widen(oracle.normal_bf16(SINGLE_N * SINGLE_K, 1, 1, 0.02), oracle.BF16).reshape(SINGLE_N, SINGLE_K)
+    t0, reps = time.perf_counter(), 0
+    while time.perf_counter() - t0 < seconds:
+        oracle.matmul_tr(x, wf)
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(SINGLE_BYTES / dt / 1e9, 3), "unit": "GB/s", "cores": oracle.max_threads(), "kind": "port",
+            "sample": f"single-Linear x[16,576].W[1536,576]^T, {reps} calls in {seconds:.0f} s",
+            "us_per_call": round(dt * 1e6, 2)}
+
+
+def single_linear(args, local):
+    """The single-Linear configuration (x F32 [16,576] ~N(0,1), W BF16 [1536,576] ~N(0,0.02), no bias)
+    through stb_linear.  One step = CALLS forwards.  Cold: a 256 MB L2 flush before every call and
+    CUDA events around each call alone (the reported value, against HBM); warm: CALLS back-to-back
+    calls between one event pair (the 1.8 MB weight stays in L2).  e2e: stb_linear_host with host
+    x and y, wall clock per call."""
+    import numpy as np
+    import torch
+    from scalatorch import ffm
+    CALLS = 100
+    torch.cuda.set_device(local)
+    hbm_peak, _, peak_kind = peaks()
+    s = ffm.B200Session(local, 4 << 30)
+    stream = torch.cuda.ExternalStream(s.stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    M, N, K = SINGLE_M, SINGLE_N, SINGLE_K
+    w = torch.empty(N * K, dtype=torch.bfloat16, device="cuda")
+    wt = ffm.DeviceTensor(s, w.data_ptr(), (K, N), ffm.STB_BF16, N * K * 2, transposed_weight=True, owner=False)
+    s.fill_normal(wt, 1, 1, 0.02)
+    hx = np.random.default_rng(1).standard_normal((M, K)).astype(np.float32)
+    hy = np.empty((M, N), np.float32)
+    x = torch.from_numpy(hx).cuda()
+    y = torch.empty(M, N, device="cuda")
+    s.sync()
+    torch.cuda.synchronize()
+
+    def call():
+        ffm.call("stb_linear", s.handle, x.data_ptr(), w.data_ptr(), ffm.STB_BF16, 0, y.data_ptr(), M, N, K)
+
+    cold, warm, e2e, clocks = [], [], [], Clocks(local)
+    launches0 = s.launches
+    with clocks:
+        for step in range(args.warmup + args.steps):
+            if step == args.warmup:
+                clocks.mark()
+                launches0 = s.launches
+            ts = []
+            for _ in range(CALLS):
+                with torch.cuda.stream(stream):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                call()
+                e1.record(stream)
+                e1.synchronize()
+                ts.append(e0.elapsed_time(e1) / 1000.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(CALLS):
+                call()
+            e1.record(stream)
+            e1.synchronize()
+            if step >= args.warmup:
+                cold.extend(ts)
+                warm.append(e0.elapsed_time(e1) / 1000.0 / CALLS)
+        clocks.mark()
+        launches = s.launches - launches0
+    for step in range(args.warmup + args.steps):
+        ts = []
+        for _ in range(CALLS):
+            t0 = time.perf_counter()
+            ffm.call("stb_linear_host", s.handle, hx.ctypes.data, w.data_ptr(), ffm.STB_BF16, 0, hy.ctypes.data, M, N, K)
+            ts.append(time.perf_counter() - t0)
+        if step >= args.warmup:
+            e2e.extend(ts)
+    s.close()
+    med = lambda v: sorted(v)[len(v) // 2]
+    t_cold, t_warm, t_e2e = med(cold), med(warm), med(e2e)
+    achieved = SINGLE_BYTES / t_cold / 1e9
+    line = {"metric": "single-Linear GB/s (x F32 [16,576] . W BF16 [1536,576]^T, L2 flushed before each call)",
+            "value": round(achieved, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_cold * CALLS * 1000, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16-weights/f32-accumulate",
+            "data": "synthetic (device counter-RNG weights seed 1 stream 1, N(0,1) activations seed 1)",
+            "config": {"workload": "single Linear", "M": M, "N": N, "K": K, "calls_per_step": CALLS,
+                       "l2": "flushed (256 MB write) before every cold call; warm calls back to back",
+                       "cold_us": round(t_cold * 1e6, 2), "warm_us": round(t_warm * 1e6, 2),
+                       "warm_GB_s": round(SINGLE_BYTES / t_warm / 1e9, 1)},
+            "gpu_launches": int(launches),
+            "roofline": {"kernel": "stb_linear (prep + gemm_skinny_kernel + fixup, M=16)", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                         "algorithmic_bytes": SINGLE_BYTES, "traffic": None},
+            "e2e": {"value": round(SINGLE_BYTES / t_e2e / 1e9, 3), "unit": "GB/s", "us_per_call": round(t_e2e * 1e6, 2),
+                    "h2d_bytes_per_step": CALLS * M * K * 4, "d2h_bytes_per_step": CALLS * M * N * 4,
+                    "note": "stb_linear_host (host x in, host y out), median wall clock per call"},
+            "clocks": clocks.summary()}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_single_linear()
+    print(json.dumps(line), flush=True)
+
+
 def cpu_baseline_70b_layer():
     """The reference CPU path on ONE Llama-3-70B-shaped decoder layer (weights generated by the same
     counter-based streams, widened to F32 as SafeTensors.readFloat does), decode at batch 1 after a
@@ -557,7 +675,16 @@ def reference_arm(args, world, rank):
         return
     import oracle
     samples = []
-    if args.workload == "llama70b":
+    unit = "tokens/s"
+    if args.workload == "single":
+        for i in range(max(args.warmup, 0) + args.steps):
+            r = cpu_single_linear(seconds=2.0)
+            if i >= args.warmup:
+                samples.append(r)
+        metric = "single-Linear GB/s (x F32 [16,576] . W BF16 [1536,576]^T, L2 flushed before each call)"
+        config = {"workload": "single Linear", "M": SINGLE_M, "N": SINGLE_N, "K": SINGLE_K}
+        scaling, unit = "weak", "GB/s"
+    elif args.workload == "llama70b":
         for i in range(max(args.warmup, 0) + args.steps):
             r = cpu_baseline_70b_layer()
             if i >= args.warmup:
@@ -577,12 +704,12 @@ def reference_arm(args, world, rank):
         scaling = "weak"
     v = sum(s["value"] for s in samples) / len(samples)
     line = {"impl": "reference", "metric": metric,
-            "value": round(v, 5), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "value": round(v, 5), "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": config,
-            "cpu_baseline": {"value": round(v, 5), "unit": "tokens/s", "cores": oracle.max_threads(), "kind": "port",
+            "cpu_baseline": {"value": round(v, 5), "unit": unit, "cores": oracle.max_threads(), "kind": "port",
                              "sample": samples[-1]["sample"]},
-            "e2e": {"value": round(v, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(v, 5), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 

@@ -325,25 +325,80 @@ def _parse_name(name: str):
     return LAYER_WEIGHTS[key], layer
 
 
+def llama_weight_shapes(config: LlamaConfig) -> dict:
+    """Every tensor name of a Llama checkpoint with its (out, in) shape (LlamaModel.shapes,
+    LlamaModel.scala:115-128); lm_head.weight is optional when the embeddings are tied."""
+    H, I, V = config.hidden_size, config.intermediate_size, config.vocab_size
+    kvw = config.num_key_value_heads * config.head_dim
+    out = {"model.embed_tokens.weight": (V, H), "model.norm.weight": (H,), "lm_head.weight": (V, H)}
+    for i in range(config.num_layers):
+        p = f"model.layers.{i}"
+        out.update({f"{p}.input_layernorm.weight": (H,), f"{p}.post_attention_layernorm.weight": (H,),
+                    f"{p}.self_attn.q_proj.weight": (H, H), f"{p}.self_attn.k_proj.weight": (kvw, H),
+                    f"{p}.self_attn.v_proj.weight": (kvw, H), f"{p}.self_attn.o_proj.weight": (H, H),
+                    f"{p}.mlp.gate_proj.weight": (I, H), f"{p}.mlp.up_proj.weight": (I, H),
+                    f"{p}.mlp.down_proj.weight": (H, I)})
+    return out
+
+
+def check_llama_archive(config: LlamaConfig, archive) -> tuple:
+    """LlamaModel.load's checks (LlamaModel.scala:158-173) before any device work: the archive holds
+    exactly the expected names (lm_head optional when tied), each with its shape and an F32 / F16 /
+    BF16 dtype, and a head stored beside tied embeddings equals them bit for bit (after widening).
+    The device keeps matrices in their on-disk half type, so the matrices must also share one of
+    BF16 / F16.  Returns (weight dtype STB_BF16 / STB_F16, whether a tied head is stored)."""
+    expected = llama_weight_shapes(config)
+    optional = {"lm_head.weight"} if config.tie_word_embeddings else set()
+    names = set(archive.tensors)
+    require(set(expected) - optional <= names <= set(expected), "Llama weight names mismatch")
+    for name in sorted(names):
+        info = archive.tensors[name]
+        require(tuple(info.shape) == expected[name] and info.dtype in ("F32", "F16", "BF16"),
+                f"Llama weight metadata mismatch: {name}")
+    uploaded = names - optional  # a head stored beside tied embeddings is checked, not uploaded
+    dtypes = {archive.tensors[n].dtype for n in uploaded if len(expected[n]) == 2}
+    require(len(dtypes) == 1 and next(iter(dtypes)) in ("BF16", "F16"),
+            "Llama matrices must share one BF16/F16 dtype (they stay half precision on the device)")
+    tied_head = config.tie_word_embeddings and "lm_head.weight" in names
+    if tied_head:
+        head, emb = archive.tensors["lm_head.weight"], archive.tensors["model.embed_tokens.weight"]
+        require(np.array_equal(_float_bits(archive.read_raw("lm_head.weight"), head.dtype),
+                               _float_bits(archive.read_raw("model.embed_tokens.weight"), emb.dtype)),
+                "conflicting tied lm_head weight")
+    return (STB_BF16 if next(iter(dtypes)) == "BF16" else STB_F16), tied_head
+
+
+def _float_bits(raw: np.ndarray, dtype: str) -> np.ndarray:
+    """Float32 bit patterns of a raw payload, widened as SafeTensors.readFloat does."""
+    if dtype == "BF16":
+        return raw.astype(np.uint32) << 16
+    if dtype == "F16":
+        return raw.view(np.float16).astype(np.float32).view(np.uint32)
+    return raw.view(np.uint32)
+
+
 def load_safetensors(session: B200Session, directory: str, weight_dtype: int | None = None,
-                     tp_rank: int = 0, tp_size: int = 1) -> BackendLlama:
-    """LlamaModel.load + BackendLlama.prepare with raw half uploads (no F32 widening on the host)."""
+                     tp_rank: int = 0, tp_size: int = 1, read_limits=None, shard_limits=None) -> BackendLlama:
+    """LlamaModel.load + BackendLlama.prepare with raw half uploads (no F32 widening on the host).
+    The checkpoint directory holds config.json and model.safetensors or model.safetensors.index.json
+    (SafeTensorSet.open).  read_limits.max_tensor_bytes bounds each raw payload read on the host
+    (default 1 GiB, as ReadLimits; a 70B-shaped lm_head needs it raised)."""
     import os
 
-    from .io import SafeTensorSet
+    from .io import ReadLimits, SafeTensorSet, ShardLimits
     with open(os.path.join(directory, "config.json")) as f:
         config = LlamaConfig.from_json(f.read())
-    archive = SafeTensorSet.open(directory)
-    dtypes = {archive.info(n).dtype for n in archive.names() if archive.info(n).shape and len(archive.info(n).shape) == 2}
-    require(len(dtypes) == 1 and next(iter(dtypes)) in ("BF16", "F16"), "Llama matrices must share one BF16/F16 dtype")
-    wdt = STB_BF16 if next(iter(dtypes)) == "BF16" else STB_F16
-    m = BackendLlama(session, config, weight_dtype or wdt, tp_rank, tp_size)
-    try:
-        for name in archive.names():
-            info = archive.info(name)
-            raw = archive.read_raw(name)
-            m.set_weight(name, raw, {"F32": STB_F32, "BF16": STB_BF16, "F16": STB_F16}[info.dtype])
-    except Exception:
-        m.close()
-        raise
+    with SafeTensorSet.open(directory, read_limits or ReadLimits(), shard_limits or ShardLimits()) as archive:
+        wdt, tied_head = check_llama_archive(config, archive)
+        m = BackendLlama(session, config, weight_dtype or wdt, tp_rank, tp_size)
+        try:
+            for name in archive.names():
+                if tied_head and name == "lm_head.weight":
+                    continue
+                info = archive.info(name)
+                dtype = {"F32": STB_F32, "BF16": STB_BF16, "F16": STB_F16}[info.dtype]
+                m.set_weight(name, archive.read_raw(name), dtype)
+        except BaseException:
+            m.close()
+            raise
     return m

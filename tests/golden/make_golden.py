@@ -57,6 +57,9 @@ def main(root):
     f32 = lambda b: list(struct.unpack(f"<{len(b)//4}f", b))
     cases["upstream_safetensors"] = {
         "cite": fx + "; nn/src/test/scala/scalatorch/nn/SafeWeightsSuite.scala:10-24",
+        # the whole archive, so the header reader is checked against the Rust serializer's layout
+        "archive_hex": open(os.path.join(root, fx), "rb").read().hex(),
+        "tensors": {n: {"dtype": t["dtype"], "shape": t["shape"]} for n, t in sorted(tensors.items())},
         "metadata": meta,
         "weight": f32(tensors["weight"]["bytes"]), "weight_shape": tensors["weight"]["shape"],
         "bias": f32(tensors["bias"]["bytes"]),

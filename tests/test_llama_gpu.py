@@ -12,7 +12,7 @@ import pytest
 
 from llama_fixtures import SMOL, TINY, named_bf16_weights, oracle_model
 from scalatorch import ffm
-from scalatorch.io import write_safetensors
+from scalatorch.io import write_index, write_safetensors
 from scalatorch.models import BackendLlama, LlamaConfig, load_safetensors
 
 pytestmark = pytest.mark.gpu
@@ -101,9 +101,12 @@ def test_safetensors_raw_upload_equals_device_init(session, tiny):
         open(os.path.join(d, "config.json"), "w").write(cfg)
         names = sorted(named)
         half = len(names) // 2
-        for i, part in enumerate((names[:half], names[half:])):  # a two-shard set
+        weight_map = {}
+        for i, part in enumerate((names[:half], names[half:])):  # a two-shard indexed set
             write_safetensors(os.path.join(d, f"model-{i}.safetensors"),
                               {n: ("BF16", named[n].shape, named[n]) for n in part})
+            weight_map.update({n: f"model-{i}.safetensors" for n in part})
+        write_index(d, weight_map, total_size=sum(named[n].nbytes for n in names))
         loaded = load_safetensors(session, d)
     prompt = [3, 1, 4, 1, 5, 9, 2, 6]
     with loaded, BackendLlama.prepare_random(session, tiny, seed=11) as gen:
