@@ -453,17 +453,8 @@ def linear_sweep(args, world, rank, local):
         line["e2e"] = {"value": round((n * k * 2 + m * k * 4 + m * n * 4) / e2e_t / 1e9, 2), "unit": "GB/s",
                        "h2d_bytes_per_step": m * k * 4, "d2h_bytes_per_step": m * n * 4,
                        "note": f"stb_linear_host on {names[0]} M={m} (host x in, host y out)"}
-    if not args.no_cpu_baseline and not prefill:
-        import oracle
-        x = np.random.default_rng(1).standard_normal((16, 576)).astype(np.float32)
-        wf = oracle.widen(oracle.normal_bf16(1536 * 576, 1, 1, 0.02), oracle.BF16).reshape(1536, 576)
-        t0, reps = time.perf_counter(), 0
-        while time.perf_counter() - t0 < 2.0:  # weights widened once, as SafeTensors.readFloat at load
-            oracle.matmul_tr(x, wf)
-            reps += 1
-        dt = (time.perf_counter() - t0) / reps
-        line["cpu_baseline"] = {"value": round(1904640 / dt / 1e9, 3), "unit": "GB/s", "cores": oracle.max_threads(),
-                                "kind": "port", "sample": f"single-Linear config x[16,576].W[1536,576]^T, {reps} calls"}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_linear_shapes([(LLAMA8B_SHAPES[r] + (r,)) for r in names], min(ms), prefill)
     print(json.dumps(line), flush=True)
 
 
@@ -471,22 +462,74 @@ SINGLE_M, SINGLE_N, SINGLE_K = 16, 1536, 576
 SINGLE_BYTES = SINGLE_N * SINGLE_K * 2 + SINGLE_M * SINGLE_K * 4 + SINGLE_M * SINGLE_N * 4  # 1,904,640 B
 
 
+def host_cores() -> dict:
+    """Host CPUs visible to this process (nproc) and in its affinity mask."""
+    try:
+        affinity = len(os.sched_getaffinity(0))
+    except AttributeError:
+        affinity = os.cpu_count()
+    return {"nproc": os.cpu_count(), "affinity": affinity}
+
+
+def _seconds_per_call(fn, seconds: float) -> tuple:
+    fn()  # first call outside the clock (page faults of the output)
+    t0, reps = time.perf_counter(), 0
+    while True:
+        fn()
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            return dt / reps, reps
+
+
 def cpu_single_linear(seconds: float = 3.0):
     """The reference CPU nn.Linear on the single-Linear configuration (weights widened to F32 once, as
-    SafeTensors.readFloat does at load; numscala's transposed-right order) on all host threads."""
+    SafeTensors.readFloat does at load; numscala's transposed-right order), on all host threads and
+    on one thread (numscala's ScalarF32Kernels are single-threaded)."""
     import numpy as np
 
     import oracle
     x = np.random.default_rng(1).standard_normal((SINGLE_M, SINGLE_K)).astype(np.float32)
     wf = oracle.widen(oracle.normal_bf16(SINGLE_N * SINGLE_K, 1, 1, 0.02), oracle.BF16).reshape(SINGLE_N, SINGLE_K)
-    t0, reps = time.perf_counter(), 0
-    while time.perf_counter() - t0 < seconds:
-        oracle.matmul_tr(x, wf)
-        reps += 1
-    dt = (time.perf_counter() - t0) / reps
-    return {"value": round(SINGLE_BYTES / dt / 1e9, 3), "unit": "GB/s", "cores": oracle.max_threads(), "kind": "port",
-            "sample": f"single-Linear x[16,576].W[1536,576]^T, {reps} calls in {seconds:.0f} s",
-            "us_per_call": round(dt * 1e6, 2)}
+    threads = oracle.max_threads()
+    dt, reps = _seconds_per_call(lambda: oracle.matmul_tr(x, wf, threads), seconds)
+    dt1, reps1 = _seconds_per_call(lambda: oracle.matmul_tr(x, wf, 1), seconds / 2)
+    return {"value": round(SINGLE_BYTES / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"single-Linear x[16,576].W[1536,576]^T: {reps} calls on {threads} threads, "
+                      f"{reps1} on 1 thread", "us_per_call": round(dt * 1e6, 2),
+            "single_thread": {"value": round(SINGLE_BYTES / dt1 / 1e9, 3), "us_per_call": round(dt1 * 1e6, 2)},
+            "host": host_cores()}
+
+
+def cpu_linear_shapes(shapes, m: int, prefill: bool, seconds: float = 1.0):
+    """The reference CPU path on each Llama-3-8B projection shape at M = m rows (weights widened to F32,
+    numscala order, all host threads), each on a bounded sample of output rows: up to 512 MB of
+    widened weights for decode shapes (larger than a host's last-level cache, so the sample streams
+    from DRAM as the full shape does), 128 rows for prefill (compute-bound).  The CPU cost is linear
+    in the output rows, so the time is scaled to the full N.  value aggregates the shapes as the GPU
+    line does: total algorithmic bytes (decode) or FLOPs (prefill) / total scaled time."""
+    import numpy as np
+
+    import oracle
+    threads = oracle.max_threads()
+    out, total_work, total_t = [], 0, 0.0
+    for i, (n, k, name) in enumerate(shapes):
+        rows = min(n, 128 if prefill else max(1, (512 << 20) // (4 * k)))
+        wf = oracle.widen(oracle.normal_bf16(rows * k, SEED, 100 + i, 0.02), oracle.BF16).reshape(rows, k)
+        x = np.random.default_rng(m).standard_normal((m, k)).astype(np.float32)
+        if prefill:  # activations rounded to BF16, as on the tensor-core path
+            x = oracle.widen(oracle.round_bf16(x), oracle.BF16)
+        dt, reps = _seconds_per_call(lambda: oracle.matmul_tr(x, wf, threads), seconds)
+        t_full = dt * n / rows
+        work = 2 * m * n * k if prefill else n * k * 2 + m * k * 4 + m * n * 4
+        total_work += work
+        total_t += t_full
+        out.append({"shape": name, "M": m, "rows_sampled": rows, "calls": reps, "ms_full": round(t_full * 1e3, 3)})
+    value = total_work / total_t / (1e12 if prefill else 1e9)
+    return {"value": round(value, 4), "unit": "TFLOP/s" if prefill else "GB/s", "cores": threads, "kind": "port",
+            "sample": f"each shape at M={m} on {'128 output rows' if prefill else 'up to 512 MB of F32 weight rows'}"
+                      " (or all), time scaled to the full N",
+            "shapes": out, "host": host_cores()}
 
 
 def single_linear(args, local):
@@ -684,6 +727,19 @@ def reference_arm(args, world, rank):
         metric = "single-Linear GB/s (x F32 [16,576] . W BF16 [1536,576]^T, L2 flushed before each call)"
         config = {"workload": "single Linear", "M": SINGLE_M, "N": SINGLE_N, "K": SINGLE_K}
         scaling, unit = "weak", "GB/s"
+    elif args.workload in ("linear", "prefill"):
+        prefill = args.workload == "prefill"
+        ms = tuple(int(v) for v in args.ms.split(",")) if args.ms else ((2048, 8192) if prefill else (1, 4, 16, 32))
+        names = [n for n in LLAMA8B_SHAPES if not args.shapes or n in args.shapes.split(",")]
+        for i in range(max(args.warmup, 0) + args.steps):
+            r = cpu_linear_shapes([(LLAMA8B_SHAPES[n] + (n,)) for n in names], min(ms), prefill, seconds=0.5)
+            if i >= args.warmup:
+                samples.append(r)
+        metric = ("prefill GEMM TFLOP/s (Llama-3-8B projections, BF16 weights, activations rounded to BF16)"
+                  if prefill else f"decode GEMV GB/s at M={min(ms)} (Llama-3-8B projections, BF16 weights, FP32 "
+                  "activations)")
+        config = {"workload": f"llama3-8b {args.workload} sweep", "M": min(ms), "shapes": names}
+        scaling, unit = "weak", samples[0]["unit"]
     elif args.workload == "llama70b":
         for i in range(max(args.warmup, 0) + args.steps):
             r = cpu_baseline_70b_layer()
