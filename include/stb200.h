@@ -133,7 +133,8 @@ typedef struct stb_adapter {
 int stb_linear_adapted(stb_session *s, uint64_t x, uint64_t w, int w_dtype, uint64_t bias,
                        const stb_adapter *adapters, int count, uint64_t y, int M, int N, int K);
 /* Host-buffer form used for end-to-end measurement: copies x from host, runs stb_linear against
- * the resident weight, copies y back.  Synchronous. */
+ * the resident weight, copies y back.  Synchronous.  Requests of up to 64 MiB of x and y keep one
+ * grow-only device buffer in the session between calls (charged to its budget). */
 int stb_linear_host(stb_session *s, const float *x_host, uint64_t w, int w_dtype, uint64_t bias,
                     float *y_host, int M, int N, int K);
 

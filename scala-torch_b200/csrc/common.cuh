@@ -71,6 +71,9 @@ struct stb_session {
   void *staging = nullptr;  // pinned host staging for pageable transfers
   uint64_t staging_bytes = 0;
   cudaEvent_t staging_done[2] = {nullptr, nullptr};
+  bool staging_pending[2] = {false, false};  // an upload from that half may still be in flight
+  int *err_host = nullptr;                   // pinned copy of the device error word, read at each sync
+  uint64_t io_buf = 0, io_bytes = 0;         // grow-only device buffer of the host-buffer Linear
   void *nccl = nullptr;  // ncclComm_t
   void *peer = nullptr;  // PeerComm (peer.cu): IPC-mapped receive buffers of the TP group
   int tp_rank = 0, tp_size = 1;
@@ -104,7 +107,9 @@ uint64_t session_scratch(stb_session *s, uint64_t bytes);
 // Device error word kernels write when a bounded wait expires (allocated and zeroed on first use).
 int *session_error_word(stb_session *s);
 // After a stream synchronisation: throws (and clears the word) if a kernel recorded an error.
-void check_device_error(stb_session *s);
+// Completes the session stream and reports an expired device wait, reading the error word with
+// the same synchronisation.
+void sync_and_check(stb_session *s);
 
 // ---------------------------------------------------------------- launch helpers
 

@@ -425,8 +425,12 @@ bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w) {
   static const int enabled = env_int("STB_SKINNY", 1);
   static const int min_rows = env_int("STB_SKINNY_MIN_ROWS", 2);
   static const int max_rows = env_int("STB_SKINNY_MAX_ROWS", 1 << 30);
+  // Below ~16M multiply-adds the three launches cost more than the SIMT GEMV's one (measured: the
+  // single-Linear 16 x 1536 x 576 takes 12.3 us on the GEMV, 13.3 us here; 32 x 1536 x 576 takes
+  // 18.4 us on the GEMV, 13.3 us here).
+  static const int min_work = env_int("STB_SKINNY_MIN_WORK", 1 << 24);
   return enabled && w_dtype == STB_BF16 && M >= std::max(1, min_rows) && M <= max_rows && K % 8 == 0 && K >= BK &&
-         N >= SK_BM && ((uintptr_t)w % 16) == 0;
+         N >= SK_BM && ((uintptr_t)w % 16) == 0 && (int64_t)M * N * K > (int64_t)min_work;
 }
 
 void skinny_prepare(int device) {

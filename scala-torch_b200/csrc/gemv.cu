@@ -228,6 +228,22 @@ int stb_linear_host(stb_session *s, const float *x_host, uint64_t w, int w_dtype
     enter(s);
     STB_REQUIRE(M >= 0 && N >= 0 && K >= 0, "Linear dimensions must be nonnegative");
     const uint64_t xb = (uint64_t)M * K * 4, yb = (uint64_t)M * N * 4;
+    const uint64_t xr = (xb + 255) & ~255ull;
+    if (xr + yb <= (64ull << 20)) {
+      // Small requests (every decode-sized call) reuse one grow-only device buffer, charged to the
+      // session budget like any allocation: no allocation, free or extra synchronisation per call.
+      if (s->io_bytes < xr + yb) {
+        if (s->io_buf) session_free(s, s->io_buf);
+        s->io_buf = 0;
+        s->io_bytes = 0;
+        s->io_buf = session_alloc(s, xr + yb);
+        s->io_bytes = xr + yb;
+      }
+      upload(s, x_host, xb, s->io_buf);
+      linear(s, s->io_buf, K, w, w_dtype, bias, s->io_buf + xr, N, M, N, K);
+      download(s, s->io_buf + xr, y_host, yb);
+      return;
+    }
     uint64_t dx = 0, dy = 0;
     try {
       dx = session_alloc(s, xb);

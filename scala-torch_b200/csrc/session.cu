@@ -70,14 +70,28 @@ int *session_error_word(stb_session *s) {
   return (int *)s->err_word;
 }
 
-void check_device_error(stb_session *s) {
+// Enqueues the copy of the device error word into pinned host memory (before a stream sync).
+static void enqueue_error_read(stb_session *s) {
   if (!s->err_word) return;
-  int code = 0;
-  STB_CUDA(cudaMemcpy(&code, (const void *)s->err_word, 4, cudaMemcpyDeviceToHost));
-  if (code) {
-    STB_CUDA(cudaMemset((void *)s->err_word, 0, 4));
-    throw Error(STB_ERR_CUDA, "a device-side wait expired (code " + std::to_string(code) + "); results are invalid");
-  }
+  if (!s->err_host) STB_CUDA(cudaHostAlloc((void **)&s->err_host, 64, cudaHostAllocDefault));
+  STB_CUDA(cudaMemcpyAsync(s->err_host, (const void *)s->err_word, 4, cudaMemcpyDeviceToHost, s->stream));
+}
+
+// After the stream sync that followed enqueue_error_read: every staged upload has landed, and a
+// nonzero error word is cleared and reported.
+static void finish_error_read(stb_session *s) {
+  s->staging_pending[0] = s->staging_pending[1] = false;
+  if (!s->err_word || !*s->err_host) return;
+  const int code = *s->err_host;
+  *s->err_host = 0;
+  STB_CUDA(cudaMemset((void *)s->err_word, 0, 4));
+  throw Error(STB_ERR_CUDA, "a device-side wait expired (code " + std::to_string(code) + "); results are invalid");
+}
+
+void sync_and_check(stb_session *s) {
+  enqueue_error_read(s);
+  STB_CUDA(cudaStreamSynchronize(s->stream));
+  finish_error_read(s);
 }
 
 void check_launch(const char *what) {
@@ -154,48 +168,50 @@ void upload(stb_session *s, const void *host, uint64_t bytes, uint64_t dst) {
   }
   // Pageable source: double-buffered pinned staging, ordered on the session stream, so the copy
   // never races a later kernel (the pageable-HtoD hazard of docs/research/backend-llama.md:40-42).
+  // The caller's buffer is free again on return (its bytes are in the staging half); a half is
+  // refilled only after its previous copy completed (its event, or a later stream sync).
   ensure_staging(s);
   uint64_t done = 0;
   int slot = 0;
-  bool used[2] = {false, false};
   while (done < bytes) {
     uint64_t n = bytes - done < kStagingChunk ? bytes - done : kStagingChunk;
     char *stage = (char *)s->staging + slot * kStagingChunk;
-    if (used[slot]) STB_CUDA(cudaEventSynchronize(s->staging_done[slot]));
+    if (s->staging_pending[slot]) STB_CUDA(cudaEventSynchronize(s->staging_done[slot]));
     std::memcpy(stage, (const char *)host + done, n);
     STB_CUDA(cudaMemcpyAsync((char *)dst + done, stage, n, cudaMemcpyHostToDevice, s->stream));
     STB_CUDA(cudaEventRecord(s->staging_done[slot], s->stream));
-    used[slot] = true;
+    s->staging_pending[slot] = true;
     done += n;
     slot ^= 1;
   }
-  for (int i = 0; i < 2; i++)
-    if (used[i]) STB_CUDA(cudaEventSynchronize(s->staging_done[i]));
 }
 
 void download(stb_session *s, uint64_t src, void *host, uint64_t bytes) {
   if (!bytes) {
-    STB_CUDA(cudaStreamSynchronize(s->stream));
-    check_device_error(s);
+    sync_and_check(s);
     return;
   }
   STB_REQUIRE(host && src, "download requires host and device buffers");
   if (is_pinned(host)) {
     STB_CUDA(cudaMemcpyAsync(host, (const void *)src, bytes, cudaMemcpyDeviceToHost, s->stream));
-    STB_CUDA(cudaStreamSynchronize(s->stream));
-    check_device_error(s);
+    sync_and_check(s);
     return;
   }
+  // Pageable destination through the staging buffer (stream order puts these copies after any
+  // staged upload still reading it).  The error word rides with the first chunk's sync.
   ensure_staging(s);
   uint64_t done = 0;
+  bool first = true;
   while (done < bytes) {
     uint64_t n = bytes - done < 2 * kStagingChunk ? bytes - done : 2 * kStagingChunk;
     STB_CUDA(cudaMemcpyAsync(s->staging, (const char *)src + done, n, cudaMemcpyDeviceToHost, s->stream));
+    if (first) enqueue_error_read(s);
     STB_CUDA(cudaStreamSynchronize(s->stream));
+    if (first) finish_error_read(s);
+    first = false;
     std::memcpy((char *)host + done, s->staging, n);
     done += n;
   }
-  check_device_error(s);
 }
 
 }  // namespace stb
@@ -245,6 +261,7 @@ int stb_session_destroy(stb_session *s) {
     for (auto &ev : s->staging_done)
       if (ev) cudaEventDestroy(ev);
     if (s->staging) cudaFreeHost(s->staging);
+    if (s->err_host) cudaFreeHost(s->err_host);
     cudaStreamDestroy(s->stream);
     s->closed = true;
     delete s;
@@ -315,8 +332,7 @@ int stb_copy(stb_session *s, uint64_t dst, uint64_t src, uint64_t bytes) {
 int stb_sync(stb_session *s) {
   return guarded([&] {
     enter(s);
-    STB_CUDA(cudaStreamSynchronize(s->stream));
-    check_device_error(s);
+    sync_and_check(s);
   });
 }
 

@@ -72,15 +72,19 @@ def test_decode_batches(session, m):
     close(run_linear(session, x, w, ffm.STB_BF16), oracle.linear(x, w, oracle.BF16))
 
 
-@pytest.mark.parametrize("m,n,k", [(2, 1000, 1000), (9, 128, 64), (16, 1000, 4104), (17, 300, 2048),
-                                   (40, 1536, 576), (64, 2500, 1000), (100, 576, 576), (300, 1536, 576)])
+SKINNY_SHAPES = [(2, 1000, 1000), (9, 128, 64), (16, 1000, 4104), (17, 300, 2048), (40, 1536, 576), (64, 2500, 1000),
+                 (100, 576, 576), (300, 1536, 576)]
+SKINNY_MIN_WORK = 1 << 24  # products up to this many multiply-adds take the GEMV
+
+
+@pytest.mark.parametrize("m,n,k", SKINNY_SHAPES)
 def test_skinny_tensor_core_form(session, m, n, k):
-    """Two or more rows with BF16 weights run on the tensor cores (per 64-row block: prologue,
-    stream-K GEMM, fixup), activations split into three BF16 terms: still within the FP32 GEMV
-    tolerance.
+    """Two or more rows with BF16 weights and more than 2^24 multiply-adds run on the tensor cores
+    (per 64-row block: prologue, stream-K GEMM, fixup), activations split into three BF16 terms:
+    still within the FP32 GEMV tolerance; smaller products take the one-launch GEMV.
     Ragged N (tile tails), K tails below one 64-wide block, bias; repeated calls are identical.
     Magnitudes as the single-Linear configuration (x ~ N(0,1), W ~ N(0, 0.02)): the bound is relative
-    to |y| ~ 1."""
+    to |y| ~ 1.  test_skinny_form_on_small_products runs the small shapes on the tensor cores too."""
     rng = np.random.default_rng(m * 7 + n)
     x = rng.standard_normal((m, k)).astype(np.float32)
     w = oracle.normal_bf16(n * k, seed=m, stream=9, std=0.02).reshape(n, k)
@@ -88,13 +92,47 @@ def test_skinny_tensor_core_form(session, m, n, k):
     xd, wd, bd = session.upload(x), session.upload_weight(w, ffm.STB_BF16), session.upload(b)
     l0 = session.launches
     y1 = session.linear(xd, wd, bd)
-    assert session.launches - l0 == 3 * ((m + 63) // 64)
+    assert session.launches - l0 == (3 * ((m + 63) // 64) if m * n * k > SKINNY_MIN_WORK else 1)
     y2 = session.linear(xd, wd, bd)
     a1, a2 = session.download(y1), session.download(y2)
     for t in (xd, wd, bd, y1, y2):
         session.release(t)
     assert np.array_equal(a1.view(np.uint32), a2.view(np.uint32))
     close(a1, oracle.linear(x, w, oracle.BF16, b))
+
+
+def test_skinny_form_on_small_products():
+    """The skinny tensor-core form forced onto the products the library routes to the GEMV
+    (STB_SKINNY_MIN_WORK=0, read once per process: a child process) keeps its tolerance and launch
+    count on every shape of test_skinny_tensor_core_form."""
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    paths = [here, os.path.dirname(here), os.path.join(os.path.dirname(here), "scala-torch_b200")]
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = {paths!r}\n"
+        "import oracle\n"
+        "from scalatorch import ffm\n"
+        "from test_linear_gpu import SKINNY_SHAPES, close\n"
+        "s = ffm.B200Session(0, 8 << 30)\n"
+        "for m, n, k in SKINNY_SHAPES:\n"
+        "    rng = np.random.default_rng(m * 7 + n)\n"
+        "    x = rng.standard_normal((m, k)).astype(np.float32)\n"
+        "    w = oracle.normal_bf16(n * k, seed=m, stream=9, std=0.02).reshape(n, k)\n"
+        "    b = rng.standard_normal(n).astype(np.float32)\n"
+        "    xd, wd, bd = s.upload(x), s.upload_weight(w, ffm.STB_BF16), s.upload(b)\n"
+        "    l0 = s.launches\n"
+        "    y = s.linear(xd, wd, bd)\n"
+        "    assert s.launches - l0 == 3 * ((m + 63) // 64), (m, n, k)\n"
+        "    close(s.download(y), oracle.linear(x, w, oracle.BF16, b))\n"
+        "    for t in (xd, wd, bd, y):\n"
+        "        s.release(t)\n"
+        "s.close()\n"
+        "print('ok')\n")
+    env = dict(os.environ, STB_SKINNY_MIN_WORK="0")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
 
 
 def test_f16_weights_and_bias(session):
