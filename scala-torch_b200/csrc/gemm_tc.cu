@@ -189,6 +189,205 @@ __global__ void __launch_bounds__(256, 1)
                               : "memory");
 }
 
+// ---- CTA-pair form: a cluster of 2 CTAs (one per SM) computes 256 x 256 output tiles with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16).  CTA rank r loads rows [128 r, 128 r + 128)
+// of the tile's x block and of its W block into its own shared memory (the MMA reads both halves of
+// B from the two SMs), and holds rows [128 r, 128 r + 128) of the accumulator in its own TMEM.
+// Per SM and K-block that is 32 KB of TMA writes and 32 KB of operand reads for 256x256x64 / 2
+// multiply-adds, two thirds of the single-CTA form's shared-memory traffic per product.
+//   both CTAs  warp 0: TMA producer; completion bytes of both CTAs count on the leader's full barrier
+//   leader     warp 1: issues the pair MMAs, commits to its own empty / accumulator barriers
+//   leader     warp 3: forwards those phases to the peer's barriers (remote mbarrier arrivals)
+//   both CTAs  warps 4..7: epilogue of their 128 rows; every epilogue thread of both CTAs arrives
+//              on the leader's accumulator-empty barrier
+// Waits are bounded as in gemm_tc_kernel and poll at CTA scope (a cluster-scope acquire on every
+// poll throttled the MMA thread to half the single-CTA rate); the cross-CTA signals are release
+// arrivals that follow completed work (MMA commits, finished TMEM loads).  Both CTAs meet at
+// cluster barriers before TMEM is freed.
+constexpr int BM2 = 256, BN2 = 256, STAGES2 = 6;
+constexpr int A2_BYTES = (BM2 / 2) * BK * 2, B2_BYTES = (BN2 / 2) * BK * 2, STAGE2_BYTES = A2_BYTES + B2_BYTES;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, TcParams p,
+                    uint32_t idesc) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *bars = (uint64_t *)(smem + STAGES2 * STAGE2_BYTES);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + STAGES2);
+  const uint32_t tfull0 = smem_u32(bars + 2 * STAGES2), tempty0 = smem_u32(bars + 2 * STAGES2 + 2);
+  const uint32_t drain = smem_u32(bars + 2 * STAGES2 + 4);
+  uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES2 + 5);
+  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+  const uint32_t rank = cluster_rank();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mtiles = (p.M + BM2 - 1) / BM2, ntiles = (p.N + BN2 - 1) / BN2;
+  const int tiles = mtiles * ntiles, kblocks = (p.K + BK - 1) / BK;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; s++) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 256);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA use
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sa0 = smem_u32(smem), sb0 = sa0 + STAGES2 * A2_BYTES;
+  const uint32_t full_lead0 = map_to_rank(full0, 0), tempty_lead0 = map_to_rank(tempty0, 0);
+
+  if (warp == 0 && lane == 0) {
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = pair; tile < tiles && !*abort_flag; tile += pairs) {
+      const int mb = tile % mtiles, nb = tile / mtiles;
+      for (int kb = 0; kb < kblocks; kb++) {
+        if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, p.err, 11)) break;
+        if (rank == 0) mbar_expect_tx(full0 + 8 * stage, 2 * STAGE2_BYTES);
+        tma_load_2d_pair(sa0 + stage * A2_BYTES, &ta, kb * BK, mb * BM2 + (int)rank * (BM2 / 2),
+                         full_lead0 + 8 * stage);
+        tma_load_2d_pair(sb0 + stage * B2_BYTES, &tb, kb * BK, nb * BN2 + (int)rank * (BN2 / 2),
+                         full_lead0 + 8 * stage);
+        if (++stage == STAGES2) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    int stage = 0, it = 0;
+    uint32_t phase = 0;
+    bool issued = false;
+    for (int tile = pair; tile < tiles && !*abort_flag; tile += pairs, it++) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, abort_flag, p.err, 12)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(acc * BN2);
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; kb++) {
+        if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, p.err, 13)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t a = smem_desc(sa0 + stage * A2_BYTES), b = smem_desc(sb0 + stage * B2_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; k++)
+          mma_f16_pair(d, a + (uint64_t)(2 * k), b + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+        issued = true;
+        mma_commit_pair(empty0 + 8 * stage);
+        if (++stage == STAGES2) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      mma_commit_pair(tfull0 + 8 * acc);
+    }
+    if (issued) {
+      mma_commit_pair(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, p.err, 14);
+    }
+  } else if (warp == 3 && lane == 0 && rank == 0) {
+    // Forwarder: the leader's empty / accumulator-full phases, in the order the MMA thread
+    // completes them, become arrivals on the peer's barriers of the same offsets.
+    const uint32_t empty_peer0 = map_to_rank(empty0, 1), tfull_peer0 = map_to_rank(tfull0, 1);
+    int stage = 0, it = 0;
+    uint32_t phase = 0;
+    for (int tile = pair; tile < tiles && !*abort_flag; tile += pairs, it++) {
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; kb++) {
+        if (!mbar_wait(empty0 + 8 * stage, phase, abort_flag, p.err, 15)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_cluster(empty_peer0 + 8 * stage);
+        if (++stage == STAGES2) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      const int acc = it & 1;
+      if (!mbar_wait(tfull0 + 8 * acc, (it >> 1) & 1, abort_flag, p.err, 16)) break;
+      mbar_arrive_cluster(tfull_peer0 + 8 * acc);
+    }
+  } else if (warp >= 4) {
+    const int q = warp & 3;
+    int it = 0;
+    for (int tile = pair; tile < tiles && !*abort_flag; tile += pairs, it++) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      const int mb = tile % mtiles, nb = tile / mtiles;
+      if (!mbar_wait(tfull0 + 8 * acc, acc_phase, abort_flag, p.err, 17)) break;
+      tc_fence_after();
+      const int row = mb * BM2 + (int)rank * (BM2 / 2) + q * 32 + lane;
+      float *yrow = p.y + (size_t)row * p.ldy;
+      const float *rrow = p.residual ? p.residual + (size_t)row * p.ldr : nullptr;
+      for (int c = 0; c < BN2 / 32; c++) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN2 + c * 32), r);
+        const int n0 = nb * BN2 + c * 32;
+        if (row < p.M && n0 < p.N) {
+          if (n0 + 32 <= p.N && (p.ldy & 3) == 0 && (!rrow || (p.ldr & 3) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                     __uint_as_float(r[j + 3]));
+              if (p.bias) {
+                v.x = v.x + p.bias[n0 + j];
+                v.y = v.y + p.bias[n0 + j + 1];
+                v.z = v.z + p.bias[n0 + j + 2];
+                v.w = v.w + p.bias[n0 + j + 3];
+              }
+              if (rrow) {
+                const float4 res = *reinterpret_cast<const float4 *>(rrow + n0 + j);
+                v.x = res.x + v.x;
+                v.y = res.y + v.y;
+                v.z = res.z + v.z;
+                v.w = res.w + v.w;
+              }
+              *reinterpret_cast<float4 *>(yrow + n0 + j) = v;
+            }
+          } else {
+            for (int j = 0; j < 32 && n0 + j < p.N; j++) {
+              float v = __uint_as_float(r[j]);
+              if (p.bias) v = v + p.bias[n0 + j];
+              if (rrow) v = rrow[n0 + j] + v;
+              yrow[n0 + j] = v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(tempty_lead0 + 8 * acc);
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no CTA frees TMEM or exits while its pair may still signal its barriers
+  tc_fence_after();
+  if (warp == 2) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                              : "memory");
+}
+
 // x (Float32) -> weight type, round to nearest even, 8 elements per thread.
 template <bool BF16>
 __global__ void round_activations_kernel(const float *x, uint16_t *out, size_t count) {
@@ -219,11 +418,62 @@ uint32_t tc_idesc(int dtype) {
   return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
+// The same for the CTA-pair MMA: M = 256, N = 256.
+static uint32_t tc2_idesc(int dtype) {
+  const uint32_t ab = dtype == STB_BF16 ? 1u : 0u;
+  return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(BN2 >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+}
+
+// Pairs of SMs the CTA-pair kernel can keep resident at once (clusters of 2 at one CTA per SM).
+static int resident_pairs(int device) {
+  static std::mutex mu;
+  static int pairs[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (device >= 0 && device < 64 && pairs[device]) return pairs[device];
+  STB_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(sm_count(device) & ~1));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = SMEM2_BYTES;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = sm_count(device) / 2;
+  }
+  if (device >= 0 && device < 64) pairs[device] = n;
+  return n;
+}
+
+static void gemm_tc2_launch(const void *xh, const void *w, int dtype, const float *bias, float *y, int ldy, int M,
+                            int N, int K, int *err, int device, cudaStream_t stream, const float *residual,
+                            int ldr) {
+  const CUtensorMap ta = make_map(xh, dtype, (uint64_t)M, (uint64_t)K, BM2 / 2);
+  const CUtensorMap tb = make_map(w, dtype, (uint64_t)N, (uint64_t)K, BN2 / 2);
+  TcParams p{M, N, K, ldy, y, bias, err, residual, ldr};
+  const int tiles = ((M + BM2 - 1) / BM2) * ((N + BN2 - 1) / BN2);
+  const int pairs = std::min(tiles, resident_pairs(device));
+  gemm_tc2_kernel<<<2 * pairs, 256, SMEM2_BYTES, stream>>>(ta, tb, p, tc2_idesc(dtype));
+  check_launch("gemm_tc2");
+}
+
 // Enqueues the prefill GEMM on `stream`.  xh: the activations already in the weight's type
 // (M x K, row-major); err: device int that receives a nonzero code if a wait expired.
 // residual (optional, may alias y): y = residual + (x.W^T + bias), the residual add of a Llama block.
+// STB_GEMM_PAIR=1 selects the CTA-pair kernel.
 void gemm_tc_launch(const void *xh, const void *w, int dtype, const float *bias, float *y, int ldy, int M, int N,
                     int K, int *err, int device, cudaStream_t stream, const float *residual, int ldr) {
+  static const int use_pair = env_int("STB_GEMM_PAIR", 0);
+  if (use_pair) {
+    gemm_tc2_launch(xh, w, dtype, bias, y, ldy, M, N, K, err, device, stream, residual, ldr);
+    return;
+  }
   const CUtensorMap ta = make_map(xh, dtype, (uint64_t)M, (uint64_t)K, BM);
   const CUtensorMap tb = make_map(w, dtype, (uint64_t)N, (uint64_t)K, BN);
   TcParams p{M, N, K, ldy, y, bias, err, residual, ldr};

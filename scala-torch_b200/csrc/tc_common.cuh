@@ -1,7 +1,8 @@
 // tcgen05 / TMA / mbarrier building blocks shared by the tensor-core kernels (gemm_tc.cu,
 // gemm_skinny.cu): bounded mbarrier waits, 2-D TMA loads, sm_100 shared-memory descriptors
 // (K-major, 128-byte swizzle), kind::f16 MMA issue/commit, TMEM loads, and the host-side tensor-map
-// encoder.  Nothing here issues a cluster-shared load: every CTA loads its own tiles.
+// encoder.  Nothing here issues a cluster-shared load: every CTA loads its own tiles (the CTA-pair
+// load only counts its bytes on the pair leader's barrier).
 #pragma once
 
 #include <cuda.h>
@@ -91,6 +92,58 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b,
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// ---- CTA-pair (cta_group::2) forms: two CTAs of a cluster compute one 256-row tile, each SM
+// holding half of A and half of B in its own shared memory and half of D in its own TMEM.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared::cluster address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+// Arrival on an mbarrier of any CTA in the cluster, ordered after this thread's prior accesses.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-D TMA load into this CTA's shared memory whose completion bytes count on an mbarrier of
+// either CTA of the pair (here: the pair leader's).  No multicast: each CTA loads its own box.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y,
+                                                 uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                             uint32_t accum) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+// Arrives once on this CTA's mbarrier when every pair MMA issued so far has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Every thread of both CTAs (the warp is reconverged first: role branches diverge within warps).
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }

@@ -90,3 +90,32 @@ def test_llama8b_prefill_shapes_sampled_rows(session):
         assert np.linalg.norm(sub - full) / np.linalg.norm(full) <= 2e-3, name
         del w, x
         torch.cuda.empty_cache()
+
+
+def test_cta_pair_kernel_matches_oracle():
+    """The opt-in CTA-pair GEMM (STB_GEMM_PAIR=1: tcgen05.mma.cta_group::2, 256 x 256 tiles split over
+    two SMs) on the shapes above, in a child process because the switch is read once per process."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    paths = [here, os.path.dirname(here), os.path.join(os.path.dirname(here), "scala-torch_b200")]
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = {paths!r}\n"
+        "import oracle\n"
+        "from scalatorch import ffm\n"
+        "from test_prefill_gpu import check, run_prefill\n"
+        "s = ffm.B200Session(0, 8 << 30)\n"
+        "for m, n, k in [(128, 256, 64), (256, 512, 576), (300, 1000, 200), (1, 8, 8), (129, 257, 136),\n"
+        "                (1000, 3000, 1024)]:\n"
+        "    rng = np.random.default_rng(m * 7 + n + k)\n"
+        "    x = rng.standard_normal((m, k)).astype(np.float32)\n"
+        "    w = oracle.normal_bf16(n * k, seed=m, stream=n, std=0.02).reshape(n, k)\n"
+        "    b = rng.standard_normal(n).astype(np.float32)\n"
+        "    check(run_prefill(s, x, w, ffm.STB_BF16, b), x, w, oracle.BF16, b)\n"
+        "s.close()\n"
+        "print('ok')\n")
+    env = dict(os.environ, STB_GEMM_PAIR="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
