@@ -138,6 +138,21 @@ def cpu_baseline_smol(seconds_budget: float = 20.0, model=None, with_model: bool
         r = {"value": NEW / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
              "sample": f"{PROMPT}-token prefill {t_prefill:.2f} s + {per_token * 1000:.1f} ms/token measured over "
                        f"{n} tokens, extrapolated to {NEW} tokens"}
+    # One host thread (numscala's ScalarF32Kernels run single-threaded): decode rate only, on a
+    # 4-token prompt, so the sample stays a few seconds.
+    model.threads = 1
+    try:
+        short = prompt[:4]
+        t0 = time.perf_counter()
+        model.generate(short, 1)
+        t1 = time.perf_counter()
+        model.generate(short, 3)
+        per_token_1 = max((time.perf_counter() - t1 - (t1 - t0)) / 2, 1e-6)
+    finally:
+        model.threads = threads
+    r["single_thread"] = {"decode_ms_per_token": round(per_token_1 * 1000, 1),
+                          "decode_tokens_s": round(1.0 / per_token_1, 3)}
+    r["host"] = host_cores()
     return (r, model) if with_model else r
 
 
@@ -645,10 +660,17 @@ def cpu_baseline_70b_layer():
     for i in range(n):
         model.decode(cache, np.array([[i + 20]]))
     per_layer = (time.perf_counter() - t0) / n
+    model.threads = 1  # one host thread, as numscala's ScalarF32Kernels
+    t0 = time.perf_counter()
+    model.decode(cache, np.array([[n + 20]]))
+    per_layer_1 = time.perf_counter() - t0
     model.free_cache(cache)
     return {"value": round(1.0 / (per_layer * 80), 5), "unit": "tokens/s", "cores": oracle.max_threads(),
             "kind": "port", "sample": f"1 of 80 decoder layers, batch 1, {n} decode steps after a 16-token context: "
-                                      f"{per_layer * 1000:.0f} ms/layer/token x 80 layers"}
+                                      f"{per_layer * 1000:.0f} ms/layer/token x 80 layers",
+            "single_thread": {"value": round(1.0 / (per_layer_1 * 80), 5),
+                              "ms_per_layer_token": round(per_layer_1 * 1e3, 1)},
+            "host": host_cores()}
 
 
 LM_HEAD_TRAFFIC_BYTES = 56_646_400
