@@ -121,6 +121,37 @@ def test_safetensors_raw_upload_equals_device_init(session, tiny):
         assert loaded.weight_bytes == 2 * half_matrices + 4 * H * (2 * L + 1) + pos * (hd // 2) * 16
 
 
+def test_tied_checkpoint_with_a_stored_head_loads_once(session):
+    """A tied checkpoint that also stores lm_head.weight (equal to the embeddings) passes
+    LlamaModel.load's check (LlamaModel.scala:169-173), uploads the embeddings once and decodes as
+    the device-initialised tied model; a differing stored head is rejected before any upload."""
+    cfg = LlamaConfig(**dict(TINY, tie_word_embeddings=True))
+    named = named_bf16_weights(cfg, seed=17)
+    text = ('{"model_type":"llama","vocab_size":1000,"hidden_size":64,"intermediate_size":128,'
+            '"num_hidden_layers":2,"num_attention_heads":4,"num_key_value_heads":2,'
+            '"max_position_embeddings":64,"tie_word_embeddings":true,"eos_token_id":null}')
+    prompt = [7, 1, 8, 2, 8]
+    for head, ok in ((named["model.embed_tokens.weight"].copy(), True),
+                     (named["model.embed_tokens.weight"] ^ np.uint16(1), False)):
+        with tempfile.TemporaryDirectory() as d:
+            open(os.path.join(d, "config.json"), "w").write(text)
+            tensors = {n: ("BF16", v.shape, v) for n, v in named.items()}
+            tensors["lm_head.weight"] = ("BF16", head.shape, head)
+            write_safetensors(os.path.join(d, "model.safetensors"), tensors)
+            if not ok:
+                held = session.allocated_bytes
+                with pytest.raises(ffm.IllegalArgumentException, match="conflicting tied"):
+                    load_safetensors(session, d)
+                assert session.allocated_bytes == held
+                continue
+            loaded = load_safetensors(session, d)
+        with loaded, BackendLlama.prepare_random(session, cfg, seed=17) as gen:
+            assert loaded.weight_bytes == gen.weight_bytes
+            la, _ = loaded.new_cache(1, 16).decode([prompt])
+            lb, _ = gen.new_cache(1, 16).decode([prompt])
+            assert np.array_equal(la, lb)
+
+
 def test_tied_head_is_stored_once(session):
     cfg = LlamaConfig(**dict(TINY, tie_word_embeddings=True))
     untied = LlamaConfig(**TINY)
