@@ -443,7 +443,7 @@ def linear_sweep(args, world, rank, local):
         secs = sum(r["us"] for r in results) / 1e6
         value, unit = flops / secs / 1e12, "TFLOP/s"
         top = max(results, key=lambda r: r["us"])
-        roof = {"kernel": f"gemm_tc_kernel ({top['shape']} M={top['M']})", "bound": "tensor",
+        roof = {"kernel": f"gemm_tc2_kernel, CTA pairs ({top['shape']} M={top['M']})", "bound": "tensor",
                 "achieved": top["TFLOP_s"], "peak": tc_peak, "unit": "TFLOP/s", "frac": top["tensor_frac"],
                 "peak_source": f"{peak_kind} bf16_tflops (burst)", "traffic": None}
         metric = "prefill GEMM TFLOP/s (Llama-3-8B projections, BF16 weights, activations rounded to BF16)"

@@ -200,11 +200,10 @@ __global__ void __launch_bounds__(256, 1)
 //   leader     warp 3: forwards those phases to the peer's barriers (remote mbarrier arrivals)
 //   both CTAs  warps 4..7: epilogue of their 128 rows; every epilogue thread of both CTAs arrives
 //              on the leader's accumulator-empty barrier
-// Waits are bounded as in gemm_tc_kernel and poll at CTA scope (a cluster-scope acquire on every
-// poll throttled the MMA thread to half the single-CTA rate); the cross-CTA signals are release
-// arrivals that follow completed work (MMA commits, finished TMEM loads).  Both CTAs meet at
+// Waits are bounded as in gemm_tc_kernel and poll at CTA scope; the cross-CTA signals are relaxed
+// remote arrivals that follow completed work (MMA commits, finished TMEM loads).  Both CTAs meet at
 // cluster barriers before TMEM is freed.
-constexpr int BM2 = 256, BN2 = 256, STAGES2 = 6;
+constexpr int BM2 = 256, BN2 = 256, STAGES2 = 7;
 constexpr int A2_BYTES = (BM2 / 2) * BK * 2, B2_BYTES = (BN2 / 2) * BK * 2, STAGE2_BYTES = A2_BYTES + B2_BYTES;
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
 
@@ -466,10 +465,10 @@ static void gemm_tc2_launch(const void *xh, const void *w, int dtype, const floa
 // Enqueues the prefill GEMM on `stream`.  xh: the activations already in the weight's type
 // (M x K, row-major); err: device int that receives a nonzero code if a wait expired.
 // residual (optional, may alias y): y = residual + (x.W^T + bias), the residual add of a Llama block.
-// STB_GEMM_PAIR=1 selects the CTA-pair kernel.
+// The CTA-pair kernel by default; STB_GEMM_PAIR=0 selects the single-CTA kernel.
 void gemm_tc_launch(const void *xh, const void *w, int dtype, const float *bias, float *y, int ldy, int M, int N,
                     int K, int *err, int device, cudaStream_t stream, const float *residual, int ldr) {
-  static const int use_pair = env_int("STB_GEMM_PAIR", 0);
+  static const int use_pair = env_int("STB_GEMM_PAIR", 1);
   if (use_pair) {
     gemm_tc2_launch(xh, w, dtype, bias, y, ldy, M, N, K, err, device, stream, residual, ldr);
     return;

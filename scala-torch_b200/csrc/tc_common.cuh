@@ -110,9 +110,12 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
   return out;
 }
 
-// Arrival on an mbarrier of any CTA in the cluster, ordered after this thread's prior accesses.
+// Arrival on an mbarrier of any CTA in the cluster.  Relaxed: the pair kernel's cross-CTA arrivals
+// carry no data through memory (the MMA's reads and writes are complete at its commit, the TMEM
+// loads at tcgen05.wait::ld), and a release at cluster scope cost ~0.8 us per arrival, serialised
+// on the forwarding thread.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // 2-D TMA load into this CTA's shared memory whose completion bytes count on an mbarrier of

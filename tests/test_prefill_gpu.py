@@ -92,9 +92,10 @@ def test_llama8b_prefill_shapes_sampled_rows(session):
         torch.cuda.empty_cache()
 
 
-def test_cta_pair_kernel_matches_oracle():
-    """The opt-in CTA-pair GEMM (STB_GEMM_PAIR=1: tcgen05.mma.cta_group::2, 256 x 256 tiles split over
-    two SMs) on the shapes above, in a child process because the switch is read once per process."""
+def test_single_cta_kernel_matches_oracle():
+    """The single-CTA GEMM (STB_GEMM_PAIR=0: tcgen05.mma.cta_group::1, 128 x 256 tiles; the default is
+    the CTA-pair kernel) on the shapes above, in a child process because the switch is read once per
+    process."""
     import os
     import subprocess
     import sys
@@ -116,6 +117,6 @@ def test_cta_pair_kernel_matches_oracle():
         "    check(run_prefill(s, x, w, ffm.STB_BF16, b), x, w, oracle.BF16, b)\n"
         "s.close()\n"
         "print('ok')\n")
-    env = dict(os.environ, STB_GEMM_PAIR="1")
+    env = dict(os.environ, STB_GEMM_PAIR="0")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
