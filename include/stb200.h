@@ -159,7 +159,8 @@ typedef struct {
   int tp_rank, tp_size; /* tensor parallel coordinates; 0/1 for a single device */
   /* Chunks of at least this many token rows run their projections on the tcgen05 tensor cores
    * with activations rounded to the weight type (the prefill tolerance); smaller chunks -- every
-   * decode step -- keep Float32 activations.  0 selects the default (512); < 0 never. */
+   * decode step -- keep Float32 activations.  0 selects the default (256, the prefill threshold of the
+   * Linear path); < 0 never. */
   int tc_prefill_rows;
 } stb_llama_config;
 

@@ -66,7 +66,7 @@ struct stb_llama {
   uint64_t rope = 0;  // double2 [max_positions][hd/2]
   std::vector<uint64_t> owned;
   uint64_t weight_bytes = 0;
-  int tc_rows = 512;  // chunks of >= tc_rows token rows use the tensor-core prefill (INT_MAX: never)
+  int tc_rows = 256;  // chunks of >= tc_rows token rows use the tensor-core prefill (INT_MAX: never)
   // the last stb_llama_generate call's cache and decode graph, reused by the next call of the same
   // shape (batch, prompt + new, new, EOS count, prefill chunk)
   stb_llama_cache *gen = nullptr;
@@ -1260,7 +1260,7 @@ int stb_llama_create(stb_session *s, const stb_llama_config *config, stb_llama *
     m->c = *config;
     m->c.tp_size = tp;
     m->tp = tp;
-    m->tc_rows = config->tc_prefill_rows == 0 ? 512 : (config->tc_prefill_rows < 0 ? INT_MAX : config->tc_prefill_rows);
+    m->tc_rows = config->tc_prefill_rows == 0 ? 256 : (config->tc_prefill_rows < 0 ? INT_MAX : config->tc_prefill_rows);
     m->rank = config->tp_rank;
     m->H = config->hidden_size;
     m->hd = config->hidden_size / config->num_attention_heads;

@@ -145,7 +145,7 @@ class BackendLlama:
     def __init__(self, session: B200Session, config: LlamaConfig, weight_dtype: int = STB_BF16,
                  tp_rank: int = 0, tp_size: int = 1, tc_prefill_rows: int = 0):
         """tc_prefill_rows: chunks with at least this many token rows use the tensor-core prefill
-        (activations rounded to the weight type); 0 = library default (512), < 0 = never."""
+        (activations rounded to the weight type); 0 = library default (256), < 0 = never."""
         _declare_llama()
         require(weight_dtype in (STB_BF16, STB_F16), "Llama weights must be BF16 or F16")
         self.session = session
