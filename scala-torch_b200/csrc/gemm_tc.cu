@@ -4,7 +4,10 @@
 // weight's type (round-to-nearest-even, SafeTensorsWriter.bfloat's rule for BF16) because a
 // kind::f16 MMA takes both operands in one 16-bit type -- that rounding is the tolerance source.
 //
-// Kernel shape (one CTA per SM, persistent over 128x256 output tiles):
+// Two forms: gemm_tc2_kernel (below, the default) runs CTA pairs over 256x256 tiles;
+// gemm_tc_kernel (STB_GEMM_PAIR=0) is the single-CTA form.
+//
+// Single-CTA kernel shape (one CTA per SM, persistent over 128x256 output tiles):
 //   warp 0      TMA producer: x tile 128x64 and W tile 256x64 per stage (SWIZZLE_128B, K-major),
 //               4-stage shared-memory ring guarded by full/empty mbarriers
 //   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16) into a TMEM accumulator and
@@ -193,8 +196,9 @@ __global__ void __launch_bounds__(256, 1)
 // tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16).  CTA rank r loads rows [128 r, 128 r + 128)
 // of the tile's x block and of its W block into its own shared memory (the MMA reads both halves of
 // B from the two SMs), and holds rows [128 r, 128 r + 128) of the accumulator in its own TMEM.
-// Per SM and K-block that is 32 KB of TMA writes and 32 KB of operand reads for 256x256x64 / 2
-// multiply-adds, two thirds of the single-CTA form's shared-memory traffic per product.
+// Per SM and K-block that is 32 KB of TMA writes for the same 128x256x64 multiply-adds per SM as the
+// single-CTA form's 48 KB, so the same shared memory holds a 7-stage ring instead of 4: the refill
+// loop (TMA latency ~1 us + commit) is covered by 1.8 us of MMA work instead of 1.0 us.
 //   both CTAs  warp 0: TMA producer; completion bytes of both CTAs count on the leader's full barrier
 //   leader     warp 1: issues the pair MMAs, commits to its own empty / accumulator barriers
 //   leader     warp 3: forwards those phases to the peer's barriers (remote mbarrier arrivals)
