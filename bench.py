@@ -203,6 +203,8 @@ def main():
                     help="single: the single-Linear configuration [16,576]x[1536,576]; roofline: only the "
                     "SmolLM2 lm_head roofline leg of the default line (for profiling)")
     ap.add_argument("--shapes", default="", help="linear/prefill: comma list of shape names to run (default all)")
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16"],
+                    help="linear/prefill: weight type (F16 prefill rounds the activations to F16)")
     ap.add_argument("--ms", default="", help="linear/prefill: comma list of token-row counts M (default 1,4,16,32 "
                     "for linear, 2048,8192 for prefill)")
     ap.add_argument("--batch", type=int, default=1, help="llama70b: decode batch (1, 8, 32)")
@@ -379,6 +381,9 @@ def linear_sweep(args, world, rank, local):
     stream = torch.cuda.ExternalStream(s.stream)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     prefill = args.workload == "prefill"
+    wdt = ffm.STB_F16 if args.dtype == "f16" else ffm.STB_BF16
+    tdt = torch.float16 if args.dtype == "f16" else torch.bfloat16
+    wname = args.dtype.upper()
     ms = (2048, 8192) if prefill else (1, 4, 16, 32)
     if args.ms:
         ms = tuple(int(v) for v in args.ms.split(","))
@@ -391,8 +396,8 @@ def linear_sweep(args, world, rank, local):
         clocks.mark()
         for si, name in enumerate(names):
             n, k = LLAMA8B_SHAPES[name]
-            w = torch.empty(n * k, dtype=torch.bfloat16, device="cuda")
-            wt = ffm.DeviceTensor(s, w.data_ptr(), (k, n), ffm.STB_BF16, n * k * 2, transposed_weight=True, owner=False)
+            w = torch.empty(n * k, dtype=tdt, device="cuda")
+            wt = ffm.DeviceTensor(s, w.data_ptr(), (k, n), wdt, n * k * 2, transposed_weight=True, owner=False)
             s.fill_normal(wt, SEED, 100 + si, 0.02)
             for m in ms:
                 x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(m))
@@ -405,7 +410,7 @@ def linear_sweep(args, world, rank, local):
                         flush.zero_()
                         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                         e0.record(stream)
-                    ffm.call(fn, s.handle, x.data_ptr(), w.data_ptr(), ffm.STB_BF16, 0, y.data_ptr(), m, n, k)
+                    ffm.call(fn, s.handle, x.data_ptr(), w.data_ptr(), wdt, 0, y.data_ptr(), m, n, k)
                     e1.record(stream)
                     e1.synchronize()
                     if it >= args.warmup:
@@ -424,8 +429,8 @@ def linear_sweep(args, world, rank, local):
     # end-to-end through the host-buffer C ABI on the first shape at the smallest M
     n, k = LLAMA8B_SHAPES[names[0]]
     m = ms[0]
-    w = torch.empty(n * k, dtype=torch.bfloat16, device="cuda")
-    wt = ffm.DeviceTensor(s, w.data_ptr(), (k, n), ffm.STB_BF16, n * k * 2, transposed_weight=True, owner=False)
+    w = torch.empty(n * k, dtype=tdt, device="cuda")
+    wt = ffm.DeviceTensor(s, w.data_ptr(), (k, n), wdt, n * k * 2, transposed_weight=True, owner=False)
     s.fill_normal(wt, SEED, 100, 0.02)
     s.sync()
     hx = np.random.default_rng(0).standard_normal((m, k)).astype(np.float32)
@@ -434,7 +439,7 @@ def linear_sweep(args, world, rank, local):
     if not prefill:
         for it in range(args.warmup + args.steps):
             t0 = time.perf_counter()
-            ffm.call("stb_linear_host", s.handle, hx.ctypes.data, w.data_ptr(), ffm.STB_BF16, 0, hy.ctypes.data, m, n, k)
+            ffm.call("stb_linear_host", s.handle, hx.ctypes.data, w.data_ptr(), wdt, 0, hy.ctypes.data, m, n, k)
             dt = time.perf_counter() - t0
             e2e_t = dt if e2e_t is None or it < args.warmup else min(e2e_t, dt)
     s.close()
@@ -446,7 +451,7 @@ def linear_sweep(args, world, rank, local):
         roof = {"kernel": f"gemm_tc2_kernel, CTA pairs ({top['shape']} M={top['M']})", "bound": "tensor",
                 "achieved": top["TFLOP_s"], "peak": tc_peak, "unit": "TFLOP/s", "frac": top["tensor_frac"],
                 "peak_source": f"{peak_kind} bf16_tflops (burst)", "traffic": None}
-        metric = "prefill GEMM TFLOP/s (Llama-3-8B projections, BF16 weights, activations rounded to BF16)"
+        metric = f"prefill GEMM TFLOP/s (Llama-3-8B projections, {wname} weights, activations rounded to {wname})"
     else:
         m1 = [r for r in results if r["M"] == min(ms)]
         byts = sum(r["N"] * r["K"] * 2 + r["K"] * 4 + r["N"] * 4 for r in m1)
@@ -456,10 +461,11 @@ def linear_sweep(args, world, rank, local):
         roof = {"kernel": f"gemv_kernel ({top['shape']} M={top['M']})", "bound": "hbm", "achieved": top["GB_s"],
                 "peak": hbm_peak, "unit": "GB/s", "frac": top["hbm_frac"], "peak_source": f"{peak_kind} hbm_gbs",
                 "algorithmic_bytes": top["N"] * top["K"] * 2 + top["K"] * 4 + top["N"] * 4, "traffic": None}
-        metric = f"decode GEMV GB/s at M={min(ms)} (Llama-3-8B projections, BF16 weights, FP32 activations)"
+        metric = f"decode GEMV GB/s at M={min(ms)} (Llama-3-8B projections, {wname} weights, FP32 activations)"
     line = {"metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs * 1000 / max(len(results), 1), 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16-weights/f32-accumulate",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": f"{args.dtype}-weights/f32-accumulate",
             "data": "synthetic (device counter-RNG weights, N(0,1) activations)",
             "config": {"workload": f"llama3-8b {args.workload} sweep", "l2": "flushed (256 MB write) before every launch",
                        "shapes": results},
