@@ -119,7 +119,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 }
 
 // 2-D TMA load into this CTA's shared memory whose completion bytes count on an mbarrier of
-// either CTA of the pair (here: the pair leader's).  No multicast: each CTA loads its own box.
+// either CTA of the pair (here: the pair leader's).  Each CTA loads only its own box.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y,
                                                  uint32_t cluster_bar) {
   asm volatile(
