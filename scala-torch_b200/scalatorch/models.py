@@ -59,6 +59,8 @@ class LlamaConfig:
         require(self.head_dim % 2 == 0, "Llama rotary head width must be even")
         require(np.isfinite(self.rms_norm_eps) and self.rms_norm_eps > 0 and np.isfinite(self.rope_theta)
                 and self.rope_theta > 0, "invalid Llama norm/rotary configuration")
+        require(np.isfinite(self.initializer_range) and self.initializer_range >= 0,
+                "invalid Llama initializer range")
         require(all(0 <= i < self.vocab_size for i in ([self.bos_token_id] if self.bos_token_id is not None else [])
                     + list(self.eos_token_ids)), "special token ID out of vocabulary")
 
@@ -68,37 +70,66 @@ class LlamaConfig:
 
     @staticmethod
     def from_json(text: str) -> "LlamaConfig":
-        """LlamaConfig.fromJson (LlamaConfig.scala:44-112): strict llama/SiLU subset."""
+        """LlamaConfig.fromJson (LlamaConfig.scala:44-112): strict llama/SiLU subset with typed fields
+        (integers in [0, 2^31), finite numbers, JSON booleans, EOS as null / id / array of at most
+        1024 ids), duplicate keys, non-finite constants and configs over 1 MiB rejected."""
+        require(isinstance(text, str) and len(text) <= 1048576, "Llama config exceeds size limit")
         try:
-            f = json.loads(text, object_pairs_hook=_no_duplicates)
+            f = json.loads(text, object_pairs_hook=_no_duplicates, parse_constant=_no_constant)
         except ValueError as e:
             raise IllegalArgumentException(f"invalid Llama config JSON: {e}") from e
         require(isinstance(f, dict), "Llama config must be an object")
+        missing = object()
+
+        def integer(key, default=missing):
+            v = f.get(key, missing)
+            if v is missing and default is not missing:
+                return default
+            require(type(v) is int and 0 <= v <= 0x7FFFFFFF, f"expected nonnegative integer config: {key}")
+            return v
+
+        def number(key, default):
+            v = f.get(key, default)
+            require(type(v) in (int, float), f"expected numeric config: {key}")
+            require(np.isfinite(v), f"nonfinite config: {key}")
+            return float(v)
+
+        def boolean(key, default):
+            v = f.get(key, default)
+            require(type(v) is bool, f"expected boolean config: {key}")
+            return v
+
         require(f.get("model_type") == "llama", "only model_type=llama is supported")
         require(f.get("hidden_act", "silu") == "silu", "only SiLU Llama MLP is supported")
         for key in ("rope_scaling", "rope_parameters", "sliding_window"):
             require(f.get(key) is None, f"unsupported Llama option: {key}")
-        require(not f.get("attention_bias", False) and not f.get("mlp_bias", False), "Llama projection biases unsupported")
-        require(f.get("attention_dropout", 0.0) == 0 and f.get("pretraining_tp", 1) == 1,
+        require(not boolean("attention_bias", False) and not boolean("mlp_bias", False),
+                "Llama projection biases unsupported")
+        require(number("attention_dropout", 0.0) == 0 and integer("pretraining_tp", 1) == 1,
                 "unsupported Llama dropout/tensor parallel setting")
-        require(f.get("partial_rotary_factor", 1.0) == 1.0, "partial rotary dimensions unsupported")
-
-        def integer(key, default=None):
-            v = f.get(key, default)
-            require(isinstance(v, int) and not isinstance(v, bool) and 0 <= v <= 0x7FFFFFFF,
-                    f"expected nonnegative integer config: {key}")
-            return v
-
+        require(number("partial_rotary_factor", 1.0) == 1.0, "partial rotary dimensions unsupported")
         heads = integer("num_attention_heads")
+        bos = f.get("bos_token_id", 1)
+        require(bos is None or type(bos) is int, "invalid BOS ID")
         eos = f.get("eos_token_id", 2)
-        eos = () if eos is None else (tuple(eos) if isinstance(eos, list) else (eos,))
+        if eos is None:
+            eos = ()
+        elif type(eos) is int:
+            eos = (eos,)
+        else:
+            require(isinstance(eos, list) and len(eos) <= 1024 and all(type(i) is int for i in eos), "invalid EOS IDs")
+            eos = tuple(eos)
         c = LlamaConfig(integer("vocab_size"), integer("hidden_size"), integer("intermediate_size"),
                         integer("num_hidden_layers"), heads, integer("num_key_value_heads", heads),
-                        integer("max_position_embeddings", 2048), float(f.get("rms_norm_eps", 1e-6)),
-                        float(f.get("rope_theta", 10000.0)), bool(f.get("tie_word_embeddings", False)),
-                        f.get("bos_token_id", 1), eos, float(f.get("initializer_range", 0.02)))
+                        integer("max_position_embeddings", 2048), number("rms_norm_eps", 1e-6),
+                        number("rope_theta", 10000.0), boolean("tie_word_embeddings", False), bos, eos,
+                        number("initializer_range", 0.02))
         require(integer("head_dim", c.head_dim) == c.head_dim, "custom Llama head_dim unsupported")
         return c
+
+
+def _no_constant(name):
+    raise ValueError(f"non-numeric JSON constant {name}")
 
 
 def _no_duplicates(pairs):
