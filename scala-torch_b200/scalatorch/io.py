@@ -217,6 +217,10 @@ class SafeTensors:
     def __exit__(self, *exc):
         self.close()
 
+    def __del__(self):  # an archive dropped without close() still releases its descriptor
+        if getattr(self, "_fd", None) is not None:
+            self.close()
+
 
 def _check_filename(name: str, what: str, min_len: int) -> None:
     require(isinstance(name, str) and name.lower().endswith(".safetensors") and len(name) > min_len
