@@ -370,8 +370,6 @@ def linear_sweep(args, world, rank, local):
     prefill: tcgen05 GEMM, M = 2048/8192) on Llama-3-8B projection shapes with
     device-generated BF16 weights ~N(0,0.02).  Each launch is timed alone with CUDA events on the
     session stream after a 256 MB L2 flush; the median of the timed launches is reported."""
-    import ctypes
-
     import numpy as np
     import torch
     from scalatorch import ffm
@@ -389,7 +387,6 @@ def linear_sweep(args, world, rank, local):
         ms = tuple(int(v) for v in args.ms.split(","))
     names = [n for n in LLAMA8B_SHAPES if not args.shapes or n in args.shapes.split(",")]
     fn = "stb_linear_prefill" if prefill else "stb_linear"
-    L = ffm.library()
     results, clocks = [], Clocks(local)
     launches0 = s.launches
     with clocks:
@@ -702,8 +699,6 @@ def decode_step_roofline(decode_tok_s, hbm_peak, peak_kind, lm_head):
 def roofline_lm_head(session, cfg, hbm_peak, peak_kind):
     """The lm_head GEMV (49152 x 576 BF16, M = 1; the largest per-token kernel) timed alone with
     CUDA events on the session stream, L2 flushed (256 MB write) before every launch."""
-    import ctypes
-
     import torch
     from scalatorch import ffm
     N, K = cfg.vocab_size, cfg.hidden_size

@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import json
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 
