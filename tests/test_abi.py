@@ -3,7 +3,6 @@ host-side validation rejects bad requests before any native call."""
 import os
 import re
 
-import numpy as np
 import pytest
 
 from scalatorch import ffm

@@ -5,7 +5,6 @@ Pins the restatement before any device result is compared with it.
 import json
 import math
 import os
-import struct
 
 import numpy as np
 import pytest
