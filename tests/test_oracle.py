@@ -63,7 +63,9 @@ def test_f16_rounding_agrees_with_numpy():
     x = np.concatenate([rng.standard_normal(50000).astype(np.float32) * 1000,
                         rng.standard_normal(5000).astype(np.float32) * 1e-6,
                         np.array([65504, 65519.99, 65520, 1e-8, 2.0 ** -25, 2.0 ** -24], np.float32)])
-    assert np.array_equal(oracle.round_f16(x), x.astype(np.float16).view(np.uint16))
+    with np.errstate(over="ignore"):  # 65520 and the large normals round to infinity on purpose
+        want = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(oracle.round_f16(x), want)
 
 
 def test_upstream_safetensors_linear_is_24_52():
