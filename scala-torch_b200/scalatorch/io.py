@@ -189,14 +189,15 @@ class SafeTensors:
     def closed(self) -> bool:
         return self._fd is None
 
-    def read_raw(self, name: str) -> np.ndarray:
-        """Exact on-disk bytes as a typed view (uint16 words for BF16/F16), owned by the caller."""
+    def _info(self, name: str) -> TensorInfo:
         if self._fd is None:
             raise IllegalStateException("SafeTensors", 6, "safetensors archive is closed")
         info = self.tensors.get(name)
         require(info is not None, f"tensor not found: {name}")
+        return info
+
+    def _payload(self, info: TensorInfo) -> np.ndarray:
         size = info.end - info.begin
-        require(size <= self.limits.max_tensor_bytes, "raw tensor exceeds configured allocation limit")
         out = np.empty(size, np.uint8)
         view, done = memoryview(out), 0
         while done < size:
@@ -204,7 +205,48 @@ class SafeTensors:
             if got <= 0:
                 raise IllegalStateException("SafeTensors", 6, "truncated safetensors file")
             done += got
-        return out.view(RAW_VIEW[info.dtype]).reshape(info.shape)
+        return out
+
+    def read_raw(self, name: str) -> np.ndarray:
+        """Exact on-disk bytes as a typed view (uint16 words for BF16/F16), owned by the caller
+        (SafeTensors.readRaw, SafeTensors.scala:53-61: the raw size counts against max_tensor_bytes)."""
+        info = self._info(name)
+        require(info.end - info.begin <= self.limits.max_tensor_bytes, "raw tensor exceeds configured allocation limit")
+        return self._payload(info).view(RAW_VIEW[info.dtype]).reshape(info.shape)
+
+    def _typed(self, name: str, allowed: tuple, out_bytes: int) -> TensorInfo:
+        """SafeTensors.entry (SafeTensors.scala:28-34): dtype allowed for the typed read, and the
+        materialised output (numel x output bytes) within max_tensor_bytes."""
+        info = self._info(name)
+        require(info.dtype in allowed, f"dtype {info.dtype} is unsupported by this typed read")
+        numel = 1
+        for d in info.shape:
+            numel *= d
+        require(numel <= 0x7FFFFFFF and numel * out_bytes <= self.limits.max_tensor_bytes,
+                "tensor materialization exceeds configured allocation limit")
+        return info
+
+    def read_float(self, name: str) -> np.ndarray:
+        """SafeTensors.readFloat (SafeTensors.scala:63-77): F32 as stored; BF16 widened by a 16-bit
+        shift and F16 converted exactly, both to Float32 (the host widening the device path skips)."""
+        info = self._typed(name, ("F32", "F16", "BF16"), 4)
+        raw = self._payload(info)
+        if info.dtype == "BF16":
+            out = (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+        elif info.dtype == "F16":
+            out = raw.view(np.float16).astype(np.float32)
+        else:
+            out = raw.view(np.float32)
+        return out.reshape(info.shape)
+
+    def read_double(self, name: str) -> np.ndarray:
+        return self._payload(self._typed(name, ("F64",), 8)).view(np.float64).reshape(self.tensors[name].shape)
+
+    def read_long(self, name: str) -> np.ndarray:
+        return self._payload(self._typed(name, ("I64",), 8)).view(np.int64).reshape(self.tensors[name].shape)
+
+    def read_boolean(self, name: str) -> np.ndarray:
+        return (self._payload(self._typed(name, ("BOOL",), 1)) != 0).reshape(self.tensors[name].shape)
 
     def close(self) -> None:
         if self._fd is not None:
@@ -334,6 +376,18 @@ class SafeTensorSet:
 
     def read_raw(self, name: str) -> np.ndarray:
         return self._owner(name).read_raw(name)
+
+    def read_float(self, name: str) -> np.ndarray:
+        return self._owner(name).read_float(name)
+
+    def read_double(self, name: str) -> np.ndarray:
+        return self._owner(name).read_double(name)
+
+    def read_long(self, name: str) -> np.ndarray:
+        return self._owner(name).read_long(name)
+
+    def read_boolean(self, name: str) -> np.ndarray:
+        return self._owner(name).read_boolean(name)
 
     def close(self) -> None:
         if not self._closed:

@@ -46,7 +46,8 @@ def bad(tmp_path, header, payload=b"", **limits):
 
 
 def test_upstream_rust_archive_reads_exactly(tmp_path):
-    """The Rust safetensors 0.6.2 fixture (SafeTensorsSuite.scala:106-124) through the raw reader."""
+    """The Rust safetensors 0.6.2 fixture (SafeTensorsSuite.scala:106-124) through the raw and typed
+    readers."""
     g = GOLDEN["upstream_safetensors"]
     path = os.path.join(str(tmp_path), "upstream.safetensors")
     open(path, "wb").write(bytes.fromhex(g["archive_hex"]))
@@ -61,6 +62,13 @@ def test_upstream_rust_archive_reads_exactly(tmp_path):
         assert f.read_raw("double").tolist() == [1.25, -2.5]
         assert f.read_raw("bool").tolist() == [0, 1]
         assert f.read_raw("empty").shape == (0, 3)
+        assert f.read_float("weight").ravel().tolist() == [1, 2, 3, 4, 5, 6]
+        assert f.read_float("half").tolist() == [1, -2, 2.0 ** -24, 65504]
+        assert math.isnan(f.read_float("bfloat")[-1])
+        assert f.read_long("long").tolist() == [9007199254740993, -7]
+        assert f.read_double("double").tolist() == [1.25, -2.5]
+        assert f.read_boolean("bool").tolist() == [False, True]
+        assert f.read_float("empty").shape == (0, 3)
 
 
 def test_typed_scalars_empty_tensors_and_metadata(tmp_path):
@@ -73,8 +81,69 @@ def test_typed_scalars_empty_tensors_and_metadata(tmp_path):
         assert f.read_raw("f").tolist() == 1.5 and f.read_raw("d").tolist() == -2.25
         assert f.read_raw("l").tolist() == 9007199254740993 and f.read_raw("b").tolist() == 1
         assert f.read_raw("z").shape == (2, 0)
+        # typed reads (SafeTensorsSuite.scala:21-35)
+        assert f.read_float("f").tolist() == 1.5 and f.read_double("d").tolist() == -2.25
+        assert f.read_long("l").tolist() == 9007199254740993 and f.read_boolean("b").tolist() is True
+        assert f.read_float("z").shape == (2, 0)
+        for bad_read in (lambda: f.read_float("l"), lambda: f.read_float("missing"), lambda: f.read_raw("missing"),
+                         lambda: f.read_double("f"), lambda: f.read_long("d"), lambda: f.read_boolean("f")):
+            with pytest.raises(IllegalArgumentException):
+                bad_read()
+
+
+def _bits_of(values):
+    return [int(v) for v in np.asarray(values, np.float32).view(np.uint32)]
+
+
+def test_f16_and_bf16_widen_subnormals_signed_zero_and_nonfinite(tmp_path):
+    """SafeTensorsSuite.scala:36-53, through read_float."""
+    half = [0x0000, 0x8000, 0x0001, 0x03FF, 0x0400, 0x3C00, 0xC000, 0x7BFF, 0x7C00, 0xFC00, 0x7E01]
+    bf = [0x3F80, 0xC000, 0x0001, 0x8000, 0x7F80, 0xFF80, 0x7FC1]
+    payload = np.array(half + bf, np.uint16).tobytes()
+    header = ('{"h":' + entry("F16", f"[{len(half)}]", 0, 2 * len(half)) + ',"b":'
+              + entry("BF16", f"[{len(bf)}]", 2 * len(half), len(payload)) + '}')
+    with SafeTensors(archive(tmp_path, header, payload)) as f:
+        h = f.read_float("h")
+        assert _bits_of(h[:8]) == _bits_of([0.0, -0.0, 2.0 ** -24, 1023 * 2.0 ** -24, 2.0 ** -14, 1, -2, 65504])
+        assert h[8] == np.inf and h[9] == -np.inf and math.isnan(h[10])
+        b = f.read_float("b")
+        assert b[:3].tolist() == [1.0, -2.0, 2.0 ** -133] and _bits_of(b[3:4]) == [0x80000000]
+        assert b[4] == np.inf and b[5] == -np.inf and math.isnan(b[6])
+
+
+def test_typed_reads_count_their_float32_output_against_the_limit(tmp_path):
+    """SafeTensorsSuite.scala:75-95: a typed read counts the widened output (4 bytes per F16 word)."""
+    half = archive(tmp_path, '{"x":' + entry("F16", "[1]", 0, 2) + '}', bytes([0, 0x3C]), name="h.safetensors")
+    with SafeTensors(half, ReadLimits(max_tensor_bytes=2)) as f:
+        assert f.tensors["x"].end == 2
         with pytest.raises(IllegalArgumentException):
-            f.read_raw("missing")
+            f.read_float("x")  # decoded Float32 needs 4 bytes
+        assert f.read_raw("x").view(np.float16).tolist() == [1.0]
+    with SafeTensors(half, ReadLimits(max_tensor_bytes=4)) as f:
+        assert f.read_float("x").tolist() == [1.0]
+
+
+def test_typed_decoders_cross_read_chunks(tmp_path):
+    """SafeTensorsSuite.scala:96-105, 135-157."""
+    n = 20000
+    vals = (np.arange(n) / 8).astype(np.float32)
+    with SafeTensors(archive(tmp_path, '{"x":' + entry("F32", f"[{n}]", 0, 4 * n) + '}', vals.tobytes())) as f:
+        assert np.array_equal(f.read_float("x"), vals)
+    n = 40000
+    for dtype, words, expected in (("F16", [0x3C00, 0xC000, 0x0001, 0x7BFF], [1.0, -2.0, 2.0 ** -24, 65504.0]),
+                                   ("BF16", [0x3F80, 0xC000, 0x0001, 0x7F7F],
+                                    [1.0, -2.0, 2.0 ** -133, (2.0 - 1.0 / 128) * 2.0 ** 127])):
+        payload = np.array(words * (n // 4), np.uint16).tobytes()
+        path = archive(tmp_path, '{"x":' + entry(dtype, f"[{n}]", 0, 2 * n) + '}', payload,
+                       name=f"{dtype}.safetensors")
+        with SafeTensors(path) as f:
+            assert np.array_equal(f.read_float("x"), np.array(expected * (n // 4), np.float32))
+    count = 10000
+    doubles = np.arange(count) + 0.125
+    path = archive(tmp_path, '{"x":' + entry("F64", f"[{count}]", 0, 8 * count) + '}', doubles.tobytes(),
+                   name="d.safetensors")
+    with SafeTensors(path) as f:
+        assert np.array_equal(f.read_double("x"), doubles)
 
 
 @pytest.mark.parametrize("header,payload", [
@@ -178,10 +247,12 @@ def test_indexed_sets_route_reads_and_close(tmp_path):
     _fixture(d)
     s = SafeTensorSet.open(d)
     assert set(s.tensors) == {"a", "b"}
-    a = s.read_raw("a")
-    assert s.read_raw("b").tolist() == [-2.0]
+    a = s.read_float("a")
+    assert s.read_float("b").tolist() == [-2.0] and s.read_raw("b").tolist() == [-2.0]
     with pytest.raises(IllegalArgumentException):
-        s.read_raw("missing")
+        s.read_float("missing")
+    with pytest.raises(IllegalArgumentException):
+        s.read_long("a")
     s.close()
     s.close()
     assert a.tolist() == [1.25]
@@ -351,3 +422,16 @@ def test_tied_head_must_equal_the_embeddings(tmp_path):
             else:
                 with pytest.raises(IllegalArgumentException, match="conflicting tied"):
                     check_llama_archive(cfg, s)
+
+
+def test_indexed_set_keeps_the_upstream_fixture_dtypes(tmp_path):
+    """ShardSuite.scala:61-74: typed reads through an index over the Rust-written archive."""
+    d = str(tmp_path)
+    g = GOLDEN["upstream_safetensors"]
+    open(os.path.join(d, "typed.safetensors"), "wb").write(bytes.fromhex(g["archive_hex"]))
+    write_index(d, {n: "typed.safetensors" for n in g["tensors"]})
+    with SafeTensorSet.open(d) as s:
+        assert s.read_double("double").tolist() == [1.25, -2.5]
+        assert s.read_long("long").tolist() == [9007199254740993, -7]
+        assert s.read_boolean("bool").tolist() == [False, True]
+        assert s.read_float("half")[0] == 1.0
