@@ -435,3 +435,65 @@ def test_indexed_set_keeps_the_upstream_fixture_dtypes(tmp_path):
         assert s.read_long("long").tolist() == [9007199254740993, -7]
         assert s.read_boolean("bool").tolist() == [False, True]
         assert s.read_float("half")[0] == 1.0
+
+
+def test_random_header_values_fail_only_as_invalid_arguments(tmp_path):
+    """Any JSON value in any field of a tensor entry either opens consistently or is rejected with
+    IllegalArgumentException (never another exception type), as the reference's parser does."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+
+    scalars = st.one_of(st.none(), st.booleans(), st.integers(-2 ** 70, 2 ** 70), st.floats(allow_nan=False),
+                        st.text(max_size=6))
+    values = st.recursive(scalars, lambda c: st.one_of(st.lists(c, max_size=3),
+                                                       st.dictionaries(st.text(max_size=4), c, max_size=3)),
+                          max_leaves=6)
+    fields = st.fixed_dictionaries({}, optional={"dtype": st.one_of(st.sampled_from(["F32", "BF16", "I64"]), values),
+                                                 "shape": st.one_of(st.lists(st.integers(0, 3), max_size=3), values),
+                                                 "data_offsets": st.one_of(st.lists(st.integers(0, 16), max_size=3),
+                                                                           values),
+                                                 "extra": values})
+
+    @settings(max_examples=300, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+    @given(fields, st.integers(0, 16))
+    def check(entry_obj, payload_len):
+        path = archive(tmp_path, json.dumps({"x": entry_obj}), bytes(payload_len), name="fuzz.safetensors")
+        try:
+            with SafeTensors(path) as f:
+                info = f.tensors["x"]
+                assert info.end - info.begin == payload_len and f.read_raw("x").nbytes == payload_len
+        except IllegalArgumentException:
+            pass
+
+    check()
+
+
+def test_random_index_documents_fail_only_as_invalid_arguments(tmp_path):
+    """Any JSON document as model.safetensors.index.json either opens or is rejected with
+    IllegalArgumentException (SafeTensorsIndex.read's contract)."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+
+    d = str(tmp_path)
+    _shard(d, "a.safetensors", "a", 1.25)
+    scalars = st.one_of(st.none(), st.booleans(), st.integers(-5, 10), st.floats(allow_nan=False),
+                        st.sampled_from(["a", "a.safetensors", "b.safetensors", "../a.safetensors", ""]))
+    values = st.recursive(scalars, lambda c: st.one_of(st.lists(c, max_size=3),
+                                                       st.dictionaries(st.sampled_from(["a", "b", "total_size"]), c,
+                                                                       max_size=3)),
+                          max_leaves=6)
+    docs = st.one_of(values, st.fixed_dictionaries({}, optional={"weight_map": values, "metadata": values,
+                                                                 "other": values}))
+
+    @settings(max_examples=300, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+    @given(docs)
+    def check(doc):
+        with open(os.path.join(d, "model.safetensors.index.json"), "w") as f:
+            json.dump(doc, f)
+        try:
+            with SafeTensorSet.open(d) as s:
+                assert set(s.tensors) == {"a"} and s.read_float("a").tolist() == [1.25]
+        except IllegalArgumentException:
+            pass
+
+    check()
