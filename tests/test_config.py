@@ -78,3 +78,33 @@ def test_weight_shapes_follow_the_config():
 def test_configs_over_one_mib_reject():
     with pytest.raises(IllegalArgumentException):
         LlamaConfig.from_json(with_field('"pad":"' + "x" * 1048576 + '"'))
+
+
+def test_random_field_values_fail_only_as_invalid_arguments():
+    """Any JSON value in any recognised field either parses into a valid LlamaConfig or raises
+    IllegalArgumentException, never another exception type."""
+    import json
+
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    keys = ["vocab_size", "hidden_size", "intermediate_size", "num_hidden_layers", "num_attention_heads",
+            "num_key_value_heads", "max_position_embeddings", "rms_norm_eps", "rope_theta", "tie_word_embeddings",
+            "bos_token_id", "eos_token_id", "initializer_range", "head_dim", "hidden_act", "attention_dropout",
+            "pretraining_tp", "rope_scaling", "model_type"]
+    scalars = st.one_of(st.none(), st.booleans(), st.integers(-3, 40), st.floats(allow_nan=False, width=32),
+                        st.sampled_from(["llama", "silu", "relu", ""]))
+    values = st.one_of(scalars, st.lists(scalars, max_size=3), st.dictionaries(st.sampled_from(["a"]), scalars))
+    base = json.loads(BASE)
+
+    @settings(max_examples=500, deadline=None)
+    @given(st.dictionaries(st.sampled_from(keys), values, max_size=4))
+    def check(changes):
+        doc = dict(base, **changes)
+        try:
+            c = LlamaConfig.from_json(json.dumps(doc))
+        except IllegalArgumentException:
+            return
+        assert c.hidden_size % c.num_attention_heads == 0 and c.head_dim % 2 == 0
+
+    check()
