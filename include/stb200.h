@@ -106,8 +106,11 @@ int stb_linear_prefill(stb_session *s, uint64_t x, uint64_t w, int w_dtype, uint
  * of the session's scratch, so M * K must not exceed 8,388,608 (larger requests are rejected with
  * STB_ERR_INVALID).  Runs on `stream` (a cudaStream_t, NULL for the legacy stream) of the current
  * device and returns after the product is complete.  All calls share the array: calls that
- * overlap on the GPU (other threads or streams) race.  The first call on a device looks up the
- * array's address; make it before any stream capture. */
+ * overlap on the GPU (other threads or streams) race.  The first call on a device is its set-up:
+ * it loads the library's device code there (with CUDA's lazy module loading, that places the
+ * 16 MiB + 256 byte array and the kernels in device memory) and looks up the array's address; make
+ * it during warm-up, before any stream capture.  Later calls allocate nothing.  A cudaDeviceReset
+ * while the library is loaded is not supported (the kept address would dangle). */
 int stb_linear_prefill_static(void *stream, uint64_t x, uint64_t w, int w_dtype, uint64_t bias, uint64_t y,
                               int M, int N, int K);
 /* One low-rank adapter term of nn.Linear.apply (nn/src/main/scala/scalatorch/nn/Linear.scala:11-17;

@@ -133,11 +133,17 @@ __global__ void __launch_bounds__(256) skinny_prep_kernel(const float *x, int ld
       v = x[(size_t)m * ldx + k];
       if (norm_w) v = __double2float_rn(__dmul_rn(__dmul_rn((double)v, inv), (double)norm_w[k]));
     }
-    const uint16_t h0 = f32_to_bf16_rne(v);
-    const float r1 = v - __uint_as_float((uint32_t)h0 << 16);  // exact
-    const uint16_t h1 = f32_to_bf16_rne(r1);
-    const float r2 = r1 - __uint_as_float((uint32_t)h1 << 16);  // exact
-    const uint16_t h2 = f32_to_bf16_rne(r2);
+    // Non-finite v keeps its class in the first term alone (Inf - Inf would make the lower terms
+    // NaN); a finite v that rounds past BF16's largest finite value (|v| > 0x1.fep127) takes the
+    // truncated first term instead, which stays finite and leaves an exact 16-bit remainder.
+    uint16_t h0 = f32_to_bf16_rne(v), h1 = 0, h2 = 0;
+    if (isfinite(v)) {
+      if ((h0 & 0x7f80u) == 0x7f80u) h0 = (uint16_t)(__float_as_uint(v) >> 16);
+      const float r1 = v - __uint_as_float((uint32_t)h0 << 16);  // exact
+      h1 = f32_to_bf16_rne(r1);
+      const float r2 = r1 - __uint_as_float((uint32_t)h1 << 16);  // exact
+      h2 = f32_to_bf16_rne(r2);
+    }
     x3[(size_t)m * K + k] = h0;
     x3[((size_t)NT + m) * K + k] = h1;
     x3[((size_t)2 * NT + m) * K + k] = h2;

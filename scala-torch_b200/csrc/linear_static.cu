@@ -11,8 +11,13 @@
 //   * the rounded activations must fit the array: M * K <= STB_PREFILL_STATIC_MAX_ELEMENTS;
 //   * every call uses the same array, so calls that overlap on the GPU (other host threads or
 //     streams) race on it; each call finishes its work before returning;
-//   * the first call on a device looks up the array's device address (cudaGetSymbolAddress) with
-//     that device current; make that first call before any stream capture.
+//   * the first call on a device is its set-up: it loads the library's device code on that device
+//     (under CUDA's lazy module loading that is where the array, 16 MiB + 256 bytes, and the kernels
+//     are placed in device memory) and looks up the array's device address (cudaGetSymbolAddress)
+//     with that device current; make that first call during warm-up, before any stream capture.
+//     Later calls allocate nothing;
+//   * the address is kept per device for the life of the process: a cudaDeviceReset while the
+//     library is loaded is not supported (the array is reloaded elsewhere, the kept address dangles).
 #include <mutex>
 
 #include "common.cuh"
@@ -77,9 +82,11 @@ int stb_linear_prefill_static(void *stream, uint64_t x, uint64_t w, int w_dtype,
     STB_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st));
     round_activations((const float *)x, (uint16_t *)scratch, (size_t)M * K, w_dtype, st);
     gemm_tc_launch(scratch, (const void *)w, w_dtype, (const float *)bias, (float *)y, N, M, N, K, err, device, st);
-    STB_CUDA(cudaStreamSynchronize(st));
+    // The error word comes back on the same stream, so the one synchronisation below waits for this
+    // call's work only (no legacy-stream copy that would also wait for other streams' work).
     int code = 0;
-    STB_CUDA(cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost));
+    STB_CUDA(cudaMemcpyAsync(&code, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    STB_CUDA(cudaStreamSynchronize(st));
     if (code) throw Error(STB_ERR_CUDA, "a device-side wait expired (code " + std::to_string(code) + ")");
   });
 }

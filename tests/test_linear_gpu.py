@@ -135,6 +135,81 @@ def test_skinny_form_on_small_products():
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
 
 
+FLT_MAX = float(np.finfo(np.float32).max)
+SPECIALS = ("inf", "-inf", "nan", "max", "-max", "subnormal")
+NONFINITE_MS = (1, 2, 17, 64)
+
+
+def nonfinite_case(m, rotation, n=256, k=576):
+    """x ~ N(0,1) [m,k] with one IEEE special per row (row r gets SPECIALS[(r + rotation) % 6] at column
+    (7 r + 3) % k; "subnormal" makes the whole row subnormal), W ~ N(0,0.02) BF16 [n,k] with row 5 all
+    zeros (0 x Inf = NaN, as the reference's CPU product gives).  One special per row keeps every
+    finite sum far from overflow, so the reduction order cannot decide a row's class."""
+    rng = np.random.default_rng(1000 * m + rotation)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    for r in range(m):
+        kind, col = SPECIALS[(r + rotation) % len(SPECIALS)], (7 * r + 3) % k
+        if kind == "subnormal":
+            x[r] = (rng.standard_normal(k) * 1e-39).astype(np.float32)
+        else:
+            x[r, col] = {"inf": np.inf, "-inf": -np.inf, "nan": np.nan, "max": FLT_MAX, "-max": -FLT_MAX}[kind]
+    w = oracle.normal_bf16(n * k, seed=m, stream=40 + rotation, std=0.02).reshape(n, k)
+    w[5] = 0
+    return x, w
+
+
+def same_class(y, ref, tol=TOL):
+    """IEEE class element for element (NaN where NaN, the same signed infinities), finite values
+    within tol * (1 + |e|)."""
+    assert np.array_equal(np.isnan(y), np.isnan(ref)), "NaN positions differ"
+    assert np.array_equal(np.isposinf(y), np.isposinf(ref)) and np.array_equal(np.isneginf(y), np.isneginf(ref)), \
+        "infinities differ"
+    fin = np.isfinite(ref)
+    close(y[fin], ref[fin], tol)
+
+
+def test_nonfinite_activations_on_the_gemv(session):
+    """The reference's CPU Linear keeps IEEE semantics (cpu/src/test/scala/scalatorch/cpu/BackendSuite.scala:22-43):
+    +-Inf, NaN, +-FLT_MAX and subnormal activations on the products the library runs as the vector GEMV
+    (M = 1, and every M below the skinny form's work threshold)."""
+    for m in NONFINITE_MS:
+        for rot in range(len(SPECIALS)):
+            x, w = nonfinite_case(m, rot)
+            same_class(run_linear(session, x, w, ffm.STB_BF16), oracle.linear(x, w, oracle.BF16))
+
+
+def test_nonfinite_activations_on_the_skinny_form():
+    """The same IEEE cases on the tensor-core skinny form (STB_SKINNY_MIN_WORK=0 routes M >= 2 there; read
+    once per process, so a child process): the three-term BF16 split keeps Inf / NaN in its first term
+    and truncates a finite value above BF16's largest, so no Inf - Inf appears."""
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    paths = [here, os.path.dirname(here), os.path.join(os.path.dirname(here), "scala-torch_b200")]
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = {paths!r}\n"
+        "import oracle\n"
+        "from scalatorch import ffm\n"
+        "from test_linear_gpu import NONFINITE_MS, SPECIALS, nonfinite_case, same_class\n"
+        "s = ffm.B200Session(0, 8 << 30)\n"
+        "for m in NONFINITE_MS:\n"
+        "    for rot in range(len(SPECIALS)):\n"
+        "        x, w = nonfinite_case(m, rot)\n"
+        "        xd, wd = s.upload(x), s.upload_weight(w, ffm.STB_BF16)\n"
+        "        l0 = s.launches\n"
+        "        y = s.linear(xd, wd)\n"
+        "        assert s.launches - l0 == (1 if m == 1 else 3), (m, s.launches - l0)\n"
+        "        same_class(s.download(y), oracle.linear(x, w, oracle.BF16))\n"
+        "        for t in (xd, wd, y):\n"
+        "            s.release(t)\n"
+        "s.close()\n"
+        "print('ok')\n")
+    env = dict(os.environ, STB_SKINNY_MIN_WORK="0")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
+
+
 def test_f16_weights_and_bias(session):
     rng = np.random.default_rng(3)
     x = rng.standard_normal((4, 4096)).astype(np.float32)
