@@ -57,7 +57,7 @@ SINGLE_BYTES = SINGLE_N * SINGLE_K * 2 + SINGLE_M * SINGLE_K * 4 + SINGLE_M * SI
 # SHA-256 (first 16 hex digits) of the generated ids (batch x new, int64, row-major) of the default
 # workload on one GPU, seed 2024: the tensor-parallel runs must reproduce it.  Keyed by
 # (batch, prompt, new, layers).  Recorded from `python bench.py` on a B200 (TP1).
-TP1_IDS_DIGEST = {}
+TP1_IDS_DIGEST = {"8/512/32/80": "e72b121d2e701b81"}
 
 # DRAM read + write bytes of one gemm_skinny_kernel launch on the dominant decode shape (70B gate/up
 # shard, M = 8, TP1: 57344 x 8192 BF16 = 939.5 MB of weights), from one ncu capture
@@ -175,7 +175,7 @@ def describe(args, world: int) -> tuple:
     if w == "single":
         return ("single-Linear GB/s (x F32 [16,576] . W BF16 [1536,576]^T, L2 flushed before each call)", "GB/s",
                 "weak", {"workload": "single Linear", "M": SINGLE_M, "N": SINGLE_N, "K": SINGLE_K,
-                         "l2": "flushed (256 MB write) before every call"})
+                         "l2": "flushed before every call (256 MB write, then 256 MB read of another buffer)"})
     prefill = w == "prefill"
     ms = sweep_ms(args)
     names = sweep_names(args)
@@ -186,7 +186,7 @@ def describe(args, world: int) -> tuple:
         metric = f"decode GEMV GB/s at M={min(ms)} (Llama-3-8B projections, {wname} weights, FP32 activations)"
     return (metric, "TFLOP/s" if prefill else "GB/s", "weak",
             {"workload": f"llama3-8b {w} sweep", "M": list(ms), "shapes": names,
-             "l2": "flushed (256 MB write) before every launch"})
+             "l2": "flushed before every launch (256 MB write, then 256 MB read of another buffer)"})
 
 
 def sweep_ms(args):
@@ -241,8 +241,24 @@ def ids_digest(ids) -> str:
     return hashlib.sha256(np.ascontiguousarray(ids, np.int64).tobytes()).hexdigest()[:16]
 
 
+class L2Flush:
+    """Evicts the timed kernel's data from the 126 MB L2 before each call: a 256 MB write (the timing
+    rule), then a 256 MB read of a second buffer, so the write's dirty lines are written back before
+    the timed kernel starts instead of during it (they would add up to 126 MB of DRAM writes that
+    are not the kernel's own)."""
+
+    def __init__(self):
+        import torch
+        self.write = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.read = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+
+    def __call__(self):
+        self.write.zero_()
+        self.read.sum()
+
+
 def timed_linear(session, fn, x_addr, w_addr, wdt, y_addr, m, n, k, reps, warm, flush):
-    """Each call alone between CUDA events on the session stream, L2 flushed (256 MB write on the same
+    """Each call alone between CUDA events on the session stream, L2 flushed (L2Flush, on the same
     stream) before every call; returns the median seconds of the `reps` calls after `warm`."""
     import torch
     from scalatorch import ffm
@@ -250,7 +266,7 @@ def timed_linear(session, fn, x_addr, w_addr, wdt, y_addr, m, n, k, reps, warm, 
     times = []
     for it in range(warm + reps):
         with torch.cuda.stream(stream):
-            flush.zero_()
+            flush()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
         ffm.call(fn, session.handle, x_addr, w_addr, wdt, 0, y_addr, m, n, k)
@@ -277,7 +293,7 @@ def linear_roofline(session, name, m, n, k, hbm_peak, peak_kind, reps=10, warm=3
     tensor-core form = prologue + gemm_skinny_kernel + fixup, three PDL-chained launches)."""
     import torch
     from scalatorch import ffm
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = L2Flush()
     w = device_weight(session, n, k, ffm.STB_BF16, SEED, 900)
     x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(m))
     y = torch.empty(m, n, device="cuda")
@@ -364,7 +380,7 @@ def run_llama70b(args, world, rank, local):
     step_gbs = model.weight_bytes / per_tok / 1e9
     roof["step"] = {"what": "decode step, all kernels: this rank's weight bytes per token / decode time per token",
                     "achieved": round(step_gbs, 1), "frac": round(step_gbs / hbm_peak, 4),
-                    "weight_bytes_per_rank": model.weight_bytes, "launches_per_token": None}
+                    "weight_bytes_per_rank": model.weight_bytes}
     if world > 1:
         dist.barrier()
 
@@ -386,7 +402,6 @@ def run_llama70b(args, world, rank, local):
         "parity": {"ids_digest": digest, "ranks_agree": agree, "tp1_digest": expected,
                    "tp_ids_match": (agree and digest == expected) if expected else None},
     }
-    roof["step"]["launches_per_token"] = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = cpu_baseline_70b_layer(batch)
@@ -509,7 +524,7 @@ def smollm2_record(local, steps, warmup, hbm_peak, peak_kind, parity=True, cpu=T
 
 def single_record(local, steps, warmup, hbm_peak, peak_kind, cpu=True, calls=100):
     """The single-Linear configuration (x F32 [16,576] ~N(0,1), W BF16 [1536,576] ~N(0,0.02), no bias)
-    through stb_linear.  Cold: a 256 MB L2 flush before every call and CUDA events around each call
+    through stb_linear.  Cold: an L2 flush (L2Flush) before every call and CUDA events around each call
     alone (the reported value, against HBM); warm: `calls` back-to-back calls between one event pair
     (the 1.8 MB weight stays in L2).  e2e: stb_linear_host with host x and y, wall clock per call."""
     import numpy as np
@@ -518,7 +533,7 @@ def single_record(local, steps, warmup, hbm_peak, peak_kind, cpu=True, calls=100
     torch.cuda.set_device(local)
     s = ffm.B200Session(local, 4 << 30)
     stream = torch.cuda.ExternalStream(s.stream)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = L2Flush()
     M, N, K = SINGLE_M, SINGLE_N, SINGLE_K
     w = device_weight(s, N, K, ffm.STB_BF16, 1, 1)
     hx = np.random.default_rng(1).standard_normal((M, K)).astype(np.float32)
@@ -565,12 +580,12 @@ def single_record(local, steps, warmup, hbm_peak, peak_kind, cpu=True, calls=100
 def linear_sweep_record(local, prefill, ms, names, dtype, steps, warmup, hbm_peak, tc_peak, peak_kind, cpu=True):
     """Llama-3-8B projection shapes: stb_linear (decode family, FP32 activations) or stb_linear_prefill
     (tcgen05 GEMM, activations rounded to the weight type), each launch timed alone with CUDA events
-    on the session stream after a 256 MB L2 flush; the median of the timed launches per shape."""
+    on the session stream after an L2 flush (L2Flush); the median of the timed launches per shape."""
     import torch
     from scalatorch import ffm
     torch.cuda.set_device(local)
     s = ffm.B200Session(local, 100 << 30)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = L2Flush()
     wdt = ffm.STB_F16 if dtype == "f16" else ffm.STB_BF16
     fn = "stb_linear_prefill" if prefill else "stb_linear"
     results = []

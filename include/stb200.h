@@ -141,6 +141,59 @@ int stb_linear_adapted(stb_session *s, uint64_t x, uint64_t w, int w_dtype, uint
 int stb_linear_host(stb_session *s, const float *x_host, uint64_t w, int w_dtype, uint64_t bias,
                     float *y_host, int M, int N, int K);
 
+/* ---------------------------------------------------------------- FloatBackend operator set
+ *
+ * The rest of trait FloatBackend (core/src/main/scala/scalatorch/FloatBackend.scala:7-31) as the
+ * reference's generic BackendLlama drives it (models/src/main/scala/scalatorch/models/
+ * BackendLlama.scala:41-111), one kernel each on the session stream.  Buffers are Float32 device
+ * addresses, packed row-major; outputs are caller-allocated (stb_alloc) and may not alias inputs
+ * unless stated.  Arithmetic is the reference CPU backend's (CpuFloatBackend.scala,
+ * CpuAttention.scala): add / multiply / scale one Float32 operation per element; SiLU, RMSNorm,
+ * RoPE and attention in double, rounded once.  Shape rules that the reference checks with
+ * require(...) are checked by the host binding before the call; the calls themselves reject what
+ * would be out of bounds (STB_ERR_INVALID).  reshape is a view (host-side: no call), fill is
+ * stb_fill_value. */
+
+/* FloatBackend.add / multiply (CpuFloatBackend.scala:61-67): y[i] = a[i] + b[i] / a[i] * b[i]. */
+int stb_op_add(stb_session *s, uint64_t a, uint64_t b, uint64_t y, uint64_t count);
+int stb_op_multiply(stb_session *s, uint64_t a, uint64_t b, uint64_t y, uint64_t count);
+/* FloatBackend.scale (CpuFloatBackend.scala:68-69): y[i] = x[i] * scalar, IEEE nonfinite included. */
+int stb_op_scale(stb_session *s, uint64_t x, uint64_t y, uint64_t count, float scalar);
+/* FloatBackend.silu (CpuFloatBackend.scala:70-77): x * sigmoid(x) in double. */
+int stb_op_silu(stb_session *s, uint64_t x, uint64_t y, uint64_t count);
+/* FloatBackend.sum (CpuFloatBackend.scala:31-32): all elements into one Float32 at y, accumulated in
+ * double (a fixed tree: deterministic for a given count). */
+int stb_op_sum(stb_session *s, uint64_t x, uint64_t count, uint64_t y);
+/* FloatBackend.expandScalar (CpuFloatBackend.scala:33-35): y[i] = *x, no host transfer. */
+int stb_op_expand_scalar(stb_session *s, uint64_t x, uint64_t y, uint64_t count);
+/* FloatBackend.rmsNorm (CpuFloatBackend.scala:78-93) over the last axis of `rows` rows of `width`:
+ * squares summed in double, y = (float)(x * (1 / sqrt(sum / width + eps)) * w[j]). */
+int stb_op_rmsnorm(stb_session *s, uint64_t x, uint64_t w, uint64_t y, uint64_t rows, int width, double eps);
+/* FloatBackend.rope (CpuAttention.scala:6-18, RotaryCoefficients AttentionLayout.scala:23-34) on
+ * (batch, heads, tokens, width): pairs (d, d + width/2) rotated by the host-computed double
+ * coefficients of positions start .. start + tokens - 1. */
+int stb_op_rope(stb_session *s, uint64_t x, uint64_t y, int batch, int heads, int tokens, int width, int start,
+                double theta);
+/* FloatBackend.transpose (CudaSession.scala:469-485): a packed copy with axes dim0 and dim1 of the
+ * rank-`rank` (<= 8) input `dims` swapped. */
+int stb_op_transpose(stb_session *s, uint64_t x, uint64_t y, int rank, const int64_t *dims, int dim0, int dim1);
+/* FloatBackend.embedding (CpuFloatBackend.scala:49-59; CudaSession.scala:487-500): rows ids[0..count) of a (rows, width) table
+ * in F32, BF16 or F16 (half rows widened exactly) into y (count, width).  ids are host int64 and
+ * must lie in [0, rows). */
+int stb_op_embedding(stb_session *s, uint64_t table, int dtype, int64_t rows, int width, const int64_t *ids,
+                     uint64_t count, uint64_t y);
+/* AttentionCache.attend's append (CudaSession.scala:414-419): src (batch, heads, tokens, width) into
+ * the cache (batch, heads, capacity, width) at token `position`. */
+int stb_op_cache_append(stb_session *s, uint64_t src, uint64_t cache, int batch, int heads, int tokens, int width,
+                        int capacity, int position);
+/* FloatBackend.causalAttention (CpuAttention.scala:20-50): q (batch, heads, tokens, width); k, v
+ * (batch, kv_heads, key_stride, width / value_width) of which the first `keys` tokens are read;
+ * query token t of the chunk sees keys j < min(keys, start + t + 1).  Scores, softmax and the
+ * weighted sum in double.  keys <= 24576 (STB_ERR_UNSUPPORTED above). */
+int stb_op_causal_attention(stb_session *s, uint64_t q, uint64_t k, uint64_t v, uint64_t y, int batch, int heads,
+                            int tokens, int width, int kv_heads, int keys, int key_stride, int value_width,
+                            int start);
+
 /* ---------------------------------------------------------------- synthetic weights */
 
 /* Counter-based N(0, std) weights rounded F32 -> half with RNE (SafeTensorsWriter.bfloat,

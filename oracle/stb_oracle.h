@@ -61,9 +61,9 @@ void oracle_linear_adapted(const float *x, const void *w, int w_dtype, const flo
                            const float *scale, const int *scoped, const float *multiplier, int count,
                            float *y, int M, int N, int K, int threads);
 
-/* CpuFloatBackend.rmsNorm, cpu/src/main/scala/scalatorch/cpu/CpuFloatBackend.scala:80-93 */
+/* CpuFloatBackend.rmsNorm, cpu/src/main/scala/scalatorch/cpu/CpuFloatBackend.scala:78-93 */
 void oracle_rmsnorm(const float *x, const float *w, float *y, int rows, int width, double eps);
-/* CpuFloatBackend.silu, CpuFloatBackend.scala:72-79 */
+/* CpuFloatBackend.silu, CpuFloatBackend.scala:70-77 */
 float oracle_silu(float x);
 /* CpuAttention.rope on (batch,heads,tokens,width), cpu/src/main/scala/scalatorch/cpu/
  * CpuAttention.scala:6-18 with RotaryCoefficients, core/src/main/scala/scalatorch/

@@ -10,7 +10,7 @@
 // so every output is produced by exactly one group in a fixed order: results are deterministic.
 //
 // Optional fused pieces for the Llama decode step:
-//   * RMSNorm prologue (CpuFloatBackend.rmsNorm, cpu/.../CpuFloatBackend.scala:80-93): the block
+//   * RMSNorm prologue (CpuFloatBackend.rmsNorm, cpu/.../CpuFloatBackend.scala:78-93): the block
 //     computes each token row's inverse RMS in double and normalises x chunks as it loads them,
 //     (float)((double)x * inverse * w), the reference's expression.
 //   * epilogues: bias, residual add (LlamaBlock h = x + f(x), LlamaModel.scala:49-52), SiLU(gate)*up
@@ -90,7 +90,7 @@ __device__ __forceinline__ int argmax_key_index(unsigned long long key) {
   return (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
 }
 
-// SiLU of CpuFloatBackend.silu (CpuFloatBackend.scala:72-79), in double.
+// SiLU of CpuFloatBackend.silu (CpuFloatBackend.scala:70-77), in double.
 __device__ __forceinline__ float silu_ref(float x) {
   double v = (double)x;
   double sigmoid;

@@ -712,7 +712,7 @@ __global__ void finalize_kernel(const unsigned long long *best_all, unsigned lon
 
 // ---- tensor-core prefill helpers (chunks of >= tc_rows token rows)
 
-// CpuFloatBackend.rmsNorm per row (CpuFloatBackend.scala:80-93), double accumulation; one block per row.
+// CpuFloatBackend.rmsNorm per row (CpuFloatBackend.scala:78-93), double accumulation; one block per row.
 __global__ void rmsnorm_rows_kernel(const float *x, const float *w, double eps, float *out, int H) {
   __shared__ double s_red[8];
   pdl_wait();

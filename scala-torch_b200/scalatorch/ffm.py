@@ -7,9 +7,10 @@ vocabulary: invalid arguments raise IllegalArgumentException *before* any native
 failures raise IllegalStateException("<fn> failed with status <code>: <message>").
 
 `B200Session` is the device FloatBackend (core/.../FloatBackend.scala:7-31, the trait CudaSession
-implements, CudaSession.scala:23-24) restricted to what the Linear / Llama hot path needs:
-upload / download / release / shape / matmul against resident (out,in) half weights, plus the
-raw half upload that replaces SafeTensors.readFloat's F32 widening.
+implements, CudaSession.scala:23-24): upload / download / release / shape / reshape / transpose /
+embedding / matmul (against resident (out,in) half weights: the hot path) / add / multiply / scale /
+fill / sum / expandScalar / silu / rmsNorm / rope / causalAttention / attentionCache, plus the raw
+half upload that replaces SafeTensors.readFloat's F32 widening.
 
 There is no fallback: if libstb200.so is missing or fails to load, every entry point raises.
 """
@@ -86,6 +87,18 @@ def _declare(L):
         "stb_linear_adapted": (_i, [_p, _u64, _u64, _i, _u64, _p, _i, _u64, _i, _i, _i]),
         "stb_fill_normal": (_i, [_p, _u64, _i, _u64, _u64, _u64, ctypes.c_double]),
         "stb_fill_value": (_i, [_p, _u64, _i, _u64, ctypes.c_float]),
+        "stb_op_add": (_i, [_p, _u64, _u64, _u64, _u64]),
+        "stb_op_multiply": (_i, [_p, _u64, _u64, _u64, _u64]),
+        "stb_op_scale": (_i, [_p, _u64, _u64, _u64, ctypes.c_float]),
+        "stb_op_silu": (_i, [_p, _u64, _u64, _u64]),
+        "stb_op_sum": (_i, [_p, _u64, _u64, _u64]),
+        "stb_op_expand_scalar": (_i, [_p, _u64, _u64, _u64]),
+        "stb_op_rmsnorm": (_i, [_p, _u64, _u64, _u64, _u64, _i, ctypes.c_double]),
+        "stb_op_rope": (_i, [_p, _u64, _u64, _i, _i, _i, _i, _i, ctypes.c_double]),
+        "stb_op_transpose": (_i, [_p, _u64, _u64, _i, _p, _i, _i]),
+        "stb_op_embedding": (_i, [_p, _u64, _i, ctypes.c_int64, _i, _p, _u64, _u64]),
+        "stb_op_cache_append": (_i, [_p, _u64, _u64, _i, _i, _i, _i, _i, _i]),
+        "stb_op_causal_attention": (_i, [_p, _u64, _u64, _u64, _u64] + [_i] * 9),
         "stb_nccl_unique_id": (_i, [_p]),
         "stb_session_init_tp": (_i, [_p, _i, _i, _p]),
         "stb_allreduce_sum_f32": (_i, [_p, _u64, _u64]),
@@ -129,6 +142,8 @@ class DeviceTensor:
     transposed_weight: bool = False
     owner: bool = True
     _alive: list = field(default_factory=lambda: [True])
+    # handles on one allocation (reshape views share it, CudaSession.scala:95-101); freed at zero
+    _refs: list = field(default_factory=lambda: [1])
 
     @property
     def numel(self) -> int:
@@ -234,7 +249,8 @@ class B200Session:
         require(t.session is self, "tensor belongs to another session")
         if t._alive[0]:
             t._alive[0] = False
-            if t.owner:
+            t._refs[0] -= 1
+            if t.owner and t._refs[0] == 0:
                 call("stb_release", self.handle, t.address)
 
     def _validate(self, t: DeviceTensor) -> None:
@@ -364,6 +380,165 @@ class B200Session:
         self._validate(t)
         call("stb_fill_normal", self.handle, t.address, t.dtype, t.numel, seed, stream, std)
 
+    def upload_weight_f32(self, w: np.ndarray) -> DeviceTensor:
+        """A Float32 (out,in) matrix used as W^T by matmul (BackendLlama.prepare uploads adapter factors
+        transposed, BackendLlama.scala:169; here the bytes stay (out,in))."""
+        require(np.ndim(w) == 2, "weight must have shape (out, in)")
+        t = self.upload(np.ascontiguousarray(w, np.float32))
+        t.shape = (t.shape[1], t.shape[0])
+        t.transposed_weight = True
+        return t
+
+    # -- FloatBackend operator set (FloatBackend.scala:7-31); each op is one kernel (csrc/ops.cu)
+    def _out(self, shape) -> DeviceTensor:
+        n = 1
+        for d in shape:
+            n *= int(d)
+        require(n <= 0x7FFFFFFF, "CUDA tensor exceeds Int indexing")
+        return self.allocate(shape, STB_F32)
+
+    def _f32(self, *ts):
+        for t in ts:
+            self._validate(t)
+            require(t.dtype == STB_F32 and not t.transposed_weight, "operation takes Float32 activations")
+
+    def _run(self, out: DeviceTensor, fn: str, *args) -> DeviceTensor:
+        try:
+            call(fn, self.handle, *args)
+        except Exception:
+            self.release(out)
+            raise
+        return out
+
+    def reshape(self, t: DeviceTensor, shape) -> DeviceTensor:
+        """A view over the same allocation (CudaSession.reshape, CudaSession.scala:95-101): released
+        independently; the memory is freed when the last handle is released."""
+        self._validate(t)
+        shape = tuple(int(d) for d in shape)
+        n = 1
+        for d in shape:
+            n *= d
+        require(n == t.numel, "reshape changes element count")
+        t._refs[0] += 1
+        return DeviceTensor(self, t.address, shape, t.dtype, t.nbytes, t.transposed_weight, t.owner, _refs=t._refs)
+
+    def transpose(self, t: DeviceTensor, dim0: int, dim1: int) -> DeviceTensor:
+        """Packed copy with two axes swapped (CudaSession.transpose, CudaSession.scala:469-485)."""
+        self._f32(t)
+        rank = len(t.shape)
+        require(0 <= dim0 < rank and 0 <= dim1 < rank, "transpose dimension out of range")
+        if dim0 == dim1:
+            return self.reshape(t, t.shape)
+        dims = list(t.shape)
+        dims[dim0], dims[dim1] = dims[dim1], dims[dim0]
+        out = self._out(dims)
+        if out.numel == 0:
+            return out
+        arr = (ctypes.c_int64 * rank)(*t.shape)
+        return self._run(out, "stb_op_transpose", t.address, out.address, rank, ctypes.cast(arr, ctypes.c_void_p),
+                         dim0, dim1)
+
+    def embedding(self, table: DeviceTensor, indices) -> DeviceTensor:
+        """Rows of `table` for host int64 ids (CpuFloatBackend.embedding, CpuFloatBackend.scala:49-59); the
+        output appends the table width.  A half table (the raw safetensors payload) is widened exactly."""
+        self._validate(table)
+        require(len(table.shape) == 2 and table.shape[1] > 0, "embedding requires a matrix with positive width")
+        rows, width = table.shape
+        if table.transposed_weight:  # an (out,in) half payload uploaded as a weight: rows = out
+            width, rows = table.shape
+        ids = np.ascontiguousarray(np.asarray(indices, np.int64))
+        require(bool(np.all((ids >= 0) & (ids < rows))), "embedding token ID out of bounds")
+        out = self._out(ids.shape + (width,))
+        if out.numel == 0:
+            return out
+        return self._run(out, "stb_op_embedding", table.address, table.dtype, rows, width, ids.ctypes.data, ids.size,
+                         out.address)
+
+    def _binary(self, fn, a, b, name):
+        self._f32(a, b)
+        require(a.shape == b.shape, f"backend {name} requires equal shapes")
+        out = self._out(a.shape)
+        return self._run(out, fn, a.address, b.address, out.address, a.numel) if a.numel else out
+
+    def add(self, a: DeviceTensor, b: DeviceTensor) -> DeviceTensor:
+        return self._binary("stb_op_add", a, b, "add")
+
+    def multiply(self, a: DeviceTensor, b: DeviceTensor) -> DeviceTensor:
+        return self._binary("stb_op_multiply", a, b, "multiply")
+
+    def scale(self, t: DeviceTensor, scalar: float) -> DeviceTensor:
+        """Elementwise Float32 scalar multiplication, IEEE nonfinite values included."""
+        self._f32(t)
+        out = self._out(t.shape)
+        return self._run(out, "stb_op_scale", t.address, out.address, t.numel, float(np.float32(scalar))) \
+            if t.numel else out
+
+    def fill(self, shape, value: float) -> DeviceTensor:
+        out = self._out(tuple(int(d) for d in shape))
+        return self._run(out, "stb_fill_value", out.address, STB_F32, out.numel, float(np.float32(value))) \
+            if out.numel else out
+
+    def sum(self, t: DeviceTensor) -> DeviceTensor:
+        """All elements into a rank-zero Float32, accumulated in double."""
+        self._f32(t)
+        out = self._out(())
+        return self._run(out, "stb_op_sum", t.address, t.numel, out.address)
+
+    def expand_scalar(self, t: DeviceTensor, shape) -> DeviceTensor:
+        """Repeat a rank-zero device value without a host transfer."""
+        self._f32(t)
+        require(len(t.shape) == 0, "expandScalar requires rank zero")
+        out = self._out(tuple(int(d) for d in shape))
+        return self._run(out, "stb_op_expand_scalar", t.address, out.address, out.numel) if out.numel else out
+
+    def silu(self, t: DeviceTensor) -> DeviceTensor:
+        self._f32(t)
+        out = self._out(t.shape)
+        return self._run(out, "stb_op_silu", t.address, out.address, t.numel) if t.numel else out
+
+    def rms_norm(self, t: DeviceTensor, weight: DeviceTensor, epsilon: float = 1e-6) -> DeviceTensor:
+        """RMSNorm over the final axis (CpuFloatBackend.rmsNorm, CpuFloatBackend.scala:78-93)."""
+        self._f32(t, weight)
+        require(math.isfinite(epsilon) and epsilon > 0, "invalid RMSNorm epsilon")
+        require(len(t.shape) > 0 and t.shape[-1] > 0 and weight.shape == (t.shape[-1],), "invalid RMSNorm shapes")
+        out = self._out(t.shape)
+        width = t.shape[-1]
+        return self._run(out, "stb_op_rmsnorm", t.address, weight.address, out.address, t.numel // width, width,
+                         float(epsilon)) if t.numel else out
+
+    def rope(self, t: DeviceTensor, position_start: int = 0, theta: float = 10000.0) -> DeviceTensor:
+        """Rotary embedding of (batch, heads, tokens, width) (CpuAttention.rope, CpuAttention.scala:6-18)."""
+        self._f32(t)
+        require(len(t.shape) == 4 and t.shape[3] > 0 and t.shape[3] % 2 == 0,
+                "RoPE requires rank 4 and positive even width")
+        require(position_start >= 0 and math.isfinite(theta) and theta > 0, "invalid rotary position or theta")
+        if t.numel == 0:
+            return self.reshape(t, t.shape)
+        b, h, n, w = t.shape
+        out = self._out(t.shape)
+        return self._run(out, "stb_op_rope", t.address, out.address, b, h, n, w, position_start, float(theta))
+
+    def causal_attention(self, query: DeviceTensor, key: DeviceTensor, value: DeviceTensor, query_start: int = 0,
+                         max_score_elements: int = 16777216) -> DeviceTensor:
+        """Causal grouped-query attention (CpuAttention.causal, CpuAttention.scala:20-50) with
+        AttentionLayout.validate's rules (AttentionLayout.scala:3-19)."""
+        self._f32(query, key, value)
+        out_shape, _ = attention_layout(query.shape, key.shape, value.shape, query_start, max_score_elements)
+        return self._attend(query, key, value, out_shape, key.shape[2], key.shape[2], query_start)
+
+    def _attend(self, q, k, v, out_shape, keys, key_stride, start):
+        out = self._out(out_shape)
+        if out.numel == 0:
+            return out
+        b, h, t, d = q.shape
+        return self._run(out, "stb_op_causal_attention", q.address, k.address, v.address, out.address, b, h, t, d,
+                         k.shape[1], keys, key_stride, v.shape[3], start)
+
+    def attention_cache(self, batch_size: int, heads: int, capacity: int, key_width: int, value_width: int,
+                        max_bytes: int = 268435456) -> "B200AttentionCache":
+        self._check()
+        return B200AttentionCache(self, batch_size, heads, capacity, key_width, value_width, max_bytes)
+
     # -- tensor parallel
     @staticmethod
     def nccl_unique_id() -> bytes:
@@ -378,3 +553,73 @@ class B200Session:
     def allreduce_sum(self, t: DeviceTensor) -> None:
         self._validate(t)
         call("stb_allreduce_sum_f32", self.handle, t.address, t.numel)
+
+
+def attention_layout(q, k, v, start: int, max_scores: int):
+    """AttentionLayout.validate (core/src/main/scala/scalatorch/AttentionLayout.scala:3-19): output shape
+    and score count, IllegalArgumentException on any violated rule."""
+    require(len(q) == 4 and len(k) == 4 and len(v) == 4, "attention expects (batch,heads,tokens,width)")
+    require(start >= 0 and max_scores >= 0, "invalid attention offset or workspace limit")
+    require(q[0] == k[0] == v[0], "attention batch mismatch")
+    require(q[1] > 0 and k[1] > 0 and k[1] == v[1] and q[1] % k[1] == 0, "invalid grouped attention heads")
+    require(q[3] > 0 and q[3] == k[3] and v[3] > 0 and k[2] == v[2], "attention width/token mismatch")
+    out = (q[0], q[1], q[2], v[3])
+    require(out[0] * out[1] * out[2] * out[3] <= 0x7FFFFFFF, "attention output exceeds Int indexing")
+    if q[0] * q[1] * q[2] * q[3] == 0:
+        return out, 0
+    require(k[2] > 0, "nonempty queries require keys")
+    scores = q[0] * q[1] * q[2] * k[2]
+    require(scores <= max_scores and scores <= 0x7FFFFFFF, "attention score workspace limit exceeded")
+    return out, scores
+
+
+class B200AttentionCache:
+    """AttentionCache on the device (CudaSession.attentionCache, CudaSession.scala:397-431; CacheLayout,
+    AttentionCache.scala:8-27): Float32 keys (batch, heads, capacity, key_width) and values, appended at
+    a written prefix and attended in one call."""
+
+    def __init__(self, session: B200Session, batch: int, heads: int, capacity: int, key_width: int,
+                 value_width: int, max_bytes: int):
+        require(batch > 0 and heads > 0 and capacity > 0 and key_width > 0 and value_width > 0 and max_bytes >= 0,
+                "invalid attention cache dimensions/budget")
+        kc, vc = batch * heads * capacity * key_width, batch * heads * capacity * value_width
+        require(kc <= 0x7FFFFFFF and vc <= 0x7FFFFFFF and (kc + vc) * 4 <= max_bytes,
+                "attention cache allocation budget exceeded")
+        self.session, self.batch, self.heads, self.capacity = session, batch, heads, capacity
+        self.key_width, self.value_width = key_width, value_width
+        self.keys = session.allocate((batch, heads, capacity, key_width))
+        try:
+            self.values = session.allocate((batch, heads, capacity, value_width))
+        except Exception:
+            session.release(self.keys)
+            raise
+        self.written = 0
+        self._closed = False
+
+    def attend(self, query: DeviceTensor, key: DeviceTensor, value: DeviceTensor, position: int,
+               max_score_elements: int = 16777216) -> DeviceTensor:
+        s = self.session
+        if self._closed:
+            raise IllegalStateException("attend", 6, "attention cache is closed")
+        s._f32(query, key, value)
+        require(len(key.shape) == 4, "cache key must have rank 4")
+        chunk = key.shape[2]
+        require(chunk > 0 and key.shape == (self.batch, self.heads, chunk, self.key_width)
+                and value.shape == (self.batch, self.heads, chunk, self.value_width), "cache append shape mismatch")
+        require(len(query.shape) == 4 and query.shape[2] == chunk, "cache query/chunk mismatch")
+        end = position + chunk
+        require(0 <= position <= self.written and end <= self.capacity, "cache append gap or capacity exceeded")
+        out_shape, _ = attention_layout(query.shape, (self.batch, self.heads, end, self.key_width),
+                                        (self.batch, self.heads, end, self.value_width), position, max_score_elements)
+        for src, dst, w in ((key, self.keys, self.key_width), (value, self.values, self.value_width)):
+            call("stb_op_cache_append", s.handle, src.address, dst.address, self.batch, self.heads, chunk, w,
+                 self.capacity, position)
+        out = s._attend(query, self.keys, self.values, out_shape, end, self.capacity, position)
+        self.written = end
+        return out
+
+    def close(self) -> None:
+        if not self._closed:
+            self._closed = True
+            self.session.release(self.keys)
+            self.session.release(self.values)

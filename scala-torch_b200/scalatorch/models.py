@@ -433,3 +433,280 @@ def load_safetensors(session: B200Session, directory: str, weight_dtype: int | N
             m.close()
             raise
     return m
+
+
+class _Scope:
+    """BackendScope (BackendLlama.scala:9-24): owns handles, releases them in reverse order, and hands
+    one result to the caller with take()."""
+
+    def __init__(self, backend: B200Session):
+        self.backend, self.owned = backend, []
+
+    def keep(self, t):
+        self.owned.append(t)
+        return t
+
+    def take(self, t):
+        for i in range(len(self.owned) - 1, -1, -1):
+            if self.owned[i] is t:
+                del self.owned[i]
+                return t
+        raise IllegalArgumentException("backend handle is not owned by this scope")
+
+    def release(self, t):
+        self.backend.release(self.take(t))
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        failure = None
+        for t in reversed(self.owned):
+            try:
+                self.backend.release(t)
+            except Exception as e:  # first failure wins, as the reference's scope
+                failure = failure or e
+        self.owned.clear()
+        if failure is not None and exc[0] is None:
+            raise failure
+
+
+class PerOpLlama:
+    """BackendLlama's per-op path (models/src/main/scala/scalatorch/models/BackendLlama.scala:27-111) on
+    the B200 FloatBackend: every operation of LlamaBlock is one device op of B200Session
+    (embedding, rmsNorm, matmul against the resident (out,in) half weights, reshape / transpose views,
+    rope, causalAttention or the attention cache, silu, multiply, add), in the reference's order and
+    with its releases.  It is the path for models the fused runtime does not take -- Linear layers
+    with low-rank adapters, applied as BackendLlama.linear does (base + ((x A^T) B^T) * (alpha / r),
+    BackendLlama.scala:41-49) -- and the drop-in form of BackendLlama.prepare(model, backend).
+
+    weights: safetensors name -> raw payload (half bits as uint16, or float32), dtype per tensor.
+    lora: projection name (e.g. "model.layers.0.self_attn.q_proj") -> (A [rank, in] f32, B [out, rank]
+    f32, alpha)."""
+
+    def __init__(self, session: B200Session, config: LlamaConfig, weights: dict, dtypes: dict, lora: dict | None = None):
+        self.session, self.config = session, config
+        c = config
+        self._owned = []
+        try:
+            def up_half(name):
+                bits = np.ascontiguousarray(weights[name])
+                if dtypes[name] == STB_F32:
+                    return self._keep(session.upload_weight_f32(bits.view(np.float32)))
+                return self._keep(session.upload_weight(bits, dtypes[name]))
+
+            def up_norm(name):
+                return self._keep(session.upload(_widen(weights[name], dtypes[name])))
+
+            emb = np.ascontiguousarray(weights["model.embed_tokens.weight"])
+            et = dtypes["model.embed_tokens.weight"]
+            self.embed = self._keep(session.upload(emb.view(np.float32)) if et == STB_F32
+                                    else session.upload_half(emb, et))
+            self.final_norm = up_norm("model.norm.weight")
+            if c.tie_word_embeddings:  # the table's (vocab, hidden) bytes are the head's (out, in) layout
+                self.lm_head = self._keep(session.reshape(self.embed, (c.hidden_size, c.vocab_size)))
+                self.lm_head.transposed_weight = True
+            else:
+                self.lm_head = up_half("lm_head.weight")
+            self.layers = []
+            for i in range(c.num_layers):
+                p = f"model.layers.{i}"
+                layer = {"in_norm": up_norm(f"{p}.input_layernorm.weight"),
+                         "post_norm": up_norm(f"{p}.post_attention_layernorm.weight")}
+                for key, name in (("q", "self_attn.q_proj"), ("k", "self_attn.k_proj"), ("v", "self_attn.v_proj"),
+                                  ("o", "self_attn.o_proj"), ("gate", "mlp.gate_proj"), ("up", "mlp.up_proj"),
+                                  ("down", "mlp.down_proj")):
+                    w = up_half(f"{p}.{name}.weight")
+                    adapter = None
+                    if lora and f"{p}.{name}" in lora:
+                        a, b, alpha = lora[f"{p}.{name}"]
+                        require(a.ndim == 2 and b.ndim == 2 and a.shape[1] == w.shape[0] and b.shape[0] == w.shape[1]
+                                and a.shape[0] == b.shape[1] and a.shape[0] > 0, "Linear adapter shape mismatch")
+                        scale = float(np.float32(alpha / a.shape[0])) if np.isfinite(alpha) and alpha > 0 else np.nan
+                        require(np.isfinite(scale) and scale > 0, "invalid adapter scale")
+                        # (A, B) uploaded as (out,in) Float32 matrices used transposed, as prepare does
+                        adapter = (self._keep(session.upload_weight_f32(a)), self._keep(session.upload_weight_f32(b)),
+                                   scale)
+                    layer[key] = (w, adapter)
+                self.layers.append(layer)
+        except BaseException:
+            self.close()
+            raise
+
+    def _keep(self, t):
+        self._owned.append(t)
+        return t
+
+    def close(self) -> None:
+        for t in reversed(self._owned):
+            self.session.release(t)
+        self._owned = []
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- BackendLlama.scala:41-111, op for op
+    def _linear(self, x, layer):
+        """BackendLlama.linear (BackendLlama.scala:41-49)."""
+        be = self.session
+        w, adapter = layer
+        if adapter is None:
+            return be.matmul(x, w)
+        a, b, scale = adapter
+        with _Scope(be) as scope:
+            base = scope.keep(be.matmul(x, w))
+            low = scope.keep(be.matmul(x, a))
+            delta = scope.keep(be.matmul(low, b))
+            scaled = scope.keep(be.scale(delta, scale))
+            return scope.take(scope.keep(be.add(base, scaled)))
+
+    def _attention(self, x, layer, b, t, position, cache):
+        be, c = self.session, self.config
+        hd = c.head_dim
+        with _Scope(be) as scope:
+            keep = scope.keep
+            flat = keep(be.reshape(x, (b * t, c.hidden_size)))
+
+            def heads(proj, count):
+                projected = keep(self._linear(flat, layer[proj]))
+                split = keep(be.reshape(projected, (b, t, count, hd)))
+                return keep(be.transpose(split, 1, 2))
+
+            q = keep(be.rope(heads("q", c.num_attention_heads), position, c.rope_theta))
+            k = keep(be.rope(heads("k", c.num_key_value_heads), position, c.rope_theta))
+            v = heads("v", c.num_key_value_heads)
+            attended = keep(cache.attend(q, k, v, position) if cache is not None else be.causal_attention(q, k, v))
+            joined = keep(be.transpose(attended, 1, 2))
+            matrix = keep(be.reshape(joined, (b * t, c.hidden_size)))
+            projected = keep(self._linear(matrix, layer["o"]))
+            return scope.take(keep(be.reshape(projected, (b, t, c.hidden_size))))
+
+    def _mlp(self, x, layer, b, t):
+        be, c = self.session, self.config
+        with _Scope(be) as scope:
+            keep = scope.keep
+            flat = keep(be.reshape(x, (b * t, c.hidden_size)))
+            gate = keep(self._linear(flat, layer["gate"]))
+            activated = keep(be.silu(gate))
+            up = keep(self._linear(flat, layer["up"]))
+            product = keep(be.multiply(activated, up))
+            down = keep(self._linear(product, layer["down"]))
+            return scope.take(keep(be.reshape(down, (b, t, c.hidden_size))))
+
+    def _block(self, x, layer, b, t, position, cache):
+        be, eps = self.session, self.config.rms_norm_eps
+        with _Scope(be) as scope:
+            keep = scope.keep
+            normalized = keep(be.rms_norm(x, layer["in_norm"], eps))
+            attended = keep(self._attention(normalized, layer, b, t, position, cache))
+            hidden = keep(be.add(x, attended))
+            post = keep(be.rms_norm(hidden, layer["post_norm"], eps))
+            feed = keep(self._mlp(post, layer, b, t))
+            return scope.take(keep(be.add(hidden, feed)))
+
+    def forward(self, tokens, position: int = 0, caches=None):
+        """BackendLlama.run (BackendLlama.scala:86-101): logits (batch, tokens, vocab) as a device tensor
+        owned by the caller."""
+        be, c = self.session, self.config
+        ids = np.asarray(tokens, np.int64)
+        require(ids.ndim == 2, "Llama tokens must have shape (batch,tokens)")
+        b, t = ids.shape
+        require(position >= 0 and position + t <= c.max_positions, "Llama context limit exceeded")
+        require(b * t * c.vocab_size <= 16777216 and b * t * c.vocab_size <= 0x7FFFFFFF,
+                "Llama logits allocation limit exceeded")
+        with _Scope(be) as scope:
+            hidden = scope.keep(be.embedding(self.embed, ids))
+            for i, layer in enumerate(self.layers):
+                nxt = scope.keep(self._block(hidden, layer, b, t, position, caches[i] if caches else None))
+                scope.release(hidden)
+                hidden = nxt
+            normalized = scope.keep(be.rms_norm(hidden, self.final_norm, c.rms_norm_eps))
+            flat = scope.keep(be.reshape(normalized, (b * t, c.hidden_size)))
+            logits = scope.keep(self._linear(flat, (self.lm_head, None)))
+            return scope.take(scope.keep(be.reshape(logits, (b, t, c.vocab_size))))
+
+    def logits(self, tokens) -> np.ndarray:
+        out = self.forward(tokens)
+        try:
+            return self.session.download(out)
+        finally:
+            self.session.release(out)
+
+    def new_cache(self, batch_size: int = 1, capacity: int | None = None) -> "PerOpCache":
+        return PerOpCache(self, batch_size, self.config.max_positions if capacity is None else capacity)
+
+    def generate_ids(self, prompt, max_new_tokens: int) -> list:
+        """Greedy BackendLlama.generateIds with the cache (BackendLlama.scala:126-141; TokenSampler's
+        strict '>' keeps the lowest id among equal logits)."""
+        c = self.config
+        ids = [int(v) for v in prompt]
+        require(len(ids) > 0 and max_new_tokens >= 0 and len(ids) + max_new_tokens <= c.max_positions,
+                "invalid generation length")
+        require(all(0 <= i < c.vocab_size for i in ids), "generation token outside vocabulary")
+        if max_new_tokens == 0:
+            return ids
+        cache = self.new_cache(1, len(ids) + max_new_tokens)
+        try:
+            chunk = list(ids)
+            for _ in range(max_new_tokens):
+                logits = cache.decode([chunk])
+                row = logits[0, -1]
+                nxt = int(np.argmax(row))  # first maximum = lowest id
+                ids.append(nxt)
+                chunk = [nxt]
+                if nxt in c.eos_token_ids:
+                    break
+        finally:
+            cache.close()
+        return ids
+
+
+class PerOpCache:
+    """BackendLlamaCache over per-layer device attention caches (BackendLlamaCache.scala:8-49): the
+    position advances only after a whole chunk succeeded."""
+
+    def __init__(self, model: PerOpLlama, batch_size: int, capacity: int):
+        c = model.config
+        require(batch_size > 0 and 0 < capacity <= c.max_positions, "invalid model cache dimensions/budget")
+        self.model, self.batch_size, self.capacity, self.position = model, batch_size, capacity, 0
+        self.layers = []
+        try:
+            for _ in range(c.num_layers):
+                self.layers.append(model.session.attention_cache(batch_size, c.num_key_value_heads, capacity,
+                                                                 c.head_dim, c.head_dim, 1 << 40))
+        except BaseException:
+            self.close()
+            raise
+
+    def decode(self, tokens) -> np.ndarray:
+        ids = np.asarray(tokens, np.int64)
+        require(ids.ndim == 2 and ids.shape[0] == self.batch_size and ids.shape[1] > 0,
+                "cache tokens must match batch with positive chunk length")
+        end = self.position + ids.shape[1]
+        require(end <= self.capacity, "model cache capacity exceeded")
+        c = self.model.config
+        require(self.batch_size * c.num_attention_heads * ids.shape[1] * end <= 16777216,
+                "cached score workspace limit exceeded")
+        out = self.model.forward(ids, self.position, self.layers)
+        try:
+            logits = self.model.session.download(out)
+        finally:
+            self.model.session.release(out)
+        self.position = end
+        return logits
+
+    def close(self) -> None:
+        for layer in self.layers:
+            layer.close()
+        self.layers = []
+
+
+def _widen(raw, dtype: int) -> np.ndarray:
+    """SafeTensors.readFloat's exact widening of a raw payload (SafeTensors.scala:63-77)."""
+    raw = np.ascontiguousarray(raw)
+    if dtype == STB_F32:
+        return raw.view(np.float32)
+    return _float_bits(raw.view(np.uint16), "BF16" if dtype == STB_BF16 else "F16").view(np.float32)
