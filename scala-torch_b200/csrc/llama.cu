@@ -24,9 +24,9 @@
 #include <mutex>
 #include <vector>
 
-#include "decode_mega.cuh"
 #include "gemv.cuh"
 #include "rng.cuh"
+#include "tc_common.cuh"
 
 namespace stb {
 void allreduce_sum_f32(stb_session *s, void *buf, uint64_t count);
@@ -71,7 +71,6 @@ struct stb_llama {
   // shape (batch, prompt + new, new, EOS count, prefill chunk)
   stb_llama_cache *gen = nullptr;
   int gen_key[5] = {};
-  uint64_t mega_layers = 0;  // MegaLayer [layers] for the persistent decode
 };
 
 struct stb_llama_cache {
@@ -90,7 +89,6 @@ struct stb_llama_cache {
   uint64_t att_part = 0, att_count = 0;  // split decode attention records and counters (batch rows)
   int att_rows = 0;
   int graph_launches = 0;  // kernels in one replay of `graph`
-  uint64_t mopart = 0, mbar = 0, mapart = 0;  // persistent decode: o partials, barrier words, split records
   uint64_t tokens = 0;  // int64 [rows]
   uint64_t state = 0;   // int32: [0] position, [1] all stopped, [2..2+batch) stopped, [2+batch..) out count
   uint64_t out_ids = 0;
@@ -427,156 +425,198 @@ __global__ void __launch_bounds__(256) flash_attention_kernel(const float *q, in
 }
 
 // Decode attention (one query token per batch row) in Float32, split over keys and shared by the
-// query heads of a KV group: block (split s, KV head, token row) takes keys [128 s, 128 s + 128) of
+// query heads of a KV group: block (split s, KV head, token row) takes keys [KPS s, KPS s + KPS) of
 // the visible range for all G = nh / kvh query heads of the group, so each K and V row is read once
-// per group.  Decode is latency-bound, so every thread issues its K half-row and its V rows into
-// registers at the start (one memory round trip for the whole block), then: scores by two threads
-// per key (FMA over half of hd, one xor shuffle), per head max and sum of exp over the split (a warp
-// per head), the weighted V sum by (key group, dimension quad) threads with the key groups added in
-// order through shared memory.  A single split writes the normalised output; otherwise each split
-// stores (max, sum, unnormalised sum) and the last split to finish (a per-(row, KV head) counter,
-// reset by that block) merges them in split order, rescaling by exp(max_s - max).
-constexpr int DA_KPS = 128, DA_GMAX = 8, DA_THREADS = 256;
+// per group.  The cache keeps a (row, KV head)'s keys contiguous, so one thread moves the split's K
+// and V rows into shared memory with two bulk copies (cp.async.bulk, TMA's 1-D form, this GPU's own
+// memory, no multicast) issued before the programmatic-dependency wait -- every row but the newest,
+// which the projection just before this kernel wrote and the threads load after the wait.  Blocks
+// are small (128 threads, 2 * KPS * hd * 4 bytes of shared memory) and KPS adapts to the grid, so
+// several blocks per SM keep the cache streaming.  Scores: each warp takes keys w, w + 4, ...; a lane
+// holds hd/32 dimensions of the G query rows and of the key row; the G partial dots are reduced
+// across the warp in one butterfly (9 shuffles for 8 heads).  Softmax per head by a warp, the
+// weighted V sum per key by the same key split, warp partials added in order through shared memory.
+// A single split writes the normalised output; otherwise each split stores (max, sum, unnormalised
+// sum) and the last split to finish (a per-(row, KV head) counter, reset by that block) merges them
+// in split order, rescaling by exp(max_s - max).  The copy wait is bounded (2 s, then the session's
+// error word is set and the block leaves without writing).
+constexpr int DA_GMAX = 8, DA_THREADS = 128, DA_WARPS = DA_THREADS / 32, DA_KPS_MIN = 32;
 
-// KPS keys per split: 128 (two threads per key) or, for head sizes up to 64 when the 128-key grid
-// would leave SMs idle, 256 (one thread per key, one split for contexts up to 256 keys).
+template <int HD, int KPS>
+constexpr size_t da_smem() {
+  return (size_t)2 * KPS * HD * 4 + (size_t)DA_GMAX * KPS * 4 + DA_GMAX * 2 * 4 + 16;
+}
+
 template <int HD, int KPS>
 __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
     const float *q, int ldq, const float *kcache, const float *vcache, float *out, int ldo, int count, int nh,
-    int kvh, int capacity, const int *pos_dev, int pos0, float *part, int *counters, int smax) {
-  static_assert(HD == 16 || HD == 32 || HD == 64 || HD == 128, "head size");
-  static_assert(KPS == 128 || KPS == 256, "keys per split");
-  constexpr int TPK = DA_THREADS / KPS, SEG = HD / TPK, NK4 = SEG / 4;
-  constexpr int F = HD / 4, KG = DA_THREADS / F, VPT = KPS / KG;
-  __shared__ __align__(16) float qs[DA_GMAX][HD];
-  __shared__ float sp[DA_GMAX][KPS];
-  __shared__ float red[DA_GMAX][2];
-  __shared__ __align__(16) float opart[KG][DA_GMAX][HD];
-  __shared__ int s_last;
-  // Before the programmatic-dependency wait: the position (written by the previous step's finalize,
-  // a graph launch earlier) and every K/V row but the newest (written by earlier steps).  The newest
-  // row and q come from the projection kernel just before this one: loaded after the wait.
+    int kvh, int capacity, const int *pos_dev, int pos0, float *part, int *counters, int smax, int *err) {
+  static_assert(HD == 32 || HD == 64 || HD == 128, "head size");
+  static_assert(KPS % DA_WARPS == 0 && KPS >= DA_KPS_MIN, "keys per split");
+  static_assert(DA_WARPS * DA_GMAX * HD <= KPS * HD, "warp partials reuse the K tile");
+  constexpr int DPL = HD / 32;  // dimensions per lane
+  extern __shared__ __align__(128) uint8_t da_raw[];
+  float *Ks = (float *)da_raw;               // [KPS][HD]
+  float *Vs = Ks + KPS * HD;                 // [KPS][HD]
+  float *sp = Vs + KPS * HD;                 // [G][KPS] scores, then probabilities
+  float *red = sp + DA_GMAX * KPS;           // [G][2] max, sum
+  uint64_t *bar = (uint64_t *)(red + DA_GMAX * 2);
+  __shared__ int s_last, s_ok;
+  __shared__ volatile int s_abort;
   pdl_trigger();
   const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
   const int G = nh / kvh;
   const int b = m / count, t = m % count;
+  // position: written by the previous step's finalize, a graph launch earlier
   const int keys = (pos_dev ? *pos_dev : pos0) + t + 1;
   const int S = (keys + KPS - 1) / KPS;
   if (split >= S) return;  // the grid covers the longest visible range
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int j0 = split * KPS, nk = min(KPS, keys - j0);
-  const int fresh = keys - 1 - j0;  // this split's index of the newest key (may be outside [0, nk))
+  const int fresh = keys - 1 - j0;      // this split's index of the newest key (in [0, nk) only in the last split)
+  const int old = fresh < nk ? fresh : nk;  // rows [0, old) were written by earlier steps
   const size_t kvrow0 = ((size_t)b * kvh + g0) * capacity + j0;
+  const uint32_t bar_a = tc::smem_u32(bar);
+  if (tid == 0) {
+    s_abort = 0;
+    tc::mbar_init(bar_a, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (old > 0) {
+      const uint32_t bytes = (uint32_t)old * HD * 4;
+      tc::mbar_expect_tx(bar_a, 2 * bytes);
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       tc::smem_u32(Ks)),
+                   "l"(kcache + kvrow0 * HD), "r"(bytes), "r"(bar_a)
+                   : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       tc::smem_u32(Vs)),
+                   "l"(vcache + kvrow0 * HD), "r"(bytes), "r"(bar_a)
+                   : "memory");
+    } else {
+      tc::mbar_arrive(bar_a);
+    }
+  }
+  __syncthreads();
+  pdl_wait();
+  if (fresh < nk) {  // the newest key, written by the projection just before this kernel
+    for (int i = tid; i < HD; i += DA_THREADS) {
+      Ks[fresh * HD + i] = kcache[(kvrow0 + fresh) * HD + i];
+      Vs[fresh * HD + i] = vcache[(kvrow0 + fresh) * HD + i];
+    }
+  }
+  float qr[DA_GMAX][DPL];
+#pragma unroll
+  for (int g = 0; g < DA_GMAX; g++)
+#pragma unroll
+    for (int d = 0; d < DPL; d++)
+      qr[g][d] = g < G ? q[(size_t)m * ldq + (size_t)(g0 * G + g) * HD + lane * DPL + d] : 0.0f;
+  if (tid == 0) {
+    s_ok = tc::mbar_wait(bar_a, 0, &s_abort, err, 40);
+    if (!s_ok) {  // leave only once the copies into this block's shared memory are done (bounded again)
+      volatile int no_abort = 0;
+      tc::mbar_wait(bar_a, 0, &no_abort, err, 41);
+    }
+  }
+  __syncthreads();
+  if (!s_ok) return;
   const float scale = (float)(1.0 / sqrt((double)HD));
 
-  // every load of the block in flight at once
-  const int jj = tid / TPK, hf = tid % TPK;  // score role: key jj, dimension segment hf
-  const int f = tid % F, kg = tid / F;    // value role: dimensions 4f..4f+3 of keys kg, kg + KG, ...
-  float4 kreg[NK4], vreg[VPT];
+  // scores: warp w takes keys w, w + 4, ...
+  for (int j = warp; j < nk; j += DA_WARPS) {
+    float a[DA_GMAX];
+    const float *kr = Ks + j * HD + lane * DPL;
+    float kv[DPL];
 #pragma unroll
-  for (int i = 0; i < NK4; i++)
-    kreg[i] = jj < nk && jj != fresh
-                  ? *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * SEG + 4 * i)
-                  : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int i = 0; i < VPT; i++) {
-    const int j = kg + i * KG;
-    vreg[i] = j < nk && j != fresh ? *reinterpret_cast<const float4 *>(vcache + (kvrow0 + j) * HD + 4 * f)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  pdl_wait();
-  if (jj == fresh) {
-#pragma unroll
-    for (int i = 0; i < NK4; i++)
-      kreg[i] = *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * SEG + 4 * i);
-  }
-#pragma unroll
-  for (int i = 0; i < VPT; i++) {
-    const int j = kg + i * KG;
-    if (j == fresh) vreg[i] = *reinterpret_cast<const float4 *>(vcache + (kvrow0 + j) * HD + 4 * f);
-  }
-  for (int i = tid; i < G * HD; i += DA_THREADS)
-    qs[i / HD][i % HD] = q[(size_t)m * ldq + (size_t)(g0 * G) * HD + i];
-  __syncthreads();
-
-  {  // scores
-    float dots[DA_GMAX];
+    for (int d = 0; d < DPL; d++) kv[d] = kr[d];
 #pragma unroll
     for (int g = 0; g < DA_GMAX; g++) {
-      dots[g] = 0.0f;
-      if (g < G) {
+      float s = 0.0f;
 #pragma unroll
-        for (int i = 0; i < NK4; i++) {
-          const float4 qv = *reinterpret_cast<const float4 *>(&qs[g][hf * SEG + 4 * i]);
-          dots[g] = fmaf(qv.x, kreg[i].x, dots[g]);
-          dots[g] = fmaf(qv.y, kreg[i].y, dots[g]);
-          dots[g] = fmaf(qv.z, kreg[i].z, dots[g]);
-          dots[g] = fmaf(qv.w, kreg[i].w, dots[g]);
-        }
-      }
+      for (int d = 0; d < DPL; d++) s = fmaf(qr[g][d], kv[d], s);
+      a[g] = s;
     }
-    if constexpr (TPK == 2) {
+    // butterfly: after the 16 / 8 / 4 steps lane l holds head ((l >> 2) & 7) summed over 8 lanes
 #pragma unroll
-      for (int g = 0; g < DA_GMAX; g++) dots[g] += __shfl_xor_sync(0xffffffffu, dots[g], 1);
+    for (int i = 0; i < 4; i++) {
+      const bool up = lane & 16;
+      const float send = up ? a[i] : a[i + 4], keep = up ? a[i + 4] : a[i];
+      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
     }
-    if (hf == 0 && jj < nk) {
 #pragma unroll
-      for (int g = 0; g < DA_GMAX; g++)
-        if (g < G) sp[g][jj] = dots[g] * scale;
+    for (int i = 0; i < 2; i++) {
+      const bool up = lane & 8;
+      const float send = up ? a[i] : a[i + 2], keep = up ? a[i + 2] : a[i];
+      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
     }
+    {
+      const bool up = lane & 4;
+      const float send = up ? a[0] : a[1], keep = up ? a[1] : a[0];
+      a[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    a[0] += __shfl_xor_sync(0xffffffffu, a[0], 2);
+    a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
+    const int h = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    if ((lane & 3) == 0 && h < G) sp[h * KPS + j] = a[0] * scale;
   }
   __syncthreads();
-  for (int g = warp; g < G; g += DA_THREADS / 32) {  // per head: max and sum of exp over the split
+  for (int g = warp; g < G; g += DA_WARPS) {  // per head: max and sum of exp over the split
     float mx = -INFINITY;
-    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sp[g][j]);
+    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sp[g * KPS + j]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     float sum = 0.0f;
     for (int j = lane; j < nk; j += 32) {
-      const float e = expf(sp[g][j] - mx);
-      sp[g][j] = e;
+      const float e = expf(sp[g * KPS + j] - mx);
+      sp[g * KPS + j] = e;
       sum += e;
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
     if (lane == 0) {
-      red[g][0] = mx;
-      red[g][1] = sum;
+      red[g * 2] = mx;
+      red[g * 2 + 1] = sum;
     }
   }
   __syncthreads();
-  {  // unnormalised weighted V sum
+  float acc[DA_GMAX][DPL];
+#pragma unroll
+  for (int g = 0; g < DA_GMAX; g++)
+#pragma unroll
+    for (int d = 0; d < DPL; d++) acc[g][d] = 0.0f;
+  for (int j = warp; j < nk; j += DA_WARPS) {  // unnormalised weighted V sum, same key split
+    float vv[DPL];
+#pragma unroll
+    for (int d = 0; d < DPL; d++) vv[d] = Vs[j * HD + lane * DPL + d];
 #pragma unroll
     for (int g = 0; g < DA_GMAX; g++) {
       if (g < G) {
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        const float p = sp[g * KPS + j];
 #pragma unroll
-        for (int i = 0; i < VPT; i++) {
-          const int j = kg + i * KG;
-          const float p = j < nk ? sp[g][j] : 0.0f;
-          a0 = fmaf(p, vreg[i].x, a0);
-          a1 = fmaf(p, vreg[i].y, a1);
-          a2 = fmaf(p, vreg[i].z, a2);
-          a3 = fmaf(p, vreg[i].w, a3);
-        }
-        *reinterpret_cast<float4 *>(&opart[kg][g][4 * f]) = make_float4(a0, a1, a2, a3);
+        for (int d = 0; d < DPL; d++) acc[g][d] = fmaf(p, vv[d], acc[g][d]);
       }
     }
   }
+  float *opart = Ks;  // [warp][G][HD]: the K tile is no longer read
+#pragma unroll
+  for (int g = 0; g < DA_GMAX; g++)
+    if (g < G)
+#pragma unroll
+      for (int d = 0; d < DPL; d++) opart[(warp * DA_GMAX + g) * HD + lane * DPL + d] = acc[g][d];
   __syncthreads();
   const size_t slot = ((size_t)m * kvh + g0) * smax;  // this (row, KV head)'s split records
   float *po = part, *pml = part + (size_t)gridDim.z * kvh * smax * DA_GMAX * HD;
   for (int i = tid; i < G * HD; i += DA_THREADS) {
     const int g = i / HD, d = i % HD;
     float o = 0.0f;
-    for (int k = 0; k < KG; k++) o += opart[k][g][d];
-    if (S == 1) out[(size_t)m * ldo + (size_t)(g0 * G + g) * HD + d] = o / red[g][1];
+#pragma unroll
+    for (int w = 0; w < DA_WARPS; w++) o += opart[(w * DA_GMAX + g) * HD + d];
+    if (S == 1) out[(size_t)m * ldo + (size_t)(g0 * G + g) * HD + d] = o / red[g * 2 + 1];
     else po[((slot + split) * DA_GMAX + g) * HD + d] = o;
   }
   if (S == 1) return;
   if (tid < G) {
-    pml[((slot + split) * DA_GMAX + tid) * 2 + 0] = red[tid][0];
-    pml[((slot + split) * DA_GMAX + tid) * 2 + 1] = red[tid][1];
+    pml[((slot + split) * DA_GMAX + tid) * 2 + 0] = red[tid * 2];
+    pml[((slot + split) * DA_GMAX + tid) * 2 + 1] = red[tid * 2 + 1];
   }
   __threadfence();
   __syncthreads();
@@ -599,44 +639,63 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   if (tid == 0) counters[(size_t)m * kvh + g0] = 0;
 }
 
-// Floats of split records decode_attention_kernel needs for `rows` token rows.
+// Floats of split records decode_attention_kernel needs for `rows` token rows (sized for the
+// smallest split, DA_KPS_MIN keys).
 size_t decode_attention_part_floats(int rows, int kvh, int capacity, int hd) {
-  const size_t smax = (size_t)(capacity + DA_KPS - 1) / DA_KPS;
+  const size_t smax = (size_t)(capacity + DA_KPS_MIN - 1) / DA_KPS_MIN;
   return (size_t)rows * kvh * smax * DA_GMAX * ((size_t)hd + 2);
 }
 
+template <int HD, int KPS>
+void da_launch(dim3 grid, bool pdl, cudaStream_t st, int device, const float *q, int ldq, const float *kc,
+               const float *vc, float *out, int ldo, int count, int nh, int kvh, int capacity, const int *posd,
+               int pos0, float *part, int *counters, int smax, int *err) {
+  constexpr size_t smem = da_smem<HD, KPS>();
+  if constexpr (smem > 48 * 1024) {
+    static std::mutex mu;
+    static bool configured[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0 || device >= 64 || !configured[device]) {
+      STB_CUDA(cudaFuncSetAttribute(decode_attention_kernel<HD, KPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem));
+      if (device >= 0 && device < 64) configured[device] = true;
+    }
+  }
+  launch_kernel(decode_attention_kernel<HD, KPS>, grid, dim3(DA_THREADS), smem, st, pdl, q, ldq, kc, vc, out, ldo,
+                count, nh, kvh, capacity, posd, pos0, part, counters, smax, err);
+}
+
 // Launches the split decode attention when the head size and group size have a form (hd in
-// {16, 32, 64, 128}, nh / kvh <= 8) and STB_DECODE_ATTENTION is not 0; returns false otherwise.
+// {32, 64, 128}, nh / kvh <= 8) and STB_DECODE_ATTENTION is not 0; returns false otherwise.  Keys per
+// split: the smallest of 32 / 64 / 128 that keeps the grid within ~6 blocks per SM.
 bool launch_decode_attention(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
                              int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
-                             float *part, int *counters, bool pdl, cudaStream_t st) {
+                             float *part, int *counters, bool pdl, cudaStream_t st, int device, int *err) {
   static const int enabled = env_int("STB_DECODE_ATTENTION", 1);
   if (!enabled || !part || !counters || nh % kvh != 0 || nh / kvh > DA_GMAX) return false;
-  const int smax128 = (capacity + DA_KPS - 1) / DA_KPS;
-  // 256-key splits when 128-key splits would not fill the SMs anyway (small batch, few KV heads)
-  const bool wide = hd <= 64 && (long)rows * kvh * smax128 < 148;
-  const int smax = wide ? (capacity + 255) / 256 : smax128;
+  if (hd != 32 && hd != 64 && hd != 128) return false;
+  static const int forced = env_int("STB_DA_KPS", 0);  // 32 / 64 / 128: fixed keys per split (tests)
+  const long units = (long)rows * kvh;
+  const long budget = 6L * tc::sm_count(device);
+  int kps = units * ((capacity + 31) / 32) <= budget ? 32 : (units * ((capacity + 63) / 64) <= budget ? 64 : 128);
+  if (forced == 32 || forced == 64 || forced == 128) kps = forced;
+  const int smax = (capacity + kps - 1) / kps;
   const dim3 grid(smax, kvh, rows);
-#define STB_DA_LAUNCH(HDV, KPSV)                                                                                   \
-  launch_kernel(decode_attention_kernel<HDV, KPSV>, grid, dim3(DA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo,   \
-                count, nh, kvh, capacity, posd, pos0, part, counters, smax)
+#define STB_DA(HDV, KPSV)                                                                                          \
+  da_launch<HDV, KPSV>(grid, pdl, st, device, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, part, \
+                       counters, smax, err)
+#define STB_DA_HD(HDV)          \
+  if (kps == 32) STB_DA(HDV, 32);   \
+  else if (kps == 64) STB_DA(HDV, 64); \
+  else STB_DA(HDV, 128);
   switch (hd) {
-    case 16:
-      if (wide) STB_DA_LAUNCH(16, 256);
-      else STB_DA_LAUNCH(16, 128);
-      return true;
-    case 32:
-      if (wide) STB_DA_LAUNCH(32, 256);
-      else STB_DA_LAUNCH(32, 128);
-      return true;
-    case 64:
-      if (wide) STB_DA_LAUNCH(64, 256);
-      else STB_DA_LAUNCH(64, 128);
-      return true;
-    case 128: STB_DA_LAUNCH(128, 128); return true;
-    default: return false;
+    case 32: STB_DA_HD(32); break;
+    case 64: STB_DA_HD(64); break;
+    default: STB_DA_HD(128); break;
   }
-#undef STB_DA_LAUNCH
+#undef STB_DA_HD
+#undef STB_DA
+  return true;
 }
 
 template <int HD>
@@ -975,9 +1034,9 @@ void ensure_rows(stb_llama_cache *c, int rows) {
       c->skin = alloc_owned(s, c->owned, need);
       c->skin_bytes = need;
       skinny_prepare(s->device);
-      session_error_word(s);  // allocated now, not inside a graph capture
     }
   }
+  session_error_word(s);  // allocated now, not inside a graph capture
   if (rows >= m->tc_rows) {
     const uint64_t widest = std::max<uint64_t>(std::max<uint64_t>(m->H, qw), m->I);
     c->xn = alloc_owned(s, c->owned, (uint64_t)rows * m->H * 4);
@@ -1110,7 +1169,8 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       if (a.count == 1 && rows <= c->att_rows)
         done = launch_decode_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc,
                                        (float *)c->att, qw, rows, 1, m->NH, m->KV, m->hd, c->capacity, posd, c->used,
-                                       (float *)c->att_part, (int *)c->att_count, true, st);
+                                       (float *)c->att_part, (int *)c->att_count, true, st, s->device,
+                                       session_error_word(s));
       else if (a.count > 1)
         done = launch_flash_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc,
                                       (float *)c->att, qw, rows, a.count, m->NH, m->KV, m->hd, c->capacity, posd,
@@ -1663,62 +1723,6 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
           STB_CUDA(cudaMemcpy2DAsync((void *)c->tokens, 8, (const void *)(c->tokens + (uint64_t)(last - 1) * 8),
                                      (size_t)last * 8, 8, batch, cudaMemcpyDeviceToDevice, s->stream));
         }
-        const bool persistent = mega_eligible(m->H, m->NH, m->KV, m->hd, m->I, m->V, (int)m->layers.size(),
-                                              c->capacity, batch, m->tp, m->c.weight_dtype, s->device);
-        if (persistent) {
-          if (!m->mega_layers) {
-            std::vector<MegaLayer> hl(m->layers.size());
-            for (size_t l = 0; l < hl.size(); l++) {
-              const Layer &L = m->layers[l];
-              hl[l] = MegaLayer{(const uint16_t *)L.qkv, (const uint16_t *)L.o, (const uint16_t *)L.gu,
-                                (const uint16_t *)L.down, (const float *)L.in_norm, (const float *)L.post_norm};
-            }
-            const uint64_t bytes = hl.size() * sizeof(MegaLayer);
-            m->mega_layers = alloc_owned(s, m->owned, bytes);
-            upload(s, hl.data(), bytes, m->mega_layers);
-          }
-          const uint64_t bar_bytes = (uint64_t)(16 + m->NH) * sizeof(unsigned);
-          if (!c->mopart) {
-            c->mopart = alloc_owned(s, c->owned, (uint64_t)m->NH * m->H * sizeof(float));
-            c->mbar = alloc_owned(s, c->owned, bar_bytes);
-            c->mapart = alloc_owned(s, c->owned, (uint64_t)m->NH * ((c->capacity + 63) / 64) * (m->hd + 2) *
-                                                     sizeof(float));
-          }
-          STB_CUDA(cudaMemsetAsync((void *)c->mbar, 0, bar_bytes, s->stream));
-          MegaArgs ma{};
-          ma.layers = (const MegaLayer *)m->mega_layers;
-          ma.L = (int)m->layers.size();
-          ma.H = m->H;
-          ma.NH = m->NH;
-          ma.KV = m->KV;
-          ma.hd = m->hd;
-          ma.I = m->I;
-          ma.V = m->V;
-          ma.capacity = c->capacity;
-          ma.eps = m->c.rms_norm_eps;
-          ma.embed = (const uint16_t *)m->embed;
-          ma.lm_head = (const uint16_t *)m->lm_head;
-          ma.final_norm = (const float *)m->final_norm;
-          ma.rope = (const double2 *)m->rope;
-          ma.kv = (float *)c->kv;
-          ma.qbuf = (float *)c->qbuf;
-          ma.opart = (float *)c->mopart;
-          ma.act = (float *)c->act;
-          ma.hid = (float *)c->sum;
-          ma.apart = (float *)c->mapart;
-          ma.tokens = (int64_t *)c->tokens;
-          ma.state = (int *)c->state;
-          ma.out_ids = (int64_t *)c->out_ids;
-          ma.out_stride = c->out_stride;
-          ma.eos = (const int64_t *)c->eos;
-          ma.eos_count = c->eos_count;
-          ma.best = (unsigned long long *)c->best;
-          ma.bar = (unsigned *)c->mbar;
-          ma.err = session_error_word(s);
-          ma.steps = max_new - 1;
-          mega_launch(ma, s->device, s->stream);
-          count_launch(s, 1);
-        }
         StepArgs d;
         d.rows = batch;
         d.count = 1;
@@ -1726,7 +1730,7 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
         d.all_logits = false;
         d.append = true;
         d.advance = 1;
-        if (!persistent && !c->graph) {
+        if (!c->graph) {
           cudaGraph_t g = nullptr;
           STB_CUDA(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
           int step_launches = 0;
@@ -1745,12 +1749,10 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
           c->graph = made;
           c->graph_launches = step_launches;
         }
-        if (!persistent) {
-          cudaGraphExec_t exec = c->graph;
-          const int step_launches = c->graph_launches;
-          for (int i = 1; i < max_new; i++) STB_CUDA(cudaGraphLaunch(exec, s->stream));
-          count_launch(s, (uint64_t)step_launches * (max_new - 1));
-        }
+        cudaGraphExec_t exec = c->graph;
+        const int step_launches = c->graph_launches;
+        for (int i = 1; i < max_new; i++) STB_CUDA(cudaGraphLaunch(exec, s->stream));
+        count_launch(s, (uint64_t)step_launches * (max_new - 1));
       }
       STB_CUDA(cudaEventRecord(ev[2], s->stream));
       std::vector<int64_t> picks((size_t)batch * max_new);

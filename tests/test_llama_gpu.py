@@ -256,28 +256,65 @@ def test_smollm2_shaped_greedy_ids_and_logits(session):
         c.close()
 
 
-def test_persistent_decode_option_matches_oracle():
-    """The opt-in persistent decode (STB_DECODE_PERSISTENT=1: every decode step in one cooperative
-    launch with grid barriers) gives the oracle's greedy ids; run in a child process because the
-    switch is read once per process."""
+def test_smollm2_full_bench_configuration_ids_and_logits(session):
+    """The benchmarked SmolLM2 configuration itself: seed 2024, a 128-token prompt of ids uniform in
+    [0, 49152) (numpy default_rng(2024)), 128 greedy tokens -- ids identical to the oracle's, and the
+    logits after the prompt within 1e-5 (1 + |e|)."""
+    cfg = LlamaConfig(**SMOL)
+    ref = oracle_model(cfg, seed=2024)
+    prompt = np.random.default_rng(2024).integers(0, cfg.vocab_size, 128).tolist()
+    with BackendLlama.prepare_random(session, cfg, seed=2024) as m:
+        assert m.generate_ids(prompt, 128) == ref.generate(prompt, 128)
+        c = m.new_cache(1, 129)
+        oc = ref.new_cache(1, 129)
+        got, _ = c.decode([prompt])
+        close(got[0, -1], ref.decode(oc, np.array([prompt]))[0, -1])
+        ref.free_cache(oc)
+        c.close()
+
+
+# head size 128 and a query group of 8 (the 70B shape's attention) on a small model
+HD128 = dict(vocab_size=512, hidden_size=1024, intermediate_size=256, num_layers=2, num_attention_heads=8,
+             num_key_value_heads=1, max_positions=512, tie_word_embeddings=False, eos_token_ids=())
+
+
+@pytest.mark.parametrize("kps", [32, 64, 128])
+def test_decode_attention_splits_head128_group8(kps):
+    """The split decode attention on head size 128 with 8 query heads per KV head, keys per split forced
+    to 32 / 64 / 128 (STB_DA_KPS, read once per process: a child process each), over 127 prompt tokens
+    (254 rows: below the tensor-core prefill threshold, so the whole run keeps Float32 activations) and 8
+    decode steps for 2 rows, so splits merge: greedy ids identical to the oracle and the logits of a
+    cached step within 1e-5 (1 + |e|)."""
     import subprocess
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     code = (
         "import sys, numpy as np\n"
         f"sys.path[:0] = [{root!r}, {os.path.join(root, 'scala-torch_b200')!r}, {os.path.join(root, 'tests')!r}]\n"
-        "from llama_fixtures import TINY, SMOL, oracle_model\n"
+        "from llama_fixtures import oracle_model\n"
+        "from test_llama_gpu import HD128, close\n"
         "from scalatorch import ffm\n"
         "from scalatorch.models import BackendLlama, LlamaConfig\n"
+        "cfg = LlamaConfig(**HD128)\n"
+        "ref = oracle_model(cfg, seed=9)\n"
+        "rng = np.random.default_rng(3)\n"
+        "prompts = rng.integers(0, cfg.vocab_size, (2, 127))\n"
         "s = ffm.B200Session(0, 8 << 30)\n"
-        "for cfg, prompt, n in ((TINY, [1, 17, 400, 999, 3], 20), (SMOL, [5, 9, 700, 12, 44, 3000], 6)):\n"
-        "    c = LlamaConfig(**cfg)\n"
-        "    with BackendLlama.prepare_random(s, c, seed=5) as m:\n"
-        "        got = m.generate_ids(prompt, n)\n"
-        "        assert m.generate_ids(prompt, n) == got\n"
-        "    assert got == oracle_model(c, seed=5).generate(prompt, n), (got,)\n"
+        "with BackendLlama.prepare_random(s, cfg, seed=9) as m:\n"
+        "    got = m.generate_ids(prompts, 8)\n"
+        "    for b in range(2):\n"
+        "        assert got[b] == ref.generate(prompts[b].tolist(), 8), b\n"
+        "    c = m.new_cache(2, 140)\n"
+        "    oc = ref.new_cache(2, 140)\n"
+        "    c.decode(prompts)\n"
+        "    ref.decode(oc, prompts)\n"
+        "    lg, _ = c.decode([[7], [300]])\n"
+        "    close(lg, ref.decode(oc, np.array([[7], [300]])))\n"
+        "    ref.free_cache(oc)\n"
+        "    c.close()\n"
         "s.close()\n"
         "print('ok')\n")
-    env = dict(os.environ, STB_DECODE_PERSISTENT="1")
+    env = dict(os.environ, STB_DA_KPS=str(kps))
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
+
