@@ -425,6 +425,219 @@ __global__ void __launch_bounds__(256) flash_attention_kernel(const float *q, in
 }
 
 // Decode attention (one query token per batch row) in Float32, split over keys and shared by the
+// query heads of a KV group: block (split s, KV head, token row) takes keys [128 s, 128 s + 128) of
+// the visible range for all G = nh / kvh query heads of the group, so each K and V row is read once
+// per group.  Decode is latency-bound, so every thread issues its K half-row and its V rows into
+// registers at the start (one memory round trip for the whole block), then: scores by two threads
+// per key (FMA over half of hd, one xor shuffle), per head max and sum of exp over the split (a warp
+// per head), the weighted V sum by (key group, dimension quad) threads with the key groups added in
+// order through shared memory.  A single split writes the normalised output; otherwise each split
+// stores (max, sum, unnormalised sum) and the last split to finish (a per-(row, KV head) counter,
+// reset by that block) merges them in split order, rescaling by exp(max_s - max).
+constexpr int RA_KPS = 128, RA_GMAX = 8, RA_THREADS = 256;
+
+// KPS keys per split: 128 (two threads per key) or, for head sizes up to 64 when the 128-key grid
+// would leave SMs idle, 256 (one thread per key, one split for contexts up to 256 keys).
+template <int HD, int KPS>
+__global__ void __launch_bounds__(RA_THREADS) decode_attention_reg_kernel(
+    const float *q, int ldq, const float *kcache, const float *vcache, float *out, int ldo, int count, int nh,
+    int kvh, int capacity, const int *pos_dev, int pos0, float *part, int *counters, int smax) {
+  static_assert(HD == 16 || HD == 32 || HD == 64 || HD == 128, "head size");
+  static_assert(KPS == 128 || KPS == 256, "keys per split");
+  constexpr int TPK = RA_THREADS / KPS, SEG = HD / TPK, NK4 = SEG / 4;
+  constexpr int F = HD / 4, KG = RA_THREADS / F, VPT = KPS / KG;
+  __shared__ __align__(16) float qs[RA_GMAX][HD];
+  __shared__ float sp[RA_GMAX][KPS];
+  __shared__ float red[RA_GMAX][2];
+  __shared__ __align__(16) float opart[KG][RA_GMAX][HD];
+  __shared__ int s_last;
+  // Before the programmatic-dependency wait: the position (written by the previous step's finalize,
+  // a graph launch earlier) and every K/V row but the newest (written by earlier steps).  The newest
+  // row and q come from the projection kernel just before this one: loaded after the wait.
+  pdl_trigger();
+  const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
+  const int G = nh / kvh;
+  const int b = m / count, t = m % count;
+  const int keys = (pos_dev ? *pos_dev : pos0) + t + 1;
+  const int S = (keys + KPS - 1) / KPS;
+  if (split >= S) return;  // the grid covers the longest visible range
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int j0 = split * KPS, nk = min(KPS, keys - j0);
+  const int fresh = keys - 1 - j0;  // this split's index of the newest key (may be outside [0, nk))
+  const size_t kvrow0 = ((size_t)b * kvh + g0) * capacity + j0;
+  const float scale = (float)(1.0 / sqrt((double)HD));
+
+  // every load of the block in flight at once
+  const int jj = tid / TPK, hf = tid % TPK;  // score role: key jj, dimension segment hf
+  const int f = tid % F, kg = tid / F;    // value role: dimensions 4f..4f+3 of keys kg, kg + KG, ...
+  float4 kreg[NK4], vreg[VPT];
+#pragma unroll
+  for (int i = 0; i < NK4; i++)
+    kreg[i] = jj < nk && jj != fresh
+                  ? *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * SEG + 4 * i)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int j = kg + i * KG;
+    vreg[i] = j < nk && j != fresh ? *reinterpret_cast<const float4 *>(vcache + (kvrow0 + j) * HD + 4 * f)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  pdl_wait();
+  if (jj == fresh) {
+#pragma unroll
+    for (int i = 0; i < NK4; i++)
+      kreg[i] = *reinterpret_cast<const float4 *>(kcache + (kvrow0 + jj) * HD + hf * SEG + 4 * i);
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; i++) {
+    const int j = kg + i * KG;
+    if (j == fresh) vreg[i] = *reinterpret_cast<const float4 *>(vcache + (kvrow0 + j) * HD + 4 * f);
+  }
+  for (int i = tid; i < G * HD; i += RA_THREADS)
+    qs[i / HD][i % HD] = q[(size_t)m * ldq + (size_t)(g0 * G) * HD + i];
+  __syncthreads();
+
+  {  // scores
+    float dots[RA_GMAX];
+#pragma unroll
+    for (int g = 0; g < RA_GMAX; g++) {
+      dots[g] = 0.0f;
+      if (g < G) {
+#pragma unroll
+        for (int i = 0; i < NK4; i++) {
+          const float4 qv = *reinterpret_cast<const float4 *>(&qs[g][hf * SEG + 4 * i]);
+          dots[g] = fmaf(qv.x, kreg[i].x, dots[g]);
+          dots[g] = fmaf(qv.y, kreg[i].y, dots[g]);
+          dots[g] = fmaf(qv.z, kreg[i].z, dots[g]);
+          dots[g] = fmaf(qv.w, kreg[i].w, dots[g]);
+        }
+      }
+    }
+    if constexpr (TPK == 2) {
+#pragma unroll
+      for (int g = 0; g < RA_GMAX; g++) dots[g] += __shfl_xor_sync(0xffffffffu, dots[g], 1);
+    }
+    if (hf == 0 && jj < nk) {
+#pragma unroll
+      for (int g = 0; g < RA_GMAX; g++)
+        if (g < G) sp[g][jj] = dots[g] * scale;
+    }
+  }
+  __syncthreads();
+  for (int g = warp; g < G; g += RA_THREADS / 32) {  // per head: max and sum of exp over the split
+    float mx = -INFINITY;
+    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sp[g][j]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.0f;
+    for (int j = lane; j < nk; j += 32) {
+      const float e = expf(sp[g][j] - mx);
+      sp[g][j] = e;
+      sum += e;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) {
+      red[g][0] = mx;
+      red[g][1] = sum;
+    }
+  }
+  __syncthreads();
+  {  // unnormalised weighted V sum
+#pragma unroll
+    for (int g = 0; g < RA_GMAX; g++) {
+      if (g < G) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPT; i++) {
+          const int j = kg + i * KG;
+          const float p = j < nk ? sp[g][j] : 0.0f;
+          a0 = fmaf(p, vreg[i].x, a0);
+          a1 = fmaf(p, vreg[i].y, a1);
+          a2 = fmaf(p, vreg[i].z, a2);
+          a3 = fmaf(p, vreg[i].w, a3);
+        }
+        *reinterpret_cast<float4 *>(&opart[kg][g][4 * f]) = make_float4(a0, a1, a2, a3);
+      }
+    }
+  }
+  __syncthreads();
+  const size_t slot = ((size_t)m * kvh + g0) * smax;  // this (row, KV head)'s split records
+  float *po = part, *pml = part + (size_t)gridDim.z * kvh * smax * RA_GMAX * HD;
+  for (int i = tid; i < G * HD; i += RA_THREADS) {
+    const int g = i / HD, d = i % HD;
+    float o = 0.0f;
+    for (int k = 0; k < KG; k++) o += opart[k][g][d];
+    if (S == 1) out[(size_t)m * ldo + (size_t)(g0 * G + g) * HD + d] = o / red[g][1];
+    else po[((slot + split) * RA_GMAX + g) * HD + d] = o;
+  }
+  if (S == 1) return;
+  if (tid < G) {
+    pml[((slot + split) * RA_GMAX + tid) * 2 + 0] = red[tid][0];
+    pml[((slot + split) * RA_GMAX + tid) * 2 + 1] = red[tid][1];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&counters[(size_t)m * kvh + g0], 1) == S - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = tid; i < G * HD; i += RA_THREADS) {
+    const int g = i / HD, d = i % HD;
+    float M = -INFINITY;
+    for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(&pml[((slot + s) * RA_GMAX + g) * 2]));
+    float num = 0.0f, den = 0.0f;
+    for (int s = 0; s < S; s++) {
+      const float w = expf(__ldcg(&pml[((slot + s) * RA_GMAX + g) * 2]) - M);
+      num = fmaf(w, __ldcg(&po[((slot + s) * RA_GMAX + g) * HD + d]), num);
+      den = fmaf(w, __ldcg(&pml[((slot + s) * RA_GMAX + g) * 2 + 1]), den);
+    }
+    out[(size_t)m * ldo + (size_t)(g0 * G + g) * HD + d] = num / den;
+  }
+  if (tid == 0) counters[(size_t)m * kvh + g0] = 0;
+}
+
+// Floats of split records decode_attention_reg_kernel needs for `rows` token rows.
+size_t decode_attention_reg_part_floats(int rows, int kvh, int capacity, int hd) {
+  const size_t smax = (size_t)(capacity + RA_KPS - 1) / RA_KPS;
+  return (size_t)rows * kvh * smax * RA_GMAX * ((size_t)hd + 2);
+}
+
+// Launches the split decode attention when the head size and group size have a form (hd in
+// {16, 32, 64, 128}, nh / kvh <= 8) and STB_DECODE_ATTENTION is not 0; returns false otherwise.
+bool launch_decode_attention_reg(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
+                             int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
+                             float *part, int *counters, bool pdl, cudaStream_t st) {
+  static const int enabled = env_int("STB_DECODE_ATTENTION", 1);
+  if (!enabled || !part || !counters || nh % kvh != 0 || nh / kvh > RA_GMAX) return false;
+  const int smax128 = (capacity + RA_KPS - 1) / RA_KPS;
+  // 256-key splits when 128-key splits would not fill the SMs anyway (small batch, few KV heads)
+  const bool wide = hd <= 64 && (long)rows * kvh * smax128 < 148;
+  const int smax = wide ? (capacity + 255) / 256 : smax128;
+  const dim3 grid(smax, kvh, rows);
+#define STB_RA_LAUNCH(HDV, KPSV)                                                                                   \
+  launch_kernel(decode_attention_reg_kernel<HDV, KPSV>, grid, dim3(RA_THREADS), 0, st, pdl, q, ldq, kc, vc, out, ldo,   \
+                count, nh, kvh, capacity, posd, pos0, part, counters, smax)
+  switch (hd) {
+    case 16:
+      if (wide) STB_RA_LAUNCH(16, 256);
+      else STB_RA_LAUNCH(16, 128);
+      return true;
+    case 32:
+      if (wide) STB_RA_LAUNCH(32, 256);
+      else STB_RA_LAUNCH(32, 128);
+      return true;
+    case 64:
+      if (wide) STB_RA_LAUNCH(64, 256);
+      else STB_RA_LAUNCH(64, 128);
+      return true;
+    case 128: STB_RA_LAUNCH(128, 128); return true;
+    default: return false;
+  }
+#undef STB_RA_LAUNCH
+}
+
+// Decode attention (one query token per batch row) in Float32, split over keys and shared by the
 // query heads of a KV group: block (split s, KV head, token row) takes keys [KPS s, KPS s + KPS) of
 // the visible range for all G = nh / kvh query heads of the group, so each K and V row is read once
 // per group.  The cache keeps a (row, KV head)'s keys contiguous, so one thread moves the split's K
@@ -452,7 +665,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
     const float *q, int ldq, const float *kcache, const float *vcache, float *out, int ldo, int count, int nh,
     int kvh, int capacity, const int *pos_dev, int pos0, float *part, int *counters, int smax, int *err) {
   static_assert(HD == 32 || HD == 64 || HD == 128, "head size");
-  static_assert(KPS % DA_WARPS == 0 && KPS >= DA_KPS_MIN, "keys per split");
+  static_assert(KPS % (4 * DA_WARPS) == 0 && KPS >= DA_KPS_MIN, "keys per split");
   static_assert(DA_WARPS * DA_GMAX * HD <= KPS * HD, "warp partials reuse the K tile");
   constexpr int DPL = HD / 32;  // dimensions per lane
   extern __shared__ __align__(128) uint8_t da_raw[];
@@ -521,42 +734,35 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   if (!s_ok) return;
   const float scale = (float)(1.0 / sqrt((double)HD));
 
-  // scores: warp w takes keys w, w + 4, ...
-  for (int j = warp; j < nk; j += DA_WARPS) {
-    float a[DA_GMAX];
-    const float *kr = Ks + j * HD + lane * DPL;
-    float kv[DPL];
+  // scores: warp w takes the key quads [4 w + 16 i, 4 w + 16 i + 4); a lane sums its dimensions for the
+  // 4 keys x 8 heads, then one reduce-scatter butterfly (31 shuffles, 5 levels) leaves lane l with
+  // the whole dot of key l / 8 and head l % 8.
+  for (int jb = 4 * warp; jb < nk; jb += 4 * DA_WARPS) {
+    float a[32];
 #pragma unroll
-    for (int d = 0; d < DPL; d++) kv[d] = kr[d];
+    for (int k = 0; k < 4; k++) {
+      float kv[DPL];
 #pragma unroll
-    for (int g = 0; g < DA_GMAX; g++) {
-      float s = 0.0f;
+      for (int d = 0; d < DPL; d++) kv[d] = jb + k < nk ? Ks[(jb + k) * HD + lane * DPL + d] : 0.0f;
 #pragma unroll
-      for (int d = 0; d < DPL; d++) s = fmaf(qr[g][d], kv[d], s);
-      a[g] = s;
-    }
-    // butterfly: after the 16 / 8 / 4 steps lane l holds head ((l >> 2) & 7) summed over 8 lanes
+      for (int g = 0; g < DA_GMAX; g++) {
+        float sacc = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const bool up = lane & 16;
-      const float send = up ? a[i] : a[i + 4], keep = up ? a[i + 4] : a[i];
-      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+        for (int d = 0; d < DPL; d++) sacc = fmaf(qr[g][d], kv[d], sacc);
+        a[k * DA_GMAX + g] = sacc;
+      }
     }
 #pragma unroll
-    for (int i = 0; i < 2; i++) {
-      const bool up = lane & 8;
-      const float send = up ? a[i] : a[i + 2], keep = up ? a[i + 2] : a[i];
-      a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    for (int half = 16; half >= 1; half >>= 1) {
+      const bool up = lane & half;
+#pragma unroll
+      for (int i = 0; i < half; i++) {
+        const float send = up ? a[i] : a[i + half], keep = up ? a[i + half] : a[i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, half);
+      }
     }
-    {
-      const bool up = lane & 4;
-      const float send = up ? a[0] : a[1], keep = up ? a[1] : a[0];
-      a[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-    a[0] += __shfl_xor_sync(0xffffffffu, a[0], 2);
-    a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
-    const int h = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-    if ((lane & 3) == 0 && h < G) sp[h * KPS + j] = a[0] * scale;
+    const int k = lane >> 3, h = lane & 7;
+    if (h < G && jb + k < nk) sp[h * KPS + jb + k] = a[0] * scale;
   }
   __syncthreads();
   for (int g = warp; g < G; g += DA_WARPS) {  // per head: max and sum of exp over the split
@@ -583,7 +789,7 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   for (int g = 0; g < DA_GMAX; g++)
 #pragma unroll
     for (int d = 0; d < DPL; d++) acc[g][d] = 0.0f;
-  for (int j = warp; j < nk; j += DA_WARPS) {  // unnormalised weighted V sum, same key split
+  for (int j = warp; j < nk; j += DA_WARPS) {  // unnormalised weighted V sum
     float vv[DPL];
 #pragma unroll
     for (int d = 0; d < DPL; d++) vv[d] = Vs[j * HD + lane * DPL + d];
@@ -674,28 +880,44 @@ bool launch_decode_attention(const float *q, int ldq, const float *kc, const flo
   static const int enabled = env_int("STB_DECODE_ATTENTION", 1);
   if (!enabled || !part || !counters || nh % kvh != 0 || nh / kvh > DA_GMAX) return false;
   if (hd != 32 && hd != 64 && hd != 128) return false;
-  static const int forced = env_int("STB_DA_KPS", 0);  // 32 / 64 / 128: fixed keys per split (tests)
+  static const int forced = env_int("STB_DA_KPS", 0);  // 32 / 64 / 128 / 256: fixed keys per split
   const long units = (long)rows * kvh;
   const long budget = 6L * tc::sm_count(device);
   int kps = units * ((capacity + 31) / 32) <= budget ? 32 : (units * ((capacity + 63) / 64) <= budget ? 64 : 128);
-  if (forced == 32 || forced == 64 || forced == 128) kps = forced;
+  if (forced == 32 || forced == 64 || forced == 128 || (forced == 256 && hd <= 64)) kps = forced;
   const int smax = (capacity + kps - 1) / kps;
   const dim3 grid(smax, kvh, rows);
 #define STB_DA(HDV, KPSV)                                                                                          \
   da_launch<HDV, KPSV>(grid, pdl, st, device, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, part, \
                        counters, smax, err)
-#define STB_DA_HD(HDV)          \
-  if (kps == 32) STB_DA(HDV, 32);   \
+#define STB_DA_HD(HDV)             \
+  if (kps == 32) STB_DA(HDV, 32);      \
   else if (kps == 64) STB_DA(HDV, 64); \
   else STB_DA(HDV, 128);
   switch (hd) {
     case 32: STB_DA_HD(32); break;
-    case 64: STB_DA_HD(64); break;
+    case 64:
+      if (kps == 256) STB_DA(64, 256);
+      else STB_DA_HD(64);
+      break;
     default: STB_DA_HD(128); break;
   }
 #undef STB_DA_HD
 #undef STB_DA
   return true;
+}
+
+// Two forms of the split decode attention: the register form (every K/V load of a block issued into
+// registers at entry, 256 threads, one memory round trip) is faster when the grid is small -- a few
+// blocks, where latency is everything (SmolLM2-shaped batch 1: 1756 vs 1607 decode tokens/s) -- and the
+// bulk-copy form when the grid spans the GPU several times (Llama-3-70B-shaped batch 8: 12 us less per
+// layer).  The register form is chosen when its grid (128-key splits) has fewer blocks than SMs;
+// STB_DA_IMPL = 0 / 1 forces the register / bulk-copy form.
+bool use_register_attention(int rows, int kvh, int hd, int capacity, int device) {
+  static const int forced = env_int("STB_DA_IMPL", -1);
+  if (forced == 0 || forced == 1) return forced == 0;
+  if (hd == 16) return true;  // the bulk-copy form has no head size 16
+  return (long)rows * kvh * ((capacity + 127) / 128) < tc::sm_count(device);
 }
 
 template <int HD>
@@ -1016,7 +1238,9 @@ void ensure_rows(stb_llama_cache *c, int rows) {
   c->xn = c->xh = c->qkvbuf = c->gubuf = 0;
   c->att_rows = c->batch;
   c->att_part = alloc_owned(s, c->owned,
-                            decode_attention_part_floats(c->batch, m->KV, c->capacity, m->hd) * sizeof(float));
+                            std::max(decode_attention_part_floats(c->batch, m->KV, c->capacity, m->hd),
+                                     decode_attention_reg_part_floats(c->batch, m->KV, c->capacity, m->hd)) *
+                                sizeof(float));
   c->att_count = alloc_owned(s, c->owned, (uint64_t)c->batch * m->KV * sizeof(int));
   STB_CUDA(cudaMemsetAsync((void *)c->att_count, 0, (size_t)c->batch * m->KV * sizeof(int), s->stream));
   c->skin = c->skin_bytes = 0;
@@ -1167,10 +1391,14 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
     {  // 2. attention: split GQA kernel for single-token steps, tiled kernel for chunks
       bool done = false;
       if (a.count == 1 && rows <= c->att_rows)
-        done = launch_decode_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc,
-                                       (float *)c->att, qw, rows, 1, m->NH, m->KV, m->hd, c->capacity, posd, c->used,
-                                       (float *)c->att_part, (int *)c->att_count, true, st, s->device,
-                                       session_error_word(s));
+        done = use_register_attention(rows, m->KV, m->hd, c->capacity, s->device)
+                   ? launch_decode_attention_reg((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc,
+                                                 (float *)c->att, qw, rows, 1, m->NH, m->KV, m->hd, c->capacity, posd,
+                                                 c->used, (float *)c->att_part, (int *)c->att_count, true, st)
+                   : launch_decode_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc,
+                                             (float *)c->att, qw, rows, 1, m->NH, m->KV, m->hd, c->capacity, posd,
+                                             c->used, (float *)c->att_part, (int *)c->att_count, true, st, s->device,
+                                             session_error_word(s));
       else if (a.count > 1)
         done = launch_flash_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc,
                                       (float *)c->att, qw, rows, a.count, m->NH, m->KV, m->hd, c->capacity, posd,

@@ -278,10 +278,11 @@ HD128 = dict(vocab_size=512, hidden_size=1024, intermediate_size=256, num_layers
              num_key_value_heads=1, max_positions=512, tie_word_embeddings=False, eos_token_ids=())
 
 
-@pytest.mark.parametrize("kps", [32, 64, 128])
-def test_decode_attention_splits_head128_group8(kps):
-    """The split decode attention on head size 128 with 8 query heads per KV head, keys per split forced
-    to 32 / 64 / 128 (STB_DA_KPS, read once per process: a child process each), over 127 prompt tokens
+@pytest.mark.parametrize("impl,kps", [(1, 32), (1, 64), (1, 128), (0, 0)])
+def test_decode_attention_splits_head128_group8(impl, kps):
+    """The split decode attention on head size 128 with 8 query heads per KV head: the bulk-copy form with
+    keys per split forced to 32 / 64 / 128, and the register form (STB_DA_IMPL / STB_DA_KPS, read once per
+    process: a child process each), over 127 prompt tokens
     (254 rows: below the tensor-core prefill threshold, so the whole run keeps Float32 activations) and 8
     decode steps for 2 rows, so splits merge: greedy ids identical to the oracle and the logits of a
     cached step within 1e-5 (1 + |e|)."""
@@ -314,7 +315,7 @@ def test_decode_attention_splits_head128_group8(kps):
         "    c.close()\n"
         "s.close()\n"
         "print('ok')\n")
-    env = dict(os.environ, STB_DA_KPS=str(kps))
+    env = dict(os.environ, STB_DA_KPS=str(kps), STB_DA_IMPL=str(impl))
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
 
