@@ -38,6 +38,9 @@ bool peer_usable(stb_session *s, uint64_t elems);
 PeerArgs peer_args(stb_session *s, int region);
 void peer_reduce_launch(stb_session *s, int region, long total, const float *residual, float *out);
 void peer_reset(stb_session *s);
+bool launch_flash_attention_tc(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
+                               int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
+                               int *err, int device, cudaStream_t st);
 }  // namespace stb
 
 using namespace stb;
@@ -1313,7 +1316,10 @@ int enqueue_layer_tc(stb_llama_cache *c, size_t l, int rows, int count, const in
   launch_kernel(rope_append_kernel, dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, st, false,
                 (const float *)c->qkvbuf, nqkv, (const double2 *)m->rope, posd, c->used, count, m->NH, m->KV, m->hd,
                 c->capacity, (float *)c->qbuf, qw, kc, vc, rows);
-  if (!launch_flash_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw,
+  if (!launch_flash_attention_tc((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att,
+                                 qw, rows, count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, err, s->device,
+                                 st) &&
+      !launch_flash_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw,
                               rows, count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, s->device, st))
     launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), attention_smem(c->capacity, m->hd), st,
                   false, (const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows,

@@ -195,27 +195,30 @@ def test_tensor_core_prefill_within_prefill_tolerance(session, tiny):
         c.close()
 
 
-@pytest.mark.parametrize("heads,kv", [(8, 2), (4, 1)])
-def test_tiled_prefill_attention_on_long_chunks(session, heads, kv):
-    """Tensor-core prefill chunks use the tiled Float32 attention (64-query x 64-key tiles, online
-    softmax).  Head sizes 64 and 128, grouped heads, two batch rows, and a second chunk that attends
-    to the first chunk's cached keys (ragged tiles on both axes): logits within the tensor-core
-    prefill tolerance, 1e-2 normwise per row."""
+@pytest.mark.parametrize("heads,kv,chunks", [(8, 2, ((0, 100), (100, 150))), (4, 1, ((0, 100), (100, 150))),
+                                             (4, 1, ((0, 300),)), (8, 8, ((0, 40), (40, 300)))])
+def test_tiled_prefill_attention_on_long_chunks(session, heads, kv, chunks):
+    """Tensor-core prefill chunks use the tcgen05 flash attention (128-query x 128-key tiles, BF16 Q / K
+    / V / P, online softmax in FP32).  Head sizes 64 and 128, grouped and ungrouped heads, two batch
+    rows, several query and key tiles with the causal diagonal inside a tile, and a second chunk that
+    attends to the first chunk's cached keys (ragged tiles on both axes): logits within the
+    tensor-core prefill tolerance, 1e-2 normwise per row."""
     cfg = LlamaConfig(vocab_size=1000, hidden_size=512, intermediate_size=1024, num_layers=1,
-                      num_attention_heads=heads, num_key_value_heads=kv, max_positions=256,
+                      num_attention_heads=heads, num_key_value_heads=kv, max_positions=512,
                       tie_word_embeddings=False, eos_token_ids=())
     ref = oracle_model(cfg, seed=23)
     rng = np.random.default_rng(23)
-    prompt = rng.integers(0, cfg.vocab_size, (2, 150))
+    end = chunks[-1][1]
+    prompt = rng.integers(0, cfg.vocab_size, (2, end))
     with BackendLlama.prepare_random(session, cfg, seed=23, tc_prefill_rows=64) as m:
-        c = m.new_cache(2, 160)
-        oc = ref.new_cache(2, 160)
-        for lo, hi in ((0, 100), (100, 150)):
+        c = m.new_cache(2, end + 10)
+        oc = ref.new_cache(2, end + 10)
+        for lo, hi in chunks:
             got, _ = c.decode(prompt[:, lo:hi])
             want = ref.decode(oc, prompt[:, lo:hi])
             rel = np.linalg.norm(got - want, axis=-1) / np.linalg.norm(want, axis=-1)
             assert rel.max() <= 1e-2, (lo, rel.max())
-        assert c.position == 150
+        assert c.position == end
         ref.free_cache(oc)
         c.close()
 
