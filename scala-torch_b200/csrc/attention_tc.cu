@@ -33,7 +33,7 @@ namespace {
 using namespace tc;
 
 constexpr int AT_Q = 128, AT_K = 128, AT_THREADS = 128;
-constexpr int AT_SMEM_FLOOR = 116 * 1024;  // keeps residency at two CTAs per SM (TMEM: 2 x 256 columns)
+constexpr int AT_SMEM_FLOOR = 100 * 1024;  // at most two CTAs per SM (TMEM: 2 x 256 columns of 512)
 
 template <int HD>
 struct AttnTcShape {
