@@ -387,53 +387,22 @@ __global__ void __launch_bounds__(256) skinny_fixup_kernel(const GemvParams p, c
   }
 }
 
-// ---------------------------------------------------------------- fused form (default)
+// ---------------------------------------------------------------- fused fixup (default)
 //
-// One kernel per 64-row block instead of three: the prologue's work (RMSNorm inverse and the
-// three-term BF16 split) moves into two converter warps that build each stage's B tile in shared
-// memory from the Float32 activations (L2-resident), and the fixup moves into the epilogue warps:
-// a tile covered by one CTA is finished from its registers; a tile split across CTAs has each
-// piece stored, and the CTA that completes the tile (a per-tile counter) adds the pieces in piece
-// (= K) order and applies the epilogue -- the same sums in the same order as the fixup kernel.
-// Roles (256 threads): warp 0 W producer (TMA, issued before the programmatic-dependency wait),
-// warp 1 MMA issuer, warps 2-5 epilogue, warps 6-7 converters; warps 2-7 first compute the rows'
-// inverse RMS.  The stage's full barrier takes the TMA bytes and one arrival per converter warp.
-// Decisions that cross warps go through one waiting thread and a named barrier, so every warp of
-// a group leaves together when a wait expires.  The per-tile counters live at the start of the
-// scratch and are left at zero by every launch (the caller zeroes them once).
+// The GEMM and the fixup in one kernel: the epilogue warps finish a tile covered by one CTA from
+// their registers; for a tile split across CTAs each piece is stored and the CTA that completes the
+// tile (a per-tile counter) adds the pieces in piece (= K) order and applies the epilogue -- the
+// same sums in the same order as the fixup kernel.  The prologue kernel stays (the split
+// activations arrive by TMA, as in the three-kernel form).  Decisions that cross the epilogue warps
+// go through one waiting thread and a named barrier, so the four warps always leave together.  The
+// per-tile counters live at the start of the scratch and every launch leaves them at zero (the
+// caller zeroes them once).
 constexpr int SKF_COUNTERS_BYTES = 64 * 1024;  // int per 128-row tile: N up to 2,097,152
 
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// Three-term split of 8 activations into the K-major swizzled B tile (rows m, NT + m, 2 NT + m).
-template <int NT>
-__device__ __forceinline__ void skf_store_chunk(uint32_t btile, int m, int c, const float (&v)[8]) {
-  uint32_t w0[4], w1[4], w2[4];
-#pragma unroll
-  for (int e = 0; e < 8; e += 2) {
-    uint16_t a0, a1, a2, b0, b1, b2;
-    skinny_split(v[e], a0, a1, a2);
-    skinny_split(v[e + 1], b0, b1, b2);
-    w0[e / 2] = (uint32_t)a0 | ((uint32_t)b0 << 16);
-    w1[e / 2] = (uint32_t)a1 | ((uint32_t)b1 << 16);
-    w2[e / 2] = (uint32_t)a2 | ((uint32_t)b2 << 16);
-  }
-  const int r0 = m, r1 = NT + m, r2 = 2 * NT + m;
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(btile + r0 * 128 + ((c ^ (r0 & 7)) << 4)), "r"(w0[0]),
-               "r"(w0[1]), "r"(w0[2]), "r"(w0[3])
-               : "memory");
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(btile + r1 * 128 + ((c ^ (r1 & 7)) << 4)), "r"(w1[0]),
-               "r"(w1[1]), "r"(w1[2]), "r"(w1[3])
-               : "memory");
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(btile + r2 * 128 + ((c ^ (r2 & 7)) << 4)), "r"(w2[0]),
-               "r"(w2[1]), "r"(w2[2]), "r"(w2[3])
-               : "memory");
-}
-
-// The vector GEMV's epilogue for output row `row` (one thread per row, lanes = consecutive rows) and
-// token rows m0 .. m0 + mb - 1 (v[m]).
 template <int NT, int EPI>
 __device__ __forceinline__ void skf_epilogue(const GemvParams &p, int row, int lane, int m0, int mb,
                                              const float (&v)[NT]) {
@@ -490,9 +459,10 @@ __device__ __forceinline__ void skf_epilogue(const GemvParams &p, int row, int l
 }
 
 template <int NT, int EPI>
-__global__ void __launch_bounds__(256, 1)
-    gemm_skinny_fused_kernel(const __grid_constant__ CUtensorMap tw, const GemvParams p, float *part, int *counters,
-                             int m0, int mb, int kbs, long long T, int pmax, uint32_t idesc, int *err) {
+__global__ void __launch_bounds__(192, 1)
+    gemm_skinny_fused_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
+                             const GemvParams p, float *part, int *counters, int m0, int mb, int kbs, long long T,
+                             int pmax, uint32_t idesc, int *err) {
   using S = SkinnyShape<NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -502,7 +472,6 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t drain = smem_u32(bars + 2 * S::STAGES + 2 * SK_ACC_MAX);
   uint32_t *tmem_slot = (uint32_t *)(bars + 2 * S::STAGES + 2 * SK_ACC_MAX + 1);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
-  __shared__ double s_inv[64];
   __shared__ int s_ok[2], s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -511,7 +480,7 @@ __global__ void __launch_bounds__(256, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; s++) {
-      mbar_init(full0 + 8 * s, 3);  // the TMA producer's expect_tx arrival + one per converter warp
+      mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
     for (int r = 0; r < S::ACC; r++) {
@@ -535,13 +504,25 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t sa0 = smem_u32(smem), sb0 = sa0 + S::STAGES * S::A_BYTES;
 
   if (warp == 0) {
-    if (lane == 0) {  // weights only: they never depend on the previous kernel
-      int stage = 0;
-      uint32_t phase = 0;
-      for (long long i = i0; i < i1; i++) {
+    if (lane == 0) {
+      // Weights never depend on the previous kernel: the first ring's W tiles load before the wait
+      // for the split activations.
+      const int pre = (int)min((long long)S::STAGES, i1 - i0);
+      for (int j = 0; j < pre; j++) {
+        const long long i = i0 + j;
+        mbar_expect_tx(full0 + 8 * j, S::STAGE);
+        tma_load_2d(sa0 + j * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * j);
+      }
+      pdl_wait();
+      for (int j = 0; j < pre; j++)
+        tma_load_2d(sb0 + j * S::B_BYTES, &tx, (int)((i0 + j) % kbs) * BK, 0, full0 + 8 * j);
+      int stage = pre % S::STAGES;
+      uint32_t phase = pre == S::STAGES ? 1u : 0u;
+      for (long long i = i0 + pre; i < i1; i++) {
         if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, 31)) break;
-        mbar_expect_tx(full0 + 8 * stage, S::A_BYTES);
+        mbar_expect_tx(full0 + 8 * stage, S::STAGE);
         tma_load_2d(sa0 + stage * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * stage);
+        tma_load_2d(sb0 + stage * S::B_BYTES, &tx, (int)(i % kbs) * BK, 0, full0 + 8 * stage);
         if (++stage == S::STAGES) {
           stage = 0;
           phase ^= 1;
@@ -583,131 +564,72 @@ __global__ void __launch_bounds__(256, 1)
         mbar_wait(drain, 0, &no_abort, err, 33);
       }
     }
-  } else {
-    pdl_wait();  // activations (and the residual / outputs) belong to the previous kernel
-    if (p.norm_w) {  // inverse RMS of each token row, as CpuFloatBackend.rmsNorm: squares summed in double
-      const int gw = warp - 2;  // 0..5
-      for (int m = gw; m < mb; m += 6) {
-        const float *xr = p.x + (size_t)(m0 + m) * p.ldx;
-        double sq = 0.0;
-        for (int k = lane; k < p.K; k += 32) {
-          const double v = (double)xr[k];
-          sq = __dadd_rn(sq, __dmul_rn(v, v));
-        }
+  } else {  // epilogue warps 2-5: TMEM lane quarter warp & 3 = tile rows 32 q .. 32 q + 31
+    pdl_wait();  // the previous kernel may still read `part` or the outputs
+    const int q = warp & 3;
+    const int et = threadIdx.x - 64;  // 0..127
+    float acc[NT];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) sq = __dadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, off));
-        if (lane == 0) s_inv[m] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(sq, (double)p.K), p.norm_eps)));
+    for (int m = 0; m < NT; m++) acc[m] = 0.0f;
+    int grp = 0, cnt = 0;
+    for (long long i = i0; i < i1; i++) {
+      if (!(++cnt == S::GK || (i + 1) % kbs == 0 || i + 1 == i1)) continue;  // inside an accumulator group
+      cnt = 0;
+      const int r = grp % S::ACC;
+      // one waiter; the flag is double-buffered so a slow reader never sees the next group's value
+      if (et == 0) s_ok[grp & 1] = mbar_wait(accf0 + 8 * r, (uint32_t)(grp / S::ACC) & 1u, abort_flag, err, 34);
+      named_sync(1, 128);
+      if (!s_ok[grp & 1]) break;
+      tc_fence_after();
+      constexpr int W = NT == 16 ? 16 : 32;
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(r * S::ACC_STRIDE);
+#pragma unroll
+      for (int c = 0; c < NT / W; c++) {  // columns t * NT + m hold term t of token row m
+        float lo[W], mid[W], hi[W];
+        tmem_ld3<W>(base + (uint32_t)(2 * NT + c * W), base + (uint32_t)(NT + c * W), base + (uint32_t)(c * W), lo,
+                    mid, hi);
+#pragma unroll
+        for (int jj = 0; jj < W; jj++) acc[c * W + jj] += (lo[jj] + mid[jj]) + hi[jj];
       }
-      named_sync(2, 192);
-    }
-    if (warp >= 6) {  // converters: the stage's [x0; x1; x2] tile for K block i % kbs
-      const int cl = threadIdx.x - 192;
-      const bool vec = (p.ldx & 3) == 0 && ((uintptr_t)p.x & 15) == 0;
-      int stage = 0;
-      uint32_t phase = 0;
-      for (long long i = i0; i < i1; i++) {
-        int got = 0;
-        if (lane == 0) got = mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, 36);
-        if (!__shfl_sync(0xffffffffu, got, 0)) break;
-        const int kb = (int)(i % kbs);
-        const uint32_t bt = sb0 + stage * S::B_BYTES;
-        for (int task = cl; task < NT * 8; task += 64) {
-          const int m = task >> 3, c = task & 7, k = kb * BK + c * 8;
-          float v[8];
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce0 + 8 * r);
+      grp++;
+      if (i + 1 == i1 || (i + 1) % kbs == 0) {  // end of this CTA's piece of tile t
+        const int t = (int)(i / kbs);
+        const int first = sk_cta_of((long long)t * kbs, T, G), last = sk_cta_of((long long)(t + 1) * kbs - 1, T, G);
+        const int np = last - first + 1, piece = cta - first;
+        const int row = t * SK_BM + q * 32 + lane;
+        if (np == 1) {
+          skf_epilogue<NT, EPI>(p, row, lane, m0, mb, acc);
+        } else {
+          if (row < p.N) {
+            float *pp = part + ((size_t)t * pmax + piece) * mb * SK_BM + q * 32 + lane;
 #pragma unroll
-          for (int e = 0; e < 8; e++) v[e] = 0.0f;
-          if (m < mb && k < p.K) {
-            const float *src = p.x + (size_t)(m0 + m) * p.ldx + k;
-            if (vec) {
-              const float4 a = *reinterpret_cast<const float4 *>(src), b = *reinterpret_cast<const float4 *>(src + 4);
-              v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; e++) v[e] = src[e];
-            }
-            if (p.norm_w) {
-              const double inv = s_inv[m];
-#pragma unroll
-              for (int e = 0; e < 8; e++)
-                v[e] = __double2float_rn(__dmul_rn(__dmul_rn((double)v[e], inv), (double)p.norm_w[k + e]));
-            }
+            for (int m = 0; m < NT; m++)
+              if (m < mb) pp[(size_t)m * SK_BM] = acc[m];
           }
-          skf_store_chunk<NT>(bt, m, c, v);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(full0 + 8 * stage);
-        if (++stage == S::STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-    } else {  // epilogue warps 2-5: TMEM lane quarter warp & 3 = tile rows 32 q .. 32 q + 31
-      const int q = warp & 3;
-      const int et = threadIdx.x - 64;  // 0..127
-      float acc[NT];
-#pragma unroll
-      for (int m = 0; m < NT; m++) acc[m] = 0.0f;
-      int grp = 0, cnt = 0;
-      for (long long i = i0; i < i1; i++) {
-        if (!(++cnt == S::GK || (i + 1) % kbs == 0 || i + 1 == i1)) continue;  // inside an accumulator group
-        cnt = 0;
-        const int r = grp % S::ACC;
-        // one waiter; the flag is double-buffered so a slow reader never sees the next group's value
-        if (et == 0) s_ok[grp & 1] = mbar_wait(accf0 + 8 * r, (uint32_t)(grp / S::ACC) & 1u, abort_flag, err, 34);
-        named_sync(1, 128);
-        if (!s_ok[grp & 1]) break;
-        tc_fence_after();
-        constexpr int W = NT == 16 ? 16 : 32;
-        const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(r * S::ACC_STRIDE);
-#pragma unroll
-        for (int c = 0; c < NT / W; c++) {  // columns t * NT + m hold term t of token row m
-          float lo[W], mid[W], hi[W];
-          tmem_ld3<W>(base + (uint32_t)(2 * NT + c * W), base + (uint32_t)(NT + c * W), base + (uint32_t)(c * W), lo,
-                      mid, hi);
-#pragma unroll
-          for (int jj = 0; jj < W; jj++) acc[c * W + jj] += (lo[jj] + mid[jj]) + hi[jj];
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acce0 + 8 * r);
-        grp++;
-        if (i + 1 == i1 || (i + 1) % kbs == 0) {  // end of this CTA's piece of tile t
-          const int t = (int)(i / kbs);
-          const int first = sk_cta_of((long long)t * kbs, T, G), last = sk_cta_of((long long)(t + 1) * kbs - 1, T, G);
-          const int np = last - first + 1, piece = cta - first;
-          const int row = t * SK_BM + q * 32 + lane;
-          if (np == 1) {
-            skf_epilogue<NT, EPI>(p, row, lane, m0, mb, acc);
-          } else {
-            if (row < p.N) {
-              float *pp = part + ((size_t)t * pmax + piece) * mb * SK_BM + q * 32 + lane;
-#pragma unroll
-              for (int m = 0; m < NT; m++)
-                if (m < mb) pp[(size_t)m * SK_BM] = acc[m];
-            }
+          __threadfence();
+          named_sync(1, 128);
+          if (et == 0) s_last = atomicAdd(&counters[t], 1) == np - 1;
+          named_sync(1, 128);
+          if (s_last) {  // every piece is stored: add them in piece order (into acc, already stored)
             __threadfence();
-            named_sync(1, 128);
-            if (et == 0) s_last = atomicAdd(&counters[t], 1) == np - 1;
-            named_sync(1, 128);
-            if (s_last) {  // every piece is stored: add them in piece order (into acc, already stored)
-              __threadfence();
-              const float *pp = part + (size_t)t * pmax * mb * SK_BM + q * 32 + lane;
+            const float *pp = part + (size_t)t * pmax * mb * SK_BM + q * 32 + lane;
 #pragma unroll
-              for (int m = 0; m < NT; m++) {
-                if (m < mb && row < p.N) {
-                  float s = __ldcg(pp + (size_t)m * SK_BM);
-                  for (int pc = 1; pc < np; pc++) s += __ldcg(pp + ((size_t)pc * mb + m) * SK_BM);
-                  acc[m] = s;
-                }
+            for (int m = 0; m < NT; m++) {
+              if (m < mb && row < p.N) {
+                float s = __ldcg(pp + (size_t)m * SK_BM);
+                for (int pc = 1; pc < np; pc++) s += __ldcg(pp + ((size_t)pc * mb + m) * SK_BM);
+                acc[m] = s;
               }
-              skf_epilogue<NT, EPI>(p, row, lane, m0, mb, acc);
-              if (et == 0) counters[t] = 0;
             }
+            skf_epilogue<NT, EPI>(p, row, lane, m0, mb, acc);
+            if (et == 0) counters[t] = 0;
           }
-#pragma unroll
-          for (int m = 0; m < NT; m++) acc[m] = 0.0f;
         }
+#pragma unroll
+        for (int m = 0; m < NT; m++) acc[m] = 0.0f;
       }
     }
   }
@@ -744,15 +666,15 @@ SkinnyPlan skinny_plan(int M, int N, int K, int device) {
   return q;
 }
 
-// STB_SKINNY_FUSED=0 keeps the three-kernel form (prologue, GEMM, fixup).
+// STB_SKINNY_FUSED=0 keeps the three-kernel form (prologue, GEMM, separate fixup).
 bool skinny_fused() {
   static const int fused = env_int("STB_SKINNY_FUSED", 1);
   return fused != 0;
 }
 
 template <int NT, int EPI>
-void launch_fused(const SkinnyPlan &q, const CUtensorMap &tw, const GemvParams &p, float *part, int *counters, int m0,
-                  int mb, int *err, int device, cudaStream_t stream) {
+void launch_fused(const SkinnyPlan &q, const CUtensorMap &tw, const CUtensorMap &tx, const GemvParams &p, float *part,
+                  int *counters, int m0, int mb, int *err, int device, cudaStream_t stream) {
   static std::mutex mu;
   static bool configured[64] = {};
   {
@@ -763,8 +685,8 @@ void launch_fused(const SkinnyPlan &q, const CUtensorMap &tw, const GemvParams &
       if (device >= 0 && device < 64) configured[device] = true;
     }
   }
-  launch_kernel(gemm_skinny_fused_kernel<NT, EPI>, dim3(q.grid), dim3(256), (size_t)SkinnyShape<NT>::SMEM, stream,
-                m0 > 0 || p.pdl, tw, p, part, counters, m0, mb, q.kbs, q.iters, q.pmax, skinny_idesc(NT), err);
+  launch_kernel(gemm_skinny_fused_kernel<NT, EPI>, dim3(q.grid), dim3(192), (size_t)SkinnyShape<NT>::SMEM, stream,
+                true, tw, tx, p, part, counters, m0, mb, q.kbs, q.iters, q.pmax, skinny_idesc(NT), err);
 }
 
 template <int NT>
@@ -809,7 +731,7 @@ void skinny_prepare(int device) {
 
 uint64_t skinny_scratch_bytes(int M, int N, int K, int device) {
   const SkinnyPlan q = skinny_plan(std::min(M, 64), N, K, device);  // one 64-row block at a time
-  return std::max<uint64_t>(q.x3_bytes + q.part_bytes, (uint64_t)SKF_COUNTERS_BYTES + q.part_bytes);
+  return (uint64_t)SKF_COUNTERS_BYTES + q.x3_bytes + q.part_bytes;
 }
 
 template <int EPI>
@@ -823,20 +745,24 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
   constexpr bool paired = EPI == EPI_SILU || EPI == EPI_QKV;
   const int units = paired ? p.N / 2 : p.N;
   int launches = 0;
-  if (skinny_fused()) {
+  if (skinny_fused()) {  // prologue + GEMM with the fixup inside, per 64-row block
     STB_REQUIRE((p.N + SK_BM - 1) / SK_BM <= SKF_COUNTERS_BYTES / 4, "skinny Linear: too many output rows");
     int *counters = (int *)scratch;
-    float *part = (float *)((char *)scratch + SKF_COUNTERS_BYTES);
     if (!counters_clean) {
       STB_CUDA(cudaMemsetAsync(counters, 0, (size_t)((p.N + SK_BM - 1) / SK_BM) * 4, stream));
     }
     for (int m0 = 0; m0 < p.M; m0 += 64) {
       const int mb = std::min(64, p.M - m0);
       const SkinnyPlan q = skinny_plan(mb, p.N, p.K, device);
-      if (q.nt == 16) launch_fused<16, EPI>(q, tw, p, part, counters, m0, mb, err, device, stream);
-      else if (q.nt == 32) launch_fused<32, EPI>(q, tw, p, part, counters, m0, mb, err, device, stream);
-      else launch_fused<64, EPI>(q, tw, p, part, counters, m0, mb, err, device, stream);
-      launches += 1;
+      uint16_t *x3 = (uint16_t *)((char *)scratch + SKF_COUNTERS_BYTES);
+      float *part = (float *)((char *)x3 + q.x3_bytes);
+      launch_kernel(skinny_prep_kernel, dim3((p.K + 1023) / 1024, q.nt), dim3(256), 0, stream, m0 > 0 || p.pdl,
+                    p.x + (size_t)m0 * p.ldx, p.ldx, p.norm_w, p.norm_eps, x3, mb, q.nt, p.K);
+      const CUtensorMap tx = make_map(x3, STB_BF16, (uint64_t)3 * q.nt, (uint64_t)p.K, 3 * q.nt);
+      if (q.nt == 16) launch_fused<16, EPI>(q, tw, tx, p, part, counters, m0, mb, err, device, stream);
+      else if (q.nt == 32) launch_fused<32, EPI>(q, tw, tx, p, part, counters, m0, mb, err, device, stream);
+      else launch_fused<64, EPI>(q, tw, tx, p, part, counters, m0, mb, err, device, stream);
+      launches += 2;
     }
     check_launch("skinny");
     return launches;
