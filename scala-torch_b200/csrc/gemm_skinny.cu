@@ -101,22 +101,6 @@ __device__ __forceinline__ int sk_cta_of(long long i, long long T, int G) {
   return c;
 }
 
-// x = h0 + h1 + h2 in BF16 (h0 = rne(x), h1 = rne(x - h0), h2 = rne(x - h0 - h1); both differences
-// exact).  Non-finite x keeps its class in the first term alone (Inf - Inf would make the lower
-// terms NaN); a finite x that rounds past BF16's largest finite value (|x| > 0x1.fep127) takes the
-// truncated first term instead, which stays finite and leaves an exact 16-bit remainder.
-__device__ __forceinline__ void skinny_split(float v, uint16_t &h0, uint16_t &h1, uint16_t &h2) {
-  h0 = f32_to_bf16_rne(v);
-  h1 = h2 = 0;
-  if (isfinite(v)) {
-    if ((h0 & 0x7f80u) == 0x7f80u) h0 = (uint16_t)(__float_as_uint(v) >> 16);
-    const float r1 = v - __uint_as_float((uint32_t)h0 << 16);  // exact
-    h1 = f32_to_bf16_rne(r1);
-    const float r2 = r1 - __uint_as_float((uint32_t)h1 << 16);  // exact
-    h2 = f32_to_bf16_rne(r2);
-  }
-}
-
 // x [M][K] (row stride ldx), optionally RMS-normalised as the vector GEMV does it, -> x3 [3][NT][K].
 // Block (kb, m) converts elements [kb * 1024, kb * 1024 + 1024) of row m, four per thread; with
 // RMSNorm every block of a row recomputes the row's inverse RMS with the GEMV's exact loop and
@@ -149,8 +133,17 @@ __global__ void __launch_bounds__(256) skinny_prep_kernel(const float *x, int ld
       v = x[(size_t)m * ldx + k];
       if (norm_w) v = __double2float_rn(__dmul_rn(__dmul_rn((double)v, inv), (double)norm_w[k]));
     }
-    uint16_t h0, h1, h2;
-    skinny_split(v, h0, h1, h2);
+    // Non-finite v keeps its class in the first term alone (Inf - Inf would make the lower terms
+    // NaN); a finite v that rounds past BF16's largest finite value (|v| > 0x1.fep127) takes the
+    // truncated first term instead, which stays finite and leaves an exact 16-bit remainder.
+    uint16_t h0 = f32_to_bf16_rne(v), h1 = 0, h2 = 0;
+    if (isfinite(v)) {
+      if ((h0 & 0x7f80u) == 0x7f80u) h0 = (uint16_t)(__float_as_uint(v) >> 16);
+      const float r1 = v - __uint_as_float((uint32_t)h0 << 16);  // exact
+      h1 = f32_to_bf16_rne(r1);
+      const float r2 = r1 - __uint_as_float((uint32_t)h1 << 16);  // exact
+      h2 = f32_to_bf16_rne(r2);
+    }
     x3[(size_t)m * K + k] = h0;
     x3[((size_t)NT + m) * K + k] = h1;
     x3[((size_t)2 * NT + m) * K + k] = h2;
@@ -387,260 +380,6 @@ __global__ void __launch_bounds__(256) skinny_fixup_kernel(const GemvParams p, c
   }
 }
 
-// ---------------------------------------------------------------- fused fixup (default)
-//
-// The GEMM and the fixup in one kernel: the epilogue warps finish a tile covered by one CTA from
-// their registers; for a tile split across CTAs each piece is stored and the CTA that completes the
-// tile (a per-tile counter) adds the pieces in piece (= K) order and applies the epilogue -- the
-// same sums in the same order as the fixup kernel.  The prologue kernel stays (the split
-// activations arrive by TMA, as in the three-kernel form).  Decisions that cross the epilogue warps
-// go through one waiting thread and a named barrier, so the four warps always leave together.  The
-// per-tile counters live at the start of the scratch and every launch leaves them at zero (the
-// caller zeroes them once).
-constexpr int SKF_COUNTERS_BYTES = 64 * 1024;  // int per 128-row tile: N up to 2,097,152
-
-__device__ __forceinline__ void named_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-template <int NT, int EPI>
-__device__ __forceinline__ void skf_epilogue(const GemvParams &p, int row, int lane, int m0, int mb,
-                                             const float (&v)[NT]) {
-  const bool in = row < p.N;
-  if constexpr (EPI == EPI_PLAIN) {
-    if (in)
-#pragma unroll
-      for (int m = 0; m < NT; m++)
-        if (m < mb) p.y[(size_t)(m0 + m) * p.ldy + row] = p.bias ? v[m] + p.bias[row] : v[m];
-  } else if constexpr (EPI == EPI_RESID) {
-    if (in)
-#pragma unroll
-      for (int m = 0; m < NT; m++)
-        if (m < mb) p.y[(size_t)(m0 + m) * p.ldy + row] = p.residual[(size_t)(m0 + m) * p.ldr + row] + v[m];
-  } else if constexpr (EPI == EPI_PEER) {
-    if (in) {
-      const uint32_t use = (uint32_t)(p.peer.my_epoch[p.peer.region] + 1ull);
-#pragma unroll
-      for (int m = 0; m < NT; m++) {
-        if (m >= mb) continue;
-        const size_t off =
-            ((size_t)p.peer.region * p.peer.tp + p.peer.rank) * p.peer.slot_elems + (size_t)(m0 + m) * p.ldy + row;
-        const unsigned long long w = peer_word(v[m], use);
-        for (int r = 0; r < p.peer.tp; r++) peer_store(p.peer.slots[r] + off, w);
-      }
-    }
-  } else if constexpr (EPI == EPI_SILU || EPI == EPI_QKV) {
-    const int pos = EPI == EPI_QKV ? (p.pos_dev ? *p.pos_dev : p.pos0) : 0;
-#pragma unroll
-    for (int m = 0; m < NT; m++) {
-      const float other = __shfl_xor_sync(0xffffffffu, v[m], 1);  // the pair's odd row
-      if (m >= mb || !in || (lane & 1)) continue;
-      if constexpr (EPI == EPI_SILU) p.y[(size_t)(m0 + m) * p.ldy + (row >> 1)] = silu_ref(v[m]) * other;
-      else qkv_store_pair(p, m0 + m, row >> 1, v[m], other, pos);
-    }
-  } else if constexpr (EPI == EPI_LOGITS) {
-#pragma unroll
-    for (int m = 0; m < NT; m++) {
-      unsigned long long key = 0ull;
-      if (in && m < mb) {
-        p.y[(size_t)(m0 + m) * p.ldy + row] = v[m];
-        key = argmax_key(v[m], row + p.row_offset);
-      }
-      if (p.best) {
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-          const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
-          key = o > key ? o : key;
-        }
-        if (lane == 0 && key) atomicMax(&p.best[m0 + m], key);
-      }
-    }
-  }
-}
-
-template <int NT, int EPI>
-__global__ void __launch_bounds__(192, 1)
-    gemm_skinny_fused_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
-                             const GemvParams p, float *part, int *counters, int m0, int mb, int kbs, long long T,
-                             int pmax, uint32_t idesc, int *err) {
-  using S = SkinnyShape<NT>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t *bars = (uint64_t *)(smem + S::STAGES * S::STAGE);
-  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S::STAGES);
-  const uint32_t accf0 = smem_u32(bars + 2 * S::STAGES), acce0 = smem_u32(bars + 2 * S::STAGES + SK_ACC_MAX);
-  const uint32_t drain = smem_u32(bars + 2 * S::STAGES + 2 * SK_ACC_MAX);
-  uint32_t *tmem_slot = (uint32_t *)(bars + 2 * S::STAGES + 2 * SK_ACC_MAX + 1);
-  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
-  __shared__ int s_ok[2], s_last;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cta = blockIdx.x, G = gridDim.x;
-  const long long i0 = sk_start(cta, T, G), i1 = sk_start(cta + 1, T, G);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S::STAGES; s++) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, 1);
-    }
-    for (int r = 0; r < S::ACC; r++) {
-      mbar_init(accf0 + 8 * r, 1);
-      mbar_init(acce0 + 8 * r, 4);
-    }
-    mbar_init(drain, 1);
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 2) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(S::TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t sa0 = smem_u32(smem), sb0 = sa0 + S::STAGES * S::A_BYTES;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // Weights never depend on the previous kernel: the first ring's W tiles load before the wait
-      // for the split activations.
-      const int pre = (int)min((long long)S::STAGES, i1 - i0);
-      for (int j = 0; j < pre; j++) {
-        const long long i = i0 + j;
-        mbar_expect_tx(full0 + 8 * j, S::STAGE);
-        tma_load_2d(sa0 + j * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * j);
-      }
-      pdl_wait();
-      for (int j = 0; j < pre; j++)
-        tma_load_2d(sb0 + j * S::B_BYTES, &tx, (int)((i0 + j) % kbs) * BK, 0, full0 + 8 * j);
-      int stage = pre % S::STAGES;
-      uint32_t phase = pre == S::STAGES ? 1u : 0u;
-      for (long long i = i0 + pre; i < i1; i++) {
-        if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, 31)) break;
-        mbar_expect_tx(full0 + 8 * stage, S::STAGE);
-        tma_load_2d(sa0 + stage * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * stage);
-        tma_load_2d(sb0 + stage * S::B_BYTES, &tx, (int)(i % kbs) * BK, 0, full0 + 8 * stage);
-        if (++stage == S::STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool issued = false;
-      int grp = 0, cnt = 0;
-      for (long long i = i0; i < i1; i++) {
-        const int r = grp % S::ACC;
-        if (cnt == 0 && !mbar_wait(acce0 + 8 * r, ((uint32_t)(grp / S::ACC) & 1u) ^ 1u, abort_flag, err, 35)) break;
-        if (!mbar_wait(full0 + 8 * stage, phase, abort_flag, err, 32)) break;
-        tc_fence_after();
-        const uint64_t a = smem_desc(sa0 + stage * S::A_BYTES);
-        const uint64_t b = smem_desc(sb0 + stage * S::B_BYTES);
-        const uint32_t d = tmem + (uint32_t)(r * S::ACC_STRIDE);
-#pragma unroll
-        for (int k = 0; k < BK / 16; k++)
-          mma_f16(d, a + (uint64_t)(2 * k), b + (uint64_t)(2 * k), idesc, cnt != 0 || k != 0);
-        issued = true;
-        mma_commit(empty0 + 8 * stage);
-        if (++cnt == S::GK || (i + 1) % kbs == 0 || i + 1 == i1) {
-          mma_commit(accf0 + 8 * r);
-          grp++;
-          cnt = 0;
-        }
-        if (++stage == S::STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
-      }
-      if (issued) {
-        mma_commit(drain);
-        volatile int no_abort = 0;
-        mbar_wait(drain, 0, &no_abort, err, 33);
-      }
-    }
-  } else {  // epilogue warps 2-5: TMEM lane quarter warp & 3 = tile rows 32 q .. 32 q + 31
-    pdl_wait();  // the previous kernel may still read `part` or the outputs
-    const int q = warp & 3;
-    const int et = threadIdx.x - 64;  // 0..127
-    float acc[NT];
-#pragma unroll
-    for (int m = 0; m < NT; m++) acc[m] = 0.0f;
-    int grp = 0, cnt = 0;
-    for (long long i = i0; i < i1; i++) {
-      if (!(++cnt == S::GK || (i + 1) % kbs == 0 || i + 1 == i1)) continue;  // inside an accumulator group
-      cnt = 0;
-      const int r = grp % S::ACC;
-      // one waiter; the flag is double-buffered so a slow reader never sees the next group's value
-      if (et == 0) s_ok[grp & 1] = mbar_wait(accf0 + 8 * r, (uint32_t)(grp / S::ACC) & 1u, abort_flag, err, 34);
-      named_sync(1, 128);
-      if (!s_ok[grp & 1]) break;
-      tc_fence_after();
-      constexpr int W = NT == 16 ? 16 : 32;
-      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(r * S::ACC_STRIDE);
-#pragma unroll
-      for (int c = 0; c < NT / W; c++) {  // columns t * NT + m hold term t of token row m
-        float lo[W], mid[W], hi[W];
-        tmem_ld3<W>(base + (uint32_t)(2 * NT + c * W), base + (uint32_t)(NT + c * W), base + (uint32_t)(c * W), lo,
-                    mid, hi);
-#pragma unroll
-        for (int jj = 0; jj < W; jj++) acc[c * W + jj] += (lo[jj] + mid[jj]) + hi[jj];
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acce0 + 8 * r);
-      grp++;
-      if (i + 1 == i1 || (i + 1) % kbs == 0) {  // end of this CTA's piece of tile t
-        const int t = (int)(i / kbs);
-        const int first = sk_cta_of((long long)t * kbs, T, G), last = sk_cta_of((long long)(t + 1) * kbs - 1, T, G);
-        const int np = last - first + 1, piece = cta - first;
-        const int row = t * SK_BM + q * 32 + lane;
-        if (np == 1) {
-          skf_epilogue<NT, EPI>(p, row, lane, m0, mb, acc);
-        } else {
-          if (row < p.N) {
-            float *pp = part + ((size_t)t * pmax + piece) * mb * SK_BM + q * 32 + lane;
-#pragma unroll
-            for (int m = 0; m < NT; m++)
-              if (m < mb) pp[(size_t)m * SK_BM] = acc[m];
-          }
-          __threadfence();
-          named_sync(1, 128);
-          if (et == 0) s_last = atomicAdd(&counters[t], 1) == np - 1;
-          named_sync(1, 128);
-          if (s_last) {  // every piece is stored: add them in piece order (into acc, already stored)
-            __threadfence();
-            const float *pp = part + (size_t)t * pmax * mb * SK_BM + q * 32 + lane;
-#pragma unroll
-            for (int m = 0; m < NT; m++) {
-              if (m < mb && row < p.N) {
-                float s = __ldcg(pp + (size_t)m * SK_BM);
-                for (int pc = 1; pc < np; pc++) s += __ldcg(pp + ((size_t)pc * mb + m) * SK_BM);
-                acc[m] = s;
-              }
-            }
-            skf_epilogue<NT, EPI>(p, row, lane, m0, mb, acc);
-            if (et == 0) counters[t] = 0;
-          }
-        }
-#pragma unroll
-        for (int m = 0; m < NT; m++) acc[m] = 0.0f;
-      }
-    }
-  }
-  pdl_trigger();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 2)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(S::TMEM_COLS) : "memory");
-}
-
 uint32_t skinny_idesc(int nt) {
   // D = F32, A = B = BF16, both K-major, N = 3 NT (>> 3 at bits 17-22), M = 128 (>> 4 at bits 24-28)
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)((3 * nt) >> 3) << 17) | ((uint32_t)(SK_BM >> 4) << 24);
@@ -664,29 +403,6 @@ SkinnyPlan skinny_plan(int M, int N, int K, int device) {
   q.x3_bytes = ((uint64_t)3 * q.nt * K * 2 + 255) & ~255ull;
   q.part_bytes = (uint64_t)q.tiles * q.pmax * M * SK_BM * 4;
   return q;
-}
-
-// STB_SKINNY_FUSED=0 keeps the three-kernel form (prologue, GEMM, separate fixup).
-bool skinny_fused() {
-  static const int fused = env_int("STB_SKINNY_FUSED", 1);
-  return fused != 0;
-}
-
-template <int NT, int EPI>
-void launch_fused(const SkinnyPlan &q, const CUtensorMap &tw, const CUtensorMap &tx, const GemvParams &p, float *part,
-                  int *counters, int m0, int mb, int *err, int device, cudaStream_t stream) {
-  static std::mutex mu;
-  static bool configured[64] = {};
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (device < 0 || device >= 64 || !configured[device]) {
-      STB_CUDA(cudaFuncSetAttribute(gemm_skinny_fused_kernel<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    SkinnyShape<NT>::SMEM));
-      if (device >= 0 && device < 64) configured[device] = true;
-    }
-  }
-  launch_kernel(gemm_skinny_fused_kernel<NT, EPI>, dim3(q.grid), dim3(192), (size_t)SkinnyShape<NT>::SMEM, stream,
-                true, tw, tx, p, part, counters, m0, mb, q.kbs, q.iters, q.pmax, skinny_idesc(NT), err);
 }
 
 template <int NT>
@@ -731,12 +447,12 @@ void skinny_prepare(int device) {
 
 uint64_t skinny_scratch_bytes(int M, int N, int K, int device) {
   const SkinnyPlan q = skinny_plan(std::min(M, 64), N, K, device);  // one 64-row block at a time
-  return (uint64_t)SKF_COUNTERS_BYTES + q.x3_bytes + q.part_bytes;
+  return q.x3_bytes + q.part_bytes;
 }
 
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
-                  cudaStream_t stream, bool counters_clean) {
+                  cudaStream_t stream) {
   STB_REQUIRE(p.M >= 1 && p.K % 8 == 0 && p.K >= BK && p.N >= SK_BM, "skinny Linear shape");
   STB_REQUIRE(p.stop == nullptr, "skinny Linear takes no stop flag");
   STB_REQUIRE(scratch && ((uintptr_t)scratch % 256) == 0 && scratch_bytes >= skinny_scratch_bytes(p.M, p.N, p.K, device),
@@ -745,28 +461,6 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
   constexpr bool paired = EPI == EPI_SILU || EPI == EPI_QKV;
   const int units = paired ? p.N / 2 : p.N;
   int launches = 0;
-  if (skinny_fused()) {  // prologue + GEMM with the fixup inside, per 64-row block
-    STB_REQUIRE((p.N + SK_BM - 1) / SK_BM <= SKF_COUNTERS_BYTES / 4, "skinny Linear: too many output rows");
-    int *counters = (int *)scratch;
-    if (!counters_clean) {
-      STB_CUDA(cudaMemsetAsync(counters, 0, (size_t)((p.N + SK_BM - 1) / SK_BM) * 4, stream));
-    }
-    for (int m0 = 0; m0 < p.M; m0 += 64) {
-      const int mb = std::min(64, p.M - m0);
-      const SkinnyPlan q = skinny_plan(mb, p.N, p.K, device);
-      uint16_t *x3 = (uint16_t *)((char *)scratch + SKF_COUNTERS_BYTES);
-      float *part = (float *)((char *)x3 + q.x3_bytes);
-      launch_kernel(skinny_prep_kernel, dim3((p.K + 1023) / 1024, q.nt), dim3(256), 0, stream, m0 > 0 || p.pdl,
-                    p.x + (size_t)m0 * p.ldx, p.ldx, p.norm_w, p.norm_eps, x3, mb, q.nt, p.K);
-      const CUtensorMap tx = make_map(x3, STB_BF16, (uint64_t)3 * q.nt, (uint64_t)p.K, 3 * q.nt);
-      if (q.nt == 16) launch_fused<16, EPI>(q, tw, tx, p, part, counters, m0, mb, err, device, stream);
-      else if (q.nt == 32) launch_fused<32, EPI>(q, tw, tx, p, part, counters, m0, mb, err, device, stream);
-      else launch_fused<64, EPI>(q, tw, tx, p, part, counters, m0, mb, err, device, stream);
-      launches += 2;
-    }
-    check_launch("skinny");
-    return launches;
-  }
   // blocks of up to 64 token rows, in order, through the same scratch (each block's prologue waits
   // for the previous block's fixup)
   for (int m0 = 0; m0 < p.M; m0 += 64) {
@@ -788,11 +482,11 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
   return launches;
 }
 
-template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_RESID>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_SILU>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_QKV>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_LOGITS>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_PEER>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
+template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_RESID>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_SILU>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_QKV>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_LOGITS>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_PEER>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
 
 }  // namespace stb

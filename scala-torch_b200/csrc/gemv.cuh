@@ -442,13 +442,10 @@ bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w);
 uint64_t skinny_scratch_bytes(int M, int N, int K, int device);
 // Sets the kernels' shared-memory limits on `device` (before a graph capture that launches them).
 void skinny_prepare(int device);
-// Enqueues prologue -> stream-K GEMM with the fixup inside (2 kernels; STB_SKINNY_FUSED=0: prologue
-// -> GEMM -> separate fixup, 3 kernels) per 64-row block, all programmatic dependents except the
-// first when !p.pdl.  The fused form keeps per-tile counters at the start of `scratch`:
-// counters_clean says the caller keeps that scratch to itself and zeroed it once (every launch leaves
-// the counters at zero); otherwise they are zeroed first.  Returns the number of kernels launched.
+// Enqueues prologue -> stream-K GEMM -> fixup/epilogue per 64-row block (3 kernels each, all
+// programmatic dependents except the first when !p.pdl).  Returns the number of kernels launched.
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
-                  cudaStream_t stream, bool counters_clean = false);
+                  cudaStream_t stream);
 
 }  // namespace stb

@@ -1260,8 +1260,6 @@ void ensure_rows(stb_llama_cache *c, int rows) {
     if (need) {
       c->skin = alloc_owned(s, c->owned, need);
       c->skin_bytes = need;
-      // the skinny GEMM's per-tile counters start at zero and every launch leaves them there
-      STB_CUDA(cudaMemsetAsync((void *)c->skin, 0, (size_t)need, s->stream));
       skinny_prepare(s->device);
     }
   }
@@ -1347,7 +1345,7 @@ int project(stb_llama_cache *c, const GemvParams &p, int wdt, GemvConfig cfg, cu
   stb_session *s = c->m->s;
   if (c->skin && skinny_eligible(p.M, p.N, p.K, wdt, p.w) &&
       skinny_scratch_bytes(p.M, p.N, p.K, s->device) <= c->skin_bytes)
-    return skinny_launch<EPI>(p, (void *)c->skin, c->skin_bytes, session_error_word(s), s->device, st, true);
+    return skinny_launch<EPI>(p, (void *)c->skin, c->skin_bytes, session_error_word(s), s->device, st);
   launch_gemv<EPI>(p, wdt, cfg, st);
   return 1;
 }

@@ -75,13 +75,12 @@ def test_decode_batches(session, m):
 SKINNY_SHAPES = [(2, 1000, 1000), (9, 128, 64), (16, 1000, 4104), (17, 300, 2048), (40, 1536, 576), (64, 2500, 1000),
                  (100, 576, 576), (300, 1536, 576)]
 SKINNY_MIN_WORK = 1 << 24  # products up to this many multiply-adds take the GEMV
-SKINNY_LAUNCHES = 2  # kernels per 64-row block of the skinny form (3 with STB_SKINNY_FUSED=0)
 
 
 @pytest.mark.parametrize("m,n,k", SKINNY_SHAPES)
 def test_skinny_tensor_core_form(session, m, n, k):
     """Two or more rows with BF16 weights and more than 2^24 multiply-adds run on the tensor cores
-    (per 64-row block: prologue, stream-K GEMM with the fixup inside), activations split into three BF16 terms:
+    (per 64-row block: prologue, stream-K GEMM, fixup), activations split into three BF16 terms:
     still within the FP32 GEMV tolerance; smaller products take the one-launch GEMV.
     Ragged N (tile tails), K tails below one 64-wide block, bias; repeated calls are identical.
     Magnitudes as the single-Linear configuration (x ~ N(0,1), W ~ N(0, 0.02)): the bound is relative
@@ -93,7 +92,7 @@ def test_skinny_tensor_core_form(session, m, n, k):
     xd, wd, bd = session.upload(x), session.upload_weight(w, ffm.STB_BF16), session.upload(b)
     l0 = session.launches
     y1 = session.linear(xd, wd, bd)
-    assert session.launches - l0 == (SKINNY_LAUNCHES * ((m + 63) // 64) if m * n * k > SKINNY_MIN_WORK else 1)
+    assert session.launches - l0 == (3 * ((m + 63) // 64) if m * n * k > SKINNY_MIN_WORK else 1)
     y2 = session.linear(xd, wd, bd)
     a1, a2 = session.download(y1), session.download(y2)
     for t in (xd, wd, bd, y1, y2):
@@ -102,12 +101,10 @@ def test_skinny_tensor_core_form(session, m, n, k):
     close(a1, oracle.linear(x, w, oracle.BF16, b))
 
 
-@pytest.mark.parametrize("fused", [1, 0])
-def test_skinny_form_on_small_products(fused):
+def test_skinny_form_on_small_products():
     """The skinny tensor-core form forced onto the products the library routes to the GEMV
     (STB_SKINNY_MIN_WORK=0, read once per process: a child process) keeps its tolerance and launch
-    count on every shape of test_skinny_tensor_core_form, in the fused form (prologue + GEMM with the
-    fixup inside per 64-row block) and the three-kernel form (STB_SKINNY_FUSED=0)."""
+    count on every shape of test_skinny_tensor_core_form."""
     import subprocess
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
@@ -127,13 +124,13 @@ def test_skinny_form_on_small_products(fused):
         "    xd, wd, bd = s.upload(x), s.upload_weight(w, ffm.STB_BF16), s.upload(b)\n"
         "    l0 = s.launches\n"
         "    y = s.linear(xd, wd, bd)\n"
-        f"    assert s.launches - l0 == {2 if fused else 3} * ((m + 63) // 64), (m, n, k)\n"
+        "    assert s.launches - l0 == 3 * ((m + 63) // 64), (m, n, k)\n"
         "    close(s.download(y), oracle.linear(x, w, oracle.BF16, b))\n"
         "    for t in (xd, wd, bd, y):\n"
         "        s.release(t)\n"
         "s.close()\n"
         "print('ok')\n")
-    env = dict(os.environ, STB_SKINNY_MIN_WORK="0", STB_SKINNY_FUSED=str(fused))
+    env = dict(os.environ, STB_SKINNY_MIN_WORK="0")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
 
@@ -202,7 +199,7 @@ def test_nonfinite_activations_on_the_skinny_form():
         "        xd, wd = s.upload(x), s.upload_weight(w, ffm.STB_BF16)\n"
         "        l0 = s.launches\n"
         "        y = s.linear(xd, wd)\n"
-        "        assert s.launches - l0 == (1 if m == 1 else 2), (m, s.launches - l0)\n"
+        "        assert s.launches - l0 == (1 if m == 1 else 3), (m, s.launches - l0)\n"
         "        same_class(s.download(y), oracle.linear(x, w, oracle.BF16))\n"
         "        for t in (xd, wd, y):\n"
         "            s.release(t)\n"
