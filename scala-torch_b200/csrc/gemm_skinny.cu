@@ -40,7 +40,6 @@ namespace {
 using namespace tc;
 
 constexpr int SK_BM = 128, SK_ACC_MAX = 4;
-constexpr int SK_L2_AHEAD = 16;  // default weight tiles prefetched to L2 beyond the ring (STB_SKINNY_L2_AHEAD)
 
 template <int NT>
 struct SkinnyShape {
@@ -154,7 +153,7 @@ __global__ void __launch_bounds__(256) skinny_prep_kernel(const float *x, int ld
 template <int NT>
 __global__ void __launch_bounds__(192, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, float *part,
-                       int M, int N, int kbs, long long T, int pmax, uint32_t idesc, int *err, int ahead) {
+                       int M, int N, int kbs, long long T, int pmax, uint32_t idesc, int *err) {
   using S = SkinnyShape<NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -204,10 +203,6 @@ __global__ void __launch_bounds__(192, 1)
         mbar_expect_tx(full0 + 8 * j, S::STAGE);
         tma_load_2d(sa0 + j * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * j);
       }
-      // The ring is full of weights while the previous kernels finish: the next `ahead` weight tiles
-      // go to L2 meanwhile, so the memory system keeps streaming through the dependency wait.
-      for (long long i = i0 + pre; i < min(i1, i0 + pre + ahead); i++)
-        tma_prefetch_l2_2d(&tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM);
       pdl_wait();
       for (int j = 0; j < pre; j++)
         tma_load_2d(sb0 + j * S::B_BYTES, &tx, (int)((i0 + j) % kbs) * BK, 0, full0 + 8 * j);
@@ -426,9 +421,8 @@ template <int NT>
 void launch_gemm(const SkinnyPlan &q, const CUtensorMap &tw, const CUtensorMap &tx, float *part, int M, int N,
                  int *err, int device, cudaStream_t stream) {
   configure<NT>(device);
-  static const int ahead = std::max(0, env_int("STB_SKINNY_L2_AHEAD", SK_L2_AHEAD));
   launch_kernel(gemm_skinny_kernel<NT>, dim3(q.grid), dim3(192), (size_t)SkinnyShape<NT>::SMEM, stream, true, tw, tx,
-                part, M, N, q.kbs, q.iters, q.pmax, skinny_idesc(NT), err, ahead);
+                part, M, N, q.kbs, q.iters, q.pmax, skinny_idesc(NT), err);
 }
 
 }  // namespace

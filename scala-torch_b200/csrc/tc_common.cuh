@@ -75,12 +75,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
-// L2 prefetch of one 2-D TMA box (no shared-memory destination, no completion to wait for).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"((uint64_t)map), "r"(x), "r"(y)
-               : "memory");
-}
-
 // Shared-memory matrix descriptor (sm_100 form): K-major, 128-byte swizzle, 8-row groups 1024 B
 // apart; start address and offsets in 16-byte units, descriptor version 1 at bit 46.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
