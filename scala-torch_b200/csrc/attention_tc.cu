@@ -77,7 +77,7 @@ template <int HD>
 __global__ void __launch_bounds__(AT_THREADS, 2)
     flash_tc_kernel(const float *q, int ldq, const float *kcache, const float *vcache, float *out, int ldo, int count,
                     int nh, int kvh, int capacity, const int *pos_dev, int pos0, uint32_t idesc_s, uint32_t idesc_o,
-                    int *err) {
+                    int *err, uint16_t *out_half, int half_bf16) {
   static_assert(HD == 64 || HD == 128, "head size");
   using S = AttnTcShape<HD>;
   extern __shared__ uint8_t at_raw[];
@@ -271,16 +271,32 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
     mbar_wait(bar, phase, &no_abort, err, 52);
   }
   if (ok) {
-    float *dst = out + ((size_t)b * count + t0 + r) * ldo + (size_t)h * HD;
+    const size_t off = ((size_t)b * count + t0 + r) * ldo + (size_t)h * HD;
     const float inv = row_valid ? 1.0f / l_run : 0.0f;
 #pragma unroll
     for (int c = 0; c < HD / 32; c++) {
       uint32_t orr[32];
       tmem_ld32(row_tmem + 128 + (uint32_t)(c * 32), orr);
-      if (row_valid) {
+      if (!row_valid) continue;
+      if (out_half) {  // the o projection's operand, rounded to the weight type (Float32 first, then half)
+        uint16_t *dst = out_half + off + c * 32;
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 8) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const float a = __uint_as_float(orr[jj + 2 * e]) * inv, bb = __uint_as_float(orr[jj + 2 * e + 1]) * inv;
+            w4[e] = half_bf16 ? pack_bf16(a, bb)
+                              : (uint32_t)__half_as_ushort(__float2half_rn(a)) |
+                                    ((uint32_t)__half_as_ushort(__float2half_rn(bb)) << 16);
+          }
+          *reinterpret_cast<uint4 *>(dst + jj) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      } else {
+        float *dst = out + off + c * 32;
 #pragma unroll
         for (int jj = 0; jj < 32; jj += 4)
-          *reinterpret_cast<float4 *>(dst + c * 32 + jj) =
+          *reinterpret_cast<float4 *>(dst + jj) =
               make_float4(__uint_as_float(orr[jj]) * inv, __uint_as_float(orr[jj + 1]) * inv,
                           __uint_as_float(orr[jj + 2]) * inv, __uint_as_float(orr[jj + 3]) * inv);
       }
@@ -298,7 +314,8 @@ uint32_t at_idesc(int n) { return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_
 
 template <int HD>
 void at_launch(dim3 grid, const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo, int count,
-               int nh, int kvh, int capacity, const int *posd, int pos0, int *err, int device, cudaStream_t st) {
+               int nh, int kvh, int capacity, const int *posd, int pos0, int *err, int device, cudaStream_t st,
+               uint16_t *out_half, int half_bf16) {
   static std::mutex mu;
   static bool configured[64] = {};
   {
@@ -310,23 +327,29 @@ void at_launch(dim3 grid, const float *q, int ldq, const float *kc, const float 
     }
   }
   launch_kernel(flash_tc_kernel<HD>, grid, dim3(AT_THREADS), (size_t)AttnTcShape<HD>::SMEM, st, false, q, ldq, kc, vc,
-                out, ldo, count, nh, kvh, capacity, posd, pos0, at_idesc(128), at_idesc(HD), err);
+                out, ldo, count, nh, kvh, capacity, posd, pos0, at_idesc(128), at_idesc(HD), err, out_half, half_bf16);
 }
 
 }  // namespace
 
 // Launches the tensor-core prefill attention for head sizes 64 and 128 (STB_TC_ATTENTION=0 keeps the
 // FP32 tiled kernel); returns false when it does not apply.  q rows are (batch row, token) with
-// `count` tokens per batch row; the chunk's keys are already in the cache.
+// `count` tokens per batch row; the chunk's keys are already in the cache.  With out_half the output
+// goes there in half_dtype (STB_BF16 / STB_F16) -- the next tensor-core GEMM's operand -- instead of
+// Float32 to out.
 bool launch_flash_attention_tc(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
                                int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
-                               int *err, int device, cudaStream_t st) {
+                               int *err, int device, cudaStream_t st, uint16_t *out_half, int half_dtype) {
   static const int enabled = env_int("STB_TC_ATTENTION", 1);
-  if (!enabled || rows % count != 0 || nh % kvh != 0 || (ldq % 4) != 0 || (ldo % 4) != 0) return false;
+  if (!enabled || rows % count != 0 || nh % kvh != 0 || (ldq % 4) != 0 || (ldo % 8) != 0) return false;
   const dim3 grid((count + AT_Q - 1) / AT_Q, nh, rows / count);
-  if (hd == 128) at_launch<128>(grid, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, err, device, st);
-  else if (hd == 64) at_launch<64>(grid, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, err, device, st);
-  else return false;
+  const int bf = half_dtype == STB_BF16 ? 1 : 0;
+  if (hd == 128)
+    at_launch<128>(grid, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, err, device, st, out_half, bf);
+  else if (hd == 64)
+    at_launch<64>(grid, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, err, device, st, out_half, bf);
+  else
+    return false;
   return true;
 }
 

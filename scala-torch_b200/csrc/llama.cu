@@ -40,7 +40,8 @@ void peer_reduce_launch(stb_session *s, int region, long total, const float *res
 void peer_reset(stb_session *s);
 bool launch_flash_attention_tc(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
                                int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
-                               int *err, int device, cudaStream_t st);
+                               int *err, int device, cudaStream_t st, uint16_t *out_half = nullptr,
+                               int half_dtype = STB_BF16);
 }  // namespace stb
 
 using namespace stb;
@@ -1049,14 +1050,71 @@ __global__ void rope_append_kernel(const float *qkv, int ldq, const double2 *rop
   }
 }
 
-// act[m][i] = silu(gate) * up from the interleaved gate/up projection row.
-__global__ void silu_mul_kernel(const float *gu, float *act, int I, long total) {
-  pdl_wait();
-  pdl_trigger();
+
+// Float32 -> the weight type (BF16 round-to-nearest-even, or F16), for tensor-core operands.
+__device__ __forceinline__ uint16_t to_half_bits(float v, bool bf16) {
+  return bf16 ? f32_to_bf16_rne(v) : __half_as_ushort(__float2half_rn(v));
+}
+
+// rmsnorm_rows_kernel's arithmetic with the result rounded straight to the weight type for the next
+// tensor-core GEMM (the Float32 row and the separate rounding pass are skipped; the two roundings,
+// double -> Float32 -> half, are the same).  One block per row; the row stays in registers between
+// the sum of squares and the scaling (H <= 8192 with 256 threads, H % 4 == 0).
+template <bool BF16>
+__global__ void __launch_bounds__(256) rmsnorm_round_kernel(const float *x, const float *w, double eps, uint16_t *out,
+                                                            int H) {
+  __shared__ double s_red[8];
+  constexpr int CH = 8;  // float4 chunks per thread
+  const float *xr = x + (size_t)blockIdx.x * H;
+  float4 v[CH];
+  double sq = 0.0;
+#pragma unroll
+  for (int j = 0; j < CH; j++) {
+    const int c = threadIdx.x + 256 * j;
+    v[j] = c * 4 < H ? *reinterpret_cast<const float4 *>(xr + c * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const double a = v[j].x, b = v[j].y, cc = v[j].z, d = v[j].w;
+    sq = __dadd_rn(sq, __dmul_rn(a, a));
+    sq = __dadd_rn(sq, __dmul_rn(b, b));
+    sq = __dadd_rn(sq, __dmul_rn(cc, cc));
+    sq = __dadd_rn(sq, __dmul_rn(d, d));
+  }
+  const double total = block_sum_double(sq, s_red);
+  const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(total, (double)H), eps)));
+  uint16_t *orow = out + (size_t)blockIdx.x * H;
+#pragma unroll
+  for (int j = 0; j < CH; j++) {
+    const int c = threadIdx.x + 256 * j;
+    if (c * 4 >= H) break;
+    const float4 wv = *reinterpret_cast<const float4 *>(w + c * 4);
+    const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint16_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      h[i] = to_half_bits(__double2float_rn(__dmul_rn(__dmul_rn((double)e[i], inv), (double)ww[i])), BF16);
+    *reinterpret_cast<uint2 *>(orow + c * 4) = make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+  }
+}
+
+// SiLU(gate) * up of the interleaved gate/up projection, rounded straight to the weight type for the
+// down projection's tensor-core GEMM.  The sigmoid is evaluated in Float32 here (the Float32 decode
+// path keeps the reference's double expression): the half rounding that follows is the prefill
+// tolerance and dominates the difference.  Four outputs per thread (I % 4 == 0).
+template <bool BF16>
+__global__ void silu_mul_round_kernel(const float *gu, uint16_t *act, int I, long total4) {
   const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-  if (i >= total) return;
-  const long m = i / I, j = i % I;
-  act[i] = silu_ref(gu[(size_t)m * 2 * I + 2 * j]) * gu[(size_t)m * 2 * I + 2 * j + 1];
+  if (i >= total4) return;
+  const long m = (i * 4) / I, j = (i * 4) % I;
+  const float *src = gu + (size_t)m * 2 * I + 2 * j;
+  const float4 a = *reinterpret_cast<const float4 *>(src), b = *reinterpret_cast<const float4 *>(src + 4);
+  const float g[4] = {a.x, a.z, b.x, b.z}, u[4] = {a.y, a.w, b.y, b.w};
+  uint16_t h[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const float sig = g[k] >= 0.0f ? 1.0f / (1.0f + expf(-g[k])) : expf(g[k]) / (1.0f + expf(g[k]));
+    const float sv = g[k] == -INFINITY ? -0.0f : g[k] * sig;
+    h[k] = to_half_bits(sv * u[k], BF16);
+  }
+  *reinterpret_cast<uint2 *>(act + (size_t)m * I + j) = make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
 }
 
 __global__ void set_position_kernel(int *state, int position) { state[0] = position; }
@@ -1292,48 +1350,73 @@ int enqueue_layer_tc(stb_llama_cache *c, size_t l, int rows, int count, const in
   cudaStream_t st = s->stream;
   const Layer &L = m->layers[l];
   const int H = m->H, qw = m->NH * m->hd, nqkv = (m->NH + 2 * m->KV) * m->hd, wdt = m->c.weight_dtype;
+  const bool bf16 = wdt == STB_BF16;
   int *err = session_error_word(s);
   int launches = 0;
-  auto gemm = [&](const float *x, int K, uint64_t w, int N, float *y, const float *residual) {
-    round_activations(x, (uint16_t *)c->xh, (size_t)rows * K, wdt, st);
-    gemm_tc_launch((const void *)c->xh, (const void *)w, wdt, nullptr, y, N, rows, N, K, err, s->device, st, residual,
+  uint16_t *xh = (uint16_t *)c->xh;  // the GEMM's activations, already in the weight type
+  auto gemm_h = [&](int K, uint64_t w, int N, float *y, const float *residual) {
+    gemm_tc_launch((const void *)xh, (const void *)w, wdt, nullptr, y, N, rows, N, K, err, s->device, st, residual,
                    residual ? N : 0);
-    launches += 2;
+    launches += 1;
   };
-  auto row_split = [&](const float *x, int K, uint64_t w) {  // o_proj / down_proj
+  auto row_split = [&](int K, uint64_t w) {  // o_proj / down_proj from xh
     if (m->tp == 1) {
-      gemm(x, K, w, H, (float *)c->hidden, (const float *)c->hidden);
+      gemm_h(K, w, H, (float *)c->hidden, (const float *)c->hidden);
     } else {
-      gemm(x, K, w, H, (float *)c->sum, m->rank == 0 ? (const float *)c->hidden : nullptr);
+      gemm_h(K, w, H, (float *)c->sum, m->rank == 0 ? (const float *)c->hidden : nullptr);
       allreduce_sum_f32(s, (void *)c->sum, (uint64_t)rows * H);
       std::swap(c->hidden, c->sum);
     }
   };
-  launch_kernel(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, st, false, (const float *)c->hidden,
-                (const float *)L.in_norm, m->c.rms_norm_eps, (float *)c->xn, H);
-  gemm((const float *)c->xn, H, L.qkv, nqkv, (float *)c->qkvbuf, nullptr);
+  // RMSNorm straight into the weight type when the row fits the register form, else Float32 + round
+  auto norm = [&](uint64_t wnorm) {
+    if (H <= 8192 && H % 4 == 0) {
+      if (bf16)
+        launch_kernel(rmsnorm_round_kernel<true>, dim3(rows), dim3(256), 0, st, false, (const float *)c->hidden,
+                      (const float *)wnorm, m->c.rms_norm_eps, xh, H);
+      else
+        launch_kernel(rmsnorm_round_kernel<false>, dim3(rows), dim3(256), 0, st, false, (const float *)c->hidden,
+                      (const float *)wnorm, m->c.rms_norm_eps, xh, H);
+      launches += 1;
+    } else {
+      launch_kernel(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, st, false, (const float *)c->hidden,
+                    (const float *)wnorm, m->c.rms_norm_eps, (float *)c->xn, H);
+      round_activations((const float *)c->xn, xh, (size_t)rows * H, wdt, st);
+      launches += 2;
+    }
+  };
+  norm(L.in_norm);
+  gemm_h(H, L.qkv, nqkv, (float *)c->qkvbuf, nullptr);
   const long pairs = (long)rows * (nqkv / 2);
   launch_kernel(rope_append_kernel, dim3((unsigned)((pairs + 255) / 256)), dim3(256), 0, st, false,
                 (const float *)c->qkvbuf, nqkv, (const double2 *)m->rope, posd, c->used, count, m->NH, m->KV, m->hd,
                 c->capacity, (float *)c->qbuf, qw, kc, vc, rows);
-  if (!launch_flash_attention_tc((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att,
-                                 qw, rows, count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, err, s->device,
-                                 st) &&
-      !launch_flash_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw,
-                              rows, count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, s->device, st))
-    launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), attention_smem(c->capacity, m->hd), st,
-                  false, (const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw, rows,
-                  count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, (const int *)nullptr);
-  launches += 3;
-  row_split((const float *)c->att, qw, L.o);
-  launch_kernel(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, st, false, (const float *)c->hidden,
-                (const float *)L.post_norm, m->c.rms_norm_eps, (float *)c->xn, H);
-  gemm((const float *)c->xn, H, L.gu, 2 * m->I, (float *)c->gubuf, nullptr);
-  const long acts = (long)rows * m->I;
-  launch_kernel(silu_mul_kernel, dim3((unsigned)((acts + 255) / 256)), dim3(256), 0, st, false,
-                (const float *)c->gubuf, (float *)c->act, m->I, acts);
-  launches += 2;
-  row_split((const float *)c->act, m->I, L.down);
+  launches += 1;
+  // attention: the tensor-core kernel writes the o projection's operand in the weight type directly
+  if (launch_flash_attention_tc((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, nullptr, qw, rows,
+                                count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, err, s->device, st, xh, wdt)) {
+    launches += 1;
+  } else {
+    if (!launch_flash_attention((const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att,
+                                qw, rows, count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, s->device, st))
+      launch_kernel(attention_kernel, dim3(rows * m->NH), dim3(ATT_THREADS), attention_smem(c->capacity, m->hd), st,
+                    false, (const float *)c->qbuf, qw, (const float *)kc, (const float *)vc, (float *)c->att, qw,
+                    rows, count, m->NH, m->KV, m->hd, c->capacity, posd, c->used, (const int *)nullptr);
+    round_activations((const float *)c->att, xh, (size_t)rows * qw, wdt, st);
+    launches += 2;
+  }
+  row_split(qw, L.o);
+  norm(L.post_norm);
+  gemm_h(H, L.gu, 2 * m->I, (float *)c->gubuf, nullptr);
+  const long acts4 = (long)rows * m->I / 4;  // I % 8 == 0 (check_config)
+  if (bf16)
+    launch_kernel(silu_mul_round_kernel<true>, dim3((unsigned)((acts4 + 255) / 256)), dim3(256), 0, st, false,
+                  (const float *)c->gubuf, xh, m->I, acts4);
+  else
+    launch_kernel(silu_mul_round_kernel<false>, dim3((unsigned)((acts4 + 255) / 256)), dim3(256), 0, st, false,
+                  (const float *)c->gubuf, xh, m->I, acts4);
+  launches += 1;
+  row_split(m->I, L.down);
   return launches;
 }
 
