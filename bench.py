@@ -61,7 +61,15 @@ SINGLE_BYTES = SINGLE_N * SINGLE_K * 2 + SINGLE_M * SINGLE_K * 4 + SINGLE_M * SI
 # how many leading ids of each row they reproduce: on an 80-layer random-weight model the argmax over
 # 128,256 near-tied logits can flip under the Float32 reassociation of a row-split sum, after which the
 # sequences diverge.  The exact check at every N is `parity.tp_small` (ids against the CPU oracle).
-TP1_IDS = {}
+TP1_IDS = {"8/512/32/80": [
+    [89289, 122223, 57117, 84874, 118673, 75253, 107876, 30747, 29566, 71866, 54375, 89189, 37853, 21649, 73888, 23536, 121691, 89094, 29020, 3133, 18731, 22227, 104517, 28954, 9324, 57596, 84645, 105391, 125094, 97141, 60628, 23650],
+    [118140, 102482, 117568, 110555, 101663, 2358, 118303, 109816, 124562, 102501, 112788, 16848, 18777, 46650, 40017, 8232, 109038, 6153, 61757, 43578, 8334, 82436, 110740, 85112, 112328, 105851, 114037, 77759, 34152, 97490, 42193, 87570],
+    [104271, 236, 20488, 1499, 70293, 38267, 69268, 73015, 32637, 82579, 106803, 28214, 95798, 49450, 70693, 24705, 95016, 99018, 32255, 30057, 64208, 77279, 63674, 103519, 20146, 126965, 26746, 28320, 31865, 29761, 58455, 79292],
+    [108529, 86287, 122692, 128030, 95374, 82016, 97715, 12170, 93104, 56973, 72629, 7061, 17348, 41548, 56687, 100415, 113228, 89077, 68058, 49080, 79181, 52486, 82643, 22568, 20011, 35784, 100791, 83208, 88724, 72817, 59760, 108916],
+    [107238, 127209, 107064, 123617, 98148, 117116, 3661, 109219, 48042, 117645, 40355, 33644, 57150, 46225, 67544, 92541, 41344, 42441, 37728, 74953, 32725, 66692, 32783, 34587, 82604, 72114, 122215, 24193, 105889, 78118, 46280, 102713],
+    [35970, 96088, 114821, 88599, 33238, 61588, 32914, 126558, 42798, 95006, 41477, 101455, 45135, 59187, 13370, 77939, 81696, 82121, 88417, 88827, 61297, 91242, 85456, 82660, 95758, 88201, 107377, 20348, 62777, 90903, 40787, 93173],
+    [58516, 28655, 113392, 68354, 66956, 127783, 24561, 4985, 100096, 119608, 66697, 97699, 54441, 101205, 31142, 34658, 60427, 84129, 8379, 37124, 44213, 23165, 88, 92379, 121439, 55649, 110081, 110210, 118406, 63133, 82297, 24909],
+    [99947, 45951, 112512, 109489, 91634, 2425, 122818, 111101, 46513, 63257, 3381, 60326, 125064, 89171, 9448, 100665, 89718, 11610, 68435, 87116, 109200, 98680, 88122, 120993, 106525, 122549, 124297, 15406, 123923, 122750, 16513, 49903]]}
 # A small model every tensor-parallel size up to 8 divides (8 heads, 8 KV heads), generated with the
 # same tensor-parallel runtime at every N and compared id for id with the CPU oracle.
 TP_SMALL = dict(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_layers=2, num_attention_heads=8,
