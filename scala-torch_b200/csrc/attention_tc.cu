@@ -53,9 +53,10 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return (uint32_t)f32_to_bf16_rne(a) | ((uint32_t)f32_to_bf16_rne(b) << 16);
 }
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
+// Plain (compiler-visible) shared-memory store: the compiler may keep the next global loads in flight
+// across it; the fences and barriers that publish the tiles to the tensor cores order it.
+__device__ __forceinline__ void st_shared_v4(uint8_t *base, uint32_t off, uint4 v) {
+  *reinterpret_cast<uint4 *>(base + off) = v;
 }
 
 // Stores 32 consecutive TMEM columns of this thread's lane (the inverse of tmem_ld32) and waits.
@@ -82,7 +83,8 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
   using S = AttnTcShape<HD>;
   extern __shared__ uint8_t at_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)at_raw + 1023) & ~(uintptr_t)1023);
-  const uint32_t qs = smem_u32(smem), kps = qs + S::Q_BYTES, vs = kps + S::KP_BYTES;
+  uint8_t *qp = smem, *kp = smem + S::Q_BYTES, *vp = kp + S::KP_BYTES;  // generic pointers of the tiles
+  const uint32_t qs = smem_u32(qp), kps = smem_u32(kp), vs = smem_u32(vp);
   uint64_t *bars = (uint64_t *)(smem + S::Q_BYTES + S::KP_BYTES + S::V_BYTES);
   const uint32_t bar = smem_u32(bars);
   uint32_t *tmem_slot = (uint32_t *)(bars + 1);
@@ -120,7 +122,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
       a = *reinterpret_cast<const float4 *>(src);
       c = *reinterpret_cast<const float4 *>(src + 4);
     }
-    st_shared_v4(qs + (ch >> 3) * 16384 + swz(r, ch & 7),
+    st_shared_v4(qp, (ch >> 3) * 16384 + swz(r, ch & 7),
                  make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(c.x, c.y), pack_bf16(c.z, c.w)));
   }
   tc_fence_before();
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
   for (int kt = 0; kt < ntiles && ok; kt++) {
     const int j0 = kt * AT_K;
     // 1. K -> BF16 [keys][hd] and V -> BF16 V^T [hd][keys] (keys past the visible range are zero)
+#pragma unroll 4
     for (int i = tid; i < AT_K * (HD / 8); i += AT_THREADS) {
       const int kr = i / (HD / 8), ch = i % (HD / 8);
       float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c = a;
@@ -149,7 +152,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
         a = *reinterpret_cast<const float4 *>(src);
         c = *reinterpret_cast<const float4 *>(src + 4);
       }
-      st_shared_v4(kps + (ch >> 3) * 16384 + swz(kr, ch & 7),
+      st_shared_v4(kp, (ch >> 3) * 16384 + swz(kr, ch & 7),
                    make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(c.x, c.y), pack_bf16(c.z, c.w)));
     }
     for (int i = tid; i < (HD / 4) * (AT_K / 8); i += AT_THREADS) {
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
 #pragma unroll
       for (int dd = 0; dd < 4; dd++) {
         const int d = dq * 4 + dd;
-        st_shared_v4(vs + (kg >> 3) * (HD * 128) + swz(d, kg & 7),
+        st_shared_v4(vp, (kg >> 3) * (HD * 128) + swz(d, kg & 7),
                      make_uint4(pack_bf16(v[0][dd], v[1][dd]), pack_bf16(v[2][dd], v[3][dd]),
                                 pack_bf16(v[4][dd], v[5][dd]), pack_bf16(v[6][dd], v[7][dd])));
       }
@@ -225,7 +228,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2)
       // keys c * 32 .. c * 32 + 31 of P: subtile (c >> 1), chunks 4 (c & 1) .. 4 (c & 1) + 3
 #pragma unroll
       for (int k8 = 0; k8 < 4; k8++)
-        st_shared_v4(kps + (c >> 1) * 16384 + swz(r, (c & 1) * 4 + k8),
+        st_shared_v4(kp, (c >> 1) * 16384 + swz(r, (c & 1) * 4 + k8),
                      make_uint4(pack_bf16(p[8 * k8], p[8 * k8 + 1]), pack_bf16(p[8 * k8 + 2], p[8 * k8 + 3]),
                                 pack_bf16(p[8 * k8 + 4], p[8 * k8 + 5]), pack_bf16(p[8 * k8 + 6], p[8 * k8 + 7])));
     }
