@@ -126,17 +126,29 @@ size_t esize(int dtype) { return dtype == STB_F32 ? 4 : 2; }
 
 // ---------------------------------------------------------------- kernels
 
+// hidden[m] = widen(table[tokens[m]]): 8 elements (one 16-byte load, H % 8 == 0) per thread, blocks
+// (chunk group, row), so a row's loads are all in flight at once.
 __global__ void embed_kernel(const int64_t *tokens, const uint16_t *table, int dtype, int H, int V, float *hidden,
                              int rows, const int *stop) {
   pdl_wait();
   if (stop && *stop) return;
-  const int m = blockIdx.x;
-  if (m >= rows) return;
+  const int m = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= rows || c * 8 >= H) return;
   int64_t id = tokens[m];
   if (id < 0 || id >= V) id = 0;  // host validates; device-fed ids come from argmax over [0, V)
-  const uint16_t *src = table + (size_t)id * H;
-  for (int k = threadIdx.x; k < H; k += blockDim.x)
-    hidden[(size_t)m * H + k] = dtype == STB_BF16 ? widen1<__nv_bfloat16>(src[k]) : widen1<__half>(src[k]);
+  const uint4 raw = *reinterpret_cast<const uint4 *>(table + (size_t)id * H + c * 8);
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float2 f = dtype == STB_BF16 ? widen2<__nv_bfloat16>(w[i]) : widen2<__half>(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+  float *dst = hidden + (size_t)m * H + c * 8;
+  *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4 *>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
 // Causal grouped-query attention of CpuAttention.causal (cpu/.../CpuAttention.scala:20-50):
@@ -1450,8 +1462,9 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
 
   // The first kernel follows host copies (or the previous graph replay): a plain launch.  Every
   // later kernel is a programmatic dependent of its predecessor (see launch_kernel / pdl_wait).
-  launch_kernel(embed_kernel, dim3(rows), dim3(128), 0, st, false, (const int64_t *)c->tokens,
-                (const uint16_t *)m->embed, wdt, H, m->c.vocab_size, (float *)c->hidden, rows, stop);
+  launch_kernel(embed_kernel, dim3((unsigned)((H / 8 + 127) / 128), rows), dim3(128), 0, st, false,
+                (const int64_t *)c->tokens, (const uint16_t *)m->embed, wdt, H, m->c.vocab_size, (float *)c->hidden,
+                rows, stop);
   launches++;
   const size_t kv_layer = (size_t)2 * c->batch * m->KV * c->capacity * m->hd;
   const size_t kv_half = kv_layer / 2;
