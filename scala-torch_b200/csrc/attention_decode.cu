@@ -1,0 +1,369 @@
+// Single-token (decode) attention for head size 128 and grouped-query groups of up to 8 query
+// heads, as a stream through shared memory, and the split merge fused into the next projection's
+// prologue.
+//
+// The reference's causal grouped-query attention (cpu/src/main/scala/scalatorch/cpu/
+// CpuAttention.scala:20-50) for one new token per batch row: scores of the query against every
+// visible key, softmax, weighted sum of the values.  On the GPU each (batch row, KV head) pair's
+// visible keys are cut into splits of `kps` keys (a multiple of 32, chosen from the cache capacity
+// so that about two blocks per SM cover all pairs: every block is resident at once, no second
+// wave).  Block (split, KV head, row), 128 threads, streams its split's K rows and then its V rows
+// in chunks of 32 keys (16 KB) through a 5-stage ring:
+//   * K chunks: four 2-D TMA box loads (32 dims x 32 keys of Float32, 128-byte swizzle) from one
+//     tensor map over the whole cache; V chunks: one bulk copy of the contiguous rows.  The first
+//     five chunks are issued before the programmatic-dependency wait (the cache rows of earlier
+//     steps never depend on the previous kernel); the newest key, which the QKV projection just
+//     wrote, is patched into its chunk from global memory after the wait.
+//   * scores: lane (key k, head quad h4) of a warp computes the dot of key k with query heads
+//     4 h4 .. 4 h4 + 3 over its warp's share of the dimensions (16 FMAs per 128-bit K load; the
+//     swizzle puts the keys a warp reads in distinct banks; the query rows are broadcast reads);
+//     the dimension shares are added in order through shared memory.
+//   * after the last K chunk: softmax statistics per head over the split (max, exp, sum);
+//   * V chunks: warp w owns output dimensions 32 w .. 32 w + 31 of every head, so each lane runs
+//     over the chunk's keys with its 8 accumulators.
+// Each block writes its split's unnormalised sums and (max, sum) per head.  The merge (rescale
+// every split by exp(max_s - max), sum in split order, divide) runs in attention_merge_split_kernel,
+// which is the o projection's prologue: it writes the three BF16 terms of the merged output that
+// the skinny GEMM reads (or the Float32 output for the other forms of the projection).
+// Every mbarrier wait is bounded (2 s; then the session's error word is set, the block waits --
+// bounded again -- for the copies it issued, and leaves without writing).
+#include "attention_decode.cuh"
+#include "tc_common.cuh"
+
+namespace stb {
+
+namespace {
+
+using namespace tc;
+
+constexpr int DS_HD = 128, DS_CH = 32, DS_RING = 5, DS_THREADS = 128, DS_GMAX = 8, DS_KPS_MAX = 256;
+constexpr int DS_CHUNK = DS_CH * DS_HD * 4;  // 16 KB: 32 K rows (4 swizzled boxes of 4 KB) or V rows
+constexpr int DS_QROW = 132;                 // padded query row (floats)
+constexpr size_t DS_SMEM = 1024 + (size_t)DS_RING * DS_CHUNK + DS_GMAX * DS_QROW * 4 + 4 * DS_CH * DS_GMAX * 4 +
+                           (size_t)DS_KPS_MAX * DS_GMAX * 4 + DS_GMAX * 2 * 4 + DS_RING * 8;
+
+// Byte offset of float d of key row r inside a K chunk: box d / 32 (4 KB), row r (128 bytes), 16-byte
+// chunk (d % 32) / 4 XOR-ed with r mod 8 (TMA's SWIZZLE_128B on a 1024-byte-aligned box).
+__device__ __forceinline__ uint32_t ds_koff(int r, int d) {
+  return (uint32_t)((d >> 5) * 4096 + r * 128 + ((((d & 31) >> 2) ^ (r & 7)) << 4) + (d & 3) * 4);
+}
+
+__global__ void __launch_bounds__(DS_THREADS) decode_attention_stream_kernel(
+    const __grid_constant__ CUtensorMap kmap, long long krow0, const float *q, int ldq, const float *kcache,
+    const float *vcache, int count, int nh, int kvh, int capacity, const int *pos_dev, int pos0, int kps,
+    float *part, int smax, int *err) {
+  extern __shared__ uint8_t ds_raw[];
+  uint8_t *ring = (uint8_t *)(((uintptr_t)ds_raw + 1023) & ~(uintptr_t)1023);
+  float *Qs = (float *)(ring + DS_RING * DS_CHUNK);  // [8][DS_QROW]
+  float *pscr = Qs + DS_GMAX * DS_QROW;              // [4 dimension shares][32 keys][8 heads]
+  float *pt = pscr + 4 * DS_CH * DS_GMAX;            // [kps][8]: scores, then exp(score - max)
+  float *red = pt + DS_KPS_MAX * DS_GMAX;            // [8][2]: max, sum
+  uint64_t *bar = (uint64_t *)(red + DS_GMAX * 2);   // [DS_RING]
+  __shared__ int s_ok;
+  __shared__ volatile int s_abort;
+  pdl_trigger();
+  const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
+  const int G = nh / kvh;
+  const int b = m / count, t = m % count;
+  const int keys = (pos_dev ? *pos_dev : pos0) + t + 1;
+  const int S = (keys + kps - 1) / kps;
+  if (split >= S) return;  // the grid covers the longest visible range
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int j0 = split * kps, nk = min(kps, keys - j0);
+  const int nck = (nk + DS_CH - 1) / DS_CH, total = 2 * nck;  // K chunks, then V chunks
+  const int fresh = keys - 1 - j0;                              // in [0, nk) only in the last split
+  const long long kvrow0 = ((long long)b * kvh + g0) * capacity + j0;
+  const uint32_t ring_a = smem_u32(ring), bar0 = smem_u32(bar);
+  int issued = 0;  // thread 0: chunks whose loads are issued
+  auto issue = [&](int c) {
+    const int st = c % DS_RING;
+    const uint32_t dst = ring_a + st * DS_CHUNK, br = bar0 + 8 * st;
+    if (c < nck) {
+      mbar_expect_tx(br, DS_CHUNK);
+      const int y = (int)(krow0 + kvrow0 + (long long)c * DS_CH);
+#pragma unroll
+      for (int bx = 0; bx < 4; bx++) tma_load_2d(dst + bx * 4096, &kmap, bx * 32, y, br);
+    } else {
+      const int cv = c - nck, rows = min(DS_CH, nk - cv * DS_CH);
+      const uint32_t bytes = (uint32_t)rows * DS_HD * 4;
+      mbar_expect_tx(br, bytes);
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                   "l"(vcache + (kvrow0 + (long long)cv * DS_CH) * DS_HD), "r"(bytes), "r"(br)
+                   : "memory");
+    }
+  };
+  if (tid == 0) {
+    s_abort = 0;
+    for (int st = 0; st < DS_RING; st++) mbar_init(bar0 + 8 * st, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (; issued < min(DS_RING, total); issued++) issue(issued);
+  }
+  pdl_wait();
+  for (int i = tid; i < DS_GMAX * (DS_HD / 4); i += DS_THREADS) {  // the group's query rows (zero past G)
+    const int g = i / (DS_HD / 4), d4 = i % (DS_HD / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g < G) v = *(const float4 *)(q + (size_t)m * ldq + (size_t)(g0 * G + g) * DS_HD + d4 * 4);
+    *(float4 *)(Qs + g * DS_QROW + d4 * 4) = v;
+  }
+  // the newest key's row, loaded now (after the wait) and stored once its chunk has landed
+  const float kf = fresh < nk ? kcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
+  const float vf = fresh < nk ? vcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
+  const float scale = (float)(1.0 / sqrt((double)DS_HD));
+  // scores: G > 4: warp (key half w & 1, dimension half w >> 1), lane (key k = lane & 15, quad lane >> 4);
+  // G <= 4: warp = dimension quarter, lane = key
+  const bool two_quads = G > 4;
+  const int sk = two_quads ? (warp & 1) * 16 + (lane & 15) : lane;
+  const int sq = two_quads ? lane >> 4 : 0;
+  const int dsh = two_quads ? warp >> 1 : warp, dlen = two_quads ? 64 : 32;
+  const int nshares = two_quads ? 2 : 4;
+  float acc[DS_GMAX];
+#pragma unroll
+  for (int g = 0; g < DS_GMAX; g++) acc[g] = 0.0f;
+  const int d = warp * 32 + lane;  // output dimension of this lane in the V phase
+
+  for (int c = 0; c < total; c++) {
+    const int st = c % DS_RING;
+    const uint8_t *chunk = ring + st * DS_CHUNK;
+    if (tid == 0) {
+      s_ok = mbar_wait(bar0 + 8 * st, (uint32_t)(c / DS_RING) & 1u, &s_abort, err, 60);
+      if (!s_ok) {  // leave only once every copy into this block's shared memory is done (bounded again)
+        volatile int no_abort = 0;
+        for (int cc = c; cc < issued; cc++) mbar_wait(bar0 + 8 * (cc % DS_RING), (uint32_t)(cc / DS_RING) & 1u, &no_abort, err, 61);
+      }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    if (c < nck) {
+      const int r = fresh - c * DS_CH;
+      if (r >= 0 && r < DS_CH) {
+        *(float *)((uint8_t *)chunk + ds_koff(r, tid)) = kf;
+        __syncthreads();
+      }
+      if (c * DS_CH + sk < nk) {
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+        const float *qr = Qs + 4 * sq * DS_QROW;
+#pragma unroll 4
+        for (int dd = dsh * dlen; dd < dsh * dlen + dlen; dd += 4) {
+          const float4 kv = *(const float4 *)(chunk + ds_koff(sk, dd));
+#pragma unroll
+          for (int h = 0; h < 4; h++) {
+            const float4 qv = *(const float4 *)(qr + h * DS_QROW + dd);
+            s4[h] = fmaf(qv.x, kv.x, s4[h]);
+            s4[h] = fmaf(qv.y, kv.y, s4[h]);
+            s4[h] = fmaf(qv.z, kv.z, s4[h]);
+            s4[h] = fmaf(qv.w, kv.w, s4[h]);
+          }
+        }
+        *(float4 *)(pscr + (dsh * DS_CH + sk) * DS_GMAX + 4 * sq) = make_float4(s4[0], s4[1], s4[2], s4[3]);
+      }
+      __syncthreads();
+      for (int e = tid; e < DS_CH * DS_GMAX; e += DS_THREADS) {  // dimension shares added in order
+        const int j = e / DS_GMAX, g = e % DS_GMAX;
+        if (c * DS_CH + j < nk && g < G) {
+          float s = pscr[j * DS_GMAX + g];
+          for (int sh = 1; sh < nshares; sh++) s += pscr[(sh * DS_CH + j) * DS_GMAX + g];
+          pt[(c * DS_CH + j) * DS_GMAX + g] = s * scale;
+        }
+      }
+      if (c == nck - 1) {  // all scores: softmax statistics per head over the split
+        __syncthreads();
+        for (int g = warp; g < G; g += DS_THREADS / 32) {
+          float mx = -INFINITY;
+          for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, pt[j * DS_GMAX + g]);
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          float sum = 0.0f;
+          for (int j = lane; j < nk; j += 32) {
+            const float e = expf(pt[j * DS_GMAX + g] - mx);
+            pt[j * DS_GMAX + g] = e;
+            sum += e;
+          }
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+          if (lane == 0) {
+            red[g * 2] = mx;
+            red[g * 2 + 1] = sum;
+          }
+        }
+      }
+    } else {
+      const int cv = c - nck, rows = min(DS_CH, nk - cv * DS_CH);
+      const float *vt = (const float *)chunk;
+      const int r = fresh - cv * DS_CH;
+      if (r >= 0 && r < DS_CH) {
+        ((float *)chunk)[r * DS_HD + tid] = vf;
+        __syncthreads();
+      }
+      const float *pr = pt + (size_t)cv * DS_CH * DS_GMAX;
+#pragma unroll 4
+      for (int j = 0; j < rows; j++) {
+        const float v = vt[j * DS_HD + d];
+        const float4 pa = *(const float4 *)(pr + j * DS_GMAX), pb = *(const float4 *)(pr + j * DS_GMAX + 4);
+        acc[0] = fmaf(pa.x, v, acc[0]);
+        acc[1] = fmaf(pa.y, v, acc[1]);
+        acc[2] = fmaf(pa.z, v, acc[2]);
+        acc[3] = fmaf(pa.w, v, acc[3]);
+        acc[4] = fmaf(pb.x, v, acc[4]);
+        acc[5] = fmaf(pb.y, v, acc[5]);
+        acc[6] = fmaf(pb.z, v, acc[6]);
+        acc[7] = fmaf(pb.w, v, acc[7]);
+      }
+    }
+    __syncthreads();  // chunk consumed: its stage takes the chunk DS_RING ahead
+    if (tid == 0 && issued < total) issue(issued++);
+  }
+  const size_t slot = ((size_t)m * kvh + g0) * smax + split;
+  float *po = part, *pml = part + (size_t)gridDim.z * kvh * smax * DS_GMAX * DS_HD;
+#pragma unroll
+  for (int g = 0; g < DS_GMAX; g++)
+    if (g < G) po[(slot * DS_GMAX + g) * DS_HD + d] = acc[g];
+  if (tid < G) {
+    pml[(slot * DS_GMAX + tid) * 2 + 0] = red[tid * 2];
+    pml[(slot * DS_GMAX + tid) * 2 + 1] = red[tid * 2 + 1];
+  }
+}
+
+// The split merge and the o projection's prologue in one: block (kb, m) takes elements
+// [kb * 1024, kb * 1024 + 1024) of token row m's attention output (four per thread, one query head),
+// merges the splits' records (max over splits, weights exp(max_s - max), numerator and denominator
+// summed in split order), and writes the three BF16 terms of each output into x3 [3][NT][K] (K = nh
+// x 128) as the skinny prologue does; rows M .. NT - 1 get zeros.  With out != null the Float32
+// outputs go there instead (the other forms of the projection).
+__global__ void __launch_bounds__(256) attention_merge_split_kernel(
+    const float *part, int kps, const int *pos_dev, int pos0, int count, int nh, int kvh, int smax, int M, int NT,
+    uint16_t *x3, float *out, int ldo) {
+  pdl_wait();
+  pdl_trigger();
+  const int K = nh * DS_HD, G = nh / kvh;
+  const int m = blockIdx.y;
+  const int k0 = blockIdx.x * 1024 + threadIdx.x * 4;
+  if (k0 >= K) return;
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  if (m < M) {
+    const int gq = k0 / DS_HD, g0 = gq / G, g = gq % G, d = k0 % DS_HD;
+    const int keys = (pos_dev ? *pos_dev : pos0) + m % count + 1;
+    const int S = (keys + kps - 1) / kps;
+    const size_t slot = ((size_t)m * kvh + g0) * smax;
+    const float *po = part, *ml = part + (size_t)M * kvh * smax * DS_GMAX * DS_HD;  // sums, then (max, sum)
+    float mx = -INFINITY;
+    for (int s = 0; s < S; s++) mx = fmaxf(mx, __ldcg(&ml[((slot + s) * DS_GMAX + g) * 2]));
+    float num[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 4) {  // four splits' loads per round trip
+      float2 r[4];
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (s0 + j < S) {
+          r[j] = __ldcg((const float2 *)&ml[((slot + s0 + j) * DS_GMAX + g) * 2]);
+          v[j] = __ldcg((const float4 *)&po[((slot + s0 + j) * DS_GMAX + g) * DS_HD + d]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (s0 + j < S) {
+          const float w = expf(r[j].x - mx);
+          num[0] = fmaf(w, v[j].x, num[0]);
+          num[1] = fmaf(w, v[j].y, num[1]);
+          num[2] = fmaf(w, v[j].z, num[2]);
+          num[3] = fmaf(w, v[j].w, num[3]);
+          den = fmaf(w, r[j].y, den);
+        }
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; e++) o[e] = num[e] / den;
+  }
+  if (out) {
+    if (m < M) *(float4 *)(out + (size_t)m * ldo + k0) = make_float4(o[0], o[1], o[2], o[3]);
+    return;
+  }
+  uint16_t h[3][4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) {
+    const float f = o[e];
+    uint16_t h0 = f32_to_bf16_rne(f), h1 = 0, h2 = 0;
+    if (isfinite(f)) {  // the skinny prologue's split (non-finite values keep their class in x0)
+      if ((h0 & 0x7f80u) == 0x7f80u) h0 = (uint16_t)(__float_as_uint(f) >> 16);
+      const float r1 = f - __uint_as_float((uint32_t)h0 << 16);
+      h1 = f32_to_bf16_rne(r1);
+      const float r2 = r1 - __uint_as_float((uint32_t)h1 << 16);
+      h2 = f32_to_bf16_rne(r2);
+    }
+    h[0][e] = h0;
+    h[1][e] = h1;
+    h[2][e] = h2;
+  }
+#pragma unroll
+  for (int tm = 0; tm < 3; tm++) {
+    uint2 u;
+    u.x = (uint32_t)h[tm][0] | ((uint32_t)h[tm][1] << 16);
+    u.y = (uint32_t)h[tm][2] | ((uint32_t)h[tm][3] << 16);
+    *(uint2 *)(x3 + ((size_t)tm * NT + m) * K + k0) = u;
+  }
+}
+
+}  // namespace
+
+DecodeStreamPlan decode_stream_plan(int rows, int kvh, int capacity, int device) {
+  static const int forced = env_int("STB_DS_KPS", 0);  // keys per split, a multiple of 32 up to 256
+  const int pairs = rows * kvh;
+  const int splits = std::max(1, 2 * sm_count(device) / std::max(pairs, 1));
+  int kps = ((capacity + splits - 1) / splits + DS_CH - 1) / DS_CH * DS_CH;
+  if (forced > 0 && forced % DS_CH == 0) kps = forced;
+  kps = std::min(std::max(kps, DS_CH), DS_KPS_MAX);
+  DecodeStreamPlan p;
+  p.kps = kps;
+  p.smax = (capacity + kps - 1) / kps;
+  return p;
+}
+
+size_t decode_stream_part_floats(int rows, int kvh, int capacity) {
+  const size_t smax = (size_t)(capacity + DS_CH - 1) / DS_CH;  // the smallest split: 32 keys
+  return (size_t)rows * kvh * smax * DS_GMAX * (DS_HD + 2);
+}
+
+CUtensorMap make_kv_map(const float *kv, uint64_t rows) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)DS_HD, rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)DS_HD * 4};
+  const cuuint32_t box[2] = {32, (cuuint32_t)DS_CH};
+  const cuuint32_t elem[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(kv), dims, strides, box, elem,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error(STB_ERR_CUDA, "cuTensorMapEncodeTiled (KV cache) failed: " + std::to_string((int)r));
+  return m;
+}
+
+bool decode_stream_applies(int hd, int nh, int kvh) {
+  static const int enabled = env_int("STB_DECODE_STREAM", 1);
+  return enabled && hd == DS_HD && nh % kvh == 0 && nh / kvh <= DS_GMAX;
+}
+
+void launch_decode_attention_stream(const CUtensorMap &kmap, long long krow0, const float *q, int ldq,
+                                    const float *kc, const float *vc, int rows, int count, int nh, int kvh,
+                                    int capacity, const int *posd, int pos0, const DecodeStreamPlan &plan,
+                                    float *part, bool pdl, cudaStream_t st, int device, int *err) {
+  {
+    static std::mutex mu;
+    static bool configured[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0 || device >= 64 || !configured[device]) {
+      STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)DS_SMEM));
+      if (device >= 0 && device < 64) configured[device] = true;
+    }
+  }
+  launch_kernel(decode_attention_stream_kernel, dim3(plan.smax, kvh, rows), dim3(DS_THREADS), DS_SMEM, st, pdl, kmap,
+                krow0, q, ldq, kc, vc, count, nh, kvh, capacity, posd, pos0, plan.kps, part, plan.smax, err);
+}
+
+void launch_attention_merge_split(const float *part, const DecodeStreamPlan &plan, const int *posd, int pos0,
+                                  int rows, int count, int nh, int kvh, int NT, uint16_t *x3, float *out, int ldo,
+                                  cudaStream_t st) {
+  const int K = nh * DS_HD;
+  launch_kernel(attention_merge_split_kernel, dim3((K + 1023) / 1024, out ? rows : NT), dim3(256), 0, st, true, part,
+                plan.kps, posd, pos0, count, nh, kvh, plan.smax, rows, NT, x3, out, ldo);
+}
+
+}  // namespace stb

@@ -104,49 +104,91 @@ __device__ __forceinline__ int sk_cta_of(long long i, long long T, int G) {
 // x [M][K] (row stride ldx), optionally RMS-normalised as the vector GEMV does it, -> x3 [3][NT][K].
 // Block (kb, m) converts elements [kb * 1024, kb * 1024 + 1024) of row m, four per thread; with
 // RMSNorm every block of a row recomputes the row's inverse RMS with the GEMV's exact loop and
-// reduction order, so all blocks (and the GEMV) agree bit for bit.
+// reduction order, so all blocks (and the GEMV) agree bit for bit.  The kernel is latency-bound
+// (a few microseconds between two GEMMs), so every global load is issued before its first use:
+// the thread's four elements and norm weights with the first 32 terms of the sum of squares, the
+// rest of the sum 32 terms per round trip, still added in the loop's order.
 __global__ void __launch_bounds__(256) skinny_prep_kernel(const float *x, int ldx, const float *norm_w,
                                                           double eps, uint16_t *x3, int M, int NT, int K) {
   __shared__ double s_scratch[8];
   pdl_wait();
   pdl_trigger();
   const int m = blockIdx.y;
+  const int k0 = blockIdx.x * 1024 + threadIdx.x * 4;
+  const bool vec = k0 + 4 <= K && (ldx & 3) == 0 && ((uintptr_t)x & 15) == 0;
+  float v[4] = {0.0f, 0.0f, 0.0f, 0.0f}, nw[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (m < M) {
+    const float *xr = x + (size_t)m * ldx;
+    if (vec) {
+      const float4 f = *(const float4 *)(xr + k0);
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+        if (k0 + e < K) v[e] = xr[k0 + e];
+    }
+    if (norm_w) {
+#pragma unroll
+      for (int e = 0; e < 4; e++)
+        if (k0 + e < K) nw[e] = norm_w[k0 + e];
+    }
+  }
   double inv = 1.0;
   if (m < M && norm_w) {
     const float *xr = x + (size_t)m * ldx;
     double sq = 0.0;
-#pragma unroll 8
-    for (int k = threadIdx.x; k < K; k += 256) {
-      const double v = (double)xr[k];
-      sq = __dadd_rn(sq, __dmul_rn(v, v));
+    int k = threadIdx.x;
+    for (; k + 31 * 256 < K; k += 32 * 256) {
+      float t[32];
+#pragma unroll
+      for (int i = 0; i < 32; i++) t[i] = xr[k + i * 256];
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        const double d = (double)t[i];
+        sq = __dadd_rn(sq, __dmul_rn(d, d));
+      }
+    }
+    for (; k < K; k += 256) {
+      const double d = (double)xr[k];
+      sq = __dadd_rn(sq, __dmul_rn(d, d));
     }
     const double total = block_sum_double(sq, s_scratch);
     inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(total, (double)K), eps)));
   }
-  const int k0 = blockIdx.x * 1024 + threadIdx.x * 4;
+  uint16_t h[3][4] = {};
 #pragma unroll
   for (int e = 0; e < 4; e++) {
-    const int k = k0 + e;
-    if (k >= K) break;
-    float v = 0.0f;
-    if (m < M) {
-      v = x[(size_t)m * ldx + k];
-      if (norm_w) v = __double2float_rn(__dmul_rn(__dmul_rn((double)v, inv), (double)norm_w[k]));
-    }
-    // Non-finite v keeps its class in the first term alone (Inf - Inf would make the lower terms
-    // NaN); a finite v that rounds past BF16's largest finite value (|v| > 0x1.fep127) takes the
+    float f = v[e];
+    if (m < M && norm_w) f = __double2float_rn(__dmul_rn(__dmul_rn((double)f, inv), (double)nw[e]));
+    // Non-finite f keeps its class in the first term alone (Inf - Inf would make the lower terms
+    // NaN); a finite f that rounds past BF16's largest finite value (|f| > 0x1.fep127) takes the
     // truncated first term instead, which stays finite and leaves an exact 16-bit remainder.
-    uint16_t h0 = f32_to_bf16_rne(v), h1 = 0, h2 = 0;
-    if (isfinite(v)) {
-      if ((h0 & 0x7f80u) == 0x7f80u) h0 = (uint16_t)(__float_as_uint(v) >> 16);
-      const float r1 = v - __uint_as_float((uint32_t)h0 << 16);  // exact
+    uint16_t h0 = f32_to_bf16_rne(f), h1 = 0, h2 = 0;
+    if (isfinite(f)) {
+      if ((h0 & 0x7f80u) == 0x7f80u) h0 = (uint16_t)(__float_as_uint(f) >> 16);
+      const float r1 = f - __uint_as_float((uint32_t)h0 << 16);  // exact
       h1 = f32_to_bf16_rne(r1);
       const float r2 = r1 - __uint_as_float((uint32_t)h1 << 16);  // exact
       h2 = f32_to_bf16_rne(r2);
     }
-    x3[(size_t)m * K + k] = h0;
-    x3[((size_t)NT + m) * K + k] = h1;
-    x3[((size_t)2 * NT + m) * K + k] = h2;
+    h[0][e] = h0;
+    h[1][e] = h1;
+    h[2][e] = h2;
+  }
+  if (k0 + 4 <= K && (K & 3) == 0) {  // rows of x3 are 8-byte aligned: one 8-byte store per term
+#pragma unroll
+    for (int tm = 0; tm < 3; tm++) {
+      uint2 u;
+      u.x = (uint32_t)h[tm][0] | ((uint32_t)h[tm][1] << 16);
+      u.y = (uint32_t)h[tm][2] | ((uint32_t)h[tm][3] << 16);
+      *(uint2 *)(x3 + ((size_t)tm * NT + m) * K + k0) = u;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; e++)
+      if (k0 + e < K)
+#pragma unroll
+        for (int tm = 0; tm < 3; tm++) x3[((size_t)tm * NT + m) * K + k0 + e] = h[tm][e];
   }
 }
 
@@ -314,8 +356,18 @@ __device__ __forceinline__ float sk_gather(const float *part, int m, int row, in
   const int t = row / SK_BM;
   const int first = sk_cta_of((long long)t * kbs, T, G), last = sk_cta_of((long long)(t + 1) * kbs - 1, T, G);
   const float *pp = part + ((size_t)t * pmax * M + m) * SK_BM + (row % SK_BM);
-  float s = pp[0];
-  for (int pc = 1; pc <= last - first; pc++) s += pp[(size_t)pc * M * SK_BM];
+  const size_t stride = (size_t)M * SK_BM;
+  const int n = last - first + 1;
+  // pieces four loads at a time (one round trip each), added in piece order
+  float s = 0.0f;
+  for (int p0 = 0; p0 < n; p0 += 4) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) v[j] = p0 + j < n ? pp[(size_t)(p0 + j) * stride] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+      if (p0 + j < n) s = p0 + j == 0 ? v[0] : s + v[j];
+  }
   return s;
 }
 
@@ -393,7 +445,7 @@ struct SkinnyPlan {
 
 SkinnyPlan skinny_plan(int M, int N, int K, int device) {
   SkinnyPlan q;
-  q.nt = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+  q.nt = skinny_nt(M);
   q.tiles = (N + SK_BM - 1) / SK_BM;
   q.kbs = (K + BK - 1) / BK;
   q.iters = (long long)q.tiles * q.kbs;
@@ -450,10 +502,13 @@ uint64_t skinny_scratch_bytes(int M, int N, int K, int device) {
   return q.x3_bytes + q.part_bytes;
 }
 
+int skinny_nt(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
+
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, bool x3_ready) {
   STB_REQUIRE(p.M >= 1 && p.K % 8 == 0 && p.K >= BK && p.N >= SK_BM, "skinny Linear shape");
+  STB_REQUIRE(!x3_ready || (p.M <= 64 && p.norm_w == nullptr), "prepared skinny activations: one block, no norm");
   STB_REQUIRE(p.stop == nullptr, "skinny Linear takes no stop flag");
   STB_REQUIRE(scratch && ((uintptr_t)scratch % 256) == 0 && scratch_bytes >= skinny_scratch_bytes(p.M, p.N, p.K, device),
               "skinny Linear scratch too small");
@@ -468,25 +523,26 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
     const SkinnyPlan q = skinny_plan(mb, p.N, p.K, device);
     uint16_t *x3 = (uint16_t *)scratch;
     float *part = (float *)((char *)scratch + q.x3_bytes);
-    launch_kernel(skinny_prep_kernel, dim3((p.K + 1023) / 1024, q.nt), dim3(256), 0, stream, m0 > 0 || p.pdl,
-                  p.x + (size_t)m0 * p.ldx, p.ldx, p.norm_w, p.norm_eps, x3, mb, q.nt, p.K);
+    if (!x3_ready)
+      launch_kernel(skinny_prep_kernel, dim3((p.K + 1023) / 1024, q.nt), dim3(256), 0, stream, m0 > 0 || p.pdl,
+                    p.x + (size_t)m0 * p.ldx, p.ldx, p.norm_w, p.norm_eps, x3, mb, q.nt, p.K);
     const CUtensorMap tx = make_map(x3, STB_BF16, (uint64_t)3 * q.nt, (uint64_t)p.K, 3 * q.nt);
     if (q.nt == 16) launch_gemm<16>(q, tw, tx, part, mb, p.N, err, device, stream);
     else if (q.nt == 32) launch_gemm<32>(q, tw, tx, part, mb, p.N, err, device, stream);
     else launch_gemm<64>(q, tw, tx, part, mb, p.N, err, device, stream);
     launch_kernel(skinny_fixup_kernel<EPI>, dim3((units + 255) / 256, mb), dim3(256), 0, stream, true, p,
                   (const float *)part, q.kbs, q.iters, q.grid, q.pmax, m0, mb);
-    launches += 3;
+    launches += x3_ready ? 2 : 3;
   }
   check_launch("skinny");
   return launches;
 }
 
-template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
-template int skinny_launch<EPI_RESID>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
-template int skinny_launch<EPI_SILU>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
-template int skinny_launch<EPI_QKV>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
-template int skinny_launch<EPI_LOGITS>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
-template int skinny_launch<EPI_PEER>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t);
+template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
+template int skinny_launch<EPI_RESID>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
+template int skinny_launch<EPI_SILU>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
+template int skinny_launch<EPI_QKV>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
+template int skinny_launch<EPI_LOGITS>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
+template int skinny_launch<EPI_PEER>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
 
 }  // namespace stb

@@ -443,9 +443,14 @@ uint64_t skinny_scratch_bytes(int M, int N, int K, int device);
 // Sets the kernels' shared-memory limits on `device` (before a graph capture that launches them).
 void skinny_prepare(int device);
 // Enqueues prologue -> stream-K GEMM -> fixup/epilogue per 64-row block (3 kernels each, all
-// programmatic dependents except the first when !p.pdl).  Returns the number of kernels launched.
+// programmatic dependents except the first when !p.pdl).  With x3_ready (M <= 64, no RMSNorm) the
+// previous kernel has already written the activation terms x3 [3][skinny_nt(M)][K] at the start of
+// the scratch, with zero rows M .. NT - 1, and the prologue is skipped.  Returns the number of
+// kernels launched.
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
-                  cudaStream_t stream);
+                  cudaStream_t stream, bool x3_ready = false);
+// Token rows of the activation-term tile for a block of M <= 64 rows: 16, 32 or 64.
+int skinny_nt(int M);
 
 }  // namespace stb

@@ -18,12 +18,14 @@
 // o/down by input columns; each row-split projection's partial sums are joined by one NCCL
 // allreduce which also carries the residual (rank 0 adds it before the reduction).  lm_head is
 // split by vocabulary; ranks exchange their (value, index) candidates with one allgather.
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstring>
 #include <mutex>
 #include <vector>
 
+#include "attention_decode.cuh"
 #include "gemv.cuh"
 #include "rng.cuh"
 #include "tc_common.cuh"
@@ -91,6 +93,8 @@ struct stb_llama_cache {
   uint64_t xn = 0, xh = 0, qkvbuf = 0, gubuf = 0;
   uint64_t skin = 0, skin_bytes = 0;  // tensor-core skinny path scratch (one 64-row block)
   uint64_t att_part = 0, att_count = 0;  // split decode attention records and counters (batch rows)
+  CUtensorMap kv_map;                    // the whole K/V cache as rows of hd Float32 (streamed attention)
+  bool kv_map_ok = false;
   int att_rows = 0;
   int graph_launches = 0;  // kernels in one replay of `graph`
   uint64_t tokens = 0;  // int64 [rows]
@@ -861,6 +865,214 @@ __global__ void __launch_bounds__(DA_THREADS) decode_attention_kernel(
   if (tid == 0) counters[(size_t)m * kvh + g0] = 0;
 }
 
+// Decode attention for head size 128, GQA groups of up to 8 query heads: the same blocks, split
+// records and merge as decode_attention_kernel, with the arithmetic arranged so that no cross-lane
+// reduction is needed.  Scores: lane (key k, head quad h4) of a warp computes the whole 128-term
+// dot of key k with query heads 4 h4 .. 4 h4 + 3 (16 FMAs per 128-bit K load; the K rows land in
+// shared memory padded to 132 floats by one bulk copy per row, so the 16 keys a warp reads fall in
+// distinct banks, and the query rows are read as broadcasts).  Weighted V sum: warp w owns output
+// dimensions 32 w .. 32 w + 31 of every head, so each lane runs over all keys with its own 8
+// accumulators and no partials are combined across warps.  K and V complete on separate
+// mbarriers: the scores start while V is still in flight.  The copy waits are bounded (2 s, then
+// the session's error word is set and the block leaves without writing).
+constexpr int DA2_KROW = 132;  // padded K row (floats)
+
+template <int KPS>
+constexpr size_t da2_smem() {
+  return (size_t)KPS * DA2_KROW * 4 + (size_t)KPS * 128 * 4 + (size_t)DA_GMAX * DA2_KROW * 4 +
+         (size_t)2 * DA_GMAX * KPS * 4 + DA_GMAX * 2 * 4 + 32;
+}
+
+template <int KPS>
+__global__ void __launch_bounds__(DA_THREADS) decode_attention_hd128_kernel(
+    const float *q, int ldq, const float *kcache, const float *vcache, float *out, int ldo, int count, int nh,
+    int kvh, int capacity, const int *pos_dev, int pos0, float *part, int *counters, int smax, int *err) {
+  constexpr int HD = 128;
+  static_assert(KPS % 16 == 0 && KPS >= DA_KPS_MIN, "keys per split");
+  extern __shared__ __align__(128) uint8_t da_raw[];
+  float *Kp = (float *)da_raw;              // [KPS][DA2_KROW]
+  float *Vs = Kp + KPS * DA2_KROW;          // [KPS][HD]
+  float *Qs = Vs + KPS * HD;                // [G][DA2_KROW]
+  float *sp = Qs + DA_GMAX * DA2_KROW;      // [G][KPS] scores, then probabilities
+  float *pt = sp + DA_GMAX * KPS;           // [KPS][8] probabilities by key
+  float *red = pt + DA_GMAX * KPS;          // [G][2] max, sum
+  uint64_t *bar = (uint64_t *)(red + DA_GMAX * 2);  // [2]: K, V
+  __shared__ int s_last, s_ok;
+  __shared__ volatile int s_abort;
+  pdl_trigger();
+  const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
+  const int G = nh / kvh;
+  const int b = m / count, t = m % count;
+  const int keys = (pos_dev ? *pos_dev : pos0) + t + 1;
+  const int S = (keys + KPS - 1) / KPS;
+  if (split >= S) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int j0 = split * KPS, nk = min(KPS, keys - j0);
+  const int fresh = keys - 1 - j0;
+  const int old = fresh < nk ? fresh : nk;  // rows [0, old) were written by earlier steps
+  const size_t kvrow0 = ((size_t)b * kvh + g0) * capacity + j0;
+  const uint32_t bar_k = tc::smem_u32(bar), bar_v = bar_k + 8;
+  if (tid == 0) {
+    s_abort = 0;
+    tc::mbar_init(bar_k, 1);
+    tc::mbar_init(bar_v, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) {
+      if (old > 0) {
+        tc::mbar_expect_tx(bar_k, (uint32_t)old * HD * 4);
+        tc::mbar_expect_tx(bar_v, (uint32_t)old * HD * 4);
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         tc::smem_u32(Vs)),
+                     "l"(vcache + kvrow0 * HD), "r"((uint32_t)old * HD * 4), "r"(bar_v)
+                     : "memory");
+      } else {
+        tc::mbar_arrive(bar_k);
+        tc::mbar_arrive(bar_v);
+      }
+    }
+    __syncwarp();
+    for (int r = lane; r < old; r += 32)  // one 512-byte copy per K row into its padded slot
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       tc::smem_u32(Kp + r * DA2_KROW)),
+                   "l"(kcache + (kvrow0 + r) * HD), "r"((uint32_t)HD * 4), "r"(bar_k)
+                   : "memory");
+  }
+  pdl_wait();
+  if (fresh < nk) {  // the newest key, written by the projection just before this kernel
+    Kp[fresh * DA2_KROW + tid] = kcache[(kvrow0 + fresh) * HD + tid];
+    Vs[fresh * HD + tid] = vcache[(kvrow0 + fresh) * HD + tid];
+  }
+  for (int i = tid; i < DA_GMAX * (HD / 4); i += DA_THREADS) {  // the group's query rows (zero past G)
+    const int g = i / (HD / 4), d4 = i % (HD / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g < G) v = *(const float4 *)(q + (size_t)m * ldq + (size_t)(g0 * G + g) * HD + d4 * 4);
+    *(float4 *)(Qs + g * DA2_KROW + d4 * 4) = v;
+  }
+  if (tid == 0) {
+    s_ok = tc::mbar_wait(bar_k, 0, &s_abort, err, 42);
+    if (!s_ok) {  // leave only once every copy into this block's shared memory is done (bounded again)
+      volatile int no_abort = 0;
+      tc::mbar_wait(bar_k, 0, &no_abort, err, 42);
+      tc::mbar_wait(bar_v, 0, &no_abort, err, 43);
+    }
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const float scale = (float)(1.0 / sqrt((double)HD));
+
+  // scores: 16 keys x 2 head quads per warp pass (32 keys x 1 quad when G <= 4)
+  {
+    const int quads = G > 4 ? 2 : 1, kpw = 32 / quads;
+    const int kk = lane % kpw, h4 = lane / kpw;
+    for (int jb = warp * kpw; jb < nk; jb += DA_WARPS * kpw) {
+      const int j = jb + kk;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      if (j < nk) {
+        const float *kr = Kp + j * DA2_KROW;
+        const float *qr = Qs + 4 * h4 * DA2_KROW;
+#pragma unroll 8
+        for (int d = 0; d < HD; d += 4) {
+          const float4 kv = *(const float4 *)(kr + d);
+#pragma unroll
+          for (int h = 0; h < 4; h++) {
+            const float4 qv = *(const float4 *)(qr + h * DA2_KROW + d);
+            acc[h] = fmaf(qv.x, kv.x, acc[h]);
+            acc[h] = fmaf(qv.y, kv.y, acc[h]);
+            acc[h] = fmaf(qv.z, kv.z, acc[h]);
+            acc[h] = fmaf(qv.w, kv.w, acc[h]);
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 4; h++)
+          if (4 * h4 + h < G) sp[(4 * h4 + h) * KPS + j] = acc[h] * scale;
+      }
+    }
+  }
+  __syncthreads();
+  for (int g = warp; g < G; g += DA_WARPS) {  // per head: max and sum of exp over the split
+    float mx = -INFINITY;
+    for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, sp[g * KPS + j]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.0f;
+    for (int j = lane; j < nk; j += 32) {
+      const float e = expf(sp[g * KPS + j] - mx);
+      pt[j * DA_GMAX + g] = e;
+      sum += e;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) {
+      red[g * 2] = mx;
+      red[g * 2 + 1] = sum;
+    }
+  }
+  if (tid == 0) {
+    s_ok = tc::mbar_wait(bar_v, 0, &s_abort, err, 43);
+    if (!s_ok) {
+      volatile int no_abort = 0;
+      tc::mbar_wait(bar_v, 0, &no_abort, err, 43);
+    }
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  // weighted V sum: lane owns dimension d of every head
+  const int d = warp * 32 + lane;
+  float acc[DA_GMAX];
+#pragma unroll
+  for (int g = 0; g < DA_GMAX; g++) acc[g] = 0.0f;
+#pragma unroll 4
+  for (int j = 0; j < nk; j++) {
+    const float v = Vs[j * HD + d];
+    const float4 pa = *(const float4 *)(pt + j * DA_GMAX), pb = *(const float4 *)(pt + j * DA_GMAX + 4);
+    acc[0] = fmaf(pa.x, v, acc[0]);
+    acc[1] = fmaf(pa.y, v, acc[1]);
+    acc[2] = fmaf(pa.z, v, acc[2]);
+    acc[3] = fmaf(pa.w, v, acc[3]);
+    acc[4] = fmaf(pb.x, v, acc[4]);
+    acc[5] = fmaf(pb.y, v, acc[5]);
+    acc[6] = fmaf(pb.z, v, acc[6]);
+    acc[7] = fmaf(pb.w, v, acc[7]);
+  }
+  const size_t slot = ((size_t)m * kvh + g0) * smax;
+  float *po = part, *pml = part + (size_t)gridDim.z * kvh * smax * DA_GMAX * HD;
+  if (S == 1) {
+#pragma unroll
+    for (int g = 0; g < DA_GMAX; g++)
+      if (g < G) out[(size_t)m * ldo + (size_t)(g0 * G + g) * HD + d] = acc[g] / red[g * 2 + 1];
+    return;
+  }
+#pragma unroll
+  for (int g = 0; g < DA_GMAX; g++)
+    if (g < G) po[((slot + split) * DA_GMAX + g) * HD + d] = acc[g];
+  if (tid < G) {
+    pml[((slot + split) * DA_GMAX + tid) * 2 + 0] = red[tid * 2];
+    pml[((slot + split) * DA_GMAX + tid) * 2 + 1] = red[tid * 2 + 1];
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&counters[(size_t)m * kvh + g0], 1) == S - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = tid; i < G * HD; i += DA_THREADS) {  // the last split merges all, in split order
+    const int g = i / HD, dd = i % HD;
+    float M = -INFINITY;
+    for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(&pml[((slot + s) * DA_GMAX + g) * 2]));
+    float num = 0.0f, den = 0.0f;
+    for (int s = 0; s < S; s++) {
+      const float w = expf(__ldcg(&pml[((slot + s) * DA_GMAX + g) * 2]) - M);
+      num = fmaf(w, __ldcg(&po[((slot + s) * DA_GMAX + g) * HD + dd]), num);
+      den = fmaf(w, __ldcg(&pml[((slot + s) * DA_GMAX + g) * 2 + 1]), den);
+    }
+    out[(size_t)m * ldo + (size_t)(g0 * G + g) * HD + dd] = num / den;
+  }
+  if (tid == 0) counters[(size_t)m * kvh + g0] = 0;
+}
+
 // Floats of split records decode_attention_kernel needs for `rows` token rows (sized for the
 // smallest split, DA_KPS_MIN keys).
 size_t decode_attention_part_floats(int rows, int kvh, int capacity, int hd) {
@@ -887,9 +1099,29 @@ void da_launch(dim3 grid, bool pdl, cudaStream_t st, int device, const float *q,
                 count, nh, kvh, capacity, posd, pos0, part, counters, smax, err);
 }
 
+template <int KPS>
+void da2_launch(dim3 grid, bool pdl, cudaStream_t st, int device, const float *q, int ldq, const float *kc,
+                const float *vc, float *out, int ldo, int count, int nh, int kvh, int capacity, const int *posd,
+                int pos0, float *part, int *counters, int smax, int *err) {
+  constexpr size_t smem = da2_smem<KPS>();
+  {
+    static std::mutex mu;
+    static bool configured[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0 || device >= 64 || !configured[device]) {
+      STB_CUDA(cudaFuncSetAttribute(decode_attention_hd128_kernel<KPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem));
+      if (device >= 0 && device < 64) configured[device] = true;
+    }
+  }
+  launch_kernel(decode_attention_hd128_kernel<KPS>, grid, dim3(DA_THREADS), smem, st, pdl, q, ldq, kc, vc, out, ldo,
+                count, nh, kvh, capacity, posd, pos0, part, counters, smax, err);
+}
+
 // Launches the split decode attention when the head size and group size have a form (hd in
 // {32, 64, 128}, nh / kvh <= 8) and STB_DECODE_ATTENTION is not 0; returns false otherwise.  Keys per
-// split: the smallest of 32 / 64 / 128 that keeps the grid within ~6 blocks per SM.
+// split: the smallest of 32 / 64 / 128 that keeps the grid within ~6 blocks per SM.  Head size 128
+// takes decode_attention_hd128_kernel unless STB_DA_HD128 is 0.
 bool launch_decode_attention(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
                              int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
                              float *part, int *counters, bool pdl, cudaStream_t st, int device, int *err) {
@@ -903,6 +1135,19 @@ bool launch_decode_attention(const float *q, int ldq, const float *kc, const flo
   if (forced == 32 || forced == 64 || forced == 128 || (forced == 256 && hd <= 64)) kps = forced;
   const int smax = (capacity + kps - 1) / kps;
   const dim3 grid(smax, kvh, rows);
+  static const int hd128 = env_int("STB_DA_HD128", 1);
+  if (hd == 128 && hd128 && kps <= 128) {
+    if (kps == 32)
+      da2_launch<32>(grid, pdl, st, device, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, part,
+                     counters, smax, err);
+    else if (kps == 64)
+      da2_launch<64>(grid, pdl, st, device, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, part,
+                     counters, smax, err);
+    else
+      da2_launch<128>(grid, pdl, st, device, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, part,
+                      counters, smax, err);
+    return true;
+  }
 #define STB_DA(HDV, KPSV)                                                                                          \
   da_launch<HDV, KPSV>(grid, pdl, st, device, q, ldq, kc, vc, out, ldo, count, nh, kvh, capacity, posd, pos0, part, \
                        counters, smax, err)
@@ -1311,8 +1556,9 @@ void ensure_rows(stb_llama_cache *c, int rows) {
   c->xn = c->xh = c->qkvbuf = c->gubuf = 0;
   c->att_rows = c->batch;
   c->att_part = alloc_owned(s, c->owned,
-                            std::max(decode_attention_part_floats(c->batch, m->KV, c->capacity, m->hd),
-                                     decode_attention_reg_part_floats(c->batch, m->KV, c->capacity, m->hd)) *
+                            std::max<size_t>({decode_attention_part_floats(c->batch, m->KV, c->capacity, m->hd),
+                                              decode_attention_reg_part_floats(c->batch, m->KV, c->capacity, m->hd),
+                                              decode_stream_part_floats(c->batch, m->KV, c->capacity)}) *
                                 sizeof(float));
   c->att_count = alloc_owned(s, c->owned, (uint64_t)c->batch * m->KV * sizeof(int));
   STB_CUDA(cudaMemsetAsync((void *)c->att_count, 0, (size_t)c->batch * m->KV * sizeof(int), s->stream));
@@ -1435,12 +1681,19 @@ int enqueue_layer_tc(stb_llama_cache *c, size_t l, int rows, int count, const in
 // One projection of a chunk: the tensor-core skinny form (three-term BF16 activations, FP32
 // accurate) when it applies to the shape and the cache holds its scratch, else the vector GEMV.
 // Returns the kernels launched.
+bool projects_skinny(const stb_llama_cache *c, int M, int N, int K, int wdt, const void *w) {
+  return c->skin && skinny_eligible(M, N, K, wdt, w) && skinny_scratch_bytes(M, N, K, c->m->s->device) <= c->skin_bytes;
+}
+
+// With x3_ready the skinny form's activation terms are already in the scratch (written by the
+// previous kernel): M <= 64, and the projection must take the skinny form.
 template <int EPI>
-int project(stb_llama_cache *c, const GemvParams &p, int wdt, GemvConfig cfg, cudaStream_t st) {
+int project(stb_llama_cache *c, const GemvParams &p, int wdt, GemvConfig cfg, cudaStream_t st,
+            bool x3_ready = false) {
   stb_session *s = c->m->s;
-  if (c->skin && skinny_eligible(p.M, p.N, p.K, wdt, p.w) &&
-      skinny_scratch_bytes(p.M, p.N, p.K, s->device) <= c->skin_bytes)
-    return skinny_launch<EPI>(p, (void *)c->skin, c->skin_bytes, session_error_word(s), s->device, st);
+  if (projects_skinny(c, p.M, p.N, p.K, wdt, p.w))
+    return skinny_launch<EPI>(p, (void *)c->skin, c->skin_bytes, session_error_word(s), s->device, st, x3_ready);
+  STB_REQUIRE(!x3_ready, "prepared activation terms need the skinny projection");
   launch_gemv<EPI>(p, wdt, cfg, st);
   return 1;
 }
@@ -1490,7 +1743,20 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.pdl = true;
       launches += project<EPI_QKV>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st);
     }
-    {  // 2. attention: split GQA kernel for single-token steps, tiled kernel for chunks
+    // the streamed single-token attention leaves split records; the o projection's prologue merges them
+    const bool stream_att = a.count == 1 && rows <= c->att_rows && c->kv_map_ok;
+    bool o_x3 = false;
+    if (stream_att) {  // 2. attention (streamed form) and the merge: as the o projection's terms or Float32
+      const DecodeStreamPlan plan = decode_stream_plan(rows, m->KV, c->capacity, s->device);
+      launch_decode_attention_stream(c->kv_map, (long long)(l * kv_layer) / m->hd, (const float *)c->qbuf, qw, kc, vc,
+                                     rows, 1, m->NH, m->KV, c->capacity, posd, c->used, plan, (float *)c->att_part,
+                                     true, st, s->device, session_error_word(s));
+      o_x3 = rows <= 64 && projects_skinny(c, rows, H, qw, wdt, (const void *)L.o);
+      launch_attention_merge_split((const float *)c->att_part, plan, posd, c->used, rows, 1, m->NH, m->KV,
+                                   skinny_nt(rows), o_x3 ? (uint16_t *)c->skin : nullptr,
+                                   o_x3 ? nullptr : (float *)c->att, qw, st);
+      launches += 2;
+    } else {  // 2. attention: split GQA kernel for single-token steps, tiled kernel for chunks
       bool done = false;
       if (a.count == 1 && rows <= c->att_rows)
         done = use_register_attention(rows, m->KV, m->hd, c->capacity, s->device)
@@ -1533,23 +1799,23 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.pdl = true;
       if (m->tp == 1) {
         p.y = (float *)c->hidden; p.ldy = H; p.residual = (const float *)c->hidden; p.ldr = H;
-        launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st);
+        launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, half == 0 && o_x3);
       } else if (peer_usable(s, (uint64_t)rows * H)) {
         // fused row-split projection: partial sums stored into every rank's slots over NVLink,
         // then summed in rank order with the residual on each rank
         p.ldy = H;
         p.peer = peer_args(s, half);
         const GemvConfig cfg = choose_gemv(rows, p.N, p.K, false);
-        launches += project<EPI_PEER>(c, p, wdt, cfg, st);
+        launches += project<EPI_PEER>(c, p, wdt, cfg, st, half == 0 && o_x3);
         peer_reduce_launch(s, half, (long)rows * H, (const float *)c->hidden, (float *)c->hidden);
         launches++;
       } else {
         p.y = (float *)c->sum; p.ldy = H;
         if (m->rank == 0) {
           p.residual = (const float *)c->hidden; p.ldr = H;
-          launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st);
+          launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, half == 0 && o_x3);
         } else {
-          launches += project<EPI_PLAIN>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st);
+          launches += project<EPI_PLAIN>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, half == 0 && o_x3);
         }
         allreduce_sum_f32(s, (void *)c->sum, (uint64_t)rows * H);
         std::swap(c->hidden, c->sum);
@@ -1877,6 +2143,10 @@ int stb_llama_cache_create(stb_llama *m, int batch, int capacity, stb_llama_cach
     try {
       const uint64_t bytes = (uint64_t)m->layers.size() * 2 * batch * m->KV * capacity * m->hd * 4;
       c->kv = alloc_owned(m->s, c->owned, bytes);
+      if (decode_stream_applies(m->hd, m->NH, m->KV)) {
+        c->kv_map = make_kv_map((const float *)c->kv, bytes / ((uint64_t)m->hd * 4));
+        c->kv_map_ok = true;
+      }
       ensure_rows(c, batch);
     } catch (...) {
       free_owned(m->s, c->owned);

@@ -281,11 +281,17 @@ HD128 = dict(vocab_size=512, hidden_size=1024, intermediate_size=256, num_layers
              num_key_value_heads=1, max_positions=512, tie_word_embeddings=False, eos_token_ids=())
 
 
-@pytest.mark.parametrize("impl,kps", [(1, 32), (1, 64), (1, 128), (0, 0)])
-def test_decode_attention_splits_head128_group8(impl, kps):
-    """The split decode attention on head size 128 with 8 query heads per KV head: the bulk-copy form with
-    keys per split forced to 32 / 64 / 128, and the register form (STB_DA_IMPL / STB_DA_KPS, read once per
-    process: a child process each), over 127 prompt tokens
+@pytest.mark.parametrize("stream,impl,kps,hd128,heads,kvh", [
+    (1, 1, 0, 1, 8, 1), (1, 1, 32, 1, 8, 1), (1, 1, 64, 1, 8, 2), (1, 1, 96, 1, 6, 2), (1, 1, 32, 1, 4, 4),
+    (0, 1, 32, 1, 8, 1), (0, 1, 64, 1, 8, 1), (0, 1, 128, 1, 8, 1), (0, 1, 64, 0, 8, 1), (0, 0, 0, 1, 8, 1),
+    (0, 1, 64, 1, 8, 2), (0, 1, 32, 1, 6, 2)])
+def test_decode_attention_splits_head128(stream, impl, kps, hd128, heads, kvh):
+    """The decode attention on head size 128 with 8, 4, 3 and 1 query heads per KV head: the streamed form
+    (decode_attention_stream_kernel + the merge in the o projection's prologue) with its keys per split
+    left to the plan or forced to 32 / 64 / 96 (STB_DS_KPS), and with STB_DECODE_STREAM=0 the split forms
+    (decode_attention_hd128_kernel, and decode_attention_kernel with STB_DA_HD128=0) with keys per split
+    forced to 32 / 64 / 128 (STB_DA_KPS) and the register form (STB_DA_IMPL) -- variables read once per
+    process: a child process each -- over 127 prompt tokens
     (254 rows: below the tensor-core prefill threshold, so the whole run keeps Float32 activations) and 8
     decode steps for 2 rows, so splits merge: greedy ids identical to the oracle and the logits of a
     cached step within 1e-5 (1 + |e|)."""
@@ -299,7 +305,8 @@ def test_decode_attention_splits_head128_group8(impl, kps):
         "from test_llama_gpu import HD128, close\n"
         "from scalatorch import ffm\n"
         "from scalatorch.models import BackendLlama, LlamaConfig\n"
-        "cfg = LlamaConfig(**HD128)\n"
+        f"cfg = LlamaConfig(**dict(HD128, hidden_size={heads * 128}, num_attention_heads={heads}, "
+        f"num_key_value_heads={kvh}))\n"
         "ref = oracle_model(cfg, seed=9)\n"
         "rng = np.random.default_rng(3)\n"
         "prompts = rng.integers(0, cfg.vocab_size, (2, 127))\n"
@@ -318,7 +325,8 @@ def test_decode_attention_splits_head128_group8(impl, kps):
         "    c.close()\n"
         "s.close()\n"
         "print('ok')\n")
-    env = dict(os.environ, STB_DA_KPS=str(kps), STB_DA_IMPL=str(impl))
+    env = dict(os.environ, STB_DECODE_STREAM=str(stream), STB_DS_KPS=str(kps if stream else 0),
+               STB_DA_KPS=str(0 if stream else kps), STB_DA_IMPL=str(impl), STB_DA_HD128=str(hd128))
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
 
