@@ -7,26 +7,29 @@
 // visible key, softmax, weighted sum of the values.  On the GPU each (batch row, KV head) pair's
 // visible keys are cut into splits of `kps` keys (a multiple of 32, chosen from the cache capacity
 // so that about two blocks per SM cover all pairs: every block is resident at once, no second
-// wave).  Block (split, KV head, row), 128 threads, streams its split's K rows and then its V rows
+// wave).  Block (split, KV head, row), 256 threads, streams its split's K rows and then its V rows
 // in chunks of 32 keys (16 KB) through a 5-stage ring:
 //   * K chunks: four 2-D TMA box loads (32 dims x 32 keys of Float32, 128-byte swizzle) from one
 //     tensor map over the whole cache; V chunks: one bulk copy of the contiguous rows.  The first
 //     five chunks are issued before the programmatic-dependency wait (the cache rows of earlier
 //     steps never depend on the previous kernel); the newest key, which the QKV projection just
 //     wrote, is patched into its chunk from global memory after the wait.
-//   * scores: lane (key k, head quad h4) of a warp computes the dot of key k with query heads
-//     4 h4 .. 4 h4 + 3 over its warp's share of the dimensions (16 FMAs per 128-bit K load; the
-//     swizzle puts the keys a warp reads in distinct banks; the query rows are broadcast reads);
-//     the dimension shares are added in order through shared memory.
-//   * after the last K chunk: softmax statistics per head over the split (max, exp, sum);
-//   * V chunks: warp w owns output dimensions 32 w .. 32 w + 31 of every head, so each lane runs
-//     over the chunk's keys with its 8 accumulators.
-// Each block writes its split's unnormalised sums and (max, sum) per head.  The merge (rescale
-// every split by exp(max_s - max), sum in split order, divide) runs in attention_merge_split_kernel,
-// which is the o projection's prologue: it writes the three BF16 terms of the merged output that
-// the skinny GEMM reads (or the Float32 output for the other forms of the projection).
-// Every mbarrier wait is bounded (2 s; then the session's error word is set, the block waits --
-// bounded again -- for the copies it issued, and leaves without writing).
+//   * scores: lane (key k, head quad h4) computes the dot of key k with query heads 4 h4 .. 4 h4 + 3
+//     over its warp's share of the dimensions (16 FMAs per 128-bit K load; the swizzle puts the keys
+//     a warp reads in distinct banks; the query rows are broadcast reads); the shares are added in
+//     order through shared memory.  Groups of more than 4 heads take two head quads per key (16
+//     keys x 2 quads per warp, 4 dimension shares); smaller groups one (32 keys, 8 shares).
+//   * after the last K chunk: softmax statistics per head over the split (max, exp, sum), a warp
+//     per head;
+//   * V chunks: warp w owns output dimensions 32 (w mod 4) .. + 31 of every head over the keys of
+//     parity w / 4, with 8 accumulators per lane; the two parities are added at the end.
+// The per-warp work is short chains of shared-memory loads and FMAs, so the block has 8 warps (16
+// per SM) to hide their latency.  Each block writes its split's unnormalised sums and (max, sum) per
+// head.  The merge (rescale every split by exp(max_s - max), sum in split order, divide) runs in
+// attention_merge_split_kernel, which is the o projection's prologue: it writes the three BF16 terms
+// of the merged output that the skinny GEMM reads (or the Float32 output for the other forms of the
+// projection).  Every mbarrier wait is bounded (2 s; then the session's error word is set, the block
+// waits -- bounded again -- for the copies it issued, and leaves without writing).
 #include "attention_decode.cuh"
 #include "tc_common.cuh"
 
@@ -36,11 +39,14 @@ namespace {
 
 using namespace tc;
 
-constexpr int DS_HD = 128, DS_CH = 32, DS_RING = 5, DS_THREADS = 128, DS_GMAX = 8, DS_KPS_MAX = 256;
+constexpr int DS_HD = 128, DS_CH = 32, DS_RING = 5, DS_THREADS = 256, DS_WARPS = DS_THREADS / 32, DS_GMAX = 8,
+              DS_KPS_MAX = 256;
 constexpr int DS_CHUNK = DS_CH * DS_HD * 4;  // 16 KB: 32 K rows (4 swizzled boxes of 4 KB) or V rows
 constexpr int DS_QROW = 132;                 // padded query row (floats)
-constexpr size_t DS_SMEM = 1024 + (size_t)DS_RING * DS_CHUNK + DS_GMAX * DS_QROW * 4 + 4 * DS_CH * DS_GMAX * 4 +
-                           (size_t)DS_KPS_MAX * DS_GMAX * 4 + DS_GMAX * 2 * 4 + DS_RING * 8;
+constexpr int DS_SHARES = 8;                 // dimension shares of the scores (at most)
+constexpr size_t DS_SMEM = 1024 + (size_t)DS_RING * DS_CHUNK + DS_GMAX * DS_QROW * 4 +
+                           (size_t)DS_SHARES * DS_CH * DS_GMAX * 4 + (size_t)DS_KPS_MAX * DS_GMAX * 4 +
+                           DS_GMAX * 2 * 4 + DS_RING * 8;
 
 // Byte offset of float d of key row r inside a K chunk: box d / 32 (4 KB), row r (128 bytes), 16-byte
 // chunk (d % 32) / 4 XOR-ed with r mod 8 (TMA's SWIZZLE_128B on a 1024-byte-aligned box).
@@ -48,15 +54,40 @@ __device__ __forceinline__ uint32_t ds_koff(int r, int d) {
   return (uint32_t)((d >> 5) * 4096 + r * 128 + ((((d & 31) >> 2) ^ (r & 7)) << 4) + (d & 3) * 4);
 }
 
-__global__ void __launch_bounds__(DS_THREADS) decode_attention_stream_kernel(
+// Partial scores of key `sk` against query heads 4 sq .. 4 sq + 3 over dimensions [d0, d0 + DLEN).
+template <int DLEN>
+__device__ __forceinline__ float4 ds_scores(const uint8_t *chunk, const float *Qs, int sk, int sq, int d0) {
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+  const float *qr = Qs + 4 * sq * DS_QROW + d0;
+  const uint8_t *kr = chunk + (d0 >> 5) * 4096 + sk * 128;
+  const int rx = sk & 7, c0 = (d0 & 31) >> 2;
+#pragma unroll
+  for (int i = 0; i < DLEN / 4; i++) {
+    const int cc = c0 + i;  // 16-byte chunk along the dimensions (boxes of 8 chunks)
+    const float4 kv = *(const float4 *)(kr + (cc >> 3) * 4096 + (((cc & 7) ^ rx) << 4));
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+      const float4 qv = *(const float4 *)(qr + h * DS_QROW + 4 * i);
+      s4[h] = fmaf(qv.x, kv.x, s4[h]);
+      s4[h] = fmaf(qv.y, kv.y, s4[h]);
+      s4[h] = fmaf(qv.z, kv.z, s4[h]);
+      s4[h] = fmaf(qv.w, kv.w, s4[h]);
+    }
+  }
+  return make_float4(s4[0], s4[1], s4[2], s4[3]);
+}
+
+// TWOQ: more than 4 query heads per KV head (two head quads per key).
+template <bool TWOQ>
+__global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_kernel(
     const __grid_constant__ CUtensorMap kmap, long long krow0, const float *q, int ldq, const float *kcache,
     const float *vcache, int count, int nh, int kvh, int capacity, const int *pos_dev, int pos0, int kps,
     float *part, int smax, int *err) {
   extern __shared__ uint8_t ds_raw[];
   uint8_t *ring = (uint8_t *)(((uintptr_t)ds_raw + 1023) & ~(uintptr_t)1023);
   float *Qs = (float *)(ring + DS_RING * DS_CHUNK);  // [8][DS_QROW]
-  float *pscr = Qs + DS_GMAX * DS_QROW;              // [4 dimension shares][32 keys][8 heads]
-  float *pt = pscr + 4 * DS_CH * DS_GMAX;            // [kps][8]: scores, then exp(score - max)
+  float *pscr = Qs + DS_GMAX * DS_QROW;              // [dimension shares][32 keys][8 heads]; V parity sums
+  float *pt = pscr + DS_SHARES * DS_CH * DS_GMAX;    // [kps][8]: scores, then exp(score - max)
   float *red = pt + DS_KPS_MAX * DS_GMAX;            // [8][2]: max, sum
   uint64_t *bar = (uint64_t *)(red + DS_GMAX * 2);   // [DS_RING]
   __shared__ int s_ok;
@@ -99,75 +130,62 @@ __global__ void __launch_bounds__(DS_THREADS) decode_attention_stream_kernel(
     for (; issued < min(DS_RING, total); issued++) issue(issued);
   }
   pdl_wait();
-  for (int i = tid; i < DS_GMAX * (DS_HD / 4); i += DS_THREADS) {  // the group's query rows (zero past G)
-    const int g = i / (DS_HD / 4), d4 = i % (DS_HD / 4);
+  {  // the group's query rows (zero past G): one float4 per thread
+    const int g = tid / (DS_HD / 4), d4 = tid % (DS_HD / 4);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (g < G) v = *(const float4 *)(q + (size_t)m * ldq + (size_t)(g0 * G + g) * DS_HD + d4 * 4);
     *(float4 *)(Qs + g * DS_QROW + d4 * 4) = v;
   }
   // the newest key's row, loaded now (after the wait) and stored once its chunk has landed
-  const float kf = fresh < nk ? kcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
-  const float vf = fresh < nk ? vcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
+  const bool patch = fresh < nk && tid < DS_HD;
+  const float kf = patch ? kcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
+  const float vf = patch ? vcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
   const float scale = (float)(1.0 / sqrt((double)DS_HD));
-  // scores: G > 4: warp (key half w & 1, dimension half w >> 1), lane (key k = lane & 15, quad lane >> 4);
-  // G <= 4: warp = dimension quarter, lane = key
-  const bool two_quads = G > 4;
-  const int sk = two_quads ? (warp & 1) * 16 + (lane & 15) : lane;
-  const int sq = two_quads ? lane >> 4 : 0;
-  const int dsh = two_quads ? warp >> 1 : warp, dlen = two_quads ? 64 : 32;
-  const int nshares = two_quads ? 2 : 4;
+  constexpr int NSH = TWOQ ? 4 : 8, DLEN = DS_HD / NSH;
+  const int sk = TWOQ ? (warp & 1) * 16 + (lane & 15) : lane;  // key of this lane in a chunk
+  const int sq = TWOQ ? lane >> 4 : 0;                          // head quad
+  const int dsh = TWOQ ? warp >> 1 : warp;                      // dimension share
   float acc[DS_GMAX];
 #pragma unroll
   for (int g = 0; g < DS_GMAX; g++) acc[g] = 0.0f;
-  const int d = warp * 32 + lane;  // output dimension of this lane in the V phase
+  const int d = (warp & 3) * 32 + lane, par = warp >> 2;  // V phase: output dimension, key parity
 
   for (int c = 0; c < total; c++) {
     const int st = c % DS_RING;
-    const uint8_t *chunk = ring + st * DS_CHUNK;
+    uint8_t *chunk = ring + st * DS_CHUNK;
     if (tid == 0) {
       s_ok = mbar_wait(bar0 + 8 * st, (uint32_t)(c / DS_RING) & 1u, &s_abort, err, 60);
       if (!s_ok) {  // leave only once every copy into this block's shared memory is done (bounded again)
         volatile int no_abort = 0;
-        for (int cc = c; cc < issued; cc++) mbar_wait(bar0 + 8 * (cc % DS_RING), (uint32_t)(cc / DS_RING) & 1u, &no_abort, err, 61);
+        for (int cc = c; cc < issued; cc++)
+          mbar_wait(bar0 + 8 * (cc % DS_RING), (uint32_t)(cc / DS_RING) & 1u, &no_abort, err, 61);
       }
     }
     __syncthreads();
     if (!s_ok) return;
     if (c < nck) {
       const int r = fresh - c * DS_CH;
-      if (r >= 0 && r < DS_CH) {
-        *(float *)((uint8_t *)chunk + ds_koff(r, tid)) = kf;
+      if (r >= 0 && r < DS_CH) {  // block-uniform
+        if (tid < DS_HD) *(float *)(chunk + ds_koff(r, tid)) = kf;
         __syncthreads();
       }
-      if (c * DS_CH + sk < nk) {
-        float s4[4] = {0.f, 0.f, 0.f, 0.f};
-        const float *qr = Qs + 4 * sq * DS_QROW;
-#pragma unroll 4
-        for (int dd = dsh * dlen; dd < dsh * dlen + dlen; dd += 4) {
-          const float4 kv = *(const float4 *)(chunk + ds_koff(sk, dd));
-#pragma unroll
-          for (int h = 0; h < 4; h++) {
-            const float4 qv = *(const float4 *)(qr + h * DS_QROW + dd);
-            s4[h] = fmaf(qv.x, kv.x, s4[h]);
-            s4[h] = fmaf(qv.y, kv.y, s4[h]);
-            s4[h] = fmaf(qv.z, kv.z, s4[h]);
-            s4[h] = fmaf(qv.w, kv.w, s4[h]);
-          }
-        }
-        *(float4 *)(pscr + (dsh * DS_CH + sk) * DS_GMAX + 4 * sq) = make_float4(s4[0], s4[1], s4[2], s4[3]);
-      }
+      if (c * DS_CH + sk < nk)
+        *(float4 *)(pscr + (dsh * DS_CH + sk) * DS_GMAX + 4 * sq) =
+            ds_scores<DLEN>(chunk, Qs, sk, sq, dsh * DLEN);
       __syncthreads();
-      for (int e = tid; e < DS_CH * DS_GMAX; e += DS_THREADS) {  // dimension shares added in order
-        const int j = e / DS_GMAX, g = e % DS_GMAX;
+      {  // dimension shares added in order: one (key, head) per thread
+        const int j = tid / DS_GMAX, g = tid % DS_GMAX;
         if (c * DS_CH + j < nk && g < G) {
-          float s = pscr[j * DS_GMAX + g];
-          for (int sh = 1; sh < nshares; sh++) s += pscr[(sh * DS_CH + j) * DS_GMAX + g];
-          pt[(c * DS_CH + j) * DS_GMAX + g] = s * scale;
+          float sc = pscr[j * DS_GMAX + g];
+#pragma unroll
+          for (int sh = 1; sh < NSH; sh++) sc += pscr[(sh * DS_CH + j) * DS_GMAX + g];
+          pt[(c * DS_CH + j) * DS_GMAX + g] = sc * scale;
         }
       }
-      if (c == nck - 1) {  // all scores: softmax statistics per head over the split
+      if (c == nck - 1) {  // all scores: softmax statistics of head `warp` over the split
         __syncthreads();
-        for (int g = warp; g < G; g += DS_THREADS / 32) {
+        const int g = warp;
+        if (g < G) {
           float mx = -INFINITY;
           for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, pt[j * DS_GMAX + g]);
 #pragma unroll
@@ -190,13 +208,13 @@ __global__ void __launch_bounds__(DS_THREADS) decode_attention_stream_kernel(
       const int cv = c - nck, rows = min(DS_CH, nk - cv * DS_CH);
       const float *vt = (const float *)chunk;
       const int r = fresh - cv * DS_CH;
-      if (r >= 0 && r < DS_CH) {
-        ((float *)chunk)[r * DS_HD + tid] = vf;
+      if (r >= 0 && r < DS_CH) {  // block-uniform
+        if (tid < DS_HD) ((float *)chunk)[r * DS_HD + tid] = vf;
         __syncthreads();
       }
       const float *pr = pt + (size_t)cv * DS_CH * DS_GMAX;
 #pragma unroll 4
-      for (int j = 0; j < rows; j++) {
+      for (int j = par; j < rows; j += 2) {
         const float v = vt[j * DS_HD + d];
         const float4 pa = *(const float4 *)(pr + j * DS_GMAX), pb = *(const float4 *)(pr + j * DS_GMAX + 4);
         acc[0] = fmaf(pa.x, v, acc[0]);
@@ -212,11 +230,18 @@ __global__ void __launch_bounds__(DS_THREADS) decode_attention_stream_kernel(
     __syncthreads();  // chunk consumed: its stage takes the chunk DS_RING ahead
     if (tid == 0 && issued < total) issue(issued++);
   }
+  // odd-key sums (warps 4-7) onto the even-key sums (warps 0-3)
+  if (par == 1) {
+#pragma unroll
+    for (int g = 0; g < DS_GMAX; g++) pscr[g * DS_HD + d] = acc[g];
+  }
+  __syncthreads();
+  if (par == 1) return;
   const size_t slot = ((size_t)m * kvh + g0) * smax + split;
   float *po = part, *pml = part + (size_t)gridDim.z * kvh * smax * DS_GMAX * DS_HD;
 #pragma unroll
   for (int g = 0; g < DS_GMAX; g++)
-    if (g < G) po[(slot * DS_GMAX + g) * DS_HD + d] = acc[g];
+    if (g < G) po[(slot * DS_GMAX + g) * DS_HD + d] = acc[g] + pscr[g * DS_HD + d];
   if (tid < G) {
     pml[(slot * DS_GMAX + tid) * 2 + 0] = red[tid * 2];
     pml[(slot * DS_GMAX + tid) * 2 + 1] = red[tid * 2 + 1];
@@ -349,13 +374,16 @@ void launch_decode_attention_stream(const CUtensorMap &kmap, long long krow0, co
     static bool configured[64] = {};
     std::lock_guard<std::mutex> lock(mu);
     if (device < 0 || device >= 64 || !configured[device]) {
-      STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)DS_SMEM));
+      STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_kernel<true>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DS_SMEM));
+      STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_kernel<false>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DS_SMEM));
       if (device >= 0 && device < 64) configured[device] = true;
     }
   }
-  launch_kernel(decode_attention_stream_kernel, dim3(plan.smax, kvh, rows), dim3(DS_THREADS), DS_SMEM, st, pdl, kmap,
-                krow0, q, ldq, kc, vc, count, nh, kvh, capacity, posd, pos0, plan.kps, part, plan.smax, err);
+  auto kernel = nh / kvh > 4 ? decode_attention_stream_kernel<true> : decode_attention_stream_kernel<false>;
+  launch_kernel(kernel, dim3(plan.smax, kvh, rows), dim3(DS_THREADS), DS_SMEM, st, pdl, kmap, krow0, q, ldq, kc, vc,
+                count, nh, kvh, capacity, posd, pos0, plan.kps, part, plan.smax, err);
 }
 
 void launch_attention_merge_split(const float *part, const DecodeStreamPlan &plan, const int *posd, int pos0,
