@@ -240,21 +240,35 @@ __global__ void __launch_bounds__(192, 1)
       // Weights never depend on the previous kernel: the first ring's W tiles load before the wait
       // for the split activations.
       const int pre = (int)min((long long)S::STAGES, i1 - i0);
+      // (tile, K block) of the next load, advanced without dividing the 64-bit iteration index
+      int t = (int)(i0 / kbs), kb = (int)(i0 % kbs);
       for (int j = 0; j < pre; j++) {
-        const long long i = i0 + j;
         mbar_expect_tx(full0 + 8 * j, S::STAGE);
-        tma_load_2d(sa0 + j * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * j);
+        tma_load_2d(sa0 + j * S::A_BYTES, &tw, kb * BK, t * SK_BM, full0 + 8 * j);
+        if (++kb == kbs) {
+          kb = 0;
+          t++;
+        }
       }
       pdl_wait();
-      for (int j = 0; j < pre; j++)
-        tma_load_2d(sb0 + j * S::B_BYTES, &tx, (int)((i0 + j) % kbs) * BK, 0, full0 + 8 * j);
+      {
+        int kx = (int)(i0 % kbs);
+        for (int j = 0; j < pre; j++) {
+          tma_load_2d(sb0 + j * S::B_BYTES, &tx, kx * BK, 0, full0 + 8 * j);
+          if (++kx == kbs) kx = 0;
+        }
+      }
       int stage = pre % S::STAGES;
       uint32_t phase = pre == S::STAGES ? 1u : 0u;
       for (long long i = i0 + pre; i < i1; i++) {
         if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, abort_flag, err, 31)) break;
         mbar_expect_tx(full0 + 8 * stage, S::STAGE);
-        tma_load_2d(sa0 + stage * S::A_BYTES, &tw, (int)(i % kbs) * BK, (int)(i / kbs) * SK_BM, full0 + 8 * stage);
-        tma_load_2d(sb0 + stage * S::B_BYTES, &tx, (int)(i % kbs) * BK, 0, full0 + 8 * stage);
+        tma_load_2d(sa0 + stage * S::A_BYTES, &tw, kb * BK, t * SK_BM, full0 + 8 * stage);
+        tma_load_2d(sb0 + stage * S::B_BYTES, &tx, kb * BK, 0, full0 + 8 * stage);
+        if (++kb == kbs) {
+          kb = 0;
+          t++;
+        }
         if (++stage == S::STAGES) {
           stage = 0;
           phase ^= 1;
@@ -268,7 +282,7 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool issued = false;
-      int grp = 0, cnt = 0;
+      int grp = 0, cnt = 0, kb = (int)(i0 % kbs);
       for (long long i = i0; i < i1; i++) {
         const int r = grp % S::ACC;
         if (cnt == 0 && !mbar_wait(acce0 + 8 * r, ((uint32_t)(grp / S::ACC) & 1u) ^ 1u, abort_flag, err, 35)) break;
@@ -282,7 +296,8 @@ __global__ void __launch_bounds__(192, 1)
           mma_f16(d, a + (uint64_t)(2 * k), b + (uint64_t)(2 * k), idesc, cnt != 0 || k != 0);
         issued = true;
         mma_commit(empty0 + 8 * stage);
-        if (++cnt == S::GK || (i + 1) % kbs == 0 || i + 1 == i1) {
+        if (++kb == kbs) kb = 0;  // kb == 0: the next iteration starts a tile
+        if (++cnt == S::GK || kb == 0 || i + 1 == i1) {
           mma_commit(accf0 + 8 * r);
           grp++;
           cnt = 0;
@@ -304,9 +319,11 @@ __global__ void __launch_bounds__(192, 1)
     float acc[NT];
 #pragma unroll
     for (int m = 0; m < NT; m++) acc[m] = 0.0f;
-    int grp = 0, cnt = 0;
+    int grp = 0, cnt = 0, kb = (int)(i0 % kbs), t = (int)(i0 / kbs);
     for (long long i = i0; i < i1; i++) {
-      if (!(++cnt == S::GK || (i + 1) % kbs == 0 || i + 1 == i1)) continue;  // inside an accumulator group
+      const bool tile_end = ++kb == kbs;
+      if (tile_end) kb = 0;
+      if (!(++cnt == S::GK || tile_end || i + 1 == i1)) continue;  // inside an accumulator group
       cnt = 0;
       const int r = grp % S::ACC;
       int got = 0;
@@ -327,8 +344,7 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(acce0 + 8 * r);
       grp++;
-      if (i + 1 == i1 || (i + 1) % kbs == 0) {  // end of this CTA's piece of tile t
-        const int t = (int)(i / kbs);
+      if (i + 1 == i1 || tile_end) {  // end of this CTA's piece of tile t
         const int piece = cta - sk_cta_of((long long)t * kbs, T, G);
         const int row = t * SK_BM + q * 32 + lane;
         if (row < N) {
@@ -339,6 +355,7 @@ __global__ void __launch_bounds__(192, 1)
         }
 #pragma unroll
         for (int m = 0; m < NT; m++) acc[m] = 0.0f;
+        t++;
       }
     }
   }
