@@ -304,20 +304,7 @@ __global__ void __launch_bounds__(256) attention_merge_split_kernel(
   }
   uint16_t h[3][4];
 #pragma unroll
-  for (int e = 0; e < 4; e++) {
-    const float f = o[e];
-    uint16_t h0 = f32_to_bf16_rne(f), h1 = 0, h2 = 0;
-    if (isfinite(f)) {  // the skinny prologue's split (non-finite values keep their class in x0)
-      if ((h0 & 0x7f80u) == 0x7f80u) h0 = (uint16_t)(__float_as_uint(f) >> 16);
-      const float r1 = f - __uint_as_float((uint32_t)h0 << 16);
-      h1 = f32_to_bf16_rne(r1);
-      const float r2 = r1 - __uint_as_float((uint32_t)h1 << 16);
-      h2 = f32_to_bf16_rne(r2);
-    }
-    h[0][e] = h0;
-    h[1][e] = h1;
-    h[2][e] = h2;
-  }
+  for (int e = 0; e < 4; e++) split3_bf16(o[e], h[0][e], h[1][e], h[2][e]);  // the skinny prologue's split
 #pragma unroll
   for (int tm = 0; tm < 3; tm++) {
     uint2 u;

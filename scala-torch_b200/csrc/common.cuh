@@ -189,4 +189,22 @@ __device__ __forceinline__ uint16_t f32_to_bf16_rne(float value) {
   return (uint16_t)((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);
 }
 
+// f = x0 + x1 + x2 in three BF16 terms: x0 = rne(f), x1 = rne(f - x0), x2 = rne(f - x0 - x1) (both
+// differences exact), which carry f's 24-bit significand.  A non-finite f keeps its class in x0 alone
+// (Inf - Inf would make the lower terms NaN); a finite f that rounds past BF16's largest finite value
+// (|f| > 0x1.fep127) takes the truncated first term instead, which stays finite and leaves an exact
+// 16-bit remainder.
+__device__ __forceinline__ void split3_bf16(float f, uint16_t &x0, uint16_t &x1, uint16_t &x2) {
+  x0 = f32_to_bf16_rne(f);
+  x1 = 0;
+  x2 = 0;
+  if (isfinite(f)) {
+    if ((x0 & 0x7f80u) == 0x7f80u) x0 = (uint16_t)(__float_as_uint(f) >> 16);
+    const float r1 = f - __uint_as_float((uint32_t)x0 << 16);  // exact
+    x1 = f32_to_bf16_rne(r1);
+    const float r2 = r1 - __uint_as_float((uint32_t)x1 << 16);  // exact
+    x2 = f32_to_bf16_rne(r2);
+  }
+}
+
 }  // namespace stb

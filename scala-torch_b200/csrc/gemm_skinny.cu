@@ -94,11 +94,13 @@ __device__ __forceinline__ void tmem_ld3(uint32_t a2, uint32_t a1, uint32_t a0, 
 // First iteration of CTA c when T iterations are cut into G ranges.
 __host__ __device__ __forceinline__ long long sk_start(int c, long long T, int G) { return (long long)c * T / G; }
 
-// The CTA whose range holds iteration i.
+// The CTA whose range holds iteration i: the largest c with floor(c T / G) <= i, which is
+// floor(((i + 1) G - 1) / T) (c T / G < i + 1  <=>  c T <= (i + 1) G - 1); in 32-bit arithmetic when
+// T G fits (a 64-bit division is a long instruction sequence on the fixups' critical path).
 __device__ __forceinline__ int sk_cta_of(long long i, long long T, int G) {
-  int c = (int)(i * G / T);
-  while (c + 1 < G && sk_start(c + 1, T, G) <= i) c++;
-  return c;
+  if ((unsigned long long)T * (unsigned)G <= 0xFFFFFFFFull)
+    return (int)(((unsigned)(i + 1) * (unsigned)G - 1u) / (unsigned)T);
+  return (int)(((unsigned long long)(i + 1) * (unsigned)G - 1ull) / (unsigned long long)T);
 }
 
 // x [M][K] (row stride ldx), optionally RMS-normalised as the vector GEMV does it, -> x3 [3][NT][K].
@@ -160,20 +162,7 @@ __global__ void __launch_bounds__(256) skinny_prep_kernel(const float *x, int ld
   for (int e = 0; e < 4; e++) {
     float f = v[e];
     if (m < M && norm_w) f = __double2float_rn(__dmul_rn(__dmul_rn((double)f, inv), (double)nw[e]));
-    // Non-finite f keeps its class in the first term alone (Inf - Inf would make the lower terms
-    // NaN); a finite f that rounds past BF16's largest finite value (|f| > 0x1.fep127) takes the
-    // truncated first term instead, which stays finite and leaves an exact 16-bit remainder.
-    uint16_t h0 = f32_to_bf16_rne(f), h1 = 0, h2 = 0;
-    if (isfinite(f)) {
-      if ((h0 & 0x7f80u) == 0x7f80u) h0 = (uint16_t)(__float_as_uint(f) >> 16);
-      const float r1 = f - __uint_as_float((uint32_t)h0 << 16);  // exact
-      h1 = f32_to_bf16_rne(r1);
-      const float r2 = r1 - __uint_as_float((uint32_t)h1 << 16);  // exact
-      h2 = f32_to_bf16_rne(r2);
-    }
-    h[0][e] = h0;
-    h[1][e] = h1;
-    h[2][e] = h2;
+    split3_bf16(f, h[0][e], h[1][e], h[2][e]);
   }
   if (k0 + 4 <= K && (K & 3) == 0) {  // rows of x3 are 8-byte aligned: one 8-byte store per term
 #pragma unroll
@@ -449,6 +438,137 @@ __global__ void __launch_bounds__(256) skinny_fixup_kernel(const GemvParams p, c
   }
 }
 
+// The next projection's prologue fused into this projection's fixup (decode chunks of one 64-row block):
+// both kernels write the next projection's activation terms x3n [3][NT][Kn] (rows M .. NT - 1 zero),
+// so the next GEMM starts on them without a prologue launch of its own.
+
+// SiLU(gate) * up of the interleaved gate/up projection (EPI_SILU's expression), split into three BF16
+// terms for the down projection (Kn = N / 2).  One thread per (token row, unit); blockIdx.y < NT.
+__global__ void __launch_bounds__(256) skinny_fixup_silu_split_kernel(const float *part, int N, int kbs, long long T,
+                                                                      int G, int pmax, int mb, uint16_t *x3n,
+                                                                      int NT) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.y, units = N / 2;
+  const int u = blockIdx.x * 256 + threadIdx.x;
+  if (u >= units) return;
+  float v = 0.0f;
+  if (m < mb) {
+    const float gate = sk_gather(part, m, 2 * u, mb, kbs, T, G, pmax);
+    const float up = sk_gather(part, m, 2 * u + 1, mb, kbs, T, G, pmax);
+    v = silu_ref(gate) * up;
+  }
+  uint16_t h0, h1, h2;
+  split3_bf16(v, h0, h1, h2);
+  x3n[((size_t)0 * NT + m) * units + u] = h0;
+  x3n[((size_t)1 * NT + m) * units + u] = h1;
+  x3n[((size_t)2 * NT + m) * units + u] = h2;
+}
+
+constexpr int SK_NORM_THREADS = 512, SK_NORM_V4 = 4;  // rows of up to 512 x 4 x 4 = 8192 values
+
+// The residual projection's fixup (EPI_RESID: y = residual + sum of the pieces in piece order) and the
+// next projection's RMSNorm prologue on the updated row, one block per token row: the row stays in
+// registers between the residual add, the sum of squares (double, each thread's values in index
+// order, then the block's fixed-order reduction) and the scaling with the GEMV's expression; the
+// normalised row is split into three BF16 terms (Kn = N).  Blocks m >= mb write zero rows.
+__global__ void __launch_bounds__(SK_NORM_THREADS) skinny_fixup_norm_kernel(
+    const GemvParams p, const float *part, int kbs, long long T, int G, int pmax, int mb, const float *norm_w,
+    double eps, uint16_t *x3n, int NT) {
+  __shared__ double s_scratch[SK_NORM_THREADS / 32];
+  pdl_wait();
+  const int m = blockIdx.x, mg = m;  // one 64-row block: its rows are the problem's own
+  const int N = p.N, n4 = N / 4;
+  const size_t stride = (size_t)mb * SK_BM;
+  float4 v[SK_NORM_V4], nw[SK_NORM_V4];
+#pragma unroll
+  for (int j = 0; j < SK_NORM_V4; j++) v[j] = nw[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  double sq = 0.0;
+  if (m < mb) {
+    // every load of the thread in flight together: per four-row group (a group never straddles a
+    // 128-row tile) the residual (into v) and the first four pieces; the pieces are added in piece
+    // order, then the residual
+    const float *pp[SK_NORM_V4];
+    int np[SK_NORM_V4];
+    float4 w[SK_NORM_V4][4];
+#pragma unroll
+    for (int j = 0; j < SK_NORM_V4; j++) {
+      const int c = threadIdx.x + j * SK_NORM_THREADS;
+      np[j] = 0;
+      if (c < n4) {
+        const int row = 4 * c, t = row / SK_BM;
+        np[j] = sk_cta_of((long long)(t + 1) * kbs - 1, T, G) - sk_cta_of((long long)t * kbs, T, G) + 1;
+        pp[j] = part + ((size_t)t * pmax * mb + m) * SK_BM + (row % SK_BM);
+        v[j] = *(const float4 *)(p.residual + (size_t)mg * p.ldr + row);
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+          if (q < np[j]) w[j][q] = __ldcg((const float4 *)(pp[j] + (size_t)q * stride));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < SK_NORM_V4; j++) {
+      const int c = threadIdx.x + j * SK_NORM_THREADS;
+      if (c >= n4) break;
+      float4 acc = w[j][0];
+#pragma unroll
+      for (int q = 1; q < 4; q++) {
+        if (q < np[j]) {
+          acc.x = acc.x + w[j][q].x;
+          acc.y = acc.y + w[j][q].y;
+          acc.z = acc.z + w[j][q].z;
+          acc.w = acc.w + w[j][q].w;
+        }
+      }
+      for (int q = 4; q < np[j]; q++) {  // more than four pieces: one more round trip each
+        const float4 x = __ldcg((const float4 *)(pp[j] + (size_t)q * stride));
+        acc.x = acc.x + x.x;
+        acc.y = acc.y + x.y;
+        acc.z = acc.z + x.z;
+        acc.w = acc.w + x.w;
+      }
+      v[j] = make_float4(v[j].x + acc.x, v[j].y + acc.y, v[j].z + acc.z, v[j].w + acc.w);
+      *(float4 *)(p.y + (size_t)mg * p.ldy + 4 * c) = v[j];
+      const double a = v[j].x, b = v[j].y, cc = v[j].z, d = v[j].w;
+      sq = __dadd_rn(sq, __dmul_rn(a, a));
+      sq = __dadd_rn(sq, __dmul_rn(b, b));
+      sq = __dadd_rn(sq, __dmul_rn(cc, cc));
+      sq = __dadd_rn(sq, __dmul_rn(d, d));
+    }
+  }
+  // The next GEMM's CTAs start streaming weights once every block triggers: after this block's
+  // loads of the pieces (triggering at entry measured slower: the weight stream delays these loads).
+  pdl_trigger();
+  if (m < mb) {  // the norm weights, in flight during the block's reduction
+#pragma unroll
+    for (int j = 0; j < SK_NORM_V4; j++) {
+      const int c = threadIdx.x + j * SK_NORM_THREADS;
+      if (c < n4) nw[j] = *(const float4 *)(norm_w + 4 * c);
+    }
+  }
+  const double total = block_sum_double(sq, s_scratch);  // uniform: every thread reaches it
+  const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(total, (double)N), eps)));
+#pragma unroll
+  for (int j = 0; j < SK_NORM_V4; j++) {
+    const int c = threadIdx.x + j * SK_NORM_THREADS;
+    if (c >= n4) break;
+    const float f[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    uint16_t h[3][4];
+    const float nws[4] = {nw[j].x, nw[j].y, nw[j].z, nw[j].w};
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float g = m < mb ? __double2float_rn(__dmul_rn(__dmul_rn((double)f[e], inv), (double)nws[e])) : 0.0f;
+      split3_bf16(g, h[0][e], h[1][e], h[2][e]);
+    }
+#pragma unroll
+    for (int tm = 0; tm < 3; tm++) {
+      uint2 u;
+      u.x = (uint32_t)h[tm][0] | ((uint32_t)h[tm][1] << 16);
+      u.y = (uint32_t)h[tm][2] | ((uint32_t)h[tm][3] << 16);
+      *(uint2 *)(x3n + ((size_t)tm * NT + m) * N + 4 * c) = u;
+    }
+  }
+}
+
 uint32_t skinny_idesc(int nt) {
   // D = F32, A = B = BF16, both K-major, N = 3 NT (>> 3 at bits 17-22), M = 128 (>> 4 at bits 24-28)
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)((3 * nt) >> 3) << 17) | ((uint32_t)(SK_BM >> 4) << 24);
@@ -521,14 +641,23 @@ uint64_t skinny_scratch_bytes(int M, int N, int K, int device) {
 
 int skinny_nt(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
+bool skinny_norm_fusable(int N) { return N % 4 == 0 && N <= SK_NORM_THREADS * SK_NORM_V4 * 4; }
+
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
-                  cudaStream_t stream, bool x3_ready) {
+                  cudaStream_t stream, const uint16_t *x3_ready, const SkinnyNext *next) {
   STB_REQUIRE(p.M >= 1 && p.K % 8 == 0 && p.K >= BK && p.N >= SK_BM, "skinny Linear shape");
-  STB_REQUIRE(!x3_ready || (p.M <= 64 && p.norm_w == nullptr), "prepared skinny activations: one block, no norm");
+  STB_REQUIRE(!x3_ready || (p.M <= 64 && p.norm_w == nullptr && ((uintptr_t)x3_ready % 16) == 0),
+              "prepared skinny activations: one block, no norm");
   STB_REQUIRE(p.stop == nullptr, "skinny Linear takes no stop flag");
   STB_REQUIRE(scratch && ((uintptr_t)scratch % 256) == 0 && scratch_bytes >= skinny_scratch_bytes(p.M, p.N, p.K, device),
               "skinny Linear scratch too small");
+  if (next) {
+    STB_REQUIRE(p.M <= 64 && next->x3 && ((uintptr_t)next->x3 % 16) == 0, "fused next prologue: one block");
+    STB_REQUIRE(EPI == EPI_SILU || (EPI == EPI_RESID && next->norm_w && p.N % 4 == 0 &&
+                                    p.N <= SK_NORM_THREADS * SK_NORM_V4 * 4 && p.ldy % 4 == 0 && p.ldr % 4 == 0),
+                "fused next prologue: SiLU split, or residual + RMSNorm on rows of at most 8192 values");
+  }
   const CUtensorMap tw = make_map(p.w, STB_BF16, (uint64_t)p.N, (uint64_t)p.K, SK_BM);
   constexpr bool paired = EPI == EPI_SILU || EPI == EPI_QKV;
   const int units = paired ? p.N / 2 : p.N;
@@ -538,28 +667,41 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
   for (int m0 = 0; m0 < p.M; m0 += 64) {
     const int mb = std::min(64, p.M - m0);
     const SkinnyPlan q = skinny_plan(mb, p.N, p.K, device);
-    uint16_t *x3 = (uint16_t *)scratch;
+    const uint16_t *x3 = x3_ready ? x3_ready : (const uint16_t *)scratch;
     float *part = (float *)((char *)scratch + q.x3_bytes);
     if (!x3_ready)
       launch_kernel(skinny_prep_kernel, dim3((p.K + 1023) / 1024, q.nt), dim3(256), 0, stream, m0 > 0 || p.pdl,
-                    p.x + (size_t)m0 * p.ldx, p.ldx, p.norm_w, p.norm_eps, x3, mb, q.nt, p.K);
+                    p.x + (size_t)m0 * p.ldx, p.ldx, p.norm_w, p.norm_eps, (uint16_t *)scratch, mb, q.nt, p.K);
     const CUtensorMap tx = make_map(x3, STB_BF16, (uint64_t)3 * q.nt, (uint64_t)p.K, 3 * q.nt);
     if (q.nt == 16) launch_gemm<16>(q, tw, tx, part, mb, p.N, err, device, stream);
     else if (q.nt == 32) launch_gemm<32>(q, tw, tx, part, mb, p.N, err, device, stream);
     else launch_gemm<64>(q, tw, tx, part, mb, p.N, err, device, stream);
-    launch_kernel(skinny_fixup_kernel<EPI>, dim3((units + 255) / 256, mb), dim3(256), 0, stream, true, p,
-                  (const float *)part, q.kbs, q.iters, q.grid, q.pmax, m0, mb);
+    if (next && EPI == EPI_SILU)
+      launch_kernel(skinny_fixup_silu_split_kernel, dim3((units + 255) / 256, q.nt), dim3(256), 0, stream, true,
+                    (const float *)part, p.N, q.kbs, q.iters, q.grid, q.pmax, mb, next->x3, q.nt);
+    else if (next)
+      launch_kernel(skinny_fixup_norm_kernel, dim3(q.nt), dim3(SK_NORM_THREADS), 0, stream, true, p,
+                    (const float *)part, q.kbs, q.iters, q.grid, q.pmax, mb, next->norm_w, next->eps, next->x3, q.nt);
+    else
+      launch_kernel(skinny_fixup_kernel<EPI>, dim3((units + 255) / 256, mb), dim3(256), 0, stream, true, p,
+                    (const float *)part, q.kbs, q.iters, q.grid, q.pmax, m0, mb);
     launches += x3_ready ? 2 : 3;
   }
   check_launch("skinny");
   return launches;
 }
 
-template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_RESID>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_SILU>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_QKV>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_LOGITS>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
-template int skinny_launch<EPI_PEER>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, bool);
+template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
+                                           const SkinnyNext *);
+template int skinny_launch<EPI_RESID>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
+                                           const SkinnyNext *);
+template int skinny_launch<EPI_SILU>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
+                                           const SkinnyNext *);
+template int skinny_launch<EPI_QKV>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
+                                           const SkinnyNext *);
+template int skinny_launch<EPI_LOGITS>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
+                                           const SkinnyNext *);
+template int skinny_launch<EPI_PEER>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
+                                           const SkinnyNext *);
 
 }  // namespace stb

@@ -442,15 +442,27 @@ bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w);
 uint64_t skinny_scratch_bytes(int M, int N, int K, int device);
 // Sets the kernels' shared-memory limits on `device` (before a graph capture that launches them).
 void skinny_prepare(int device);
+// The next projection's prologue done by this projection's fixup (one 64-row block): its activation
+// terms go to x3 [3][skinny_nt(M)][Kn] -- EPI_SILU: SiLU(gate) * up split for the down projection
+// (Kn = N / 2, norm_w unused); EPI_RESID: the residual add, then RMSNorm with norm_w / eps and the split
+// (Kn = N, skinny_norm_fusable(N)).  The buffer must not overlap the scratch.
+struct SkinnyNext {
+  uint16_t *x3 = nullptr;
+  const float *norm_w = nullptr;
+  double eps = 1e-6;
+};
 // Enqueues prologue -> stream-K GEMM -> fixup/epilogue per 64-row block (3 kernels each, all
 // programmatic dependents except the first when !p.pdl).  With x3_ready (M <= 64, no RMSNorm) the
-// previous kernel has already written the activation terms x3 [3][skinny_nt(M)][K] at the start of
-// the scratch, with zero rows M .. NT - 1, and the prologue is skipped.  Returns the number of
+// previous kernel has already written the activation terms x3 [3][skinny_nt(M)][K] there (16-byte
+// aligned; at the start of the scratch, or a SkinnyNext buffer) and the prologue is skipped.  With
+// next, the fixup also writes the next projection's terms (SkinnyNext).  Returns the number of
 // kernels launched.
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
-                  cudaStream_t stream, bool x3_ready = false);
+                  cudaStream_t stream, const uint16_t *x3_ready = nullptr, const SkinnyNext *next = nullptr);
 // Token rows of the activation-term tile for a block of M <= 64 rows: 16, 32 or 64.
 int skinny_nt(int M);
+// Whether a residual projection of N outputs can do the next projection's RMSNorm prologue (SkinnyNext).
+bool skinny_norm_fusable(int N);
 
 }  // namespace stb

@@ -14,6 +14,13 @@
 // output and advances the device-side position.  A decode step therefore needs no host
 // interaction and is captured once as a CUDA graph and replayed per generated token.
 //
+// Batched decode rows (2 .. 64 per chunk) take the tensor-core skinny form of each projection
+// (gemm_skinny.cu: prologue, stream-K GEMM, fixup).  On one GPU the prologues are folded into the
+// previous kernel: the attention merge writes the o projection's activation terms, the o fixup adds
+// the residual and does the post-attention RMSNorm and split for gate/up, the gate/up fixup writes
+// SiLU(gate)*up as the down projection's terms, and the down fixup adds the residual and does the
+// next layer's input RMSNorm and split -- 9 launches per layer instead of 13.
+//
 // Tensor parallel (tp_size > 1): q/k/v/gate/up are split by output rows (heads / intermediate),
 // o/down by input columns; each row-split projection's partial sums are joined by one NCCL
 // allreduce which also carries the residual (rank 0 adds it before the reduction).  lm_head is
@@ -92,6 +99,7 @@ struct stb_llama_cache {
   // paired q/k/v projection, interleaved gate/up projection
   uint64_t xn = 0, xh = 0, qkvbuf = 0, gubuf = 0;
   uint64_t skin = 0, skin_bytes = 0;  // tensor-core skinny path scratch (one 64-row block)
+  uint64_t skin_next = 0;             // next projection's activation terms written by a fused fixup (TP1)
   uint64_t att_part = 0, att_count = 0;  // split decode attention records and counters (batch rows)
   CUtensorMap kv_map;                    // the whole K/V cache as rows of hd Float32 (streamed attention)
   bool kv_map_ok = false;
@@ -1562,7 +1570,7 @@ void ensure_rows(stb_llama_cache *c, int rows) {
                                 sizeof(float));
   c->att_count = alloc_owned(s, c->owned, (uint64_t)c->batch * m->KV * sizeof(int));
   STB_CUDA(cudaMemsetAsync((void *)c->att_count, 0, (size_t)c->batch * m->KV * sizeof(int), s->stream));
-  c->skin = c->skin_bytes = 0;
+  c->skin = c->skin_bytes = c->skin_next = 0;
   {  // the largest scratch any projection of a chunk of up to min(rows, 64) rows takes
     const int sm = std::min(rows, 64);
     const int wdt = m->c.weight_dtype;
@@ -1577,6 +1585,8 @@ void ensure_rows(stb_llama_cache *c, int rows) {
       c->skin = alloc_owned(s, c->owned, need);
       c->skin_bytes = need;
       skinny_prepare(s->device);
+      if (m->tp == 1)  // terms [3][NT][K] of the widest K a fused fixup writes (hidden or intermediate)
+        c->skin_next = alloc_owned(s, c->owned, (uint64_t)3 * skinny_nt(sm) * std::max(m->H, m->I) * 2);
     }
   }
   session_error_word(s);  // allocated now, not inside a graph capture
@@ -1685,15 +1695,17 @@ bool projects_skinny(const stb_llama_cache *c, int M, int N, int K, int wdt, con
   return c->skin && skinny_eligible(M, N, K, wdt, w) && skinny_scratch_bytes(M, N, K, c->m->s->device) <= c->skin_bytes;
 }
 
-// With x3_ready the skinny form's activation terms are already in the scratch (written by the
-// previous kernel): M <= 64, and the projection must take the skinny form.
+// With x3_ready the skinny form's activation terms are already there (written by the previous
+// kernel), and with next this projection's fixup writes the next one's: M <= 64, and the projection
+// must take the skinny form.
 template <int EPI>
 int project(stb_llama_cache *c, const GemvParams &p, int wdt, GemvConfig cfg, cudaStream_t st,
-            bool x3_ready = false) {
+            const uint16_t *x3_ready = nullptr, const SkinnyNext *next = nullptr) {
   stb_session *s = c->m->s;
   if (projects_skinny(c, p.M, p.N, p.K, wdt, p.w))
-    return skinny_launch<EPI>(p, (void *)c->skin, c->skin_bytes, session_error_word(s), s->device, st, x3_ready);
-  STB_REQUIRE(!x3_ready, "prepared activation terms need the skinny projection");
+    return skinny_launch<EPI>(p, (void *)c->skin, c->skin_bytes, session_error_word(s), s->device, st, x3_ready,
+                              next);
+  STB_REQUIRE(!x3_ready && !next, "prepared activation terms need the skinny projection");
   launch_gemv<EPI>(p, wdt, cfg, st);
   return 1;
 }
@@ -1723,6 +1735,16 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
   const size_t kv_half = kv_layer / 2;
   const int qw = m->NH * m->hd;
   const bool tensor_cores = rows >= m->tc_rows && c->xh != 0;
+  // Single-GPU chunks of up to 64 rows on the skinny form: the o, gate/up and down fixups also write
+  // the next projection's activation terms (RMSNorm and split, SiLU*up and split), whose prologue
+  // launch is then skipped.  `pending` holds those terms for the next projection.
+  static const int fuse_enabled = env_int("STB_FUSE_NEXT", 1);
+  const bool fuse_next = fuse_enabled && m->tp == 1 && c->skin_next && rows <= 64 && !tensor_cores;
+  const bool fuse_norm = fuse_next && skinny_norm_fusable(H);
+  const uint16_t *pending = nullptr;
+  SkinnyNext next;
+  next.x3 = (uint16_t *)c->skin_next;
+  next.eps = m->c.rms_norm_eps;
   for (size_t l = 0; l < m->layers.size(); l++) {
     const Layer &L = m->layers[l];
     float *kc = (float *)c->kv + l * kv_layer;
@@ -1736,12 +1758,13 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.x = (const float *)c->hidden; p.ldx = H; p.w = (const void *)L.qkv;
       p.M = rows; p.N = (m->NH + 2 * m->KV) * m->hd; p.K = H;
       p.y = (float *)c->qbuf; p.ldy = qw;
-      p.norm_w = (const float *)L.in_norm; p.norm_eps = m->c.rms_norm_eps;
+      p.norm_w = pending ? nullptr : (const float *)L.in_norm; p.norm_eps = m->c.rms_norm_eps;
       p.rope = (const double2 *)m->rope; p.pos_dev = posd; p.pos0 = c->used; p.count = a.count;
       p.nh = m->NH; p.kvh = m->KV; p.hd = m->hd; p.capacity = c->capacity; p.k_cache = kc; p.v_cache = vc;
       p.stop = stop;
       p.pdl = true;
-      launches += project<EPI_QKV>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st);
+      launches += project<EPI_QKV>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st, pending);
+      pending = nullptr;
     }
     // the streamed single-token attention leaves split records; the o projection's prologue merges them
     const bool stream_att = a.count == 1 && rows <= c->att_rows && c->kv_map_ok;
@@ -1779,16 +1802,26 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       }
       launches++;
     }
+    const bool o_sk = projects_skinny(c, rows, H, qw, wdt, (const void *)L.o);
+    const bool gu_sk = projects_skinny(c, rows, 2 * m->I, H, wdt, (const void *)L.gu);
+    const bool down_sk = projects_skinny(c, rows, H, m->I, wdt, (const void *)L.down);
+    const bool qkv_next_sk = l + 1 < m->layers.size() &&
+                             projects_skinny(c, rows, (m->NH + 2 * m->KV) * m->hd, H, wdt,
+                                             (const void *)m->layers[l + 1].qkv);
     for (int half = 0; half < 2; half++) {  // 3. O (+residual)   then   4./5. MLP (+residual)
       if (half == 1) {
         GemvParams p;
         p.x = (const float *)c->hidden; p.ldx = H; p.w = (const void *)L.gu;
         p.M = rows; p.N = 2 * m->I; p.K = H;
         p.y = (float *)c->act; p.ldy = m->I;
-        p.norm_w = (const float *)L.post_norm; p.norm_eps = m->c.rms_norm_eps;
+        p.norm_w = pending ? nullptr : (const float *)L.post_norm; p.norm_eps = m->c.rms_norm_eps;
         p.stop = stop;
         p.pdl = true;
-        launches += project<EPI_SILU>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st);
+        const bool fuse = fuse_next && gu_sk && down_sk;
+        next.norm_w = nullptr;
+        launches += project<EPI_SILU>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st, pending,
+                                      fuse ? &next : nullptr);
+        pending = fuse ? next.x3 : nullptr;
       }
       GemvParams p;
       p.x = (const float *)(half == 0 ? c->att : c->act);
@@ -1799,23 +1832,31 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.pdl = true;
       if (m->tp == 1) {
         p.y = (float *)c->hidden; p.ldy = H; p.residual = (const float *)c->hidden; p.ldr = H;
-        launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, half == 0 && o_x3);
+        const uint16_t *x3 = half == 0 ? (o_x3 ? (const uint16_t *)c->skin : nullptr) : pending;
+        // o: the gate/up projection's RMSNorm prologue; down: the next layer's QKV RMSNorm prologue
+        const bool fuse = fuse_norm && (half == 0 ? o_sk && gu_sk : down_sk && qkv_next_sk);
+        next.norm_w = half == 0 ? (const float *)L.post_norm
+                                : (l + 1 < m->layers.size() ? (const float *)m->layers[l + 1].in_norm : nullptr);
+        launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, x3, fuse ? &next : nullptr);
+        pending = fuse ? next.x3 : nullptr;
       } else if (peer_usable(s, (uint64_t)rows * H)) {
         // fused row-split projection: partial sums stored into every rank's slots over NVLink,
         // then summed in rank order with the residual on each rank
         p.ldy = H;
         p.peer = peer_args(s, half);
         const GemvConfig cfg = choose_gemv(rows, p.N, p.K, false);
-        launches += project<EPI_PEER>(c, p, wdt, cfg, st, half == 0 && o_x3);
+        launches += project<EPI_PEER>(c, p, wdt, cfg, st, half == 0 && o_x3 ? (const uint16_t *)c->skin : nullptr);
         peer_reduce_launch(s, half, (long)rows * H, (const float *)c->hidden, (float *)c->hidden);
         launches++;
       } else {
         p.y = (float *)c->sum; p.ldy = H;
         if (m->rank == 0) {
           p.residual = (const float *)c->hidden; p.ldr = H;
-          launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, half == 0 && o_x3);
+          launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st,
+                                         half == 0 && o_x3 ? (const uint16_t *)c->skin : nullptr);
         } else {
-          launches += project<EPI_PLAIN>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, half == 0 && o_x3);
+          launches += project<EPI_PLAIN>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st,
+                                         half == 0 && o_x3 ? (const uint16_t *)c->skin : nullptr);
         }
         allreduce_sum_f32(s, (void *)c->sum, (uint64_t)rows * H);
         std::swap(c->hidden, c->sum);

@@ -36,9 +36,11 @@ def named_bf16_weights(config: LlamaConfig, seed: int):
     return out
 
 
-def oracle_model(config: LlamaConfig, seed: int, threads: int = 0) -> oracle.OracleLlama:
-    """The reference CPU path's view of the same model: weights widened to Float32 (SafeTensors.readFloat)."""
+def oracle_model(config: LlamaConfig, seed: int, threads: int = 0, replace: dict | None = None) -> oracle.OracleLlama:
+    """The reference CPU path's view of the same model: weights widened to Float32 (SafeTensors.readFloat).
+    replace: name -> BF16 bits of tensors uploaded over the generated ones (BackendLlama.set_weight)."""
     named = named_bf16_weights(config, seed)
+    named.update(replace or {})
     wide = {k: oracle.widen(v, oracle.BF16) for k, v in named.items()}
     embed = wide["model.embed_tokens.weight"]
     head = embed if config.tie_word_embeddings else wide["lm_head.weight"]

@@ -330,3 +330,59 @@ def test_decode_attention_splits_head128(stream, impl, kps, hd128, heads, kvh):
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
 
+
+
+@pytest.mark.parametrize("batch,fuse", [(3, 1), (3, 0), (20, 1), (40, 1), (40, 0)])
+def test_skinny_decode_with_fused_prologues(batch, fuse):
+    """Decode steps whose every projection takes the tensor-core skinny form (STB_SKINNY_MIN_WORK=0, batch
+    rows 3 / 20 / 40: 16-, 32- and 64-row term tiles), with the next projection's prologue done by the
+    fixups (STB_FUSE_NEXT=1: o -> RMSNorm + split for gate/up, SiLU*up -> split for down, down -> RMSNorm
+    + split for the next layer's q/k/v) or by their own prologue kernels (0).  RMSNorm weights are
+    random, not ones, so each fused norm must use its own layer's weights.  The prompt pass stays on the
+    Float32 path (tensor-core prefill off).  Child processes (variables read
+    once per process): greedy ids identical to the oracle and the logits of a cached step within
+    1e-5 (1 + |e|)."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys, numpy as np\n"
+        f"sys.path[:0] = [{root!r}, {os.path.join(root, 'scala-torch_b200')!r}, {os.path.join(root, 'tests')!r}]\n"
+        "import oracle\n"
+        "from llama_fixtures import oracle_model\n"
+        "from test_llama_gpu import HD128, close\n"
+        "from scalatorch import ffm\n"
+        "from scalatorch.models import BackendLlama, LlamaConfig\n"
+        "cfg = LlamaConfig(**dict(HD128, hidden_size=1024, num_attention_heads=8, num_key_value_heads=2, "
+        "intermediate_size=384, max_positions=64))\n"
+        "rng = np.random.default_rng(5)\n"
+        "norms = {'model.norm.weight': oracle.round_bf16((1 + 0.25 * rng.standard_normal(1024)).astype(np.float32))}\n"
+        "for l in range(cfg.num_layers):\n"
+        "    for n in ('input_layernorm', 'post_attention_layernorm'):\n"
+        "        norms[f'model.layers.{l}.{n}.weight'] = oracle.round_bf16("
+        "(1 + 0.25 * rng.standard_normal(1024)).astype(np.float32))\n"
+        "ref = oracle_model(cfg, seed=9, replace=norms)\n"
+        f"prompts = rng.integers(0, cfg.vocab_size, ({batch}, 20))\n"
+        "s = ffm.B200Session(0, 8 << 30)\n"
+        "with BackendLlama.prepare_random(s, cfg, seed=9, tc_prefill_rows=-1) as m:\n"
+        "    for name, bits in norms.items():\n"
+        "        m.set_weight(name, bits, ffm.STB_BF16)\n"
+        "    got = m.generate_ids(prompts, 6)\n"
+        f"    for b in range({batch}):\n"
+        "        assert got[b] == ref.generate(prompts[b].tolist(), 6), b\n"
+        f"    c = m.new_cache({batch}, 40)\n"
+        f"    oc = ref.new_cache({batch}, 40)\n"
+        "    c.decode(prompts)\n"
+        "    ref.decode(oc, prompts)\n"
+        f"    nxt = rng.integers(0, cfg.vocab_size, ({batch}, 1))\n"
+        "    lg, _ = c.decode(nxt)\n"
+        "    close(lg, ref.decode(oc, nxt))\n"
+        "    lg, _ = c.decode(nxt[::-1].copy())\n"
+        "    close(lg, ref.decode(oc, nxt[::-1].copy()))\n"
+        "    ref.free_cache(oc)\n"
+        "    c.close()\n"
+        "s.close()\n"
+        "print('ok')\n")
+    env = dict(os.environ, STB_SKINNY_MIN_WORK="0", STB_FUSE_NEXT=str(fuse))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
