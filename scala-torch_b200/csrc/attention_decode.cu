@@ -248,6 +248,233 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_kernel(
   }
 }
 
+// Groups of 5 to 8 query heads per KV head (the Llama-3-70B shape): the same blocks, ring and split
+// records as decode_attention_stream_kernel, with the arithmetic laid out so that a chunk costs few
+// shared-memory loads and no cross-warp reduction:
+//   * scores: warp w takes keys 4 w .. 4 w + 3 of each K chunk; lane (head quad hq = lane / 16, dimension
+//     group dg = lane % 16) keeps its 8 query dimensions of heads 4 hq .. 4 hq + 3 in registers (16-byte
+//     chunk dg % 8 of boxes dg / 8 and dg / 8 + 2, the same 16 chunks of every key row: with the 128-byte
+//     swizzle the 16 lanes of a quad read two whole 128-byte rows, no bank conflict), forms the 4 keys x
+//     4 heads partial dots over them (8 K loads, 128 FMAs), and one reduce-scatter butterfly over the 16
+//     lanes of its quad (15 shuffles) leaves lane dg with the whole dot of key dg / 4 and head dg % 4;
+//   * softmax statistics per head over the split, as before;
+//   * weighted V sum: warp w takes the same 4 keys of each V chunk, lane l owns dimensions 4 l .. 4 l + 3
+//     of all 8 heads (32 accumulators; one 16-byte V load and two broadcast loads of the 8 weights per
+//     key), and the 8 warps' sums are added in warp order at the end through the (then idle) ring.
+constexpr size_t DS8_SMEM = 1024 + (size_t)DS_RING * DS_CHUNK + (size_t)DS_KPS_MAX * DS_GMAX * 4 +
+                            DS_GMAX * 2 * 4 + DS_RING * 8;
+static_assert(DS_RING * DS_CHUNK >= DS_WARPS * DS_GMAX * DS_HD * 4, "the ring holds the warps' value sums");
+
+__global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kernel(
+    const __grid_constant__ CUtensorMap kmap, long long krow0, const float *q, int ldq, const float *kcache,
+    const float *vcache, int count, int nh, int kvh, int capacity, const int *pos_dev, int pos0, int kps,
+    float *part, int smax, int *err) {
+  extern __shared__ uint8_t ds_raw[];
+  uint8_t *ring = (uint8_t *)(((uintptr_t)ds_raw + 1023) & ~(uintptr_t)1023);
+  float *pt = (float *)(ring + DS_RING * DS_CHUNK);  // [kps][8]: scores, then exp(score - max)
+  float *red = pt + DS_KPS_MAX * DS_GMAX;            // [8][2]: max, sum
+  uint64_t *bar = (uint64_t *)(red + DS_GMAX * 2);   // [DS_RING]
+  __shared__ int s_ok;
+  __shared__ volatile int s_abort;
+  pdl_trigger();
+  const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
+  const int G = nh / kvh;
+  const int b = m / count, t = m % count;
+  const int keys = (pos_dev ? *pos_dev : pos0) + t + 1;
+  const int S = (keys + kps - 1) / kps;
+  if (split >= S) return;  // the grid covers the longest visible range
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int j0 = split * kps, nk = min(kps, keys - j0);
+  const int nck = (nk + DS_CH - 1) / DS_CH, total = 2 * nck;  // K chunks, then V chunks
+  const int fresh = keys - 1 - j0;                              // in [0, nk) only in the last split
+  const long long kvrow0 = ((long long)b * kvh + g0) * capacity + j0;
+  const uint32_t ring_a = smem_u32(ring), bar0 = smem_u32(bar);
+  int issued = 0;  // thread 0: chunks whose loads are issued
+  auto issue = [&](int c) {
+    const int st = c % DS_RING;
+    const uint32_t dst = ring_a + st * DS_CHUNK, br = bar0 + 8 * st;
+    if (c < nck) {
+      mbar_expect_tx(br, DS_CHUNK);
+      const int y = (int)(krow0 + kvrow0 + (long long)c * DS_CH);
+#pragma unroll
+      for (int bx = 0; bx < 4; bx++) tma_load_2d(dst + bx * 4096, &kmap, bx * 32, y, br);
+    } else {
+      const int cv = c - nck, rows = min(DS_CH, nk - cv * DS_CH);
+      const uint32_t bytes = (uint32_t)rows * DS_HD * 4;
+      mbar_expect_tx(br, bytes);
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                   "l"(vcache + (kvrow0 + (long long)cv * DS_CH) * DS_HD), "r"(bytes), "r"(br)
+                   : "memory");
+    }
+  };
+  if (tid == 0) {
+    s_abort = 0;
+    for (int st = 0; st < DS_RING; st++) mbar_init(bar0 + 8 * st, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (; issued < min(DS_RING, total); issued++) issue(issued);
+  }
+  pdl_wait();
+  const int hq = lane >> 4, dg = lane & 15;
+  const int box = dg >> 3, ck = dg & 7;  // this lane's dimensions: 32 box + 4 ck .. + 3 and 32 (box + 2) + 4 ck .. + 3
+  float qa[4][4], qb[4][4];
+#pragma unroll
+  for (int h = 0; h < 4; h++) {
+    const int g = 4 * hq + h;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c4 = a;
+    if (g < G) {
+      const float *qr = q + (size_t)m * ldq + (size_t)(g0 * G + g) * DS_HD;
+      a = *(const float4 *)(qr + 32 * box + 4 * ck);
+      c4 = *(const float4 *)(qr + 32 * (box + 2) + 4 * ck);
+    }
+    qa[h][0] = a.x; qa[h][1] = a.y; qa[h][2] = a.z; qa[h][3] = a.w;
+    qb[h][0] = c4.x; qb[h][1] = c4.y; qb[h][2] = c4.z; qb[h][3] = c4.w;
+  }
+  // the newest key's row, loaded now (after the wait) and stored once its chunk has landed
+  const bool patch = fresh < nk && tid < DS_HD;
+  const float kf = patch ? kcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
+  const float vf = patch ? vcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
+  const float scale = (float)(1.0 / sqrt((double)DS_HD));
+  float acc[DS_GMAX][4];
+#pragma unroll
+  for (int g = 0; g < DS_GMAX; g++) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
+
+  for (int c = 0; c < total; c++) {
+    const int st = c % DS_RING;
+    uint8_t *chunk = ring + st * DS_CHUNK;
+    if (tid == 0) {
+      s_ok = mbar_wait(bar0 + 8 * st, (uint32_t)(c / DS_RING) & 1u, &s_abort, err, 62);
+      if (!s_ok) {  // leave only once every copy into this block's shared memory is done (bounded again)
+        volatile int no_abort = 0;
+        for (int cc = c; cc < issued; cc++)
+          mbar_wait(bar0 + 8 * (cc % DS_RING), (uint32_t)(cc / DS_RING) & 1u, &no_abort, err, 63);
+      }
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    if (c < nck) {
+      const int r = fresh - c * DS_CH;
+      if (r >= 0 && r < DS_CH) {  // block-uniform
+        if (tid < DS_HD) *(float *)(chunk + ds_koff(r, tid)) = kf;
+        __syncthreads();
+      }
+      float v[16];  // [key j][head h]: partial dots over this lane's 8 dimensions
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int kr = 4 * warp + j;
+        const uint32_t sw = (uint32_t)((ck ^ (kr & 7)) << 4);
+        const float4 ka = *(const float4 *)(chunk + box * 4096 + kr * 128 + sw);
+        const float4 kb = *(const float4 *)(chunk + (box + 2) * 4096 + kr * 128 + sw);
+        const float kd[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+        for (int h = 0; h < 4; h += 2) {  // heads h, h + 1 in one packed FP32 FMA (each lane an IEEE fma)
+          float2 x = make_float2(qa[h][0] * kd[0], qa[h + 1][0] * kd[0]);
+#pragma unroll
+          for (int e = 1; e < 8; e++) {
+            const float2 qq = e < 4 ? make_float2(qa[h][e], qa[h + 1][e]) : make_float2(qb[h][e - 4], qb[h + 1][e - 4]);
+            x = __ffma2_rn(qq, make_float2(kd[e], kd[e]), x);
+          }
+          v[4 * j + h] = x.x;
+          v[4 * j + h + 1] = x.y;
+        }
+      }
+      // reduce-scatter over the 16 lanes of the quad: after the level of offset o, a lane keeps the half
+      // of its values selected by its bit o
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) {
+        const bool up = (dg & o) != 0;
+#pragma unroll
+        for (int i = 0; i < o; i++) {
+          const float send = up ? v[i] : v[i + o];
+          const float keep = up ? v[i + o] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      {  // lane dg: key dg / 4 of the warp's four, head 4 hq + dg % 4
+        const int kr = 4 * warp + (dg >> 2), g = 4 * hq + (dg & 3);
+        if (c * DS_CH + kr < nk && g < G) pt[(c * DS_CH + kr) * DS_GMAX + g] = v[0] * scale;
+      }
+      if (c == nck - 1) {  // all scores: softmax statistics of head `warp` over the split
+        __syncthreads();
+        const int g = warp;
+        if (g < G) {
+          float mx = -INFINITY;
+          for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, pt[j * DS_GMAX + g]);
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          float sum = 0.0f;
+          for (int j = lane; j < nk; j += 32) {
+            const float e = expf(pt[j * DS_GMAX + g] - mx);
+            pt[j * DS_GMAX + g] = e;
+            sum += e;
+          }
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+          if (lane == 0) {
+            red[g * 2] = mx;
+            red[g * 2 + 1] = sum;
+          }
+        }
+      }
+    } else {
+      const int cv = c - nck, rows = min(DS_CH, nk - cv * DS_CH);
+      const int r = fresh - cv * DS_CH;
+      if (r >= 0 && r < DS_CH) {  // block-uniform
+        if (tid < DS_HD) ((float *)chunk)[r * DS_HD + tid] = vf;
+        __syncthreads();
+      }
+      const float *pr = pt + (size_t)cv * DS_CH * DS_GMAX;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int kr = 4 * warp + j;
+        if (kr < rows) {
+          const float4 vv = *(const float4 *)(chunk + kr * (DS_HD * 4) + lane * 16);
+          const float4 pa = *(const float4 *)(pr + kr * DS_GMAX), pb = *(const float4 *)(pr + kr * DS_GMAX + 4);
+          const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+          for (int g = 0; g < DS_GMAX; g++) {  // packed FP32 FMAs: two dimensions per instruction
+            const float2 pp = make_float2(p8[g], p8[g]);
+            const float2 lo = __ffma2_rn(pp, make_float2(vv.x, vv.y), make_float2(acc[g][0], acc[g][1]));
+            const float2 hi = __ffma2_rn(pp, make_float2(vv.z, vv.w), make_float2(acc[g][2], acc[g][3]));
+            acc[g][0] = lo.x;
+            acc[g][1] = lo.y;
+            acc[g][2] = hi.x;
+            acc[g][3] = hi.y;
+          }
+        }
+      }
+    }
+    __syncthreads();  // chunk consumed: its stage takes the chunk DS_RING ahead
+    if (tid == 0 && issued < total) issue(issued++);
+  }
+  // the warps' value sums, added in warp order through the ring (every copy into it has completed)
+  float *ws = (float *)ring;  // [warp][8 heads][128]
+#pragma unroll
+  for (int g = 0; g < DS_GMAX; g++)
+    *(float4 *)(ws + (warp * DS_GMAX + g) * DS_HD + 4 * lane) = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+  __syncthreads();
+  const size_t slot = ((size_t)m * kvh + g0) * smax + split;
+  float *po = part, *pml = part + (size_t)gridDim.z * kvh * smax * DS_GMAX * DS_HD;
+  {  // thread: head tid / 32, dimensions 4 (tid % 32) .. + 3
+    const int g = tid >> 5, d = 4 * lane;
+    if (g < G) {
+      float4 sum = *(const float4 *)(ws + g * DS_HD + d);
+#pragma unroll
+      for (int w = 1; w < DS_WARPS; w++) {
+        const float4 x = *(const float4 *)(ws + (w * DS_GMAX + g) * DS_HD + d);
+        sum.x += x.x;
+        sum.y += x.y;
+        sum.z += x.z;
+        sum.w += x.w;
+      }
+      *(float4 *)(po + (slot * DS_GMAX + g) * DS_HD + d) = sum;
+    }
+  }
+  if (tid < G) {
+    pml[(slot * DS_GMAX + tid) * 2 + 0] = red[tid * 2];
+    pml[(slot * DS_GMAX + tid) * 2 + 1] = red[tid * 2 + 1];
+  }
+}
+
 // The split merge and the o projection's prologue in one: block (kb, m) takes elements
 // [kb * 1024, kb * 1024 + 1024) of token row m's attention output (four per thread, one query head),
 // merges the splits' records (max over splits, weights exp(max_s - max), numerator and denominator
@@ -365,8 +592,16 @@ void launch_decode_attention_stream(const CUtensorMap &kmap, long long krow0, co
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DS_SMEM));
       STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_kernel<false>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DS_SMEM));
+      STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_g8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)DS8_SMEM));
       if (device >= 0 && device < 64) configured[device] = true;
     }
+  }
+  static const int g8 = env_int("STB_DS_G8", 1);  // 0: groups above 4 heads take the general kernel
+  if (nh / kvh > 4 && g8) {
+    launch_kernel(decode_attention_stream_g8_kernel, dim3(plan.smax, kvh, rows), dim3(DS_THREADS), DS8_SMEM, st, pdl,
+                  kmap, krow0, q, ldq, kc, vc, count, nh, kvh, capacity, posd, pos0, plan.kps, part, plan.smax, err);
+    return;
   }
   auto kernel = nh / kvh > 4 ? decode_attention_stream_kernel<true> : decode_attention_stream_kernel<false>;
   launch_kernel(kernel, dim3(plan.smax, kvh, rows), dim3(DS_THREADS), DS_SMEM, st, pdl, kmap, krow0, q, ldq, kc, vc,

@@ -281,14 +281,16 @@ HD128 = dict(vocab_size=512, hidden_size=1024, intermediate_size=256, num_layers
              num_key_value_heads=1, max_positions=512, tie_word_embeddings=False, eos_token_ids=())
 
 
-@pytest.mark.parametrize("stream,impl,kps,hd128,heads,kvh", [
-    (1, 1, 0, 1, 8, 1), (1, 1, 32, 1, 8, 1), (1, 1, 64, 1, 8, 2), (1, 1, 96, 1, 6, 2), (1, 1, 32, 1, 4, 4),
-    (0, 1, 32, 1, 8, 1), (0, 1, 64, 1, 8, 1), (0, 1, 128, 1, 8, 1), (0, 1, 64, 0, 8, 1), (0, 0, 0, 1, 8, 1),
-    (0, 1, 64, 1, 8, 2), (0, 1, 32, 1, 6, 2)])
-def test_decode_attention_splits_head128(stream, impl, kps, hd128, heads, kvh):
-    """The decode attention on head size 128 with 8, 4, 3 and 1 query heads per KV head: the streamed form
-    (decode_attention_stream_kernel + the merge in the o projection's prologue) with its keys per split
-    left to the plan or forced to 32 / 64 / 96 (STB_DS_KPS), and with STB_DECODE_STREAM=0 the split forms
+@pytest.mark.parametrize("stream,impl,kps,hd128,heads,kvh,g8", [
+    (1, 1, 0, 1, 8, 1, 1), (1, 1, 32, 1, 8, 1, 1), (1, 1, 64, 1, 6, 1, 1), (1, 1, 96, 1, 5, 1, 1),
+    (1, 1, 32, 1, 8, 1, 0), (1, 1, 64, 1, 8, 2, 1), (1, 1, 96, 1, 6, 2, 1), (1, 1, 32, 1, 4, 4, 1),
+    (0, 1, 32, 1, 8, 1, 1), (0, 1, 64, 1, 8, 1, 1), (0, 1, 128, 1, 8, 1, 1), (0, 1, 64, 0, 8, 1, 1),
+    (0, 0, 0, 1, 8, 1, 1), (0, 1, 64, 1, 8, 2, 1), (0, 1, 32, 1, 6, 2, 1)])
+def test_decode_attention_splits_head128(stream, impl, kps, hd128, heads, kvh, g8):
+    """The decode attention on head size 128 with 8, 6, 5, 4, 3 and 1 query heads per KV head: the streamed
+    form (decode_attention_stream_g8_kernel for 5 to 8 heads per KV head, or decode_attention_stream_kernel
+    with STB_DS_G8=0 and for smaller groups, + the merge in the o projection's prologue) with its keys per
+    split left to the plan or forced to 32 / 64 / 96 (STB_DS_KPS), and with STB_DECODE_STREAM=0 the split forms
     (decode_attention_hd128_kernel, and decode_attention_kernel with STB_DA_HD128=0) with keys per split
     forced to 32 / 64 / 128 (STB_DA_KPS) and the register form (STB_DA_IMPL) -- variables read once per
     process: a child process each -- over 127 prompt tokens
@@ -326,7 +328,7 @@ def test_decode_attention_splits_head128(stream, impl, kps, hd128, heads, kvh):
         "s.close()\n"
         "print('ok')\n")
     env = dict(os.environ, STB_DECODE_STREAM=str(stream), STB_DS_KPS=str(kps if stream else 0),
-               STB_DA_KPS=str(0 if stream else kps), STB_DA_IMPL=str(impl), STB_DA_HD128=str(hd128))
+               STB_DA_KPS=str(0 if stream else kps), STB_DA_IMPL=str(impl), STB_DA_HD128=str(hd128), STB_DS_G8=str(g8))
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
 
