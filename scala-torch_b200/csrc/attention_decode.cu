@@ -31,6 +31,7 @@
 // projection).  Every mbarrier wait is bounded (2 s; then the session's error word is set, the block
 // waits -- bounded again -- for the copies it issued, and leaves without writing).
 #include "attention_decode.cuh"
+#include "gemv.cuh"
 #include "tc_common.cuh"
 
 namespace stb {
@@ -248,6 +249,95 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_kernel(
   }
 }
 
+// Sum of the stream-K pieces of 4 consecutive outputs (n0 % 4 == 0) of row m, in piece order.
+__device__ __forceinline__ float4 ds_gather4(const DecodeStreamFused &fu, int m, int n0) {
+  const int t = n0 >> 7;
+  const int first = skinny_cta_of((long long)t * fu.kbs, fu.T, fu.G);
+  const int n = skinny_cta_of((long long)(t + 1) * fu.kbs - 1, fu.T, fu.G) - first + 1;
+  const float *pp = fu.part + ((size_t)t * fu.pmax * fu.M + m) * 128 + (n0 & 127);
+  const size_t stride = (size_t)fu.M * 128;
+  float4 w[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++)
+    if (j < n) w[j] = __ldcg((const float4 *)(pp + j * stride));
+  float4 a = w[0];
+#pragma unroll
+  for (int j = 1; j < 4; j++)
+    if (j < n) {
+      a.x = a.x + w[j].x;
+      a.y = a.y + w[j].y;
+      a.z = a.z + w[j].z;
+      a.w = a.w + w[j].w;
+    }
+  for (int j = 4; j < n; j++) {  // more than four pieces: one round trip each
+    const float4 c = __ldcg((const float4 *)(pp + j * stride));
+    a.x = a.x + c.x;
+    a.y = a.y + c.y;
+    a.z = a.z + c.z;
+    a.w = a.w + c.w;
+  }
+  return a;
+}
+
+// The same for 2 consecutive outputs (n0 even).
+__device__ __forceinline__ float2 ds_gather2(const DecodeStreamFused &fu, int m, int n0) {
+  const int t = n0 >> 7;
+  const int first = skinny_cta_of((long long)t * fu.kbs, fu.T, fu.G);
+  const int n = skinny_cta_of((long long)(t + 1) * fu.kbs - 1, fu.T, fu.G) - first + 1;
+  const float *pp = fu.part + ((size_t)t * fu.pmax * fu.M + m) * 128 + (n0 & 127);
+  const size_t stride = (size_t)fu.M * 128;
+  float2 w[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++)
+    if (j < n) w[j] = __ldcg((const float2 *)(pp + j * stride));
+  float2 a = w[0];
+#pragma unroll
+  for (int j = 1; j < 4; j++)
+    if (j < n) {
+      a.x = a.x + w[j].x;
+      a.y = a.y + w[j].y;
+    }
+  for (int j = 4; j < n; j++) {
+    const float2 c = __ldcg((const float2 *)(pp + j * stride));
+    a.x = a.x + c.x;
+    a.y = a.y + c.y;
+  }
+  return a;
+}
+
+// Merge of the S split records of (row, KV head) at slot `base` for head g, dimensions d .. d + 3:
+// max over splits, weights exp(max_s - max), numerator and denominator summed in split order.
+__device__ __forceinline__ void ds_merge4(const float *po, const float *ml, size_t base, int S, int g, int d,
+                                          float (&o)[4]) {
+  float mx = -INFINITY;
+  for (int s = 0; s < S; s++) mx = fmaxf(mx, __ldcg(&ml[((base + s) * DS_GMAX + g) * 2]));
+  float num[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.0f;
+  for (int s0 = 0; s0 < S; s0 += 4) {  // four splits' loads per round trip
+    float2 r[4];
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      if (s0 + j < S) {
+        r[j] = __ldcg((const float2 *)&ml[((base + s0 + j) * DS_GMAX + g) * 2]);
+        v[j] = __ldcg((const float4 *)&po[((base + s0 + j) * DS_GMAX + g) * DS_HD + d]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      if (s0 + j < S) {
+        const float w = expf(r[j].x - mx);
+        num[0] = fmaf(w, v[j].x, num[0]);
+        num[1] = fmaf(w, v[j].y, num[1]);
+        num[2] = fmaf(w, v[j].z, num[2]);
+        num[3] = fmaf(w, v[j].w, num[3]);
+        den = fmaf(w, r[j].y, den);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; e++) o[e] = num[e] / den;
+}
+
 // Groups of 5 to 8 query heads per KV head (the Llama-3-70B shape): the same blocks, ring and split
 // records as decode_attention_stream_kernel, with the arithmetic laid out so that a chunk costs few
 // shared-memory loads and no cross-warp reduction:
@@ -262,19 +352,25 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_kernel(
 //     of all 8 heads (32 accumulators; one 16-byte V load and two broadcast loads of the 8 weights per
 //     key), and the 8 warps' sums are added in warp order at the end through the (then idle) ring.
 constexpr size_t DS8_SMEM = 1024 + (size_t)DS_RING * DS_CHUNK + (size_t)DS_KPS_MAX * DS_GMAX * 4 +
-                            DS_GMAX * 2 * 4 + DS_RING * 8;
+                            DS_GMAX * 2 * 4 + (size_t)(DS_GMAX + 2) * DS_HD * 4 + DS_RING * 8;
 static_assert(DS_RING * DS_CHUNK >= DS_WARPS * DS_GMAX * DS_HD * 4, "the ring holds the warps' value sums");
 
+// FUSED: the QKV projection's fixup and the split merge happen here too (see DecodeStreamFused): q, and
+// in the block holding the newest key its k (rotated) and v, are summed from the projection's stream-K
+// pieces right after the dependency wait, the newest k / v row is written to the cache, and the last
+// block of each (row, KV head) to finish merges the splits' records as attention_merge_split_kernel does.
+template <bool FUSED>
 __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kernel(
-    const __grid_constant__ CUtensorMap kmap, long long krow0, const float *q, int ldq, const float *kcache,
-    const float *vcache, int count, int nh, int kvh, int capacity, const int *pos_dev, int pos0, int kps,
-    float *part, int smax, int *err) {
+    const __grid_constant__ CUtensorMap kmap, long long krow0, const float *q, int ldq, float *kcache, float *vcache,
+    int count, int nh, int kvh, int capacity, const int *pos_dev, int pos0, int kps, float *part, int smax, int *err,
+    const DecodeStreamFused fu) {
   extern __shared__ uint8_t ds_raw[];
   uint8_t *ring = (uint8_t *)(((uintptr_t)ds_raw + 1023) & ~(uintptr_t)1023);
   float *pt = (float *)(ring + DS_RING * DS_CHUNK);  // [kps][8]: scores, then exp(score - max)
   float *red = pt + DS_KPS_MAX * DS_GMAX;            // [8][2]: max, sum
-  uint64_t *bar = (uint64_t *)(red + DS_GMAX * 2);   // [DS_RING]
-  __shared__ int s_ok;
+  float *Qs = red + DS_GMAX * 2;                     // FUSED: [8][128] query rows, then the newest k and v rows
+  uint64_t *bar = (uint64_t *)(Qs + (DS_GMAX + 2) * DS_HD);  // [DS_RING]
+  __shared__ int s_ok, s_last;
   __shared__ volatile int s_abort;
   pdl_trigger();
   const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
@@ -316,23 +412,91 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kern
   pdl_wait();
   const int hq = lane >> 4, dg = lane & 15;
   const int box = dg >> 3, ck = dg & 7;  // this lane's dimensions: 32 box + 4 ck .. + 3 and 32 (box + 2) + 4 ck .. + 3
+  const int pos = keys - 1;               // this token's position
   float qa[4][4], qb[4][4];
-#pragma unroll
-  for (int h = 0; h < 4; h++) {
-    const int g = 4 * hq + h;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c4 = a;
+  // The newest key's row, stored into its chunk once that has landed: thread tid < 128 holds dimension
+  // tid of k and v (kf0, vf0) -- or, FUSED, they sit in shared memory after the query rows.
+  float kf0 = 0.f, vf0 = 0.f;
+  float *kvnew = Qs + DS_GMAX * DS_HD;  // FUSED: [2][128] newest k, v
+  if constexpr (FUSED) {
+    // One round trip for all of it: thread (head g = tid / 32, j = tid % 32) sums the pieces of q rows
+    // 4 j .. 4 j + 3 of head hg -- rows 2 (hg 64 + d) and 2 (hg 64 + d) + 1 hold the rotary pair
+    // (d, d + 64), so these are the pairs d = 2 j, 2 j + 1 -- rotates them into the shared query rows;
+    // threads below 128 also sum the newest key's k pair d = tid (rotated) or v pair d = tid - 64,
+    // write it to the cache and keep it for the chunk that holds that key.
+    const int g = tid >> 5, j = tid & 31;
+    float4 qv = make_float4(0.f, 0.f, 0.f, 0.f);
+    double2 cq[2];
     if (g < G) {
-      const float *qr = q + (size_t)m * ldq + (size_t)(g0 * G + g) * DS_HD;
-      a = *(const float4 *)(qr + 32 * box + 4 * ck);
-      c4 = *(const float4 *)(qr + 32 * (box + 2) + 4 * ck);
+      cq[0] = fu.rope[(size_t)pos * 64 + 2 * j];
+      cq[1] = fu.rope[(size_t)pos * 64 + 2 * j + 1];
+      qv = ds_gather4(fu, m, 2 * ((g0 * G + g) * 64) + 4 * j);
     }
-    qa[h][0] = a.x; qa[h][1] = a.y; qa[h][2] = a.z; qa[h][3] = a.w;
-    qb[h][0] = c4.x; qb[h][1] = c4.y; qb[h][2] = c4.z; qb[h][3] = c4.w;
+    const bool kv = fresh < nk && tid < 2 * 64;
+    const bool isv = tid >= 64;
+    float2 ab = make_float2(0.f, 0.f);
+    double2 crk = make_double2(0.0, 0.0);
+    if (kv) {
+      if (!isv) crk = fu.rope[(size_t)pos * 64 + tid];
+      ab = ds_gather2(fu, m, 2 * (nh * 64 + (isv ? kvh * 64 : 0) + g0 * 64 + (tid & 63)));
+    }
+    if (g < G) {
+      const float in[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+      for (int i = 0; i < 2; i++) {  // EPI_QKV's rotation: (a c - b s, b c + a s) in double
+        const double a = (double)in[2 * i], bb = (double)in[2 * i + 1];
+        Qs[g * DS_HD + 2 * j + i] = __double2float_rn(__dsub_rn(__dmul_rn(a, cq[i].x), __dmul_rn(bb, cq[i].y)));
+        Qs[g * DS_HD + 2 * j + i + 64] = __double2float_rn(__dadd_rn(__dmul_rn(bb, cq[i].x), __dmul_rn(a, cq[i].y)));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2; i++) Qs[g * DS_HD + 2 * j + i] = Qs[g * DS_HD + 2 * j + i + 64] = 0.0f;
+    }
+    if (kv) {
+      const int d = tid & 63;
+      const size_t row = (size_t)(kvrow0 + fresh) * DS_HD;
+      if (!isv) {
+        const double a = (double)ab.x, bb = (double)ab.y;
+        const float k0 = __double2float_rn(__dsub_rn(__dmul_rn(a, crk.x), __dmul_rn(bb, crk.y)));
+        const float k1 = __double2float_rn(__dadd_rn(__dmul_rn(bb, crk.x), __dmul_rn(a, crk.y)));
+        kcache[row + d] = k0;
+        kcache[row + d + 64] = k1;
+        kvnew[d] = k0;
+        kvnew[d + 64] = k1;
+      } else {
+        vcache[row + d] = ab.x;
+        vcache[row + d + 64] = ab.y;
+        kvnew[DS_HD + d] = ab.x;
+        kvnew[DS_HD + d + 64] = ab.y;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+      const float *qr = Qs + (4 * hq + h) * DS_HD;
+      const float4 a = *(const float4 *)(qr + 32 * box + 4 * ck);
+      const float4 c4 = *(const float4 *)(qr + 32 * (box + 2) + 4 * ck);
+      qa[h][0] = a.x; qa[h][1] = a.y; qa[h][2] = a.z; qa[h][3] = a.w;
+      qb[h][0] = c4.x; qb[h][1] = c4.y; qb[h][2] = c4.z; qb[h][3] = c4.w;
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < 4; h++) {
+      const int g = 4 * hq + h;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), c4 = a;
+      if (g < G) {
+        const float *qr = q + (size_t)m * ldq + (size_t)(g0 * G + g) * DS_HD;
+        a = *(const float4 *)(qr + 32 * box + 4 * ck);
+        c4 = *(const float4 *)(qr + 32 * (box + 2) + 4 * ck);
+      }
+      qa[h][0] = a.x; qa[h][1] = a.y; qa[h][2] = a.z; qa[h][3] = a.w;
+      qb[h][0] = c4.x; qb[h][1] = c4.y; qb[h][2] = c4.z; qb[h][3] = c4.w;
+    }
+    // the newest key's row, loaded now (after the wait) and stored once its chunk has landed
+    const bool patch = fresh < nk && tid < DS_HD;
+    kf0 = patch ? kcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
+    vf0 = patch ? vcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
   }
-  // the newest key's row, loaded now (after the wait) and stored once its chunk has landed
-  const bool patch = fresh < nk && tid < DS_HD;
-  const float kf = patch ? kcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
-  const float vf = patch ? vcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
   const float scale = (float)(1.0 / sqrt((double)DS_HD));
   float acc[DS_GMAX][4];
 #pragma unroll
@@ -354,7 +518,7 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kern
     if (c < nck) {
       const int r = fresh - c * DS_CH;
       if (r >= 0 && r < DS_CH) {  // block-uniform
-        if (tid < DS_HD) *(float *)(chunk + ds_koff(r, tid)) = kf;
+        if (tid < DS_HD) *(float *)(chunk + ds_koff(r, tid)) = FUSED ? kvnew[tid] : kf0;
         __syncthreads();
       }
       float v[16];  // [key j][head h]: partial dots over this lane's 8 dimensions
@@ -419,7 +583,7 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kern
       const int cv = c - nck, rows = min(DS_CH, nk - cv * DS_CH);
       const int r = fresh - cv * DS_CH;
       if (r >= 0 && r < DS_CH) {  // block-uniform
-        if (tid < DS_HD) ((float *)chunk)[r * DS_HD + tid] = vf;
+        if (tid < DS_HD) ((float *)chunk)[r * DS_HD + tid] = FUSED ? kvnew[DS_HD + tid] : vf0;
         __syncthreads();
       }
       const float *pr = pt + (size_t)cv * DS_CH * DS_GMAX;
@@ -473,6 +637,33 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kern
     pml[(slot * DS_GMAX + tid) * 2 + 0] = red[tid * 2];
     pml[(slot * DS_GMAX + tid) * 2 + 1] = red[tid * 2 + 1];
   }
+  if constexpr (FUSED) {
+    // the last of the S blocks of (row, KV head) to get here merges their records
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&fu.counter[m * kvh + g0], 1) == S - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int g = tid >> 5, d = 4 * lane;  // head, dimensions d .. d + 3
+    if (g < G) {
+      const size_t base = ((size_t)m * kvh + g0) * smax;
+      float o[4];
+      ds_merge4(po, pml, base, S, g, d, o);
+      const int K = nh * DS_HD, k0 = (g0 * G + g) * DS_HD + d;
+      uint16_t h[3][4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) split3_bf16(o[e], h[0][e], h[1][e], h[2][e]);  // the skinny prologue's split
+#pragma unroll
+      for (int tm = 0; tm < 3; tm++) {
+        uint2 u;
+        u.x = (uint32_t)h[tm][0] | ((uint32_t)h[tm][1] << 16);
+        u.y = (uint32_t)h[tm][2] | ((uint32_t)h[tm][3] << 16);
+        *(uint2 *)(fu.x3 + ((size_t)tm * fu.NT + m) * K + k0) = u;
+      }
+    }
+    if (tid == 0) fu.counter[m * kvh + g0] = 0;  // for the next launch
+  }
 }
 
 // The split merge and the o projection's prologue in one: block (kb, m) takes elements
@@ -495,35 +686,8 @@ __global__ void __launch_bounds__(256) attention_merge_split_kernel(
     const int gq = k0 / DS_HD, g0 = gq / G, g = gq % G, d = k0 % DS_HD;
     const int keys = (pos_dev ? *pos_dev : pos0) + m % count + 1;
     const int S = (keys + kps - 1) / kps;
-    const size_t slot = ((size_t)m * kvh + g0) * smax;
     const float *po = part, *ml = part + (size_t)M * kvh * smax * DS_GMAX * DS_HD;  // sums, then (max, sum)
-    float mx = -INFINITY;
-    for (int s = 0; s < S; s++) mx = fmaxf(mx, __ldcg(&ml[((slot + s) * DS_GMAX + g) * 2]));
-    float num[4] = {0.f, 0.f, 0.f, 0.f}, den = 0.0f;
-    for (int s0 = 0; s0 < S; s0 += 4) {  // four splits' loads per round trip
-      float2 r[4];
-      float4 v[4];
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        if (s0 + j < S) {
-          r[j] = __ldcg((const float2 *)&ml[((slot + s0 + j) * DS_GMAX + g) * 2]);
-          v[j] = __ldcg((const float4 *)&po[((slot + s0 + j) * DS_GMAX + g) * DS_HD + d]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        if (s0 + j < S) {
-          const float w = expf(r[j].x - mx);
-          num[0] = fmaf(w, v[j].x, num[0]);
-          num[1] = fmaf(w, v[j].y, num[1]);
-          num[2] = fmaf(w, v[j].z, num[2]);
-          num[3] = fmaf(w, v[j].w, num[3]);
-          den = fmaf(w, r[j].y, den);
-        }
-      }
-    }
-#pragma unroll
-    for (int e = 0; e < 4; e++) o[e] = num[e] / den;
+    ds_merge4(po, ml, ((size_t)m * kvh + g0) * smax, S, g, d, o);
   }
   if (out) {
     if (m < M) *(float4 *)(out + (size_t)m * ldo + k0) = make_float4(o[0], o[1], o[2], o[3]);
@@ -574,15 +738,20 @@ CUtensorMap make_kv_map(const float *kv, uint64_t rows) {
   return m;
 }
 
+bool decode_stream_fusable(int nh, int kvh) {
+  static const int g8 = env_int("STB_DS_G8", 1);  // 0: groups above 4 heads take the general kernel
+  return g8 && nh % kvh == 0 && nh / kvh > 4 && nh / kvh <= DS_GMAX;
+}
+
 bool decode_stream_applies(int hd, int nh, int kvh) {
   static const int enabled = env_int("STB_DECODE_STREAM", 1);
   return enabled && hd == DS_HD && nh % kvh == 0 && nh / kvh <= DS_GMAX;
 }
 
-void launch_decode_attention_stream(const CUtensorMap &kmap, long long krow0, const float *q, int ldq,
-                                    const float *kc, const float *vc, int rows, int count, int nh, int kvh,
-                                    int capacity, const int *posd, int pos0, const DecodeStreamPlan &plan,
-                                    float *part, bool pdl, cudaStream_t st, int device, int *err) {
+void launch_decode_attention_stream(const CUtensorMap &kmap, long long krow0, const float *q, int ldq, float *kc,
+                                    float *vc, int rows, int count, int nh, int kvh, int capacity, const int *posd,
+                                    int pos0, const DecodeStreamPlan &plan, float *part, bool pdl, cudaStream_t st,
+                                    int device, int *err, const DecodeStreamFused *fused) {
   {
     static std::mutex mu;
     static bool configured[64] = {};
@@ -592,15 +761,27 @@ void launch_decode_attention_stream(const CUtensorMap &kmap, long long krow0, co
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DS_SMEM));
       STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_kernel<false>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DS_SMEM));
-      STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_g8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)DS8_SMEM));
+      STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_g8_kernel<false>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DS8_SMEM));
+      STB_CUDA(cudaFuncSetAttribute(decode_attention_stream_g8_kernel<true>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DS8_SMEM));
       if (device >= 0 && device < 64) configured[device] = true;
     }
   }
-  static const int g8 = env_int("STB_DS_G8", 1);  // 0: groups above 4 heads take the general kernel
-  if (nh / kvh > 4 && g8) {
-    launch_kernel(decode_attention_stream_g8_kernel, dim3(plan.smax, kvh, rows), dim3(DS_THREADS), DS8_SMEM, st, pdl,
-                  kmap, krow0, q, ldq, kc, vc, count, nh, kvh, capacity, posd, pos0, plan.kps, part, plan.smax, err);
+  STB_REQUIRE(!fused || decode_stream_fusable(nh, kvh), "fused decode attention: 5 to 8 query heads per KV head");
+  if (fused) {
+    STB_REQUIRE(fused->part && fused->rope && fused->counter && fused->x3 && fused->M == rows && count == 1 &&
+                    fused->NT >= rows,
+                "fused decode attention arguments");
+    launch_kernel(decode_attention_stream_g8_kernel<true>, dim3(plan.smax, kvh, rows), dim3(DS_THREADS), DS8_SMEM, st,
+                  pdl, kmap, krow0, q, ldq, kc, vc, count, nh, kvh, capacity, posd, pos0, plan.kps, part, plan.smax,
+                  err, *fused);
+    return;
+  }
+  if (decode_stream_fusable(nh, kvh)) {
+    launch_kernel(decode_attention_stream_g8_kernel<false>, dim3(plan.smax, kvh, rows), dim3(DS_THREADS), DS8_SMEM,
+                  st, pdl, kmap, krow0, q, ldq, kc, vc, count, nh, kvh, capacity, posd, pos0, plan.kps, part,
+                  plan.smax, err, DecodeStreamFused{});
     return;
   }
   auto kernel = nh / kvh > 4 ? decode_attention_stream_kernel<true> : decode_attention_stream_kernel<false>;

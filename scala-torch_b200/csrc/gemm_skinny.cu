@@ -94,14 +94,7 @@ __device__ __forceinline__ void tmem_ld3(uint32_t a2, uint32_t a1, uint32_t a0, 
 // First iteration of CTA c when T iterations are cut into G ranges.
 __host__ __device__ __forceinline__ long long sk_start(int c, long long T, int G) { return (long long)c * T / G; }
 
-// The CTA whose range holds iteration i: the largest c with floor(c T / G) <= i, which is
-// floor(((i + 1) G - 1) / T) (c T / G < i + 1  <=>  c T <= (i + 1) G - 1); in 32-bit arithmetic when
-// T G fits (a 64-bit division is a long instruction sequence on the fixups' critical path).
-__device__ __forceinline__ int sk_cta_of(long long i, long long T, int G) {
-  if ((unsigned long long)T * (unsigned)G <= 0xFFFFFFFFull)
-    return (int)(((unsigned)(i + 1) * (unsigned)G - 1u) / (unsigned)T);
-  return (int)(((unsigned long long)(i + 1) * (unsigned)G - 1ull) / (unsigned long long)T);
-}
+__device__ __forceinline__ int sk_cta_of(long long i, long long T, int G) { return skinny_cta_of(i, T, G); }
 
 // x [M][K] (row stride ldx), optionally RMS-normalised as the vector GEMV does it, -> x3 [3][NT][K].
 // Block (kb, m) converts elements [kb * 1024, kb * 1024 + 1024) of row m, four per thread; with
@@ -645,8 +638,9 @@ bool skinny_norm_fusable(int N) { return N % 4 == 0 && N <= SK_NORM_THREADS * SK
 
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
-                  cudaStream_t stream, const uint16_t *x3_ready, const SkinnyNext *next) {
+                  cudaStream_t stream, const uint16_t *x3_ready, const SkinnyNext *next, SkinnyParts *deferred) {
   STB_REQUIRE(p.M >= 1 && p.K % 8 == 0 && p.K >= BK && p.N >= SK_BM, "skinny Linear shape");
+  STB_REQUIRE(!deferred || (p.M <= 64 && !next), "deferred fixup: one block, no fused next prologue");
   STB_REQUIRE(!x3_ready || (p.M <= 64 && p.norm_w == nullptr && ((uintptr_t)x3_ready % 16) == 0),
               "prepared skinny activations: one block, no norm");
   STB_REQUIRE(p.stop == nullptr, "skinny Linear takes no stop flag");
@@ -676,6 +670,16 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
     if (q.nt == 16) launch_gemm<16>(q, tw, tx, part, mb, p.N, err, device, stream);
     else if (q.nt == 32) launch_gemm<32>(q, tw, tx, part, mb, p.N, err, device, stream);
     else launch_gemm<64>(q, tw, tx, part, mb, p.N, err, device, stream);
+    if (deferred) {  // the consumer adds the pieces itself
+      deferred->part = part;
+      deferred->kbs = q.kbs;
+      deferred->T = q.iters;
+      deferred->G = q.grid;
+      deferred->pmax = q.pmax;
+      deferred->M = mb;
+      launches += x3_ready ? 1 : 2;
+      continue;
+    }
     if (next && EPI == EPI_SILU)
       launch_kernel(skinny_fixup_silu_split_kernel, dim3((units + 255) / 256, q.nt), dim3(256), 0, stream, true,
                     (const float *)part, p.N, q.kbs, q.iters, q.grid, q.pmax, mb, next->x3, q.nt);
@@ -692,16 +696,16 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
 }
 
 template int skinny_launch<EPI_PLAIN>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
-                                           const SkinnyNext *);
+                                           const SkinnyNext *, SkinnyParts *);
 template int skinny_launch<EPI_RESID>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
-                                           const SkinnyNext *);
+                                           const SkinnyNext *, SkinnyParts *);
 template int skinny_launch<EPI_SILU>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
-                                           const SkinnyNext *);
+                                           const SkinnyNext *, SkinnyParts *);
 template int skinny_launch<EPI_QKV>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
-                                           const SkinnyNext *);
+                                           const SkinnyNext *, SkinnyParts *);
 template int skinny_launch<EPI_LOGITS>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
-                                           const SkinnyNext *);
+                                           const SkinnyNext *, SkinnyParts *);
 template int skinny_launch<EPI_PEER>(const GemvParams &, void *, uint64_t, int *, int, cudaStream_t, const uint16_t *,
-                                           const SkinnyNext *);
+                                           const SkinnyNext *, SkinnyParts *);
 
 }  // namespace stb

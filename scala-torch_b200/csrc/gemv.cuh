@@ -451,15 +451,37 @@ struct SkinnyNext {
   const float *norm_w = nullptr;
   double eps = 1e-6;
 };
+// The stream-K pieces of a skinny GEMM whose fixup is left to its consumer: output (m, n) is the sum
+// over pieces c = first .. last of part[((t * pmax + c - first) * M + m) * 128 + n % 128], t = n / 128,
+// first = skinny_cta_of(t * kbs, T, G), last = skinny_cta_of((t + 1) * kbs - 1, T, G), in piece order.
+struct SkinnyParts {
+  const float *part = nullptr;
+  int kbs = 0;
+  long long T = 0;
+  int G = 0, pmax = 0, M = 0;
+};
+
+// The CTA whose stream-K range (CTA c covers iterations [floor(c T / G), floor((c + 1) T / G))) holds
+// iteration i: the largest c with floor(c T / G) <= i, which is floor(((i + 1) G - 1) / T)
+// (c T / G < i + 1  <=>  c T <= (i + 1) G - 1); in 32-bit arithmetic when T G fits (a 64-bit
+// division is a long instruction sequence on the fixups' critical path).
+__device__ __forceinline__ int skinny_cta_of(long long i, long long T, int G) {
+  if ((unsigned long long)T * (unsigned)G <= 0xFFFFFFFFull)
+    return (int)(((unsigned)(i + 1) * (unsigned)G - 1u) / (unsigned)T);
+  return (int)(((unsigned long long)(i + 1) * (unsigned)G - 1ull) / (unsigned long long)T);
+}
+
 // Enqueues prologue -> stream-K GEMM -> fixup/epilogue per 64-row block (3 kernels each, all
 // programmatic dependents except the first when !p.pdl).  With x3_ready (M <= 64, no RMSNorm) the
 // previous kernel has already written the activation terms x3 [3][skinny_nt(M)][K] there (16-byte
 // aligned; at the start of the scratch, or a SkinnyNext buffer) and the prologue is skipped.  With
-// next, the fixup also writes the next projection's terms (SkinnyNext).  Returns the number of
-// kernels launched.
+// next, the fixup also writes the next projection's terms (SkinnyNext).  With deferred (M <= 64) no fixup
+// is launched: the pieces stay in the scratch for the next kernel, described in *deferred.  Returns the
+// number of kernels launched.
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
-                  cudaStream_t stream, const uint16_t *x3_ready = nullptr, const SkinnyNext *next = nullptr);
+                  cudaStream_t stream, const uint16_t *x3_ready = nullptr, const SkinnyNext *next = nullptr,
+                  SkinnyParts *deferred = nullptr);
 // Token rows of the activation-term tile for a block of M <= 64 rows: 16, 32 or 64.
 int skinny_nt(int M);
 // Whether a residual projection of N outputs can do the next projection's RMSNorm prologue (SkinnyNext).

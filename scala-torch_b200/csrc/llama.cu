@@ -1700,12 +1700,12 @@ bool projects_skinny(const stb_llama_cache *c, int M, int N, int K, int wdt, con
 // must take the skinny form.
 template <int EPI>
 int project(stb_llama_cache *c, const GemvParams &p, int wdt, GemvConfig cfg, cudaStream_t st,
-            const uint16_t *x3_ready = nullptr, const SkinnyNext *next = nullptr) {
+            const uint16_t *x3_ready = nullptr, const SkinnyNext *next = nullptr, SkinnyParts *deferred = nullptr) {
   stb_session *s = c->m->s;
   if (projects_skinny(c, p.M, p.N, p.K, wdt, p.w))
     return skinny_launch<EPI>(p, (void *)c->skin, c->skin_bytes, session_error_word(s), s->device, st, x3_ready,
-                              next);
-  STB_REQUIRE(!x3_ready && !next, "prepared activation terms need the skinny projection");
+                              next, deferred);
+  STB_REQUIRE(!x3_ready && !next && !deferred, "prepared activation terms need the skinny projection");
   launch_gemv<EPI>(p, wdt, cfg, st);
   return 1;
 }
@@ -1753,6 +1753,16 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       launches += enqueue_layer_tc(c, l, rows, a.count, posd, kc, vc);
       continue;
     }
+    // the streamed single-token attention leaves split records; the o projection's prologue merges them
+    // -- or, for 5 to 8 query heads per KV head on the skinny QKV form, the attention itself adds the QKV
+    // projection's pieces (RoPE + cache append) and merges its splits (two launches fewer)
+    const bool stream_att = a.count == 1 && rows <= c->att_rows && c->kv_map_ok;
+    const int qkv_n = (m->NH + 2 * m->KV) * m->hd;
+    static const int fuse_att_enabled = env_int("STB_FUSE_ATT", 1);
+    const bool fuse_att = fuse_att_enabled && stream_att && rows <= 64 && decode_stream_fusable(m->NH, m->KV) &&
+                          projects_skinny(c, rows, qkv_n, H, wdt, (const void *)L.qkv) &&
+                          projects_skinny(c, rows, H, qw, wdt, (const void *)L.o);
+    SkinnyParts qkv_parts;
     {  // 1. QKV + RoPE + cache append
       GemvParams p;
       p.x = (const float *)c->hidden; p.ldx = H; p.w = (const void *)L.qkv;
@@ -1763,22 +1773,35 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
       p.nh = m->NH; p.kvh = m->KV; p.hd = m->hd; p.capacity = c->capacity; p.k_cache = kc; p.v_cache = vc;
       p.stop = stop;
       p.pdl = true;
-      launches += project<EPI_QKV>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st, pending);
+      launches += project<EPI_QKV>(c, p, wdt, choose_gemv(rows, p.N, p.K, true), st, pending, nullptr,
+                                   fuse_att ? &qkv_parts : nullptr);
       pending = nullptr;
     }
-    // the streamed single-token attention leaves split records; the o projection's prologue merges them
-    const bool stream_att = a.count == 1 && rows <= c->att_rows && c->kv_map_ok;
     bool o_x3 = false;
     if (stream_att) {  // 2. attention (streamed form) and the merge: as the o projection's terms or Float32
       const DecodeStreamPlan plan = decode_stream_plan(rows, m->KV, c->capacity, s->device);
-      launch_decode_attention_stream(c->kv_map, (long long)(l * kv_layer) / m->hd, (const float *)c->qbuf, qw, kc, vc,
-                                     rows, 1, m->NH, m->KV, c->capacity, posd, c->used, plan, (float *)c->att_part,
-                                     true, st, s->device, session_error_word(s));
       o_x3 = rows <= 64 && projects_skinny(c, rows, H, qw, wdt, (const void *)L.o);
-      launch_attention_merge_split((const float *)c->att_part, plan, posd, c->used, rows, 1, m->NH, m->KV,
-                                   skinny_nt(rows), o_x3 ? (uint16_t *)c->skin : nullptr,
-                                   o_x3 ? nullptr : (float *)c->att, qw, st);
-      launches += 2;
+      if (fuse_att) {
+        DecodeStreamFused fu;
+        fu.part = qkv_parts.part; fu.kbs = qkv_parts.kbs; fu.T = qkv_parts.T; fu.G = qkv_parts.G;
+        fu.pmax = qkv_parts.pmax; fu.M = qkv_parts.M;
+        fu.rope = (const double2 *)m->rope;
+        fu.counter = (int *)c->att_count;
+        fu.x3 = (uint16_t *)c->skin;  // o takes the skinny form (a condition of fuse_att): o_x3
+        fu.NT = skinny_nt(rows);
+        launch_decode_attention_stream(c->kv_map, (long long)(l * kv_layer) / m->hd, (const float *)c->qbuf, qw, kc,
+                                       vc, rows, 1, m->NH, m->KV, c->capacity, posd, c->used, plan,
+                                       (float *)c->att_part, true, st, s->device, session_error_word(s), &fu);
+        launches += 1;
+      } else {
+        launch_decode_attention_stream(c->kv_map, (long long)(l * kv_layer) / m->hd, (const float *)c->qbuf, qw, kc,
+                                       vc, rows, 1, m->NH, m->KV, c->capacity, posd, c->used, plan,
+                                       (float *)c->att_part, true, st, s->device, session_error_word(s));
+        launch_attention_merge_split((const float *)c->att_part, plan, posd, c->used, rows, 1, m->NH, m->KV,
+                                     skinny_nt(rows), o_x3 ? (uint16_t *)c->skin : nullptr,
+                                     o_x3 ? nullptr : (float *)c->att, qw, st);
+        launches += 2;
+      }
     } else {  // 2. attention: split GQA kernel for single-token steps, tiled kernel for chunks
       bool done = false;
       if (a.count == 1 && rows <= c->att_rows)

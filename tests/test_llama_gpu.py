@@ -334,12 +334,16 @@ def test_decode_attention_splits_head128(stream, impl, kps, hd128, heads, kvh, g
 
 
 
-@pytest.mark.parametrize("batch,fuse", [(3, 1), (3, 0), (20, 1), (40, 1), (40, 0)])
-def test_skinny_decode_with_fused_prologues(batch, fuse):
+@pytest.mark.parametrize("batch,fuse,heads,kvh", [(3, 1, 8, 2), (3, 0, 8, 2), (20, 1, 8, 2), (40, 1, 8, 2),
+                                                 (40, 0, 8, 2), (3, 1, 8, 1), (3, 0, 8, 1), (20, 1, 6, 1),
+                                                 (40, 1, 8, 1)])
+def test_skinny_decode_with_fused_prologues(batch, fuse, heads, kvh):
     """Decode steps whose every projection takes the tensor-core skinny form (STB_SKINNY_MIN_WORK=0, batch
     rows 3 / 20 / 40: 16-, 32- and 64-row term tiles), with the next projection's prologue done by the
     fixups (STB_FUSE_NEXT=1: o -> RMSNorm + split for gate/up, SiLU*up -> split for down, down -> RMSNorm
-    + split for the next layer's q/k/v) or by their own prologue kernels (0).  RMSNorm weights are
+    + split for the next layer's q/k/v) or by their own prologue kernels (0); with 8 or 6 query heads per
+    KV head (head size 128) the attention also adds the QKV projection's pieces (RoPE, cache append) and
+    merges its own splits (STB_FUSE_ATT=1) instead of the QKV fixup and merge kernels (0).  RMSNorm weights are
     random, not ones, so each fused norm must use its own layer's weights.  The prompt pass stays on the
     Float32 path (tensor-core prefill off).  Child processes (variables read
     once per process): greedy ids identical to the oracle and the logits of a cached step within
@@ -355,14 +359,15 @@ def test_skinny_decode_with_fused_prologues(batch, fuse):
         "from test_llama_gpu import HD128, close\n"
         "from scalatorch import ffm\n"
         "from scalatorch.models import BackendLlama, LlamaConfig\n"
-        "cfg = LlamaConfig(**dict(HD128, hidden_size=1024, num_attention_heads=8, num_key_value_heads=2, "
-        "intermediate_size=384, max_positions=64))\n"
+        f"cfg = LlamaConfig(**dict(HD128, hidden_size={heads * 128}, num_attention_heads={heads}, "
+        f"num_key_value_heads={kvh}, intermediate_size=384, max_positions=64))\n"
         "rng = np.random.default_rng(5)\n"
-        "norms = {'model.norm.weight': oracle.round_bf16((1 + 0.25 * rng.standard_normal(1024)).astype(np.float32))}\n"
+        "H = cfg.hidden_size\n"
+        "norms = {'model.norm.weight': oracle.round_bf16((1 + 0.25 * rng.standard_normal(H)).astype(np.float32))}\n"
         "for l in range(cfg.num_layers):\n"
         "    for n in ('input_layernorm', 'post_attention_layernorm'):\n"
         "        norms[f'model.layers.{l}.{n}.weight'] = oracle.round_bf16("
-        "(1 + 0.25 * rng.standard_normal(1024)).astype(np.float32))\n"
+        "(1 + 0.25 * rng.standard_normal(H)).astype(np.float32))\n"
         "ref = oracle_model(cfg, seed=9, replace=norms)\n"
         f"prompts = rng.integers(0, cfg.vocab_size, ({batch}, 20))\n"
         "s = ffm.B200Session(0, 8 << 30)\n"
@@ -385,6 +390,6 @@ def test_skinny_decode_with_fused_prologues(batch, fuse):
         "    c.close()\n"
         "s.close()\n"
         "print('ok')\n")
-    env = dict(os.environ, STB_SKINNY_MIN_WORK="0", STB_FUSE_NEXT=str(fuse))
+    env = dict(os.environ, STB_SKINNY_MIN_WORK="0", STB_FUSE_NEXT=str(fuse), STB_FUSE_ATT=str(fuse))
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
