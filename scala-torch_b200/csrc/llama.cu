@@ -19,7 +19,10 @@
 // previous kernel: the attention merge writes the o projection's activation terms, the o fixup adds
 // the residual and does the post-attention RMSNorm and split for gate/up, the gate/up fixup writes
 // SiLU(gate)*up as the down projection's terms, and the down fixup adds the residual and does the
-// next layer's input RMSNorm and split -- 9 launches per layer instead of 13.
+// next layer's input RMSNorm and split -- 9 launches per layer instead of 13.  With 5 to 8 query heads
+// per KV head the attention also takes over the QKV fixup (RoPE, cache append) and its own split
+// merge (attention_decode.cu): 8 launches per layer -- QKV GEMM, attention, o GEMM + fixup, gate/up
+// GEMM + fixup, down GEMM + fixup.
 //
 // Tensor parallel (tp_size > 1): q/k/v/gate/up are split by output rows (heads / intermediate),
 // o/down by input columns; each row-split projection's partial sums are joined by one NCCL
