@@ -436,129 +436,146 @@ __global__ void __launch_bounds__(256) skinny_fixup_kernel(const GemvParams p, c
 // so the next GEMM starts on them without a prologue launch of its own.
 
 // SiLU(gate) * up of the interleaved gate/up projection (EPI_SILU's expression), split into three BF16
-// terms for the down projection (Kn = N / 2).  One thread per (token row, unit); blockIdx.y < NT.
+// terms for the down projection (Kn = N / 2).  Thread (token row, units 4 u .. 4 u + 3): the 8
+// interleaved projection rows of its 4 units are two float4 per stream-K piece, every piece's loads in
+// flight together; one 8-byte store per term.  blockIdx.y < NT; rows mb .. NT - 1 get zeros.
 __global__ void __launch_bounds__(256) skinny_fixup_silu_split_kernel(const float *part, int N, int kbs, long long T,
                                                                       int G, int pmax, int mb, uint16_t *x3n,
                                                                       int NT) {
   pdl_wait();
-  pdl_trigger();
   const int m = blockIdx.y, units = N / 2;
-  const int u = blockIdx.x * 256 + threadIdx.x;
-  if (u >= units) return;
-  float v = 0.0f;
+  const int u0 = 4 * (blockIdx.x * 256 + threadIdx.x);
+  if (u0 >= units) return;
+  float f[4] = {0.f, 0.f, 0.f, 0.f};
   if (m < mb) {
-    const float gate = sk_gather(part, m, 2 * u, mb, kbs, T, G, pmax);
-    const float up = sk_gather(part, m, 2 * u + 1, mb, kbs, T, G, pmax);
-    v = silu_ref(gate) * up;
+    const int row = 2 * u0, t = row / SK_BM;  // 8 rows, within one 128-row tile
+    const int first = sk_cta_of((long long)t * kbs, T, G);
+    const int n = sk_cta_of((long long)(t + 1) * kbs - 1, T, G) - first + 1;
+    const float *pp = part + ((size_t)t * pmax * mb + m) * SK_BM + (row % SK_BM);
+    const size_t stride = (size_t)mb * SK_BM;
+    float4 w[4][2];
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+      if (q < n) {
+        w[q][0] = __ldcg((const float4 *)(pp + q * stride));
+        w[q][1] = __ldcg((const float4 *)(pp + q * stride + 4));
+      }
+    float4 a = w[0][0], b = w[0][1];
+#pragma unroll
+    for (int q = 1; q < 4; q++)
+      if (q < n) {
+        a.x = a.x + w[q][0].x; a.y = a.y + w[q][0].y; a.z = a.z + w[q][0].z; a.w = a.w + w[q][0].w;
+        b.x = b.x + w[q][1].x; b.y = b.y + w[q][1].y; b.z = b.z + w[q][1].z; b.w = b.w + w[q][1].w;
+      }
+    for (int q = 4; q < n; q++) {  // more than four pieces: one round trip each
+      const float4 c = __ldcg((const float4 *)(pp + q * stride)), d = __ldcg((const float4 *)(pp + q * stride + 4));
+      a.x = a.x + c.x; a.y = a.y + c.y; a.z = a.z + c.z; a.w = a.w + c.w;
+      b.x = b.x + d.x; b.y = b.y + d.y; b.z = b.z + d.z; b.w = b.w + d.w;
+    }
+    f[0] = silu_ref(a.x) * a.y;  // (gate, up) pairs
+    f[1] = silu_ref(a.z) * a.w;
+    f[2] = silu_ref(b.x) * b.y;
+    f[3] = silu_ref(b.z) * b.w;
   }
-  uint16_t h0, h1, h2;
-  split3_bf16(v, h0, h1, h2);
-  x3n[((size_t)0 * NT + m) * units + u] = h0;
-  x3n[((size_t)1 * NT + m) * units + u] = h1;
-  x3n[((size_t)2 * NT + m) * units + u] = h2;
+  pdl_trigger();  // after this thread's loads: the next GEMM's weight stream would delay them
+  uint16_t h[3][4];
+#pragma unroll
+  for (int e = 0; e < 4; e++) split3_bf16(f[e], h[0][e], h[1][e], h[2][e]);
+#pragma unroll
+  for (int tm = 0; tm < 3; tm++) {
+    uint2 v;
+    v.x = (uint32_t)h[tm][0] | ((uint32_t)h[tm][1] << 16);
+    v.y = (uint32_t)h[tm][2] | ((uint32_t)h[tm][3] << 16);
+    *(uint2 *)(x3n + ((size_t)tm * NT + m) * units + u0) = v;
+  }
 }
 
-constexpr int SK_NORM_THREADS = 512, SK_NORM_V4 = 4;  // rows of up to 512 x 4 x 4 = 8192 values
+constexpr int SK_NORM_CTAS = 8, SK_NORM_THREADS = 256;  // a cluster per row: 8 x 256 x 4 = 8192 values
+
+__device__ __forceinline__ double ld_cluster_f64(uint32_t cluster_addr) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
 
 // The residual projection's fixup (EPI_RESID: y = residual + sum of the pieces in piece order) and the
-// next projection's RMSNorm prologue on the updated row, one block per token row: the row stays in
-// registers between the residual add, the sum of squares (double, each thread's values in index
-// order, then the block's fixed-order reduction) and the scaling with the GEMV's expression; the
-// normalised row is split into three BF16 terms (Kn = N).  Blocks m >= mb write zero rows.
-__global__ void __launch_bounds__(SK_NORM_THREADS) skinny_fixup_norm_kernel(
+// next projection's RMSNorm prologue on the updated row.  A cluster of 8 CTAs per token row, one float4
+// of the row per thread (every load in flight together); each CTA reduces its sum of squares (double,
+// the block's fixed order) and the row's total is its CTAs' sums added in cluster-rank order through
+// distributed shared memory; then each thread scales its values with the GEMV's expression and writes
+// their three BF16 terms (Kn = N).  Clusters of rows m >= mb write zero rows.
+__global__ void __cluster_dims__(SK_NORM_CTAS, 1, 1) __launch_bounds__(SK_NORM_THREADS) skinny_fixup_norm_kernel(
     const GemvParams p, const float *part, int kbs, long long T, int G, int pmax, int mb, const float *norm_w,
     double eps, uint16_t *x3n, int NT) {
   __shared__ double s_scratch[SK_NORM_THREADS / 32];
+  __shared__ double s_cta, s_total;
   pdl_wait();
-  const int m = blockIdx.x, mg = m;  // one 64-row block: its rows are the problem's own
+  const int m = blockIdx.y, mg = m;  // one 64-row block: its rows are the problem's own
   const int N = p.N, n4 = N / 4;
-  const size_t stride = (size_t)mb * SK_BM;
-  float4 v[SK_NORM_V4], nw[SK_NORM_V4];
-#pragma unroll
-  for (int j = 0; j < SK_NORM_V4; j++) v[j] = nw[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int c = blockIdx.x * SK_NORM_THREADS + threadIdx.x;  // float4 of the row
+  const bool live = m < mb && c < n4;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f), nw = v;
   double sq = 0.0;
-  if (m < mb) {
-    // every load of the thread in flight together: per four-row group (a group never straddles a
-    // 128-row tile) the residual (into v) and the first four pieces; the pieces are added in piece
-    // order, then the residual
-    const float *pp[SK_NORM_V4];
-    int np[SK_NORM_V4];
-    float4 w[SK_NORM_V4][4];
+  if (live) {
+    const int row = 4 * c, t = row / SK_BM;  // a four-row group never straddles a 128-row tile
+    const int n = sk_cta_of((long long)(t + 1) * kbs - 1, T, G) - sk_cta_of((long long)t * kbs, T, G) + 1;
+    const float *pp = part + ((size_t)t * pmax * mb + m) * SK_BM + (row % SK_BM);
+    const size_t stride = (size_t)mb * SK_BM;
+    v = *(const float4 *)(p.residual + (size_t)mg * p.ldr + row);
+    nw = *(const float4 *)(norm_w + row);
+    float4 w[4];
 #pragma unroll
-    for (int j = 0; j < SK_NORM_V4; j++) {
-      const int c = threadIdx.x + j * SK_NORM_THREADS;
-      np[j] = 0;
-      if (c < n4) {
-        const int row = 4 * c, t = row / SK_BM;
-        np[j] = sk_cta_of((long long)(t + 1) * kbs - 1, T, G) - sk_cta_of((long long)t * kbs, T, G) + 1;
-        pp[j] = part + ((size_t)t * pmax * mb + m) * SK_BM + (row % SK_BM);
-        v[j] = *(const float4 *)(p.residual + (size_t)mg * p.ldr + row);
+    for (int q = 0; q < 4; q++)
+      if (q < n) w[q] = __ldcg((const float4 *)(pp + q * stride));
+    float4 acc = w[0];
 #pragma unroll
-        for (int q = 0; q < 4; q++)
-          if (q < np[j]) w[j][q] = __ldcg((const float4 *)(pp[j] + (size_t)q * stride));
+    for (int q = 1; q < 4; q++)
+      if (q < n) {
+        acc.x = acc.x + w[q].x; acc.y = acc.y + w[q].y; acc.z = acc.z + w[q].z; acc.w = acc.w + w[q].w;
       }
+    for (int q = 4; q < n; q++) {  // more than four pieces: one round trip each
+      const float4 x = __ldcg((const float4 *)(pp + q * stride));
+      acc.x = acc.x + x.x; acc.y = acc.y + x.y; acc.z = acc.z + x.z; acc.w = acc.w + x.w;
     }
-#pragma unroll
-    for (int j = 0; j < SK_NORM_V4; j++) {
-      const int c = threadIdx.x + j * SK_NORM_THREADS;
-      if (c >= n4) break;
-      float4 acc = w[j][0];
-#pragma unroll
-      for (int q = 1; q < 4; q++) {
-        if (q < np[j]) {
-          acc.x = acc.x + w[j][q].x;
-          acc.y = acc.y + w[j][q].y;
-          acc.z = acc.z + w[j][q].z;
-          acc.w = acc.w + w[j][q].w;
-        }
-      }
-      for (int q = 4; q < np[j]; q++) {  // more than four pieces: one more round trip each
-        const float4 x = __ldcg((const float4 *)(pp[j] + (size_t)q * stride));
-        acc.x = acc.x + x.x;
-        acc.y = acc.y + x.y;
-        acc.z = acc.z + x.z;
-        acc.w = acc.w + x.w;
-      }
-      v[j] = make_float4(v[j].x + acc.x, v[j].y + acc.y, v[j].z + acc.z, v[j].w + acc.w);
-      *(float4 *)(p.y + (size_t)mg * p.ldy + 4 * c) = v[j];
-      const double a = v[j].x, b = v[j].y, cc = v[j].z, d = v[j].w;
-      sq = __dadd_rn(sq, __dmul_rn(a, a));
-      sq = __dadd_rn(sq, __dmul_rn(b, b));
-      sq = __dadd_rn(sq, __dmul_rn(cc, cc));
-      sq = __dadd_rn(sq, __dmul_rn(d, d));
-    }
+    v = make_float4(v.x + acc.x, v.y + acc.y, v.z + acc.z, v.w + acc.w);
+    *(float4 *)(p.y + (size_t)mg * p.ldy + row) = v;
+    const double a = v.x, b = v.y, cc = v.z, d = v.w;
+    sq = __dadd_rn(sq, __dmul_rn(a, a));
+    sq = __dadd_rn(sq, __dmul_rn(b, b));
+    sq = __dadd_rn(sq, __dmul_rn(cc, cc));
+    sq = __dadd_rn(sq, __dmul_rn(d, d));
   }
-  // The next GEMM's CTAs start streaming weights once every block triggers: after this block's
-  // loads of the pieces (triggering at entry measured slower: the weight stream delays these loads).
+  // The next GEMM's CTAs start streaming weights once every block triggers: after this block's loads
+  // (triggering at entry measured slower: the weight stream delays these loads).
   pdl_trigger();
-  if (m < mb) {  // the norm weights, in flight during the block's reduction
-#pragma unroll
-    for (int j = 0; j < SK_NORM_V4; j++) {
-      const int c = threadIdx.x + j * SK_NORM_THREADS;
-      if (c < n4) nw[j] = *(const float4 *)(norm_w + 4 * c);
+  double inv = 0.0;
+  if (m < mb) {  // uniform over the cluster (one row)
+    const double bs = block_sum_double(sq, s_scratch);
+    if (threadIdx.x == 0) s_cta = bs;
+    cluster_sync_all();  // every CTA's sum is in its shared memory
+    if (threadIdx.x == 0) {
+      double total = 0.0;
+      const uint32_t a = smem_u32(&s_cta);
+      for (int r = 0; r < SK_NORM_CTAS; r++) total += ld_cluster_f64(map_to_rank(a, (uint32_t)r));
+      s_total = total;
     }
+    cluster_sync_all();  // no CTA leaves while its sum may still be read; s_total visible in the CTA
+    inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s_total, (double)N), eps)));
   }
-  const double total = block_sum_double(sq, s_scratch);  // uniform: every thread reaches it
-  const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(total, (double)N), eps)));
+  if (c >= n4) return;
+  const float f[4] = {v.x, v.y, v.z, v.w}, nws[4] = {nw.x, nw.y, nw.z, nw.w};
+  uint16_t h[3][4];
 #pragma unroll
-  for (int j = 0; j < SK_NORM_V4; j++) {
-    const int c = threadIdx.x + j * SK_NORM_THREADS;
-    if (c >= n4) break;
-    const float f[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-    uint16_t h[3][4];
-    const float nws[4] = {nw[j].x, nw[j].y, nw[j].z, nw[j].w};
+  for (int e = 0; e < 4; e++) {
+    const float g = m < mb ? __double2float_rn(__dmul_rn(__dmul_rn((double)f[e], inv), (double)nws[e])) : 0.0f;
+    split3_bf16(g, h[0][e], h[1][e], h[2][e]);
+  }
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      const float g = m < mb ? __double2float_rn(__dmul_rn(__dmul_rn((double)f[e], inv), (double)nws[e])) : 0.0f;
-      split3_bf16(g, h[0][e], h[1][e], h[2][e]);
-    }
-#pragma unroll
-    for (int tm = 0; tm < 3; tm++) {
-      uint2 u;
-      u.x = (uint32_t)h[tm][0] | ((uint32_t)h[tm][1] << 16);
-      u.y = (uint32_t)h[tm][2] | ((uint32_t)h[tm][3] << 16);
-      *(uint2 *)(x3n + ((size_t)tm * NT + m) * N + 4 * c) = u;
-    }
+  for (int tm = 0; tm < 3; tm++) {
+    uint2 u;
+    u.x = (uint32_t)h[tm][0] | ((uint32_t)h[tm][1] << 16);
+    u.y = (uint32_t)h[tm][2] | ((uint32_t)h[tm][3] << 16);
+    *(uint2 *)(x3n + ((size_t)tm * NT + m) * N + 4 * c) = u;
   }
 }
 
@@ -634,7 +651,7 @@ uint64_t skinny_scratch_bytes(int M, int N, int K, int device) {
 
 int skinny_nt(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
-bool skinny_norm_fusable(int N) { return N % 4 == 0 && N <= SK_NORM_THREADS * SK_NORM_V4 * 4; }
+bool skinny_norm_fusable(int N) { return N % 4 == 0 && N <= SK_NORM_CTAS * SK_NORM_THREADS * 4; }
 
 template <int EPI>
 int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, int *err, int device,
@@ -648,9 +665,10 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
               "skinny Linear scratch too small");
   if (next) {
     STB_REQUIRE(p.M <= 64 && next->x3 && ((uintptr_t)next->x3 % 16) == 0, "fused next prologue: one block");
-    STB_REQUIRE(EPI == EPI_SILU || (EPI == EPI_RESID && next->norm_w && p.N % 4 == 0 &&
-                                    p.N <= SK_NORM_THREADS * SK_NORM_V4 * 4 && p.ldy % 4 == 0 && p.ldr % 4 == 0),
-                "fused next prologue: SiLU split, or residual + RMSNorm on rows of at most 8192 values");
+    STB_REQUIRE((EPI == EPI_SILU && p.N % 8 == 0) ||
+                    (EPI == EPI_RESID && next->norm_w && skinny_norm_fusable(p.N) && p.ldy % 4 == 0 && p.ldr % 4 == 0),
+                "fused next prologue: SiLU split (N a multiple of 8), or residual + RMSNorm on rows of at most 8192 "
+                "values");
   }
   const CUtensorMap tw = make_map(p.w, STB_BF16, (uint64_t)p.N, (uint64_t)p.K, SK_BM);
   constexpr bool paired = EPI == EPI_SILU || EPI == EPI_QKV;
@@ -681,10 +699,10 @@ int skinny_launch(const GemvParams &p, void *scratch, uint64_t scratch_bytes, in
       continue;
     }
     if (next && EPI == EPI_SILU)
-      launch_kernel(skinny_fixup_silu_split_kernel, dim3((units + 255) / 256, q.nt), dim3(256), 0, stream, true,
+      launch_kernel(skinny_fixup_silu_split_kernel, dim3((units / 4 + 255) / 256, q.nt), dim3(256), 0, stream, true,
                     (const float *)part, p.N, q.kbs, q.iters, q.grid, q.pmax, mb, next->x3, q.nt);
     else if (next)
-      launch_kernel(skinny_fixup_norm_kernel, dim3(q.nt), dim3(SK_NORM_THREADS), 0, stream, true, p,
+      launch_kernel(skinny_fixup_norm_kernel, dim3(SK_NORM_CTAS, q.nt), dim3(SK_NORM_THREADS), 0, stream, true, p,
                     (const float *)part, q.kbs, q.iters, q.grid, q.pmax, mb, next->norm_w, next->eps, next->x3, q.nt);
     else
       launch_kernel(skinny_fixup_kernel<EPI>, dim3((units + 255) / 256, mb), dim3(256), 0, stream, true, p,
