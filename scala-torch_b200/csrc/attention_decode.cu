@@ -5,7 +5,7 @@
 // The reference's causal grouped-query attention (cpu/src/main/scala/scalatorch/cpu/
 // CpuAttention.scala:20-50) for one new token per batch row: scores of the query against every
 // visible key, softmax, weighted sum of the values.  On the GPU each (batch row, KV head) pair's
-// visible keys are cut into splits of `kps` keys (a multiple of 32, chosen from the cache capacity
+// visible keys are cut into splits of `kps` keys (a multiple of 8, chosen from the cache capacity
 // so that about two blocks per SM cover all pairs: every block is resident at once, no second
 // wave).  Block (split, KV head, row), 256 threads, streams its split's K rows and then its V rows
 // in chunks of 32 keys (16 KB) through a 5-stage ring:
@@ -708,11 +708,13 @@ __global__ void __launch_bounds__(256) attention_merge_split_kernel(
 }  // namespace
 
 DecodeStreamPlan decode_stream_plan(int rows, int kvh, int capacity, int device) {
-  static const int forced = env_int("STB_DS_KPS", 0);  // keys per split, a multiple of 32 up to 256
+  static const int forced = env_int("STB_DS_KPS", 0);  // keys per split, a multiple of 8 up to 256
   const int pairs = rows * kvh;
   const int splits = std::max(1, 2 * sm_count(device) / std::max(pairs, 1));
-  int kps = ((capacity + splits - 1) / splits + DS_CH - 1) / DS_CH * DS_CH;
-  if (forced > 0 && forced % DS_CH == 0) kps = forced;
+  // equal splits (rounded to 8 keys, not to whole 32-key chunks: the last chunk of a split is partly
+  // masked), so the SMs that hold two blocks carry as few keys as possible
+  int kps = ((capacity + splits - 1) / splits + 7) / 8 * 8;
+  if (forced > 0 && forced % 8 == 0) kps = forced;
   kps = std::min(std::max(kps, DS_CH), DS_KPS_MAX);
   DecodeStreamPlan p;
   p.kps = kps;

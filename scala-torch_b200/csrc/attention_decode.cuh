@@ -8,7 +8,7 @@
 
 namespace stb {
 
-// Keys per split (a multiple of 32, at most 256) and the grid's split count for a cache capacity.
+// Keys per split (a multiple of 8, 32 .. 256) and the grid's split count for a cache capacity.
 struct DecodeStreamPlan {
   int kps = 32, smax = 1;
 };

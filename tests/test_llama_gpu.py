@@ -283,6 +283,7 @@ HD128 = dict(vocab_size=512, hidden_size=1024, intermediate_size=256, num_layers
 
 @pytest.mark.parametrize("stream,impl,kps,hd128,heads,kvh,g8", [
     (1, 1, 0, 1, 8, 1, 1), (1, 1, 32, 1, 8, 1, 1), (1, 1, 64, 1, 6, 1, 1), (1, 1, 96, 1, 5, 1, 1),
+    (1, 1, 40, 1, 8, 1, 1), (1, 1, 72, 1, 8, 2, 1),
     (1, 1, 32, 1, 8, 1, 0), (1, 1, 64, 1, 8, 2, 1), (1, 1, 96, 1, 6, 2, 1), (1, 1, 32, 1, 4, 4, 1),
     (0, 1, 32, 1, 8, 1, 1), (0, 1, 64, 1, 8, 1, 1), (0, 1, 128, 1, 8, 1, 1), (0, 1, 64, 0, 8, 1, 1),
     (0, 0, 0, 1, 8, 1, 1), (0, 1, 64, 1, 8, 2, 1), (0, 1, 32, 1, 6, 2, 1)])
@@ -290,7 +291,8 @@ def test_decode_attention_splits_head128(stream, impl, kps, hd128, heads, kvh, g
     """The decode attention on head size 128 with 8, 6, 5, 4, 3 and 1 query heads per KV head: the streamed
     form (decode_attention_stream_g8_kernel for 5 to 8 heads per KV head, or decode_attention_stream_kernel
     with STB_DS_G8=0 and for smaller groups, + the merge in the o projection's prologue) with its keys per
-    split left to the plan or forced to 32 / 64 / 96 (STB_DS_KPS), and with STB_DECODE_STREAM=0 the split forms
+    split left to the plan or forced to 32 / 40 / 64 / 72 / 96 (STB_DS_KPS; 40 and 72 end splits inside a
+    32-key chunk), and with STB_DECODE_STREAM=0 the split forms
     (decode_attention_hd128_kernel, and decode_attention_kernel with STB_DA_HD128=0) with keys per split
     forced to 32 / 64 / 128 (STB_DA_KPS) and the register form (STB_DA_IMPL) -- variables read once per
     process: a child process each -- over 127 prompt tokens
