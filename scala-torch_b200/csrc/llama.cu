@@ -49,6 +49,9 @@ void round_activations(const float *x, uint16_t *out, size_t count, int dtype, c
 bool peer_usable(stb_session *s, uint64_t elems);
 PeerArgs peer_args(stb_session *s, int region);
 void peer_reduce_launch(stb_session *s, int region, long total, const float *residual, float *out);
+bool peer_norm_fusable(int H);
+void peer_reduce_norm_launch(stb_session *s, int region, int rows, int H, const float *residual, float *out,
+                             const float *norm_w, double eps, uint16_t *x3n, int NT);
 void peer_reset(stb_session *s);
 bool launch_flash_attention_tc(const float *q, int ldq, const float *kc, const float *vc, float *out, int ldo,
                                int rows, int count, int nh, int kvh, int hd, int capacity, const int *posd, int pos0,
@@ -102,7 +105,7 @@ struct stb_llama_cache {
   // paired q/k/v projection, interleaved gate/up projection
   uint64_t xn = 0, xh = 0, qkvbuf = 0, gubuf = 0;
   uint64_t skin = 0, skin_bytes = 0;  // tensor-core skinny path scratch (one 64-row block)
-  uint64_t skin_next = 0;             // next projection's activation terms written by a fused fixup (TP1)
+  uint64_t skin_next = 0;             // next projection's activation terms written by a fused fixup
   uint64_t att_part = 0, att_count = 0;  // split decode attention records and counters (batch rows)
   CUtensorMap kv_map;                    // the whole K/V cache as rows of hd Float32 (streamed attention)
   bool kv_map_ok = false;
@@ -1588,8 +1591,8 @@ void ensure_rows(stb_llama_cache *c, int rows) {
       c->skin = alloc_owned(s, c->owned, need);
       c->skin_bytes = need;
       skinny_prepare(s->device);
-      if (m->tp == 1)  // terms [3][NT][K] of the widest K a fused fixup writes (hidden or intermediate)
-        c->skin_next = alloc_owned(s, c->owned, (uint64_t)3 * skinny_nt(sm) * std::max(m->H, m->I) * 2);
+      // terms [3][NT][K] of the widest K a fused fixup writes (hidden or intermediate)
+      c->skin_next = alloc_owned(s, c->owned, (uint64_t)3 * skinny_nt(sm) * std::max(m->H, m->I) * 2);
     }
   }
   session_error_word(s);  // allocated now, not inside a graph capture
@@ -1738,12 +1741,13 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
   const size_t kv_half = kv_layer / 2;
   const int qw = m->NH * m->hd;
   const bool tensor_cores = rows >= m->tc_rows && c->xh != 0;
-  // Single-GPU chunks of up to 64 rows on the skinny form: the o, gate/up and down fixups also write
-  // the next projection's activation terms (RMSNorm and split, SiLU*up and split), whose prologue
-  // launch is then skipped.  `pending` holds those terms for the next projection.
+  // Chunks of up to 64 rows on the skinny form: the o, gate/up and down fixups (under tensor
+  // parallelism: the gate/up fixup and the peer reduces) also write the next projection's activation
+  // terms (RMSNorm and split, SiLU*up and split), whose prologue launch is then skipped.  `pending`
+  // holds those terms for the next projection.
   static const int fuse_enabled = env_int("STB_FUSE_NEXT", 1);
-  const bool fuse_next = fuse_enabled && m->tp == 1 && c->skin_next && rows <= 64 && !tensor_cores;
-  const bool fuse_norm = fuse_next && skinny_norm_fusable(H);
+  const bool fuse_next = fuse_enabled && c->skin_next && rows <= 64 && !tensor_cores;
+  const bool fuse_norm = fuse_next && (m->tp == 1 ? skinny_norm_fusable(H) : peer_norm_fusable(H));
   const uint16_t *pending = nullptr;
   SkinnyNext next;
   next.x3 = (uint16_t *)c->skin_next;
@@ -1871,21 +1875,31 @@ int enqueue_step(stb_llama_cache *c, const StepArgs &a) {
         p.ldy = H;
         p.peer = peer_args(s, half);
         const GemvConfig cfg = choose_gemv(rows, p.N, p.K, false);
-        launches += project<EPI_PEER>(c, p, wdt, cfg, st, half == 0 && o_x3 ? (const uint16_t *)c->skin : nullptr);
-        peer_reduce_launch(s, half, (long)rows * H, (const float *)c->hidden, (float *)c->hidden);
+        const uint16_t *x3 = half == 0 ? (o_x3 ? (const uint16_t *)c->skin : nullptr) : pending;
+        launches += project<EPI_PEER>(c, p, wdt, cfg, st, x3);
+        // o: the reduce also does the gate/up projection's RMSNorm prologue; down: the next layer's
+        const bool fuse = fuse_norm && (half == 0 ? o_sk && gu_sk : down_sk && qkv_next_sk);
+        if (fuse) {
+          const float *nw = half == 0 ? (const float *)L.post_norm : (const float *)m->layers[l + 1].in_norm;
+          peer_reduce_norm_launch(s, half, rows, H, (const float *)c->hidden, (float *)c->hidden, nw,
+                                  m->c.rms_norm_eps, next.x3, skinny_nt(rows));
+        } else {
+          peer_reduce_launch(s, half, (long)rows * H, (const float *)c->hidden, (float *)c->hidden);
+        }
+        pending = fuse ? next.x3 : nullptr;
         launches++;
       } else {
         p.y = (float *)c->sum; p.ldy = H;
+        const uint16_t *x3 = half == 0 ? (o_x3 ? (const uint16_t *)c->skin : nullptr) : pending;
         if (m->rank == 0) {
           p.residual = (const float *)c->hidden; p.ldr = H;
-          launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st,
-                                         half == 0 && o_x3 ? (const uint16_t *)c->skin : nullptr);
+          launches += project<EPI_RESID>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, x3);
         } else {
-          launches += project<EPI_PLAIN>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st,
-                                         half == 0 && o_x3 ? (const uint16_t *)c->skin : nullptr);
+          launches += project<EPI_PLAIN>(c, p, wdt, choose_gemv(rows, p.N, p.K, false), st, x3);
         }
         allreduce_sum_f32(s, (void *)c->sum, (uint64_t)rows * H);
         std::swap(c->hidden, c->sum);
+        pending = nullptr;
       }
     }
   }

@@ -6,7 +6,9 @@
 #include <cstring>
 #include <vector>
 
+#include "gemv.cuh"
 #include "peer.cuh"
+#include "tc_common.cuh"
 
 namespace stb {
 
@@ -155,6 +157,133 @@ void peer_reduce_launch(stb_session *s, int region, long total, const float *res
   long blocks = (total + 255) / 256;
   if (blocks > 148) blocks = 148;
   launch_kernel(peer_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, s->stream, true, pa, total, residual, out);
+}
+
+// peer_reduce_kernel and the next projection's RMSNorm prologue in one (decode chunks of up to 64 rows
+// on the skinny form): a cluster of 8 CTAs per token row, one float4 of the row per thread.  Every slot
+// word of the thread is loaded at once (one round trip when the peers' stores have landed; words of an
+// older use are then waited for one by one, bounded), the slots are added in rank order and the
+// residual after them as peer_reduce_kernel does; the CTAs' double sums of squares are added in rank
+// order through distributed shared memory, and each thread writes the three BF16 terms of its
+// normalised values (the GEMV's expression) into x3n [3][NT][H].  Rows >= rows get zero terms.  The
+// last block to finish advances the region's epoch.
+constexpr int PR_CTAS = 8, PR_THREADS = 256;
+
+__device__ __forceinline__ double pr_ld_cluster_f64(uint32_t cluster_addr) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
+__global__ void __cluster_dims__(PR_CTAS, 1, 1) __launch_bounds__(PR_THREADS) peer_reduce_norm_kernel(
+    PeerArgs pa, int rows, int H, const float *residual, float *out, const float *norm_w, double eps, uint16_t *x3n,
+    int NT) {
+  __shared__ double s_scratch[PR_THREADS / 32];
+  __shared__ double s_cta, s_total;
+  pdl_wait();
+  const uint32_t use = (uint32_t)(pa.my_epoch[pa.region] + 1ull);
+  const unsigned long long *base = pa.my_slots + (size_t)pa.region * pa.tp * pa.slot_elems;
+  const int m = blockIdx.y, n4 = H / 4;
+  const int c = blockIdx.x * PR_THREADS + threadIdx.x;  // float4 of the row
+  const bool live = m < rows && c < n4;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f), nw = v;
+  double sq = 0.0;
+  bool ok = true;
+  if (live) {
+    const size_t i0 = (size_t)m * H + 4 * c;
+    unsigned long long w[kMaxPeers][4];
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; r++)
+      if (r < pa.tp)
+#pragma unroll
+        for (int e = 0; e < 4; e++) w[r][e] = peer_load(base + (size_t)r * pa.slot_elems + i0 + e);
+    v = *(const float4 *)(residual + i0);
+    nw = *(const float4 *)(norm_w + 4 * c);
+    float a[4];
+    bool ready = true;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; r++) {
+        if (r < pa.tp) {
+          ready = ready && (uint32_t)(w[r][e] >> 32) == use;
+          const float x = __uint_as_float((uint32_t)w[r][e]);
+          acc = r == 0 ? x : acc + x;
+        }
+      }
+      a[e] = acc;
+    }
+    if (!ready) {  // some peer's words of this use had not landed: wait for each (bounded), same order
+      for (int e = 0; e < 4; e++) {
+        float acc = 0.0f;
+        for (int r = 0; r < pa.tp; r++) {
+          const float x = peer_take(base + (size_t)r * pa.slot_elems + i0 + e, use, pa.wait_ns, pa.err,
+                                    16 + pa.region, &ok);
+          acc = r == 0 ? x : acc + x;
+        }
+        a[e] = acc;
+      }
+    }
+    v = make_float4(v.x + a[0], v.y + a[1], v.z + a[2], v.w + a[3]);
+    *(float4 *)(out + i0) = v;
+    const double d0 = v.x, d1 = v.y, d2 = v.z, d3 = v.w;
+    sq = __dadd_rn(sq, __dmul_rn(d0, d0));
+    sq = __dadd_rn(sq, __dmul_rn(d1, d1));
+    sq = __dadd_rn(sq, __dmul_rn(d2, d2));
+    sq = __dadd_rn(sq, __dmul_rn(d3, d3));
+  }
+  pdl_trigger();  // after this thread's loads: the next GEMM's weight stream would delay them
+  double inv = 0.0;
+  if (m < rows) {  // uniform over the cluster (one row)
+    const double bs = block_sum_double(sq, s_scratch);
+    if (threadIdx.x == 0) s_cta = bs;
+    tc::cluster_sync_all();  // every CTA's sum is in its shared memory
+    if (threadIdx.x == 0) {
+      double total = 0.0;
+      const uint32_t sa = tc::smem_u32(&s_cta);
+      for (int r = 0; r < PR_CTAS; r++) total += pr_ld_cluster_f64(tc::map_to_rank(sa, (uint32_t)r));
+      s_total = total;
+    }
+    tc::cluster_sync_all();  // no CTA leaves while its sum may still be read; s_total visible in the CTA
+    inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(s_total, (double)H), eps)));
+  }
+  if (c < n4) {
+    const float f[4] = {v.x, v.y, v.z, v.w}, nws[4] = {nw.x, nw.y, nw.z, nw.w};
+    uint16_t h[3][4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float g = m < rows ? __double2float_rn(__dmul_rn(__dmul_rn((double)f[e], inv), (double)nws[e])) : 0.0f;
+      split3_bf16(g, h[0][e], h[1][e], h[2][e]);
+    }
+#pragma unroll
+    for (int tm = 0; tm < 3; tm++) {
+      uint2 u;
+      u.x = (uint32_t)h[tm][0] | ((uint32_t)h[tm][1] << 16);
+      u.y = (uint32_t)h[tm][2] | ((uint32_t)h[tm][3] << 16);
+      *(uint2 *)(x3n + ((size_t)tm * NT + m) * H + 4 * c) = u;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(pa.my_done + pa.region, 1u);
+    if (prev == gridDim.x * gridDim.y - 1) {
+      pa.my_done[pa.region] = 0u;
+      pa.my_epoch[pa.region] += 1ull;
+      __threadfence();
+    }
+  }
+}
+
+bool peer_norm_fusable(int H) { return H % 4 == 0 && H <= PR_CTAS * PR_THREADS * 4; }
+
+void peer_reduce_norm_launch(stb_session *s, int region, int rows, int H, const float *residual, float *out,
+                             const float *norm_w, double eps, uint16_t *x3n, int NT) {
+  STB_REQUIRE(rows >= 1 && rows <= NT && peer_norm_fusable(H) && x3n && norm_w, "fused peer reduce + RMSNorm shape");
+  PeerArgs pa = peer_args(s, region);
+  launch_kernel(peer_reduce_norm_kernel, dim3(PR_CTAS, NT), dim3(PR_THREADS), 0, s->stream, true, pa, rows, H, residual,
+                out, norm_w, eps, x3n, NT);
 }
 
 __global__ void wait_probe_kernel(const unsigned long long *counter, unsigned long long wait_ns, int *err) {
