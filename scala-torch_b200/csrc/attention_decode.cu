@@ -352,7 +352,7 @@ __device__ __forceinline__ void ds_merge4(const float *po, const float *ml, size
 //     of all 8 heads (32 accumulators; one 16-byte V load and two broadcast loads of the 8 weights per
 //     key), and the 8 warps' sums are added in warp order at the end through the (then idle) ring.
 constexpr size_t DS8_SMEM = 1024 + (size_t)DS_RING * DS_CHUNK + (size_t)DS_KPS_MAX * DS_GMAX * 4 +
-                            DS_GMAX * 2 * 4 + (size_t)(DS_GMAX + 2) * DS_HD * 4 + DS_RING * 8;
+                            DS_GMAX * 2 * 4 + (size_t)(DS_GMAX + 2) * DS_HD * 4 + 2 * DS_RING * 8;
 static_assert(DS_RING * DS_CHUNK >= DS_WARPS * DS_GMAX * DS_HD * 4, "the ring holds the warps' value sums");
 
 // FUSED: the QKV projection's fixup and the split merge happen here too (see DecodeStreamFused): q, and
@@ -369,8 +369,8 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kern
   float *pt = (float *)(ring + DS_RING * DS_CHUNK);  // [kps][8]: scores, then exp(score - max)
   float *red = pt + DS_KPS_MAX * DS_GMAX;            // [8][2]: max, sum
   float *Qs = red + DS_GMAX * 2;                     // FUSED: [8][128] query rows, then the newest k and v rows
-  uint64_t *bar = (uint64_t *)(Qs + (DS_GMAX + 2) * DS_HD);  // [DS_RING]
-  __shared__ int s_ok, s_last;
+  uint64_t *bar = (uint64_t *)(Qs + (DS_GMAX + 2) * DS_HD);  // [DS_RING] full, then [DS_RING] empty
+  __shared__ int s_last;
   __shared__ volatile int s_abort;
   pdl_trigger();
   const int split = blockIdx.x, g0 = blockIdx.y, m = blockIdx.z;
@@ -405,7 +405,10 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kern
   };
   if (tid == 0) {
     s_abort = 0;
-    for (int st = 0; st < DS_RING; st++) mbar_init(bar0 + 8 * st, 1);
+    for (int st = 0; st < DS_RING; st++) {
+      mbar_init(bar0 + 8 * st, 1);                            // full: the copies' bytes
+      mbar_init(bar0 + 8 * (DS_RING + st), DS_WARPS);         // empty: one arrival per warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (; issued < min(DS_RING, total); issued++) issue(issued);
   }
@@ -492,123 +495,142 @@ __global__ void __launch_bounds__(DS_THREADS, 2) decode_attention_stream_g8_kern
       qa[h][0] = a.x; qa[h][1] = a.y; qa[h][2] = a.z; qa[h][3] = a.w;
       qb[h][0] = c4.x; qb[h][1] = c4.y; qb[h][2] = c4.z; qb[h][3] = c4.w;
     }
-    // the newest key's row, loaded now (after the wait) and stored once its chunk has landed
+    // the newest key's row, loaded now (after the wait): the copies issued earlier may predate it
     const bool patch = fresh < nk && tid < DS_HD;
     kf0 = patch ? kcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
     vf0 = patch ? vcache[(kvrow0 + fresh) * DS_HD + tid] : 0.0f;
+    if (patch) {
+      kvnew[tid] = kf0;
+      kvnew[DS_HD + tid] = vf0;
+    }
+    __syncthreads();
   }
   const float scale = (float)(1.0 / sqrt((double)DS_HD));
   float acc[DS_GMAX][4];
 #pragma unroll
   for (int g = 0; g < DS_GMAX; g++) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
 
-  for (int c = 0; c < total; c++) {
-    const int st = c % DS_RING;
-    uint8_t *chunk = ring + st * DS_CHUNK;
+  // The warps consume the ring independently: lane 0 of each warp waits for a chunk's copies itself, and
+  // a warp done with a chunk arrives on its stage's `empty` barrier (8 arrivals); thread 0 refills the
+  // stage once all eight have.  The newest key's row is read from kvnew, not from its chunk.  If a wait
+  // expires the abort flag makes every later wait return at once: the warps run on over stale data
+  // (every barrier of the block is still reached) and the block writes nothing.
+  const uint32_t empty0 = bar0 + 8 * DS_RING;
+  auto wait_full = [&](int c) {
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(bar0 + 8 * (c % DS_RING), (uint32_t)(c / DS_RING) & 1u, &s_abort, err, 62);
+    __syncwarp();
+    return __shfl_sync(0xffffffffu, ok, 0);
+  };
+  auto release = [&](int c) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * (c % DS_RING));
+    if (tid == 0 && c + DS_RING < total &&
+        mbar_wait(empty0 + 8 * (c % DS_RING), (uint32_t)(c / DS_RING) & 1u, &s_abort, err, 64))
+      issue(issued++);  // chunk c + DS_RING into the stage chunk c held
+  };
+  for (int c = 0; c < nck; c++) {  // scores
+    wait_full(c);
+    const uint8_t *chunk = ring + (c % DS_RING) * DS_CHUNK;
+    float v[16];  // [key j][head h]: partial dots over this lane's 8 dimensions
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int kr = 4 * warp + j;
+      const uint32_t sw = (uint32_t)((ck ^ (kr & 7)) << 4);
+      const bool isf = c * DS_CH + kr == fresh;
+      const float4 ka = isf ? *(const float4 *)(kvnew + 32 * box + 4 * ck)
+                            : *(const float4 *)(chunk + box * 4096 + kr * 128 + sw);
+      const float4 kb = isf ? *(const float4 *)(kvnew + 32 * (box + 2) + 4 * ck)
+                            : *(const float4 *)(chunk + (box + 2) * 4096 + kr * 128 + sw);
+      const float kd[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+      for (int h = 0; h < 4; h += 2) {  // heads h, h + 1 in one packed FP32 FMA (each lane an IEEE fma)
+        float2 x = make_float2(qa[h][0] * kd[0], qa[h + 1][0] * kd[0]);
+#pragma unroll
+        for (int e = 1; e < 8; e++) {
+          const float2 qq = e < 4 ? make_float2(qa[h][e], qa[h + 1][e]) : make_float2(qb[h][e - 4], qb[h + 1][e - 4]);
+          x = __ffma2_rn(qq, make_float2(kd[e], kd[e]), x);
+        }
+        v[4 * j + h] = x.x;
+        v[4 * j + h + 1] = x.y;
+      }
+    }
+    release(c);  // the chunk's K rows are in registers now
+    // reduce-scatter over the 16 lanes of the quad: after the level of offset o, a lane keeps the half
+    // of its values selected by its bit o
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) {
+      const bool up = (dg & o) != 0;
+#pragma unroll
+      for (int i = 0; i < o; i++) {
+        const float send = up ? v[i] : v[i + o];
+        const float keep = up ? v[i + o] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    {  // lane dg: key dg / 4 of the warp's four, head 4 hq + dg % 4
+      const int kr = 4 * warp + (dg >> 2), g = 4 * hq + (dg & 3);
+      if (c * DS_CH + kr < nk && g < G) pt[(c * DS_CH + kr) * DS_GMAX + g] = v[0] * scale;
+    }
+  }
+  __syncthreads();  // all scores: softmax statistics of head `warp` over the split
+  {
+    const int g = warp;
+    if (g < G) {
+      float mx = -INFINITY;
+      for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, pt[j * DS_GMAX + g]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      float sum = 0.0f;
+      for (int j = lane; j < nk; j += 32) {
+        const float e = expf(pt[j * DS_GMAX + g] - mx);
+        pt[j * DS_GMAX + g] = e;
+        sum += e;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (lane == 0) {
+        red[g * 2] = mx;
+        red[g * 2 + 1] = sum;
+      }
+    }
+  }
+  __syncthreads();
+  for (int c = nck; c < total; c++) {  // weighted V sum
+    wait_full(c);
+    const uint8_t *chunk = ring + (c % DS_RING) * DS_CHUNK;
+    const int cv = c - nck, rows = min(DS_CH, nk - cv * DS_CH);
+    const float *pr = pt + (size_t)cv * DS_CH * DS_GMAX;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int kr = 4 * warp + j;
+      if (kr < rows) {
+        const float4 vv = cv * DS_CH + kr == fresh ? *(const float4 *)(kvnew + DS_HD + 4 * lane)
+                                                   : *(const float4 *)(chunk + kr * (DS_HD * 4) + lane * 16);
+        const float4 pa = *(const float4 *)(pr + kr * DS_GMAX), pb = *(const float4 *)(pr + kr * DS_GMAX + 4);
+        const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+        for (int g = 0; g < DS_GMAX; g++) {  // packed FP32 FMAs: two dimensions per instruction
+          const float2 pp = make_float2(p8[g], p8[g]);
+          const float2 lo = __ffma2_rn(pp, make_float2(vv.x, vv.y), make_float2(acc[g][0], acc[g][1]));
+          const float2 hi = __ffma2_rn(pp, make_float2(vv.z, vv.w), make_float2(acc[g][2], acc[g][3]));
+          acc[g][0] = lo.x;
+          acc[g][1] = lo.y;
+          acc[g][2] = hi.x;
+          acc[g][3] = hi.y;
+        }
+      }
+    }
+    release(c);
+  }
+  __syncthreads();
+  if (s_abort) {  // leave only once every copy into this block's shared memory is done (bounded again)
     if (tid == 0) {
-      s_ok = mbar_wait(bar0 + 8 * st, (uint32_t)(c / DS_RING) & 1u, &s_abort, err, 62);
-      if (!s_ok) {  // leave only once every copy into this block's shared memory is done (bounded again)
-        volatile int no_abort = 0;
-        for (int cc = c; cc < issued; cc++)
-          mbar_wait(bar0 + 8 * (cc % DS_RING), (uint32_t)(cc / DS_RING) & 1u, &no_abort, err, 63);
-      }
+      volatile int no_abort = 0;
+      for (int cc = max(0, issued - DS_RING); cc < issued; cc++)
+        mbar_wait(bar0 + 8 * (cc % DS_RING), (uint32_t)(cc / DS_RING) & 1u, &no_abort, err, 63);
     }
-    __syncthreads();
-    if (!s_ok) return;
-    if (c < nck) {
-      const int r = fresh - c * DS_CH;
-      if (r >= 0 && r < DS_CH) {  // block-uniform
-        if (tid < DS_HD) *(float *)(chunk + ds_koff(r, tid)) = FUSED ? kvnew[tid] : kf0;
-        __syncthreads();
-      }
-      float v[16];  // [key j][head h]: partial dots over this lane's 8 dimensions
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int kr = 4 * warp + j;
-        const uint32_t sw = (uint32_t)((ck ^ (kr & 7)) << 4);
-        const float4 ka = *(const float4 *)(chunk + box * 4096 + kr * 128 + sw);
-        const float4 kb = *(const float4 *)(chunk + (box + 2) * 4096 + kr * 128 + sw);
-        const float kd[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
-#pragma unroll
-        for (int h = 0; h < 4; h += 2) {  // heads h, h + 1 in one packed FP32 FMA (each lane an IEEE fma)
-          float2 x = make_float2(qa[h][0] * kd[0], qa[h + 1][0] * kd[0]);
-#pragma unroll
-          for (int e = 1; e < 8; e++) {
-            const float2 qq = e < 4 ? make_float2(qa[h][e], qa[h + 1][e]) : make_float2(qb[h][e - 4], qb[h + 1][e - 4]);
-            x = __ffma2_rn(qq, make_float2(kd[e], kd[e]), x);
-          }
-          v[4 * j + h] = x.x;
-          v[4 * j + h + 1] = x.y;
-        }
-      }
-      // reduce-scatter over the 16 lanes of the quad: after the level of offset o, a lane keeps the half
-      // of its values selected by its bit o
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1) {
-        const bool up = (dg & o) != 0;
-#pragma unroll
-        for (int i = 0; i < o; i++) {
-          const float send = up ? v[i] : v[i + o];
-          const float keep = up ? v[i + o] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-      }
-      {  // lane dg: key dg / 4 of the warp's four, head 4 hq + dg % 4
-        const int kr = 4 * warp + (dg >> 2), g = 4 * hq + (dg & 3);
-        if (c * DS_CH + kr < nk && g < G) pt[(c * DS_CH + kr) * DS_GMAX + g] = v[0] * scale;
-      }
-      if (c == nck - 1) {  // all scores: softmax statistics of head `warp` over the split
-        __syncthreads();
-        const int g = warp;
-        if (g < G) {
-          float mx = -INFINITY;
-          for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, pt[j * DS_GMAX + g]);
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-          float sum = 0.0f;
-          for (int j = lane; j < nk; j += 32) {
-            const float e = expf(pt[j * DS_GMAX + g] - mx);
-            pt[j * DS_GMAX + g] = e;
-            sum += e;
-          }
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-          if (lane == 0) {
-            red[g * 2] = mx;
-            red[g * 2 + 1] = sum;
-          }
-        }
-      }
-    } else {
-      const int cv = c - nck, rows = min(DS_CH, nk - cv * DS_CH);
-      const int r = fresh - cv * DS_CH;
-      if (r >= 0 && r < DS_CH) {  // block-uniform
-        if (tid < DS_HD) ((float *)chunk)[r * DS_HD + tid] = FUSED ? kvnew[DS_HD + tid] : vf0;
-        __syncthreads();
-      }
-      const float *pr = pt + (size_t)cv * DS_CH * DS_GMAX;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int kr = 4 * warp + j;
-        if (kr < rows) {
-          const float4 vv = *(const float4 *)(chunk + kr * (DS_HD * 4) + lane * 16);
-          const float4 pa = *(const float4 *)(pr + kr * DS_GMAX), pb = *(const float4 *)(pr + kr * DS_GMAX + 4);
-          const float p8[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
-#pragma unroll
-          for (int g = 0; g < DS_GMAX; g++) {  // packed FP32 FMAs: two dimensions per instruction
-            const float2 pp = make_float2(p8[g], p8[g]);
-            const float2 lo = __ffma2_rn(pp, make_float2(vv.x, vv.y), make_float2(acc[g][0], acc[g][1]));
-            const float2 hi = __ffma2_rn(pp, make_float2(vv.z, vv.w), make_float2(acc[g][2], acc[g][3]));
-            acc[g][0] = lo.x;
-            acc[g][1] = lo.y;
-            acc[g][2] = hi.x;
-            acc[g][3] = hi.y;
-          }
-        }
-      }
-    }
-    __syncthreads();  // chunk consumed: its stage takes the chunk DS_RING ahead
-    if (tid == 0 && issued < total) issue(issued++);
+    return;
   }
   // the warps' value sums, added in warp order through the ring (every copy into it has completed)
   float *ws = (float *)ring;  // [warp][8 heads][128]
