@@ -20,10 +20,11 @@
 // Three kernels:
 //   1. prologue: RMSNorm (the GEMV's expression) and the split into x3[3][NT][K] (NT = M rounded up
 //      to 16, 32 or 64; rows M..NT-1 zero), one block per 1024 elements of a row;
-//   2. stream-K GEMM: one persistent CTA per SM.  The iterations (128-row weight tile t, 64-wide
-//      K block kb), t-major, are cut into gridDim.x equal contiguous ranges, so every SM streams
-//      the same number of weight bytes whatever the tile count.  Warp 0 issues TMA loads of the
-//      W tile and the matching 3 x NT x 64 slice of x3 through a 5-9 stage ring (SWIZZLE_128B,
+//   2. stream-K GEMM: persistent CTAs, two per SM (one for 64-row term tiles).  The iterations
+//      (128-row weight tile t, 64-wide K block kb), t-major, are cut into gridDim.x equal contiguous
+//      ranges, so every SM streams the same number of weight bytes whatever the tile count.  Warp 0
+//      issues TMA loads of the W tile and the matching 3 x NT x 64 slice of x3 through a 3-5 stage
+//      ring (SWIZZLE_128B,
 //      K-major; the first stages' W loads go out before the programmatic-dependency wait, since
 //      weights never depend on the previous kernel), warp 1 issues
 //      tcgen05.mma.cta_group::1.kind::f16 (M = 128, N = 3 NT), warps 2-5 sum the accumulators and
@@ -43,17 +44,22 @@ constexpr int SK_BM = 128, SK_ACC_MAX = 4;
 
 template <int NT>
 struct SkinnyShape {
-  static constexpr int STAGES = NT == 16 ? 9 : (NT == 32 ? 7 : 5);
+  // Two CTAs per SM for 16- and 32-row term tiles (their MMA and epilogue latencies overlap: the 70B
+  // gate/up shard at M = 8 took 169 us with one 9-stage CTA per SM and 155 us with two 5-stage CTAs),
+  // one for 64-row tiles, whose stages are too large to fit two rings.
+  static constexpr int CTAS_PER_SM = NT == 64 ? 1 : 2;
+  static constexpr int STAGES = NT == 16 ? 5 : (NT == 32 ? 3 : 5);
   static constexpr int A_BYTES = SK_BM * BK * 2;
   static constexpr int B_BYTES = 3 * NT * BK * 2;  // multiple of 1024: the tile stays swizzle-aligned
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
   static constexpr int ACC_STRIDE = NT == 16 ? 64 : (NT == 32 ? 128 : 256);  // >= 3 NT TMEM columns
-  static constexpr int ACC = NT == 64 ? 2 : 4;                                // accumulators in the ring
+  static constexpr int ACC = NT == 16 ? 4 : 2;                                // accumulators in the ring
   static constexpr int GK = NT == 16 ? 1 : (NT == 32 ? 4 : 8);  // K blocks per accumulator (4 GK MMAs per chain)
   static constexpr int TMEM_COLS = ACC * ACC_STRIDE;                          // 256 or 512
   static_assert(SMEM <= 232448, "shared memory per CTA");
-  static_assert(TMEM_COLS <= 512 && ACC <= SK_ACC_MAX, "tensor memory");
+  static_assert(CTAS_PER_SM * (SMEM + 1024) <= 233472, "shared memory per SM");
+  static_assert(CTAS_PER_SM * TMEM_COLS <= 512 && ACC <= SK_ACC_MAX, "tensor memory");
   static_assert((2 * STAGES + 2 * SK_ACC_MAX + 1) * 8 + 8 <= 256, "barrier area");
 };
 
@@ -175,7 +181,7 @@ __global__ void __launch_bounds__(256) skinny_prep_kernel(const float *x, int ld
 }
 
 template <int NT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, float *part,
                        int M, int N, int kbs, long long T, int pmax, uint32_t idesc, int *err) {
   using S = SkinnyShape<NT>;
@@ -596,7 +602,9 @@ SkinnyPlan skinny_plan(int M, int N, int K, int device) {
   q.tiles = (N + SK_BM - 1) / SK_BM;
   q.kbs = (K + BK - 1) / BK;
   q.iters = (long long)q.tiles * q.kbs;
-  q.grid = (int)std::min<long long>(sm_count(device), q.iters);
+  const int per_sm = q.nt == 16 ? SkinnyShape<16>::CTAS_PER_SM
+                                : (q.nt == 32 ? SkinnyShape<32>::CTAS_PER_SM : SkinnyShape<64>::CTAS_PER_SM);
+  q.grid = (int)std::min<long long>((long long)per_sm * sm_count(device), q.iters);
   const long long per = q.iters / q.grid;  // every range holds per or per + 1 iterations
   q.pmax = (int)std::min<long long>(q.grid, (q.kbs + per - 1) / per + 1);
   q.x3_bytes = ((uint64_t)3 * q.nt * K * 2 + 255) & ~255ull;
