@@ -76,11 +76,11 @@ TP_SMALL = dict(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_la
                 num_key_value_heads=8, max_positions=64, tie_word_embeddings=False, eos_token_ids=())
 
 # DRAM read + write bytes of one gemm_skinny_kernel launch on the dominant decode shape (70B gate/up
-# shard, M = 8, TP1: 57344 x 8192 BF16 = 939.5 MB of weights): dram__bytes_read.sum 941,520,640 +
-# dram__bytes_write.sum 5,536,256 from one ncu capture (--set full, --clock-control none) of
-# `bench.py --workload kernel --steps 2 --warmup 0` on a B200 with the current kernel.  Keyed by the
-# tensor-parallel size (the other sizes' shard shapes were not captured).
-SKINNY_GATE_UP_TRAFFIC = {1: 947_056_896}
+# shard, M = 8, TP1: 57344 x 8192 BF16 = 939.5 MB of weights): dram__bytes_read.sum 942,707,712 +
+# dram__bytes_write.sum 6,144,512 from one ncu capture (--set full, --clock-control none) of
+# `bench.py --workload kernel --steps 2 --warmup 0` on a B200 with the current kernel (two CTAs per SM).
+# Keyed by the tensor-parallel size (the other sizes' shard shapes were not captured).
+SKINNY_GATE_UP_TRAFFIC = {1: 948_852_224}
 
 
 def peaks():
