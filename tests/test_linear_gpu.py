@@ -171,7 +171,7 @@ def same_class(y, ref, tol=TOL):
 def test_nonfinite_activations_on_the_gemv(session):
     """The reference's CPU Linear keeps IEEE semantics (cpu/src/test/scala/scalatorch/cpu/BackendSuite.scala:22-43):
     +-Inf, NaN, +-FLT_MAX and subnormal activations on the products the library runs as the vector GEMV
-    (M = 1, and every M below the skinny form's work threshold)."""
+    (every M below the skinny form's work threshold, these included)."""
     for m in NONFINITE_MS:
         for rot in range(len(SPECIALS)):
             x, w = nonfinite_case(m, rot)
@@ -302,7 +302,8 @@ def _adapter(session, rng, n, k, rank, alpha, zero_b=False):
 def test_linear_with_adapters_matches_oracle(session, m):
     """nn.Linear.apply with its own LoRA adapter, two LinearAdapterScope entries (one with a negative
     multiplier) and a bias (Linear.scala:11-17), in the reference's operation order; the base
-    product takes the GEMV (M = 1) or the skinny tensor-core form (M >= 2)."""
+    product takes the GEMV below the skinny form's work threshold (M = 1, 3, 16 here) or the skinny
+    tensor-core form (M = 40)."""
     rng = np.random.default_rng(m)
     n, k = 1536, 576
     x = rng.standard_normal((m, k)).astype(np.float32)
