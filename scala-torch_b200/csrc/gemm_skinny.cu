@@ -636,7 +636,10 @@ void launch_gemm(const SkinnyPlan &q, const CUtensorMap &tw, const CUtensorMap &
 
 bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w) {
   static const int enabled = env_int("STB_SKINNY", 1);
-  static const int min_rows = env_int("STB_SKINNY_MIN_ROWS", 2);
+  // One row too: above the work threshold the form streams weights faster than the SIMT GEMV even for
+  // a single token (70B gate/up shard at M = 1: 146 us here, 160 us on the GEMV; the 70B-shaped
+  // batch-1 decode 42.7 vs 31.5 tok/s).
+  static const int min_rows = env_int("STB_SKINNY_MIN_ROWS", 1);
   static const int max_rows = env_int("STB_SKINNY_MAX_ROWS", 1 << 30);
   // Below ~16M multiply-adds the three launches cost more than the SIMT GEMV's one (measured: the
   // single-Linear 16 x 1536 x 576 takes 12.3 us on the GEMV, 13.3 us here; 32 x 1536 x 576 takes

@@ -2399,10 +2399,16 @@ int stb_llama_generate(stb_llama *m, const int64_t *prompt, int batch, int promp
       }
       STB_CUDA(cudaEventRecord(ev[1], s->stream));
       if (max_new > 1) {
-        // decode: tokens[b*count + count-1] was rewritten in place; compact them to rows 0..batch
+        // decode: tokens[b*count + count-1] was rewritten in place; compact them to rows 0..batch.  The
+        // strided source and the packed destination overlap once batch > last - 1 (row 0's token sits
+        // at index last - 1, which row last - 1's destination overwrites), and overlapping copies are
+        // undefined: gather into best_all (batch * 8 bytes at least, rewritten before its next read)
+        // and copy back.
         if (last > 1) {
-          STB_CUDA(cudaMemcpy2DAsync((void *)c->tokens, 8, (const void *)(c->tokens + (uint64_t)(last - 1) * 8),
+          STB_CUDA(cudaMemcpy2DAsync((void *)c->best_all, 8, (const void *)(c->tokens + (uint64_t)(last - 1) * 8),
                                      (size_t)last * 8, 8, batch, cudaMemcpyDeviceToDevice, s->stream));
+          STB_CUDA(cudaMemcpyAsync((void *)c->tokens, (const void *)c->best_all, (size_t)batch * 8,
+                                   cudaMemcpyDeviceToDevice, s->stream));
         }
         StepArgs d;
         d.rows = batch;

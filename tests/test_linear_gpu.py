@@ -179,9 +179,9 @@ def test_nonfinite_activations_on_the_gemv(session):
 
 
 def test_nonfinite_activations_on_the_skinny_form():
-    """The same IEEE cases on the tensor-core skinny form (STB_SKINNY_MIN_WORK=0 routes M >= 2 there; read
-    once per process, so a child process): the three-term BF16 split keeps Inf / NaN in its first term
-    and truncates a finite value above BF16's largest, so no Inf - Inf appears."""
+    """The same IEEE cases on the tensor-core skinny form (STB_SKINNY_MIN_WORK=0 routes every M there, one
+    row included; read once per process, so a child process): the three-term BF16 split keeps Inf / NaN
+    in its first term and truncates a finite value above BF16's largest, so no Inf - Inf appears."""
     import subprocess
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
@@ -199,7 +199,7 @@ def test_nonfinite_activations_on_the_skinny_form():
         "        xd, wd = s.upload(x), s.upload_weight(w, ffm.STB_BF16)\n"
         "        l0 = s.launches\n"
         "        y = s.linear(xd, wd)\n"
-        "        assert s.launches - l0 == (1 if m == 1 else 3), (m, s.launches - l0)\n"
+        "        assert s.launches - l0 == 3, (m, s.launches - l0)\n"
         "        same_class(s.download(y), oracle.linear(x, w, oracle.BF16))\n"
         "        for t in (xd, wd, y):\n"
         "            s.release(t)\n"
