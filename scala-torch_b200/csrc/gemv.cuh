@@ -437,7 +437,7 @@ int gemv_grid_blocks(int M, int N, GemvConfig cfg, int epi);
 // activations split into three BF16 terms (FP32-accurate), with the same prologue (RMSNorm) and
 // epilogues as the vector kernel.  p.stop must be null.  skinny_eligible() says whether a
 // problem takes it (STB_SKINNY=0 keeps the vector kernel; STB_SKINNY_MIN_ROWS / _MAX_ROWS bound
-// M, default 2 .. unbounded); skinny_scratch_bytes() is the scratch one call of (M, N, K) needs.
+// M, default 1 .. unbounded); skinny_scratch_bytes() is the scratch one call of (M, N, K) needs.
 bool skinny_eligible(int M, int N, int K, int w_dtype, const void *w);
 uint64_t skinny_scratch_bytes(int M, int N, int K, int device);
 // Sets the kernels' shared-memory limits on `device` (before a graph capture that launches them).
