@@ -87,8 +87,10 @@ int stb_host_free(void *host);
  *   y[M,N] = x[M,K] . W[N,K]^T (+ bias[N])
  * x, y, bias: Float32 row-major device buffers; W: the (out,in) weight exactly as stored in the
  * safetensors payload (w_dtype STB_BF16 or STB_F16; STB_F32 is accepted too), widened in
- * registers.  FP32 activations, FP32 FMA accumulation (decode GEMV family).  M = 0 / N = 0 are
- * no-ops; K = 0 writes bias or zeros.  bias may be 0. */
+ * registers.  FP32-accurate activations: the SIMT GEMV (FP32 FMA accumulation), or, for BF16 products
+ * above 2^24 multiply-adds, the tcgen05 skinny form (activations split into three BF16 terms, FP32
+ * accumulation); both within 1e-5 relative of the FP32 product.  M = 0 / N = 0 are no-ops; K = 0
+ * writes bias or zeros.  bias may be 0. */
 int stb_linear(stb_session *s, uint64_t x, uint64_t w, int w_dtype, uint64_t bias, uint64_t y,
                int M, int N, int K);
 /* Same product with explicit leading dimensions (elements) for x and y. */
